@@ -1,0 +1,175 @@
+/*
+ * tvara_capi -- C ABI of the B200 decode/prefill engine.
+ *
+ * The first eleven functions replace, with identical signatures and
+ * semantics, the reference engine's ABI in core/include/tvara/c_api.h:13-24
+ * (implemented in core/src/c_api.cpp:38-78), so the reference's
+ * python/tvara/native.py (NativeModel) and speculative.py bind this library
+ * unchanged through TVARA_LIBRARY.  Everything after them is additive.
+ *
+ * Conventions (as in the reference): every call clears the calling thread's
+ * error string first; failures return NULL / 0 / -1 and leave a message
+ * readable with tvara_last_error() until the next call on that thread.  One
+ * mutex per handle serialises the sequence and step calls.  Output buffers
+ * are caller-owned host memory; logits are F32 row-major [rows, vocab].
+ */
+#ifndef TVARA_CAPI_H
+#define TVARA_CAPI_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define TVARA_API __declspec(dllexport)
+#else
+#define TVARA_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct tvara_model tvara_model;
+
+/* ---- reference ABI (core/include/tvara/c_api.h:13-24) ------------------ */
+
+/* c_api.h:13 / c_api.cpp:38-43.  Loads a Llama GGUF (F32, F16, Q4_0, Q8_0,
+ * Q4_K tensors) onto the current CUDA device, keeping quantised blocks packed
+ * in HBM, with a paged KV pool of max_blocks blocks of block_tokens positions
+ * (F32 KV, one GPU).  NULL on error. */
+TVARA_API tvara_model* tvara_model_open(const char* utf8_path, size_t max_blocks, size_t block_tokens);
+/* c_api.h:14.  Releases the handle and its device memory; NULL-safe. */
+TVARA_API void tvara_model_close(tvara_model* model);
+/* c_api.h:15-16.  0 with "closed model" for a NULL handle. */
+TVARA_API size_t tvara_model_vocab_size(tvara_model* model);
+TVARA_API size_t tvara_model_context_size(tvara_model* model);
+/* c_api.h:17.  Thread-local message of the last failed call. */
+TVARA_API const char* tvara_last_error(void);
+/* c_api.h:18.  JSON object of every GGUF metadata key, serialised as the
+ * reference does (c_api.cpp:19-41); owned by the handle. */
+TVARA_API const char* tvara_model_metadata(tvara_model* model);
+/* c_api.h:19.  New empty sequence; ids start at 1; 0 on error. */
+TVARA_API uint64_t tvara_sequence_create(tvara_model* model);
+/* c_api.h:20.  Appends one token and writes its vocab logits; count must
+ * equal the vocabulary.  All-or-nothing: on failure the sequence is
+ * unchanged.  0 / -1. */
+TVARA_API int tvara_sequence_decode(tvara_model* model, uint64_t sequence, uint32_t token, float* logits,
+                                    size_t count);
+/* c_api.h:21.  Releases the sequence's KV blocks.  0 / -1. */
+TVARA_API int tvara_sequence_drop(tvara_model* model, uint64_t sequence);
+/* c_api.h:22 / c_api.cpp:63-72.  Appends token_count tokens of one sequence
+ * (a prefill chunk or a speculative verify) and writes every row's logits;
+ * count must equal token_count*vocab.  On failure the sequence is truncated
+ * back to its entry length.  0 / -1. */
+TVARA_API int tvara_sequence_decode_batch(tvara_model* model, uint64_t sequence, const uint32_t* tokens,
+                                          size_t token_count, float* logits, size_t count);
+/* c_api.h:24.  Shortens a sequence (never extends it).  0 / -1. */
+TVARA_API int tvara_sequence_truncate(tvara_model* model, uint64_t sequence, size_t length);
+
+/* ---- additive: open options ------------------------------------------- */
+
+enum { TVARA_KV_F32 = 0, TVARA_KV_F16 = 1 };
+
+typedef struct tvara_open_options {
+    uint32_t struct_size;      /* sizeof(tvara_open_options) */
+    int32_t device;            /* CUDA ordinal; -1 keeps the current device */
+    uint32_t kv_dtype;         /* TVARA_KV_F32 (reference numerics) or TVARA_KV_F16 */
+    uint32_t max_step_tokens;  /* tokens per device step (scratch sizing); 0 = 2048 */
+    uint32_t tp_rank;          /* tensor-parallel rank of this handle */
+    uint32_t tp_size;          /* tensor-parallel group size; 0 or 1 = no TP */
+    const void* nccl_id;       /* 128-byte ncclUniqueId shared by the group (tp_size > 1) */
+} tvara_open_options;
+
+/* tvara_model_open with options; NULL options equal tvara_model_open. */
+TVARA_API tvara_model* tvara_model_open_ex(const char* utf8_path, size_t max_blocks, size_t block_tokens,
+                                           const tvara_open_options* options);
+
+/* ---- additive: ragged multi-sequence step ----------------------------- */
+
+enum {
+    TVARA_STEP_ALL_LOGITS = 1  /* one logits row per token instead of per sequence */
+};
+
+/* One device step over a ragged batch: sequence i appends
+ * tokens[cu_tokens[i] .. cu_tokens[i+1]) (cu_tokens has n_seq+1 entries,
+ * cu_tokens[0] == 0, each range non-empty, each sequence listed once).
+ * Prefill chunks and single decode tokens mix freely; this is the
+ * scheduler's iteration (python/tvara/scheduler.py:98-122) as one call.
+ * Outputs (either may be NULL):
+ *   logits  F32 [rows, vocab], rows = n_seq (last token of each sequence)
+ *           or total tokens with TVARA_STEP_ALL_LOGITS; count = rows*vocab
+ *   argmax  uint32 [rows], the first index of each row's maximum
+ * All-or-nothing: on failure every listed sequence is truncated back to its
+ * length at entry.  0 / -1. */
+TVARA_API int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t* sequences,
+                               const uint32_t* cu_tokens, const uint32_t* tokens, uint32_t flags, float* logits,
+                               size_t count, uint32_t* argmax, size_t argmax_count);
+
+/* ---- additive: sequence management (core/include/tvara/kv.hpp) -------- */
+
+/* PagedCache::fork (kv.hpp:123-129): a new sequence sharing every block;
+ * later appends copy a shared partial tail (copy-on-write).  0 on error. */
+TVARA_API uint64_t tvara_sequence_fork(tvara_model* model, uint64_t sequence);
+/* Committed length of a sequence.  0 / -1. */
+TVARA_API int tvara_sequence_length(tvara_model* model, uint64_t sequence, size_t* length);
+/* Pool state: free blocks and capacity.  0 / -1. */
+TVARA_API int tvara_kv_stats(tvara_model* model, size_t* available, size_t* max_blocks);
+/* PagedCache::audit (kv.hpp:138-146) including prefix-cache references.
+ * 0 when the invariants hold, -1 with the violated invariant otherwise. */
+TVARA_API int tvara_kv_audit(tvara_model* model);
+/* Block table of a sequence: up to capacity (id, generation) pairs; returns
+ * the table length through *count.  0 / -1. */
+TVARA_API int tvara_sequence_blocks(tvara_model* model, uint64_t sequence, uint64_t* ids, uint64_t* generations,
+                                    size_t capacity, size_t* count);
+/* Reference count of pool block `id` (BlockPool::references_by_id). */
+TVARA_API int tvara_kv_references(tvara_model* model, size_t id, size_t* references);
+
+/* ---- additive: radix prefix cache (core/include/tvara/radix.hpp) ------ */
+
+/* RadixCache::insert + attach (radix.hpp:41-79): caches `sequence`'s KV
+ * under its token path (length must equal token_count); returns the node id,
+ * 0 on error. */
+TVARA_API uint64_t tvara_prefix_insert(tvara_model* model, const int32_t* tokens, size_t token_count,
+                                       uint64_t sequence);
+/* RadixCache::reuse (radix.hpp:90-96): a new sequence importing the longest
+ * cached prefix of tokens (whole blocks unless partial != 0); the reused
+ * length is written to *reused.  0 on error. */
+TVARA_API uint64_t tvara_prefix_reuse(tvara_model* model, const int32_t* tokens, size_t token_count, int partial,
+                                      size_t* reused);
+/* RadixCache::lookup: node and matched token count. */
+TVARA_API int tvara_prefix_lookup(tvara_model* model, const int32_t* tokens, size_t token_count, uint64_t* node,
+                                  size_t* matched);
+/* pin / unpin / touch a node and its ancestors (radix.hpp:99-105). */
+TVARA_API int tvara_prefix_pin(tvara_model* model, uint64_t node);
+TVARA_API int tvara_prefix_unpin(tvara_model* model, uint64_t node);
+TVARA_API int tvara_prefix_touch(tvara_model* model, uint64_t node);
+/* RadixCache::evict_one (radix.hpp:113-117): 1 evicted, 0 nothing to evict,
+ * -1 error. */
+TVARA_API int tvara_prefix_evict_one(tvara_model* model);
+/* Number of cached nodes (RadixCache::size). */
+TVARA_API size_t tvara_prefix_size(tvara_model* model);
+
+/* ---- additive: host-only KV accounting book --------------------------- */
+/* The engine's block accounting (kv.hpp:36-165 semantics) without a model or
+ * GPU, so callers and tests can replay operation sequences.  Handles are
+ * independent of any model. */
+typedef struct tvara_kv_book tvara_kv_book;
+TVARA_API tvara_kv_book* tvara_kv_book_new(size_t layers, size_t kv_heads, size_t head_dim, size_t block_tokens,
+                                           size_t max_blocks);
+TVARA_API void tvara_kv_book_free(tvara_kv_book* book);
+TVARA_API uint64_t tvara_kv_book_create(tvara_kv_book* book);
+/* Returns 0, -1 on error, -2 when the pool is exhausted (state unchanged). */
+TVARA_API int tvara_kv_book_append(tvara_kv_book* book, uint64_t sequence);
+TVARA_API int tvara_kv_book_drop(tvara_kv_book* book, uint64_t sequence);
+TVARA_API uint64_t tvara_kv_book_fork(tvara_kv_book* book, uint64_t sequence);
+TVARA_API int tvara_kv_book_truncate(tvara_kv_book* book, uint64_t sequence, size_t length);
+TVARA_API uint64_t tvara_kv_book_import(tvara_kv_book* book, uint64_t sequence, size_t length);
+TVARA_API size_t tvara_kv_book_available(tvara_kv_book* book);
+TVARA_API size_t tvara_kv_book_references(tvara_kv_book* book, size_t id);
+TVARA_API int tvara_kv_book_table(tvara_kv_book* book, uint64_t sequence, uint64_t* ids, uint64_t* generations,
+                                  size_t capacity, size_t* count);
+TVARA_API int tvara_kv_book_audit(tvara_kv_book* book);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TVARA_CAPI_H */

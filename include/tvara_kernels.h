@@ -1,0 +1,77 @@
+/*
+ * tvara_kernels -- kernel-level C ABI of the B200 engine (device pointers).
+ *
+ * These expose single hot-path kernels without a model handle, for callers
+ * that manage their own device memory (and for the standalone GEMV and
+ * attention benchmarks).  Pointers marked "device" are CUDA device memory of
+ * the current device; `stream` is a cudaStream_t (NULL = legacy default).
+ * Every function returns 0 on success and -1 on failure, with the message in
+ * tvara_last_error() (include/tvara_capi.h).  Launches are asynchronous.
+ */
+#ifndef TVARA_KERNELS_H
+#define TVARA_KERNELS_H
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tvara_capi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGUF storage types (reference core/include/tvara/gguf.hpp:152-170). */
+enum { TVARA_F32 = 0, TVARA_F16 = 1, TVARA_Q4_0 = 2, TVARA_Q8_0 = 8, TVARA_Q4_K = 12 };
+
+/* Replaces quant::dequantize_q8_0 / q4_0 / q4_k and half_to_float
+ * (core/include/tvara/quant.hpp:14-84): `blocks` GGUF blocks (device) ->
+ * F32 (device), bit-identical to the reference. */
+TVARA_API int tvara_dequantize(int type, const void* blocks, size_t nblocks, float* out, void* stream);
+
+/* Bytes of the engine's packed layout for a [rows][cols] matrix: the codes of
+ * every row (16-byte aligned rows) followed, at a 256-byte aligned offset, by
+ * the block headers. */
+TVARA_API size_t tvara_packed_bytes(int type, size_t rows, size_t cols);
+/* GGUF rows (device) -> engine layout (device, tvara_packed_bytes long). */
+TVARA_API int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream);
+
+/* Replaces quant::matvec_f32 over dequantised weights / Matrix::multiply and
+ * prefill_reference (quant.hpp:163-196, prefill.hpp:12-18):
+ * y[t][r] = sum_k W[r][k] * x[t][k] for t < tokens, W packed (device), x and y
+ * F32 row-major (device).  Dequantisation happens in registers; F32
+ * accumulation. */
+TVARA_API int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, const float* x,
+                                 size_t tokens, float* y, void* stream);
+
+/* Paged GQA attention, replacing fused_paged_attention /
+ * fused_prompt_attention (core/include/tvara/attention.hpp:57-89) for many
+ * query rows at once.  Query row i attends to positions [0, visible[i]) of its
+ * block list tables[table_offset[i] ..]; query head h reads KV head
+ * h / (heads / kv_heads).  Pool layout (elements of kv_dtype): block b, layer
+ * l, kind (0 K, 1 V), KV head g, slot s, element e at
+ *   ((((b*layers + l)*2 + kind)*kv_heads + g)*block_tokens + s)*head_dim + e. */
+typedef struct tvara_attention_args {
+    uint32_t struct_size;       /* sizeof(tvara_attention_args) */
+    uint32_t kv_dtype;          /* TVARA_KV_F32 or TVARA_KV_F16 */
+    uint32_t heads, kv_heads, head_dim, block_tokens;
+    uint32_t layers, layer;
+    size_t max_blocks;
+    size_t n_queries;
+    const float* q;             /* device [n_queries][heads*head_dim] */
+    float* out;                 /* device [n_queries][heads*head_dim] */
+    const void* pool;           /* device KV pool */
+    const int32_t* tables;      /* host: concatenated block ids */
+    size_t tables_len;
+    const uint32_t* table_offset; /* host [n_queries] */
+    const uint32_t* visible;      /* host [n_queries], each >= 1 */
+} tvara_attention_args;
+
+/* Device scratch (bytes) tvara_paged_attention needs for these arguments. */
+TVARA_API size_t tvara_paged_attention_workspace(const tvara_attention_args* args);
+/* Runs the attention; workspace is device memory of at least the size above. */
+TVARA_API int tvara_paged_attention(const tvara_attention_args* args, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TVARA_KERNELS_H */

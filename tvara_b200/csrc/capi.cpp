@@ -1,0 +1,406 @@
+// C ABI of the engine (include/tvara_capi.h).  The first eleven entry points
+// keep the reference's contract (core/src/c_api.cpp:38-78): each clears the
+// thread's error string, catches every exception into it, and serialises
+// work on a handle with one mutex.
+#include "../../include/tvara_capi.h"
+
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <mutex>
+#include <string>
+
+#include "engine.hpp"
+
+struct tvara_model {
+    std::unique_ptr<tvara::Engine> engine;
+    std::mutex mutex;
+};
+
+struct tvara_kv_book {
+    tvara::PagedBook book;
+    explicit tvara_kv_book(tvara::CacheGeometry g) : book(g) {}
+};
+
+namespace tvara {
+std::string& last_error() {
+    thread_local std::string message;
+    return message;
+}
+}  // namespace tvara
+
+// The calling thread's message (evaluated per use: the string is thread-local).
+#define error_message (::tvara::last_error())
+
+namespace {
+
+template <class R, class F>
+R guarded(R fail, F&& body) {
+    error_message.clear();
+    try {
+        return body();
+    } catch (const std::exception& e) {
+        error_message = e.what();
+        return fail;
+    } catch (...) {
+        error_message = "unknown native error";
+        return fail;
+    }
+}
+
+tvara::Engine& engine_of(tvara_model* m) {
+    if (!m || !m->engine) throw std::invalid_argument("closed model");
+    TVARA_CUDA(cudaSetDevice(m->engine->device()));
+    return *m->engine;
+}
+
+tvara_model* open_model(const char* path, size_t blocks, size_t tokens, const tvara_open_options* o) {
+    if (!path || !*path) throw std::invalid_argument("empty model path");
+    tvara::EngineOptions opt;
+    if (o) {
+        if (o->struct_size < sizeof(tvara_open_options)) throw std::invalid_argument("invalid open options size");
+        opt.device = o->device;
+        if (o->kv_dtype > TVARA_KV_F16) throw std::invalid_argument("invalid KV dtype");
+        opt.kv_f16 = o->kv_dtype == TVARA_KV_F16;
+        if (o->max_step_tokens) opt.max_step_tokens = int(o->max_step_tokens);
+        opt.tp_rank = int(o->tp_rank);
+        opt.tp_size = o->tp_size ? int(o->tp_size) : 1;
+        if (o->nccl_id) {
+            std::memcpy(opt.nccl_id.data(), o->nccl_id, opt.nccl_id.size());
+            opt.has_nccl_id = true;
+        }
+    }
+    auto m = std::make_unique<tvara_model>();
+    m->engine = std::make_unique<tvara::Engine>(path, blocks, tokens, opt);
+    return m.release();
+}
+}  // namespace
+
+extern "C" {
+
+tvara_model* tvara_model_open(const char* path, size_t max_blocks, size_t block_tokens) {
+    return guarded<tvara_model*>(nullptr, [&] { return open_model(path, max_blocks, block_tokens, nullptr); });
+}
+
+tvara_model* tvara_model_open_ex(const char* path, size_t max_blocks, size_t block_tokens,
+                                 const tvara_open_options* options) {
+    return guarded<tvara_model*>(nullptr, [&] { return open_model(path, max_blocks, block_tokens, options); });
+}
+
+void tvara_model_close(tvara_model* model) {
+    if (model && model->engine) cudaSetDevice(model->engine->device());
+    delete model;
+}
+
+size_t tvara_model_vocab_size(tvara_model* model) {
+    if (!model) {
+        error_message = "closed model";
+        return 0;
+    }
+    return model->engine->config().vocab;
+}
+
+size_t tvara_model_context_size(tvara_model* model) {
+    if (!model) {
+        error_message = "closed model";
+        return 0;
+    }
+    return model->engine->config().context;
+}
+
+const char* tvara_last_error(void) { return error_message.c_str(); }
+
+const char* tvara_model_metadata(tvara_model* model) {
+    if (!model) {
+        error_message = "closed model";
+        return nullptr;
+    }
+    return model->engine->metadata().c_str();
+}
+
+uint64_t tvara_sequence_create(tvara_model* model) {
+    return guarded<uint64_t>(0, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        return e.book().create_sequence();
+    });
+}
+
+int tvara_sequence_decode(tvara_model* model, uint64_t sequence, uint32_t token, float* logits, size_t count) {
+    return guarded<int>(-1, [&] {
+        if (!model || !logits || count != model->engine->config().vocab)
+            throw std::invalid_argument("invalid logit output buffer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const uint32_t cu[2] = {0, 1};
+        e.step({&sequence, 1}, {cu, 2}, {&token, 1}, false, logits, nullptr);
+        return 0;
+    });
+}
+
+int tvara_sequence_drop(tvara_model* model, uint64_t sequence) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.book().drop(sequence);
+        return 0;
+    });
+}
+
+int tvara_sequence_decode_batch(tvara_model* model, uint64_t sequence, const uint32_t* tokens, size_t token_count,
+                                float* logits, size_t count) {
+    return guarded<int>(-1, [&] {
+        if (!model || (!tokens && token_count) || (!logits && count)) throw std::invalid_argument("invalid batch buffers");
+        const auto vocab = model->engine->config().vocab;
+        if (token_count > std::numeric_limits<size_t>::max() / vocab || count != token_count * vocab)
+            throw std::invalid_argument("invalid batch dimensions");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const auto length = e.book().sequence(sequence).length;
+        if (token_count > e.config().context - length) throw std::invalid_argument("batch exceeds context");
+        for (size_t i = 0; i < token_count; ++i)
+            if (tokens[i] >= vocab) throw std::invalid_argument("invalid batch token");
+        if (!token_count) return 0;
+        const uint32_t cu[2] = {0, uint32_t(token_count)};
+        e.step({&sequence, 1}, {cu, 2}, {tokens, token_count}, true, logits, nullptr);
+        return 0;
+    });
+}
+
+int tvara_sequence_truncate(tvara_model* model, uint64_t sequence, size_t length) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.book().truncate(sequence, length);
+        return 0;
+    });
+}
+
+int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t* sequences, const uint32_t* cu_tokens,
+                     const uint32_t* tokens, uint32_t flags, float* logits, size_t count, uint32_t* argmax,
+                     size_t argmax_count) {
+    return guarded<int>(-1, [&] {
+        if (!model || !n_seq || !sequences || !cu_tokens || !tokens) throw std::invalid_argument("invalid batch buffers");
+        if (flags & ~uint32_t(TVARA_STEP_ALL_LOGITS)) throw std::invalid_argument("unknown step flags");
+        const size_t total = cu_tokens[n_seq];
+        const bool all = flags & TVARA_STEP_ALL_LOGITS;
+        const size_t rows = all ? total : n_seq;
+        const auto vocab = model->engine->config().vocab;
+        if (rows > std::numeric_limits<size_t>::max() / vocab) throw std::invalid_argument("invalid batch dimensions");
+        if (logits && count != rows * vocab) throw std::invalid_argument("invalid logit output buffer");
+        if (argmax && argmax_count != rows) throw std::invalid_argument("invalid argmax output buffer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.step({sequences, n_seq}, {cu_tokens, n_seq + 1}, {tokens, total}, all, logits, argmax);
+        return 0;
+    });
+}
+
+uint64_t tvara_sequence_fork(tvara_model* model, uint64_t sequence) {
+    return guarded<uint64_t>(0, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        return e.book().fork(sequence);
+    });
+}
+
+int tvara_sequence_length(tvara_model* model, uint64_t sequence, size_t* length) {
+    return guarded<int>(-1, [&] {
+        if (!length) throw std::invalid_argument("invalid output pointer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        *length = e.book().sequence(sequence).length;
+        return 0;
+    });
+}
+
+int tvara_kv_stats(tvara_model* model, size_t* available, size_t* max_blocks) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        if (available) *available = e.book().pool().available();
+        if (max_blocks) *max_blocks = e.book().geometry().max_blocks;
+        return 0;
+    });
+}
+
+int tvara_kv_audit(tvara_model* model) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const auto ext = e.radix().external_references();
+        e.book().audit(ext);
+        return 0;
+    });
+}
+
+int tvara_sequence_blocks(tvara_model* model, uint64_t sequence, uint64_t* ids, uint64_t* generations,
+                          size_t capacity, size_t* count) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const auto& t = e.book().sequence(sequence);
+        if (count) *count = t.blocks.size();
+        for (size_t i = 0; i < t.blocks.size() && i < capacity; ++i) {
+            if (ids) ids[i] = t.blocks[i].id;
+            if (generations) generations[i] = t.blocks[i].generation;
+        }
+        return 0;
+    });
+}
+
+int tvara_kv_references(tvara_model* model, size_t id, size_t* references) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        if (references) *references = e.book().pool().references_by_id(id);
+        return 0;
+    });
+}
+
+uint64_t tvara_prefix_insert(tvara_model* model, const int32_t* tokens, size_t token_count, uint64_t sequence) {
+    return guarded<uint64_t>(0, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const auto node = e.radix().insert({tokens, token_count});
+        e.radix().attach(node, sequence);
+        return node;
+    });
+}
+
+uint64_t tvara_prefix_reuse(tvara_model* model, const int32_t* tokens, size_t token_count, int partial,
+                            size_t* reused) {
+    return guarded<uint64_t>(0, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        auto r = e.radix().reuse({tokens, token_count}, partial != 0);
+        if (reused) *reused = r.second;
+        return r.first;
+    });
+}
+
+int tvara_prefix_lookup(tvara_model* model, const int32_t* tokens, size_t token_count, uint64_t* node,
+                        size_t* matched) {
+    return guarded<int>(-1, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        auto r = e.radix().lookup({tokens, token_count});
+        if (node) *node = r.first;
+        if (matched) *matched = r.second;
+        return 0;
+    });
+}
+
+int tvara_prefix_pin(tvara_model* model, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.radix().pin(node);
+        return 0;
+    });
+}
+
+int tvara_prefix_unpin(tvara_model* model, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.radix().unpin(node);
+        return 0;
+    });
+}
+
+int tvara_prefix_touch(tvara_model* model, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.radix().touch(node);
+        return 0;
+    });
+}
+
+int tvara_prefix_evict_one(tvara_model* model) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        return e.radix().evict_one() ? 1 : 0;
+    });
+}
+
+size_t tvara_prefix_size(tvara_model* model) {
+    return guarded<size_t>(0, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        return e.radix().size();
+    });
+}
+
+// ---- host-only accounting book ---------------------------------------------
+tvara_kv_book* tvara_kv_book_new(size_t layers, size_t kv_heads, size_t head_dim, size_t block_tokens,
+                                 size_t max_blocks) {
+    return guarded<tvara_kv_book*>(nullptr, [&] {
+        return new tvara_kv_book(tvara::CacheGeometry{layers, kv_heads, head_dim, block_tokens, max_blocks});
+    });
+}
+void tvara_kv_book_free(tvara_kv_book* book) { delete book; }
+uint64_t tvara_kv_book_create(tvara_kv_book* b) {
+    return guarded<uint64_t>(0, [&] { return b->book.create_sequence(); });
+}
+int tvara_kv_book_append(tvara_kv_book* b, uint64_t s) {
+    error_message.clear();
+    try {
+        b->book.append(s);
+        return 0;
+    } catch (const tvara::CacheExhausted& e) {
+        error_message = e.what();
+        return -2;
+    } catch (const std::exception& e) {
+        error_message = e.what();
+        return -1;
+    }
+}
+int tvara_kv_book_drop(tvara_kv_book* b, uint64_t s) {
+    return guarded<int>(-1, [&] {
+        b->book.drop(s);
+        return 0;
+    });
+}
+uint64_t tvara_kv_book_fork(tvara_kv_book* b, uint64_t s) {
+    return guarded<uint64_t>(0, [&] { return b->book.fork(s); });
+}
+int tvara_kv_book_truncate(tvara_kv_book* b, uint64_t s, size_t n) {
+    return guarded<int>(-1, [&] {
+        b->book.truncate(s, n);
+        return 0;
+    });
+}
+uint64_t tvara_kv_book_import(tvara_kv_book* b, uint64_t s, size_t n) {
+    return guarded<uint64_t>(0, [&] { return b->book.import_sequence(b->book.sequence(s), n); });
+}
+size_t tvara_kv_book_available(tvara_kv_book* b) { return b->book.pool().available(); }
+size_t tvara_kv_book_references(tvara_kv_book* b, size_t id) {
+    return guarded<size_t>(0, [&] { return b->book.pool().references_by_id(id); });
+}
+int tvara_kv_book_table(tvara_kv_book* b, uint64_t s, uint64_t* ids, uint64_t* gens, size_t capacity, size_t* count) {
+    return guarded<int>(-1, [&] {
+        const auto& t = b->book.sequence(s);
+        if (count) *count = t.blocks.size();
+        for (size_t i = 0; i < t.blocks.size() && i < capacity; ++i) {
+            if (ids) ids[i] = t.blocks[i].id;
+            if (gens) gens[i] = t.blocks[i].generation;
+        }
+        return 0;
+    });
+}
+int tvara_kv_book_audit(tvara_kv_book* b) {
+    return guarded<int>(-1, [&] {
+        b->book.audit();
+        return 0;
+    });
+}
+
+}  // extern "C"

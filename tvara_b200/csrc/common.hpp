@@ -1,0 +1,73 @@
+// Shared host/device definitions for the B200 decode/prefill engine.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace tvara {
+
+// GGUF storage types on this path (reference gguf.hpp:152-170).
+enum TensorType : int { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ8_0 = 8, kQ4_K = 12 };
+
+inline bool block_shape(int type, std::size_t& elems, std::size_t& bytes) {
+    switch (type) {
+        case kF32: elems = 1; bytes = 4; return true;
+        case kF16: elems = 1; bytes = 2; return true;
+        case kQ4_0: elems = 32; bytes = 18; return true;
+        case kQ8_0: elems = 32; bytes = 34; return true;
+        case kQ4_K: elems = 256; bytes = 144; return true;
+        default: return false;
+    }
+}
+
+// A weight matrix [rows][cols] resident in HBM in the engine's split layout:
+//   qs   -- per row, the quantised codes (F32/F16: the values)
+//            Q8_0: int8 [cols]; Q4_0: 16 B per 32 (GGUF nibble order);
+//            Q4_K: 128 B per 256 (GGUF nibble order); F16: half; F32: float
+//   meta -- per row, the block headers: Q8_0/Q4_0 fp16 d per 32; Q4_K the
+//            16-byte {d, dmin, scales[12]} per 256; none for F32/F16.
+// Splitting headers from codes keeps every row 16-byte aligned so kernels
+// stream it with 128-bit loads; the arithmetic is unchanged.
+struct DeviceMatrix {
+    int type = kF32;
+    int rows = 0, cols = 0;
+    const std::uint8_t* qs = nullptr;
+    const std::uint8_t* meta = nullptr;
+    std::size_t qs_row = 0;    // bytes per row in qs
+    std::size_t meta_row = 0;  // bytes per row in meta
+};
+
+inline std::size_t qs_row_bytes(int type, std::size_t cols) {
+    switch (type) {
+        case kF32: return cols * 4;
+        case kF16: return cols * 2;
+        case kQ8_0: return cols;
+        case kQ4_0: return cols / 2;
+        case kQ4_K: return cols / 2;
+    }
+    return 0;
+}
+inline std::size_t meta_row_bytes(int type, std::size_t cols) {
+    switch (type) {
+        case kQ8_0:
+        case kQ4_0: return cols / 32 * 2;
+        case kQ4_K: return cols / 256 * 16;
+    }
+    return 0;
+}
+
+class CudaError : public std::runtime_error {
+public:
+    using std::runtime_error::runtime_error;
+};
+
+}  // namespace tvara
+
+#define TVARA_CUDA(call)                                                                      \
+    do {                                                                                      \
+        cudaError_t err__ = (call);                                                           \
+        if (err__ != cudaSuccess)                                                             \
+            throw ::tvara::CudaError(std::string("CUDA error: ") + cudaGetErrorString(err__) + \
+                                     " at " + __FILE__ + ":" + std::to_string(__LINE__));     \
+    } while (0)

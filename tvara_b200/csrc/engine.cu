@@ -1,0 +1,563 @@
+// Engine: loading, KV pool, and the ragged step.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <set>
+
+#include "attention_plan.hpp"
+#include "collective.hpp"
+
+namespace tvara {
+namespace {
+
+std::size_t align256(std::size_t n) { return (n + 255) & ~std::size_t(255); }
+
+struct Segment {
+    std::string name;
+    int row0, rows, col0, cols;
+};
+
+// Raw GGUF rows of one or more tensors (same type and width), optionally
+// interleaving two tensors row by row (gate/up).
+struct RawMatrix {
+    int type = 0, rows = 0, cols = 0;
+    std::vector<std::uint8_t> bytes;
+};
+
+RawMatrix gather(const gguf::File& f, const std::vector<Segment>& segs, bool interleave) {
+    RawMatrix m;
+    m.type = static_cast<int>(f.info(segs[0].name).type);
+    m.cols = segs[0].cols;
+    std::size_t elems = 0, width = 0;
+    if (!block_shape(m.type, elems, width)) throw std::invalid_argument("unsupported native weight type");
+    if (m.cols % elems) throw std::invalid_argument("tensor-parallel split is not a whole number of blocks");
+    const std::size_t out_row = std::size_t(m.cols) / elems * width;
+    for (const auto& s : segs) {
+        if (static_cast<int>(f.info(s.name).type) != m.type || s.cols != m.cols)
+            throw std::invalid_argument("fused tensors must share type and width");
+        m.rows += s.rows;
+    }
+    m.bytes.resize(std::size_t(m.rows) * out_row);
+    std::size_t r_out = 0;
+    std::vector<std::span<const std::byte>> payloads;
+    for (const auto& s : segs) payloads.push_back(f.payload(s.name));
+    auto copy_row = [&](std::size_t si, int r, std::size_t dst_row) {
+        const auto& s = segs[si];
+        const auto& info = f.info(s.name);
+        const std::size_t in_row = std::size_t(info.dims[0]) / elems * width;
+        const std::size_t off = std::size_t(s.row0 + r) * in_row + std::size_t(s.col0) / elems * width;
+        std::memcpy(m.bytes.data() + dst_row * out_row, payloads[si].data() + off, out_row);
+    };
+    if (interleave) {
+        for (int r = 0; r < segs[0].rows; ++r)
+            for (std::size_t si = 0; si < segs.size(); ++si) copy_row(si, r, r_out++);
+    } else {
+        for (std::size_t si = 0; si < segs.size(); ++si)
+            for (int r = 0; r < segs[si].rows; ++r) copy_row(si, r, r_out++);
+    }
+    return m;
+}
+
+std::size_t matrix_bytes(int type, int rows, int cols) {
+    return align256(qs_row_bytes(type, cols) * rows) + align256(meta_row_bytes(type, cols) * rows);
+}
+
+}  // namespace
+
+Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t block_tokens, const EngineOptions& opt)
+    : opt_(opt) {
+    if (opt.device >= 0) TVARA_CUDA(cudaSetDevice(opt.device));
+    TVARA_CUDA(cudaGetDevice(&device_));
+    gguf::File f(path);
+    cfg_ = gguf::llama_config(f.doc());
+    gguf::validate_llama_tensors(f.doc(), cfg_);
+    metadata_ = f.metadata_json();
+    const int tp = std::max(1, opt.tp_size);
+    if (opt.tp_rank < 0 || opt.tp_rank >= tp) throw std::invalid_argument("invalid tensor-parallel rank");
+    if (cfg_.heads % tp || cfg_.kv_heads % tp || cfg_.ffn % tp)
+        throw std::invalid_argument("tensor-parallel size must divide the head counts and FFN width");
+    hidden_ = int(cfg_.hidden);
+    vocab_ = int(cfg_.vocab);
+    layers_ = int(cfg_.layers);
+    dim_ = int(cfg_.head_dim());
+    hq_ = int(cfg_.heads) / tp;
+    hkv_ = int(cfg_.kv_heads) / tp;
+    ffn_ = int(cfg_.ffn) / tp;
+    qkv_w_ = (hq_ + 2 * hkv_) * dim_;
+    if (hq_ / hkv_ > 8) throw std::invalid_argument("unsupported query/KV head ratio (1..8)");
+    if (dim_ != 16 && dim_ != 32 && dim_ != 64 && dim_ != 128 && dim_ != 256)
+        throw std::invalid_argument("unsupported head_dim (16, 32, 64, 128, 256)");
+    tmax_ = std::max(1, opt.max_step_tokens);
+
+    CacheGeometry g{cfg_.layers, cfg_.kv_heads, cfg_.head_dim(), block_tokens, max_blocks};
+    book_ = std::make_unique<PagedBook>(g);
+    radix_ = std::make_unique<RadixBook>(*book_, "tvara-b200-engine");
+
+    TVARA_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (tp > 1) {
+        if (!opt.has_nccl_id) throw std::invalid_argument("tensor parallelism needs an NCCL unique id");
+        coll_ = std::make_unique<Collective>(opt.nccl_id.data(), opt.tp_rank, tp);
+    }
+    try {
+        load(f);
+    } catch (...) {
+        if (weights_) cudaFree(weights_);
+        weights_ = nullptr;
+        cudaStreamDestroy(stream_);
+        throw;
+    }
+}
+
+Engine::~Engine() {
+    if (stream_) cudaStreamSynchronize(stream_);
+    radix_.reset();
+    coll_.reset();
+    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
+                    static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_)})
+        if (p) cudaFree(p);
+    if (meta_host_) cudaFreeHost(meta_host_);
+    if (err_host_) cudaFreeHost(err_host_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::load(const gguf::File& f) {
+    const int r = opt_.tp_rank, tp = std::max(1, opt_.tp_size);
+    const int D = hidden_, d = dim_;
+    const bool tied = !f.has("output.weight");
+    // ---- plan every device matrix
+    struct Plan {
+        std::vector<Segment> segs;
+        bool interleave = false;
+        DeviceMatrix* out = nullptr;
+    };
+    std::vector<Plan> plans;
+    std::vector<std::pair<std::string, const float**>> norms;
+    lw_.assign(layers_, {});
+    plans.push_back({{{"token_embd.weight", 0, vocab_, 0, D}}, false, &embed_});
+    if (!tied) plans.push_back({{{"output.weight", 0, vocab_, 0, D}}, false, &head_});
+    norms.push_back({"output_norm.weight", &final_norm_});
+    auto type_of = [&](const std::string& n) { return static_cast<int>(f.info(n).type); };
+    for (int l = 0; l < layers_; ++l) {
+        const auto p = "blk." + std::to_string(l) + ".";
+        auto& L = lw_[l];
+        norms.push_back({p + "attn_norm.weight", &L.attn_norm});
+        norms.push_back({p + "ffn_norm.weight", &L.ffn_norm});
+        const Segment sq{p + "attn_q.weight", r * hq_ * d, hq_ * d, 0, D};
+        const Segment sk{p + "attn_k.weight", r * hkv_ * d, hkv_ * d, 0, D};
+        const Segment sv{p + "attn_v.weight", r * hkv_ * d, hkv_ * d, 0, D};
+        if (type_of(sq.name) == type_of(sk.name) && type_of(sq.name) == type_of(sv.name)) {
+            L.qkv.resize(1);
+            plans.push_back({{sq, sk, sv}, false, &L.qkv[0]});
+        } else {
+            L.qkv.resize(3);
+            plans.push_back({{sq}, false, &L.qkv[0]});
+            plans.push_back({{sk}, false, &L.qkv[1]});
+            plans.push_back({{sv}, false, &L.qkv[2]});
+        }
+        plans.push_back({{{p + "attn_output.weight", 0, D, r * hq_ * d, hq_ * d}}, false, &L.o});
+        const Segment sg{p + "ffn_gate.weight", r * ffn_, ffn_, 0, D};
+        const Segment su{p + "ffn_up.weight", r * ffn_, ffn_, 0, D};
+        if (type_of(sg.name) == type_of(su.name)) {
+            L.gateup.resize(1);
+            plans.push_back({{sg, su}, true, &L.gateup[0]});
+        } else {
+            gate_up_fused_ = false;
+            L.gateup.resize(2);
+            plans.push_back({{sg}, false, &L.gateup[0]});
+            plans.push_back({{su}, false, &L.gateup[1]});
+        }
+        plans.push_back({{{p + "ffn_down.weight", 0, D, r * ffn_, ffn_}}, false, &L.down});
+    }
+    // ---- sizes: one allocation for every matrix, norm and the rope tables
+    std::size_t total = 0, staging = 0;
+    for (const auto& pl : plans) {
+        int rows = 0;
+        for (const auto& s : pl.segs) rows += s.rows;
+        const int type = type_of(pl.segs[0].name);
+        total += matrix_bytes(type, rows, pl.segs[0].cols);
+        std::size_t e = 0, w = 0;
+        block_shape(type, e, w);
+        staging = std::max(staging, std::size_t(rows) * (pl.segs[0].cols / e) * w);
+    }
+    for (const auto& n : norms) {
+        total += align256(std::size_t(D) * 4);
+        staging = std::max(staging, gguf::tensor_bytes(f.info(n.first)));
+    }
+    weight_bytes_ = total;
+    TVARA_CUDA(cudaMalloc(&weights_, total));
+    std::uint8_t* staging_dev = nullptr;
+    TVARA_CUDA(cudaMalloc(&staging_dev, align256(staging)));
+    std::uint8_t* cursor = weights_;
+    int* flag = nullptr;
+    TVARA_CUDA(cudaMalloc(&flag, sizeof(int)));
+    TVARA_CUDA(cudaMemset(flag, 0, sizeof(int)));
+    try {
+        for (const auto& pl : plans) {
+            RawMatrix raw = gather(f, pl.segs, pl.interleave);
+            TVARA_CUDA(cudaMemcpyAsync(staging_dev, raw.bytes.data(), raw.bytes.size(), cudaMemcpyHostToDevice, stream_));
+            DeviceMatrix m;
+            m.type = raw.type;
+            m.rows = raw.rows;
+            m.cols = raw.cols;
+            m.qs_row = qs_row_bytes(raw.type, raw.cols);
+            m.meta_row = meta_row_bytes(raw.type, raw.cols);
+            std::uint8_t* qs = cursor;
+            cursor += align256(m.qs_row * m.rows);
+            std::uint8_t* meta = cursor;
+            cursor += align256(m.meta_row * m.rows);
+            launch_repack(raw.type, staging_dev, raw.rows, raw.cols, qs, meta, stream_);
+            m.qs = qs;
+            m.meta = meta;
+            launch_finite_check(m, flag, stream_);
+            *pl.out = m;
+            TVARA_CUDA(cudaStreamSynchronize(stream_));  // raw host buffer is released next iteration
+        }
+        for (const auto& n : norms) {
+            const auto& info = f.info(n.first);
+            auto bytes = f.payload(n.first);
+            TVARA_CUDA(cudaMemcpyAsync(staging_dev, bytes.data(), bytes.size(), cudaMemcpyHostToDevice, stream_));
+            std::size_t e = 0, w = 0;
+            if (!block_shape(static_cast<int>(info.type), e, w)) throw std::invalid_argument("unsupported native weight type");
+            float* out = reinterpret_cast<float*>(cursor);
+            cursor += align256(std::size_t(D) * 4);
+            launch_dequantize(static_cast<int>(info.type), staging_dev, std::size_t(D) / e, out, stream_);
+            DeviceMatrix nm;
+            nm.type = kF32;
+            nm.rows = 1;
+            nm.cols = D;
+            nm.qs = reinterpret_cast<const std::uint8_t*>(out);
+            nm.qs_row = std::size_t(D) * 4;
+            launch_finite_check(nm, flag, stream_);
+            *n.second = out;
+        }
+        if (tied) head_ = embed_;
+        int bad = 0;
+        TVARA_CUDA(cudaMemcpyAsync(&bad, flag, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+        TVARA_CUDA(cudaStreamSynchronize(stream_));
+        if (bad) throw std::invalid_argument("nonfinite model weight");
+    } catch (...) {
+        cudaFree(staging_dev);
+        cudaFree(flag);
+        throw;
+    }
+    cudaFree(staging_dev);
+    cudaFree(flag);
+
+    // ---- RoPE table with the reference's float expression (model.hpp:71-72)
+    const std::size_t half = d / 2;
+    std::vector<float> cs(cfg_.context * half), sn(cfg_.context * half);
+    for (std::size_t p = 0; p < cfg_.context; ++p)
+        for (std::size_t i = 0; i < half; ++i) {
+            const float angle = static_cast<float>(p) / std::pow(cfg_.theta, static_cast<float>(2 * i) / static_cast<float>(d));
+            cs[p * half + i] = std::cos(angle);
+            sn[p * half + i] = std::sin(angle);
+        }
+    TVARA_CUDA(cudaMalloc(&rope_cos_, cs.size() * 4));
+    TVARA_CUDA(cudaMalloc(&rope_sin_, sn.size() * 4));
+    TVARA_CUDA(cudaMemcpy(rope_cos_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    TVARA_CUDA(cudaMemcpy(rope_sin_, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+
+    // ---- KV pool: [block][layer][K|V][kv head][slot][d]
+    const auto& g = book_->geometry();
+    const std::size_t es = opt_.kv_f16 ? 2 : 4;
+    kind_stride_ = (long long)hkv_ * g.tokens_per_block * d;
+    layer_stride_ = 2 * kind_stride_;
+    block_stride_ = (long long)layers_ * layer_stride_;
+    const std::size_t pool_bytes = std::size_t(block_stride_) * es * g.max_blocks;
+    std::size_t free_b = 0, total_b = 0;
+    TVARA_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    if (pool_bytes > free_b) throw std::runtime_error("KV pool does not fit in device memory");
+    TVARA_CUDA(cudaMalloc(&kv_, pool_bytes));
+
+    // ---- scratch for tmax_ tokens (one allocation)
+    const std::size_t T = tmax_;
+    partial_cap_ = 8192;
+    const std::size_t ff_w = std::size_t(ffn_) * (gate_up_fused_ ? 1 : 2);
+    const std::size_t floats = T * D * 2 + T * qkv_w_ + T * hq_ * d * 2 + T * ff_w + T * vocab_ +
+                               partial_cap_ * hq_ * (d + 2) + 64 * 8;
+    std::size_t bytes = floats * 4 + T * 4 + 4096;
+    TVARA_CUDA(cudaMalloc(&x_, bytes));
+    float* c = x_;
+    auto take = [&](std::size_t n) {
+        float* p = c;
+        c += (n + 63) & ~std::size_t(63);
+        return p;
+    };
+    x_ = take(T * D);
+    xn_ = take(T * D);
+    qkv_ = take(T * qkv_w_);
+    q_ = take(T * hq_ * d);
+    att_ = take(T * hq_ * d);
+    ff_ = take(T * ffn_);
+    ffu_ = gate_up_fused_ ? nullptr : take(T * ffn_);
+    logits_ = take(T * vocab_);
+    partial_ = take(partial_cap_ * hq_ * (d + 2));
+    argmax_ = reinterpret_cast<unsigned*>(take(T));
+    TVARA_CUDA(cudaMalloc(&err_, sizeof(int)));
+    TVARA_CUDA(cudaMemset(err_, 0, sizeof(int)));
+    TVARA_CUDA(cudaHostAlloc(&err_host_, sizeof(int), cudaHostAllocDefault));
+}
+
+void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi) {
+    GemmArgs a;
+    a.w = w;
+    a.x = x;
+    a.ldx = ldx;
+    a.tokens = tokens;
+    a.y = y;
+    a.ldy = ldy;
+    a.epilogue = epi;
+    launch_projection(a, nullptr, 0, stream_);
+}
+
+void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
+                  std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax) {
+    const std::size_t n = seqs.size();
+    if (!n || cu.size() != n + 1 || cu[0] != 0) throw std::invalid_argument("invalid batch layout");
+    for (std::size_t i = 0; i < n; ++i)
+        if (cu[i + 1] <= cu[i]) throw std::invalid_argument("invalid batch layout");
+    if (tokens.size() != cu[n]) throw std::invalid_argument("invalid batch layout");
+    {
+        std::set<std::uint64_t> uniq(seqs.begin(), seqs.end());
+        if (uniq.size() != n) throw std::invalid_argument("sequence listed twice in one step");
+    }
+    std::vector<std::size_t> entry(n);
+    for (std::size_t i = 0; i < n; ++i) {
+        entry[i] = book_->sequence(seqs[i]).length;
+        const std::size_t count = cu[i + 1] - cu[i];
+        if (entry[i] + count > cfg_.context) throw std::invalid_argument("paged decode exceeds token/context limits");
+        for (std::size_t j = cu[i]; j < cu[i + 1]; ++j)
+            if (tokens[j] >= cfg_.vocab) throw std::invalid_argument("paged decode exceeds token/context limits");
+    }
+    // ---- accounting: all-or-nothing over the call
+    const std::size_t T = tokens.size();
+    const std::size_t tpb = book_->geometry().tokens_per_block;
+    std::vector<int> blk(T), slot(T);
+    std::vector<int2> copies;
+    std::size_t touched = 0;
+    try {
+        for (std::size_t i = 0; i < n; ++i) {
+            touched = i + 1;
+            for (std::size_t j = cu[i]; j < cu[i + 1]; ++j) {
+                BlockCopy c{SIZE_MAX, SIZE_MAX};
+                book_->append(seqs[i], &c);
+                if (c.from != SIZE_MAX) copies.push_back(make_int2(int(c.from), int(c.to)));
+                const auto& t = book_->sequence(seqs[i]);
+                blk[j] = int(t.blocks.back().id);
+                slot[j] = int((t.length - 1) % tpb);
+            }
+        }
+    } catch (...) {
+        if (!copies.empty()) {  // replacement blocks stay in the tables: give them their data
+            int2* dev = nullptr;
+            if (cudaMalloc(&dev, copies.size() * sizeof(int2)) == cudaSuccess) {
+                cudaMemcpy(dev, copies.data(), copies.size() * sizeof(int2), cudaMemcpyHostToDevice);
+                launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), dev, int(copies.size()), stream_);
+                cudaStreamSynchronize(stream_);
+                cudaFree(dev);
+            }
+        }
+        for (std::size_t i = 0; i < touched; ++i) book_->truncate(seqs[i], entry[i]);
+        throw;
+    }
+    try {
+        // ---- split into device sub-steps of at most tmax_ tokens
+        std::size_t i = 0, j = 0;  // sequence, token offset within it
+        bool first = true;
+        const std::size_t rows_total = all_logits ? T : n;
+        while (i < n) {
+            Sub sub;
+            if (first) sub.copies = copies;
+            first = false;
+            std::size_t room = std::size_t(tmax_);
+            std::vector<std::size_t> seq_ids;
+            while (i < n && room) {
+                const std::size_t count = cu[i + 1] - cu[i];
+                const std::size_t take = std::min(room, count - j);
+                const int si = int(seq_ids.size());
+                seq_ids.push_back(i);
+                const auto& table = book_->sequence(seqs[i]);
+                sub.table_off.push_back(int(sub.tables.size()));
+                for (auto b : table.blocks) sub.tables.push_back(int(b.id));
+                for (std::size_t k = 0; k < take; ++k) {
+                    const std::size_t g = cu[i] + j + k;
+                    sub.tok.push_back(int(tokens[g]));
+                    sub.pos.push_back(int(entry[i] + j + k));
+                    sub.blk.push_back(blk[g]);
+                    sub.slot.push_back(slot[g]);
+                    sub.seq_of.push_back(si);
+                    const bool last = j + k + 1 == count;
+                    if (all_logits || last) {
+                        sub.out_rows.push_back(int(sub.tok.size() - 1));
+                        sub.out_dest.push_back(all_logits ? (long long)g : (long long)i);
+                    }
+                }
+                room -= take;
+                j += take;
+                if (j == count) {
+                    ++i;
+                    j = 0;
+                }
+            }
+            run(sub, logits, argmax, rows_total);
+        }
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        for (std::size_t k = 0; k < n; ++k) book_->truncate(seqs[k], entry[k]);
+        throw;
+    }
+}
+
+void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
+    const int T = int(s.tok.size());
+    const int d = dim_, D = hidden_;
+    const int tpb = int(book_->geometry().tokens_per_block);
+    // ---- attention work list
+    std::vector<int> vis(T), toff(T);
+    for (int t = 0; t < T; ++t) {
+        vis[t] = s.pos[t] + 1;
+        toff[t] = s.table_off[s.seq_of[t]];
+    }
+    AttnPlan plan = plan_attention(vis, toff, tpb, hkv_, partial_cap_);
+    auto& work = plan.work;
+    auto& comb = plan.comb;
+    auto& wpart = plan.part;
+    // ---- pack metadata into one pinned buffer and upload
+    const int R = int(s.out_rows.size());
+    const std::size_t need = std::size_t(T) * 4 + s.tables.size() + work.size() * 5 + comb.size() * 4 +
+                             s.copies.size() * 2 + R + 64;
+    if (need > meta_cap_) {
+        TVARA_CUDA(cudaStreamSynchronize(stream_));
+        if (meta_dev_) cudaFree(meta_dev_);
+        if (meta_host_) cudaFreeHost(meta_host_);
+        meta_cap_ = std::max(need * 2, std::size_t(1) << 16);
+        TVARA_CUDA(cudaMalloc(&meta_dev_, meta_cap_ * 4));
+        TVARA_CUDA(cudaHostAlloc(&meta_host_, meta_cap_ * 4, cudaHostAllocDefault));
+    } else {
+        TVARA_CUDA(cudaStreamSynchronize(stream_));  // previous step done with the host mirror
+    }
+    std::size_t at = 0;
+    auto put = [&](const void* src, std::size_t ints) -> int* {
+        at = (at + 3) & ~std::size_t(3);  // 16-byte alignment for int4 arrays
+        std::memcpy(meta_host_ + at, src, ints * 4);
+        int* dev = meta_dev_ + at;
+        at += ints;
+        return dev;
+    };
+    int* d_tok = put(s.tok.data(), T);
+    int* d_pos = put(s.pos.data(), T);
+    int* d_blk = put(s.blk.data(), T);
+    int* d_slot = put(s.slot.data(), T);
+    int* d_tables = put(s.tables.data(), s.tables.size());
+    int4* d_work = reinterpret_cast<int4*>(put(work.data(), work.size() * 4));
+    int* d_wpart = put(wpart.data(), wpart.size());
+    int4* d_comb = reinterpret_cast<int4*>(put(comb.data(), comb.size() * 4));
+    int2* d_copy = reinterpret_cast<int2*>(put(s.copies.data(), s.copies.size() * 2));
+    int* d_rows = put(s.out_rows.data(), R);
+    TVARA_CUDA(cudaMemcpyAsync(meta_dev_, meta_host_, at * 4, cudaMemcpyHostToDevice, stream_));
+
+    const std::size_t es = opt_.kv_f16 ? 2 : 4;
+    launch_block_copy(kv_, block_stride_ * es, d_copy, int(s.copies.size()), stream_);
+    launch_embed(embed_, d_tok, T, x_, D, stream_);
+    for (int l = 0; l < layers_; ++l) {
+        const auto& L = lw_[l];
+        launch_rmsnorm(x_, D, nullptr, T, D, L.attn_norm, cfg_.eps, xn_, D, stream_);
+        if (L.qkv.size() == 1) {
+            projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
+        } else {
+            projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
+            projection(L.qkv[1], xn_, D, T, qkv_ + hq_ * d, qkv_w_, kStore);
+            projection(L.qkv[2], xn_, D, T, qkv_ + (hq_ + hkv_) * d, qkv_w_, kStore);
+        }
+        RopeArgs ra;
+        ra.qkv = qkv_;
+        ra.ldqkv = qkv_w_;
+        ra.q = q_;
+        ra.tokens = T;
+        ra.hq = hq_;
+        ra.hkv = hkv_;
+        ra.dim = d;
+        ra.interleaved = cfg_.interleaved;
+        ra.cosines = rope_cos_;
+        ra.sines = rope_sin_;
+        ra.positions = d_pos;
+        ra.slot_block = d_blk;
+        ra.slot_index = d_slot;
+        ra.kv = kv_;
+        ra.kv_f16 = opt_.kv_f16;
+        ra.block_stride = block_stride_;
+        ra.layer_offset = (long long)l * layer_stride_;
+        ra.kind_stride = kind_stride_;
+        ra.tpb = tpb;
+        ra.max_blocks = int(book_->geometry().max_blocks);
+        ra.err = err_;
+        launch_rope_kv(ra, stream_);
+        AttnArgs aa;
+        aa.q = q_;
+        aa.out = att_;
+        aa.kv = kv_;
+        aa.kv_f16 = opt_.kv_f16;
+        aa.hq = hq_;
+        aa.hkv = hkv_;
+        aa.dim = d;
+        aa.tpb = tpb;
+        aa.block_stride = block_stride_;
+        aa.layer_offset = (long long)l * layer_stride_;
+        aa.kind_stride = kind_stride_;
+        aa.tables = d_tables;
+        aa.work = d_work;
+        aa.work_part = d_wpart;
+        aa.n_work = int(work.size());
+        aa.partial = partial_;
+        aa.combine = d_comb;
+        aa.n_combine = int(comb.size());
+        aa.max_blocks = int(book_->geometry().max_blocks);
+        aa.err = err_;
+        launch_attention(aa, stream_);
+        const bool lead = opt_.tp_rank == 0;
+        projection(L.o, att_, hq_ * d, T, x_, D, lead ? kAdd : kStore);
+        if (coll_) coll_->allreduce_sum(x_, std::size_t(T) * D, stream_);
+        launch_rmsnorm(x_, D, nullptr, T, D, L.ffn_norm, cfg_.eps, xn_, D, stream_);
+        if (L.gateup.size() == 1) {
+            projection(L.gateup[0], xn_, D, T, ff_, ffn_, kSwiGLU);
+        } else {
+            projection(L.gateup[0], xn_, D, T, ff_, ffn_, kStore);
+            projection(L.gateup[1], xn_, D, T, ffu_, ffn_, kStore);
+            launch_swiglu(ff_, ffu_, T * ffn_, stream_);
+        }
+        projection(L.down, ff_, ffn_, T, x_, D, lead ? kAdd : kStore);
+        if (coll_) coll_->allreduce_sum(x_, std::size_t(T) * D, stream_);
+    }
+    if (R > 0) {
+        launch_rmsnorm(x_, D, d_rows, R, D, final_norm_, cfg_.eps, xn_, D, stream_);
+        projection(head_, xn_, D, R, logits_, vocab_, kStore);
+        if (argmax) launch_argmax(logits_, R, vocab_, argmax_, stream_);
+    }
+    TVARA_CUDA(cudaMemcpyAsync(err_host_, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    // ---- results to the caller: contiguous destination runs, one copy each
+    std::vector<unsigned> am(argmax ? R : 0);
+    if (argmax && R) TVARA_CUDA(cudaMemcpyAsync(am.data(), argmax_, R * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits) {
+        int k = 0;
+        while (k < R) {
+            int e = k + 1;
+            while (e < R && s.out_dest[e] == s.out_dest[e - 1] + 1) ++e;
+            TVARA_CUDA(cudaMemcpyAsync(logits + s.out_dest[k] * vocab_, logits_ + (long long)k * vocab_,
+                                       std::size_t(e - k) * vocab_ * 4, cudaMemcpyDeviceToHost, stream_));
+            k = e;
+        }
+    }
+    TVARA_CUDA(cudaStreamSynchronize(stream_));
+    if (*err_host_) {
+        const int code = *err_host_;
+        TVARA_CUDA(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
+        throw std::runtime_error("device bounds check failed (code " + std::to_string(code) + ")");
+    }
+    if (argmax)
+        for (int k = 0; k < R; ++k) argmax[s.out_dest[k]] = am[k];
+}
+
+}  // namespace tvara

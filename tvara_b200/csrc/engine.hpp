@@ -1,0 +1,116 @@
+// The B200 decode/prefill engine behind the C ABI: packed weights and the
+// paged KV pool in HBM, host-side block accounting, and one device step per
+// ragged batch (the reference's PagedModelExecutor::decode, paged_model.hpp:
+// 12-28, for many sequences and tokens at once).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <memory>
+#include <span>
+#include <string>
+#include <vector>
+
+#include "common.hpp"
+#include "gguf.hpp"
+#include "kernels.cuh"
+#include "kvbook.hpp"
+
+namespace tvara {
+
+struct EngineOptions {
+    int device = -1;
+    bool kv_f16 = false;
+    int max_step_tokens = 2048;
+    int tp_rank = 0, tp_size = 1;
+    bool has_nccl_id = false;
+    std::array<char, 128> nccl_id{};
+};
+
+class Collective;  // NCCL communicator of a tensor-parallel group (collective.cpp)
+
+struct LayerWeights {
+    const float* attn_norm = nullptr;
+    const float* ffn_norm = nullptr;
+    std::vector<DeviceMatrix> qkv;     // one fused matrix, or q, k, v
+    DeviceMatrix o;
+    std::vector<DeviceMatrix> gateup;  // interleaved gate/up rows, or gate, up
+    DeviceMatrix down;
+};
+
+class Engine {
+public:
+    Engine(const std::string& path, std::size_t max_blocks, std::size_t block_tokens, const EngineOptions& opt);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    const gguf::LlamaConfig& config() const { return cfg_; }
+    const std::string& metadata() const { return metadata_; }
+    PagedBook& book() { return *book_; }
+    RadixBook& radix() { return *radix_; }
+    const EngineOptions& options() const { return opt_; }
+
+    // One ragged step; see tvara_batch_step.  Rows of logits / argmax are
+    // written to host memory (either may be null).
+    void step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
+              std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax);
+
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+private:
+    struct Sub {  // one device launch sequence over <= max_step_tokens tokens
+        std::vector<int> tok, pos, blk, slot;
+        std::vector<int> seq_of;           // index into the sub-step's sequence list
+        std::vector<int> table_off;        // per sequence
+        std::vector<int> tables;
+        std::vector<int> out_rows;         // token indices whose logits are wanted
+        std::vector<long long> out_dest;   // destination row in the caller's buffer
+        std::vector<int2> copies;
+    };
+    void load(const gguf::File& f);
+    DeviceMatrix upload_matrix(const gguf::File& f, const std::string& name, int row0, int rows, int col0, int cols,
+                               std::uint8_t*& cursor);
+    void run(Sub& sub, float* logits, std::uint32_t* argmax, std::size_t vocab_rows_total);
+    void projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi);
+
+    gguf::LlamaConfig cfg_;
+    EngineOptions opt_;
+    std::string metadata_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::unique_ptr<PagedBook> book_;
+    std::unique_ptr<RadixBook> radix_;
+    std::unique_ptr<Collective> coll_;
+
+    // local (per tensor-parallel rank) shapes
+    int hq_ = 0, hkv_ = 0, dim_ = 0, ffn_ = 0, hidden_ = 0, vocab_ = 0, layers_ = 0, qkv_w_ = 0;
+    bool gate_up_fused_ = true;
+
+    // device memory
+    std::uint8_t* weights_ = nullptr;
+    std::size_t weight_bytes_ = 0;
+    DeviceMatrix embed_, head_;
+    const float* final_norm_ = nullptr;
+    std::vector<LayerWeights> lw_;
+    float* rope_cos_ = nullptr;
+    float* rope_sin_ = nullptr;
+    void* kv_ = nullptr;
+    long long block_stride_ = 0, layer_stride_ = 0, kind_stride_ = 0;
+
+    int tmax_ = 0;
+    float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ff_ = nullptr,
+          *ffu_ = nullptr, *logits_ = nullptr, *partial_ = nullptr, *xo_ = nullptr;
+    unsigned* argmax_ = nullptr;
+    int* err_ = nullptr;
+    std::size_t partial_cap_ = 0;  // partial rows (part x hq)
+    // per-step metadata (device + pinned host mirror)
+    int* meta_dev_ = nullptr;
+    int* meta_host_ = nullptr;
+    std::size_t meta_cap_ = 0;     // ints
+    int* err_host_ = nullptr;
+};
+
+}  // namespace tvara

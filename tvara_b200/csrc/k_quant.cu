@@ -1,0 +1,513 @@
+// Quantised block unpack, repack and the CUDA-core projection (decode GEMV).
+//
+// Device layout of a projection (see DeviceMatrix): qs streams the codes of
+// each row, meta the block headers.  Q4_K codes are regrouped at load so a
+// 16-byte unit holds one 32-element sub-block in Q4_0's nibble order (byte j:
+// element j low, element j+16 high); the value of every element is still
+// d*sc*q - dmin*m of reference core/include/tvara/quant.hpp:70-84.
+#include <cstdint>
+
+#include "kernels.cuh"
+
+namespace tvara {
+namespace {
+
+constexpr int kWarps = 8;  // warps per CTA of the GEMV
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Reference half_to_float (quant.hpp:14-29) in integer arithmetic, so NaN
+// payloads and subnormals come out bit-identical.
+__device__ __forceinline__ float half_bits_to_float(unsigned h) {
+    const unsigned sign = (h & 0x8000u) << 16;
+    unsigned e = (h >> 10) & 31u, m = h & 1023u, bits;
+    if (e == 0) {
+        if (!m) {
+            bits = sign;
+        } else {
+            int ex = -14;
+            while ((m & 1024u) == 0) {
+                m <<= 1;
+                --ex;
+            }
+            bits = sign | (unsigned(ex + 127) << 23) | ((m & 1023u) << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    return __uint_as_float(bits);
+}
+
+__device__ __forceinline__ float h2f(unsigned short h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ void q4k_scale_min(const unsigned char* s, int g, unsigned& sc, unsigned& m) {
+    if (g < 4) {
+        sc = s[g] & 63u;
+        m = s[g + 4] & 63u;
+    } else {
+        sc = (s[g + 4] & 15u) | ((unsigned)(s[g - 4] >> 6) << 4);
+        m = (s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
+    }
+}
+// Same decode from the 12 scale bytes held in three words.
+__device__ __forceinline__ void q4k_scale_min_w(unsigned w0, unsigned w1, unsigned w2, int g, float& sc, float& m) {
+    auto byte = [&](int j) -> unsigned {
+        const unsigned w = j < 4 ? w0 : (j < 8 ? w1 : w2);
+        return (w >> (8 * (j & 3))) & 255u;
+    };
+    unsigned s, mm;
+    if (g < 4) {
+        s = byte(g) & 63u;
+        mm = byte(g + 4) & 63u;
+    } else {
+        s = (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
+        mm = (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
+    }
+    sc = float(s);
+    m = float(mm);
+}
+
+// ------------------------------------------------------------------ unpack
+// The reference is built for x86-64, where SSE arithmetic returns the first
+// NaN operand (quieted) and an invalid operation (inf*0, inf-inf) returns the
+// negative default NaN 0xFFC00000; the GPU returns a canonical NaN instead.
+// For bit-identical unpacking of blocks whose scales are NaN or inf, the
+// unpack kernel applies the x86 rule; finite results are plain IEEE _rn ops.
+__device__ __forceinline__ float x86_nan(float a) { return __uint_as_float(__float_as_uint(a) | 0x00400000u); }
+__device__ __forceinline__ float x86_mul(float a, float b) {
+    if (isnan(a)) return x86_nan(a);
+    if (isnan(b)) return x86_nan(b);
+    const float r = __fmul_rn(a, b);
+    return isnan(r) ? __uint_as_float(0xFFC00000u) : r;
+}
+__device__ __forceinline__ float x86_sub(float a, float b) {
+    if (isnan(a)) return x86_nan(a);
+    if (isnan(b)) return x86_nan(b);
+    const float r = __fsub_rn(a, b);
+    return isnan(r) ? __uint_as_float(0xFFC00000u) : r;
+}
+
+// One thread per output element; arithmetic and rounding order as the
+// reference dequantisers (no contraction).
+__global__ void dequant_kernel(int type, const unsigned char* src, std::size_t nblocks, float* out) {
+    const std::size_t per = type == kQ4_K ? 256 : (type == kQ8_0 || type == kQ4_0) ? 32 : 1;
+    const std::size_t total = nblocks * per;
+    for (std::size_t i = blockIdx.x * std::size_t(blockDim.x) + threadIdx.x; i < total;
+         i += std::size_t(gridDim.x) * blockDim.x) {
+        const std::size_t b = i / per, e = i % per;
+        float v;
+        if (type == kF32) {
+            v = __uint_as_float(src[4 * b] | (src[4 * b + 1] << 8) | (src[4 * b + 2] << 16) | (unsigned(src[4 * b + 3]) << 24));
+        } else if (type == kF16) {
+            v = half_bits_to_float(src[2 * b] | (src[2 * b + 1] << 8));
+        } else if (type == kQ8_0) {
+            const unsigned char* blk = src + b * 34;
+            v = x86_mul(half_bits_to_float(blk[0] | (blk[1] << 8)), float((signed char)blk[2 + e]));
+        } else if (type == kQ4_0) {
+            const unsigned char* blk = src + b * 18;
+            const unsigned q = e < 16 ? (blk[2 + e] & 15u) : (blk[2 + e - 16] >> 4);
+            v = x86_mul(half_bits_to_float(blk[0] | (blk[1] << 8)), float(int(q) - 8));
+        } else {  // Q4_K
+            const unsigned char* blk = src + b * 144;
+            const float d = half_bits_to_float(blk[0] | (blk[1] << 8));
+            const float dmin = half_bits_to_float(blk[2] | (blk[3] << 8));
+            const int g = int(e / 32), j = int(e % 32);
+            unsigned sc, m;
+            q4k_scale_min(blk + 4, g, sc, m);
+            const unsigned packed = blk[16 + (g / 2) * 32 + j];
+            const unsigned q = (g % 2) ? (packed >> 4) : (packed & 15u);
+            v = x86_sub(x86_mul(x86_mul(d, float(sc)), float(q)), x86_mul(dmin, float(m)));
+        }
+        out[i] = v;
+    }
+}
+
+// GGUF rows -> (qs, meta).  One thread per output block.
+__global__ void repack_kernel(int type, const unsigned char* src, int rows, int cols, unsigned char* qs,
+                              unsigned char* meta) {
+    const int per = type == kQ4_K ? 256 : 32;
+    const int nb = cols / per;
+    const std::size_t in_row = std::size_t(nb) * (type == kQ4_K ? 144 : type == kQ8_0 ? 34 : 18);
+    const std::size_t total = std::size_t(rows) * nb;
+    for (std::size_t i = blockIdx.x * std::size_t(blockDim.x) + threadIdx.x; i < total;
+         i += std::size_t(gridDim.x) * blockDim.x) {
+        const std::size_t r = i / nb, b = i % nb;
+        if (type == kQ8_0) {
+            const unsigned char* blk = src + r * in_row + b * 34;
+            unsigned char* q = qs + r * std::size_t(cols) + b * 32;
+            for (int j = 0; j < 32; ++j) q[j] = blk[2 + j];
+            meta[(r * nb + b) * 2] = blk[0];
+            meta[(r * nb + b) * 2 + 1] = blk[1];
+        } else if (type == kQ4_0) {
+            const unsigned char* blk = src + r * in_row + b * 18;
+            unsigned char* q = qs + r * std::size_t(cols / 2) + b * 16;
+            for (int j = 0; j < 16; ++j) q[j] = blk[2 + j];
+            meta[(r * nb + b) * 2] = blk[0];
+            meta[(r * nb + b) * 2 + 1] = blk[1];
+        } else {  // Q4_K: regroup each 32-element sub-block into one 16-byte unit
+            const unsigned char* blk = src + r * in_row + b * 144;
+            unsigned char* q = qs + r * std::size_t(cols / 2) + b * 128;
+            for (int g = 0; g < 8; ++g)
+                for (int j = 0; j < 16; ++j) {
+                    const unsigned lo = g % 2 ? blk[16 + (g / 2) * 32 + j] >> 4 : blk[16 + (g / 2) * 32 + j] & 15u;
+                    const unsigned hi =
+                        g % 2 ? blk[16 + (g / 2) * 32 + j + 16] >> 4 : blk[16 + (g / 2) * 32 + j + 16] & 15u;
+                    q[g * 16 + j] = (unsigned char)(lo | (hi << 4));
+                }
+            for (int j = 0; j < 16; ++j) meta[(r * nb + b) * 16 + j] = blk[j];
+        }
+    }
+}
+
+// Value of element k of row r in the engine layout (embedding gather and
+// the finite check).  Same operation order as the reference dequantisers.
+__device__ __forceinline__ float element(const DeviceMatrix& w, long long r, int k) {
+    const unsigned char* qs = w.qs + r * w.qs_row;
+    const unsigned char* meta = w.meta + r * w.meta_row;
+    switch (w.type) {
+        case kF32: return reinterpret_cast<const float*>(qs)[k];
+        case kF16: return h2f(reinterpret_cast<const unsigned short*>(qs)[k]);
+        case kQ8_0: {
+            const unsigned short d = reinterpret_cast<const unsigned short*>(meta)[k / 32];
+            return __fmul_rn(half_bits_to_float(d), float((signed char)qs[k]));
+        }
+        case kQ4_0: {
+            const unsigned short d = reinterpret_cast<const unsigned short*>(meta)[k / 32];
+            const unsigned char byte = qs[(k / 32) * 16 + (k % 16)];
+            const unsigned q = (k % 32) < 16 ? (byte & 15u) : (byte >> 4);
+            return __fmul_rn(half_bits_to_float(d), float(int(q) - 8));
+        }
+        default: {  // Q4_K
+            const int b = k / 256, g = (k % 256) / 32, j = k % 32;
+            const unsigned char* m = meta + b * 16;
+            const float d = half_bits_to_float(m[0] | (m[1] << 8));
+            const float dmin = half_bits_to_float(m[2] | (m[3] << 8));
+            unsigned sc, mn;
+            q4k_scale_min(m + 4, g, sc, mn);
+            const unsigned char byte = qs[(k / 32) * 16 + (j % 16)];
+            const unsigned q = j < 16 ? (byte & 15u) : (byte >> 4);
+            return __fsub_rn(__fmul_rn(__fmul_rn(d, float(sc)), float(q)), __fmul_rn(dmin, float(mn)));
+        }
+    }
+}
+
+__global__ void finite_kernel(DeviceMatrix w, int* flag) {
+    const long long total = (long long)w.rows * w.cols;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const float v = element(w, i / w.cols, int(i % w.cols));
+        if (!isfinite(v)) atomicExch(flag, 1);
+    }
+}
+
+__global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx) {
+    const int t = blockIdx.x;
+    const long long r = tokens[t];
+    for (int k = threadIdx.x; k < w.cols; k += blockDim.x) x[(long long)t * ldx + k] = element(w, r, k);
+}
+
+// ----------------------------------------------------------------- GEMV
+// x is staged in shared memory, padded by 4 floats every 128 so that the
+// lanes of a quarter-warp read distinct banks, with the per-32 sums S that
+// let the 4-bit kernels work on 1+q/16 instead of q (see dot_q4).
+__host__ __device__ __forceinline__ int xpad(int k) { return k + ((k >> 7) << 2); }
+
+// 8 nibbles of a word prepared as 0x80|q<<3 per byte, then one PRMT per
+// nibble builds the float 1 + q/16 (exponent byte 0x3F, q in the top of the
+// mantissa).  Exact for q in 0..15.
+__device__ __forceinline__ float nib(unsigned prep, int k) {
+    const unsigned sel = 5u | (5u << 4) | (unsigned(k) << 8) | (4u << 12);
+    return __uint_as_float(__byte_perm(prep, 0x3Fu, sel));
+}
+
+// A = sum over a 32-element unit of (1 + q_e/16) * x_e.  Byte j of the unit:
+// element j in the low nibble, element j+16 in the high nibble.
+__device__ __forceinline__ float dot_q4_unit(uint4 w, const float* xs) {
+    const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const unsigned lo = ((ws[i] << 3) & 0x78787878u) | 0x80808080u;
+        const unsigned hi = ((ws[i] >> 1) & 0x78787878u) | 0x80808080u;
+        const float4 xl = *reinterpret_cast<const float4*>(xs + 4 * i);
+        const float4 xh = *reinterpret_cast<const float4*>(xs + 16 + 4 * i);
+        a0 = fmaf(nib(lo, 0), xl.x, a0);
+        a1 = fmaf(nib(lo, 1), xl.y, a1);
+        a0 = fmaf(nib(lo, 2), xl.z, a0);
+        a1 = fmaf(nib(lo, 3), xl.w, a1);
+        a0 = fmaf(nib(hi, 0), xh.x, a0);
+        a1 = fmaf(nib(hi, 1), xh.y, a1);
+        a0 = fmaf(nib(hi, 2), xh.z, a0);
+        a1 = fmaf(nib(hi, 3), xh.w, a1);
+    }
+    return a0 + a1;
+}
+
+// sum over 16 int8 codes of q*x, q made exact with the 2^23 magic.
+__device__ __forceinline__ float dot_q8_unit(uint4 w, const float* xs) {
+    const unsigned ws[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + 4 * i);
+        // byte k -> 0x4B0000bb = 2^23 + (q + 128); minus (2^23 + 128) = q exactly
+        const float q0 = __uint_as_float(__byte_perm(ws[i], 0x4Bu, 0x4550u)) - 8388736.f;
+        const float q1 = __uint_as_float(__byte_perm(ws[i], 0x4Bu, 0x4551u)) - 8388736.f;
+        const float q2 = __uint_as_float(__byte_perm(ws[i], 0x4Bu, 0x4552u)) - 8388736.f;
+        const float q3 = __uint_as_float(__byte_perm(ws[i], 0x4Bu, 0x4553u)) - 8388736.f;
+        a0 = fmaf(q0, xv.x, a0);
+        a1 = fmaf(q1, xv.y, a1);
+        a0 = fmaf(q2, xv.z, a0);
+        a1 = fmaf(q3, xv.w, a1);
+    }
+    return a0 + a1;
+}
+
+template <int TYPE>
+struct Unit {
+    // elements per 16-byte unit of qs
+    static constexpr int kElems = TYPE == kQ8_0 ? 16 : (TYPE == kF16 ? 8 : (TYPE == kF32 ? 4 : 32));
+};
+
+template <int TYPE>
+__device__ __forceinline__ float unit_dot(uint4 w, const float* xs, float s, int u, const unsigned char* meta) {
+    if constexpr (TYPE == kQ8_0) {
+        const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[u >> 1]);
+        return d * dot_q8_unit(w, xs);
+    } else if constexpr (TYPE == kQ4_0) {
+        const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[u]);
+        // sum d*(q-8)*x = d*(16*A - 24*S)
+        return d * fmaf(16.f, dot_q4_unit(w, xs), -24.f * s);
+    } else if constexpr (TYPE == kQ4_K) {
+        const uint4 m = __ldg(reinterpret_cast<const uint4*>(meta) + (u >> 3));
+        const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xffff)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
+        float sc, mn;
+        q4k_scale_min_w(m.y, m.z, m.w, u & 7, sc, mn);
+        // sum (d*sc*q - dmin*m)*x = 16*d*sc*A - (16*d*sc + dmin*m)*S
+        const float ds = 16.f * d * sc;
+        return fmaf(ds, dot_q4_unit(w, xs), -fmaf(dmin, mn, ds) * s);
+    } else if constexpr (TYPE == kF16) {
+        const __half2* h = reinterpret_cast<const __half2*>(&w);
+        const float4 x0 = *reinterpret_cast<const float4*>(xs);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + 4);
+        const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]),
+                     e = __half22float2(h[3]);
+        float r = a.x * x0.x;
+        r = fmaf(a.y, x0.y, r);
+        r = fmaf(b.x, x0.z, r);
+        r = fmaf(b.y, x0.w, r);
+        r = fmaf(c.x, x1.x, r);
+        r = fmaf(c.y, x1.y, r);
+        r = fmaf(e.x, x1.z, r);
+        return fmaf(e.y, x1.w, r);
+    } else {
+        const float4 x0 = *reinterpret_cast<const float4*>(xs);
+        float r = __uint_as_float(w.x) * x0.x;
+        r = fmaf(__uint_as_float(w.y), x0.y, r);
+        r = fmaf(__uint_as_float(w.z), x0.z, r);
+        return fmaf(__uint_as_float(w.w), x0.w, r);
+    }
+}
+
+// The reference SwiGLU (model.hpp:120-124): gate * (sigmoid(gate) * up).
+__device__ __forceinline__ float swiglu(float g, float up) {
+    const float small = expf(-fabsf(g));
+    const float sig = g >= 0.f ? 1.f / (1.f + small) : small / (1.f + small);
+    return __fmul_rn(g, __fmul_rn(sig, up));
+}
+
+// R rows per warp, NT tokens per pass; each warp streams its rows once per
+// pass over the K chunk held in shared memory.
+template <int TYPE, int R, int NT>
+__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemmArgs a, int kc) {
+    extern __shared__ float smem[];
+    constexpr int E = Unit<TYPE>::kElems;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row0 = (blockIdx.x * kWarps + warp) * R;
+    const int K = a.w.cols;
+    const int kcp = xpad(kc);  // padded chunk stride
+    float* xs = smem;                 // [NT][kcp]
+    float* s32 = smem + NT * kcp;     // [NT][kc/32]
+    for (int t0 = 0; t0 < a.tokens; t0 += NT) {
+        const int nt = min(NT, a.tokens - t0);
+        float acc[R][NT];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+        for (int k0 = 0; k0 < K; k0 += kc) {
+            const int klen = min(kc, K - k0);
+            __syncthreads();
+            for (int i = threadIdx.x; i < NT * (klen / 4); i += blockDim.x) {
+                const int t = i / (klen / 4), k = (i % (klen / 4)) * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < nt) v = __ldg(reinterpret_cast<const float4*>(a.x + (long long)(t0 + t) * a.ldx + k0 + k));
+                *reinterpret_cast<float4*>(xs + t * kcp + xpad(k)) = v;
+            }
+            __syncthreads();
+            if (TYPE == kQ4_0 || TYPE == kQ4_K) {
+                for (int i = threadIdx.x; i < NT * (klen / 32); i += blockDim.x) {
+                    const int t = i / (klen / 32), g = i % (klen / 32);
+                    const float* p = xs + t * kcp + xpad(g * 32);
+                    float s = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) s += p[j];
+                    s32[t * (kc / 32) + g] = s;
+                }
+                __syncthreads();
+            }
+            if (row0 < a.w.rows) {
+                const int units = klen / E, ubase = k0 / E;
+#pragma unroll 2
+                for (int u = lane; u < units; u += 32) {
+                    uint4 wv[R];
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const int row = min(row0 + r, a.w.rows - 1);
+                        wv[r] = ld_stream(a.w.qs + (long long)row * a.w.qs_row + (long long)(ubase + u) * 16);
+                    }
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if (t < nt) {
+                            const float* xp = xs + t * kcp + xpad(u * E);
+                            const float sv = (TYPE == kQ4_0 || TYPE == kQ4_K) ? s32[t * (kc / 32) + u] : 0.f;
+#pragma unroll
+                            for (int r = 0; r < R; ++r) {
+                                const int row = min(row0 + r, a.w.rows - 1);
+                                const unsigned char* meta = a.w.meta + (long long)row * a.w.meta_row;
+                                acc[r][t] += unit_dot<TYPE>(wv[r], xp, sv, ubase + u, meta);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (row0 < a.w.rows) {
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    float v = acc[r][t];
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    acc[r][t] = v;
+                }
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= nt) continue;
+                    float* y = a.y + (long long)(t0 + t) * a.ldy;
+                    if (a.epilogue == kSwiGLU) {
+#pragma unroll
+                        for (int r = 0; r + 1 < R; r += 2)
+                            if (row0 + r + 1 < a.w.rows) y[(row0 + r) / 2] = swiglu(acc[r][t], acc[r + 1][t]);
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            if (row0 + r >= a.w.rows) continue;
+                            if (a.epilogue == kAdd) y[row0 + r] += acc[r][t];
+                            else y[row0 + r] = acc[r][t];
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <int TYPE, int R, int NT>
+void run_gemv(const GemmArgs& a, cudaStream_t s) {
+    constexpr int E = Unit<TYPE>::kElems;
+    // K chunk: largest multiple of 256 whose staged activations fit 48 KB.
+    const int budget = 48 * 1024;
+    int kc = (budget / (NT * 4)) * 128 / 136 / 256 * 256;  // padding of 4 per 128
+    kc = kc - kc % 256;
+    if (kc >= a.w.cols) kc = a.w.cols;
+    (void)E;
+    const std::size_t smem = std::size_t(NT) * (xpad(kc) + kc / 32 + 4) * sizeof(float);
+    const int rows_per_cta = kWarps * R;
+    const int grid = (a.w.rows + rows_per_cta - 1) / rows_per_cta;
+    gemv_kernel<TYPE, R, NT><<<grid, kWarps * 32, smem, s>>>(a, kc);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+template <int TYPE>
+void dispatch_tokens(const GemmArgs& a, cudaStream_t s) {
+    if (a.tokens <= 1) run_gemv<TYPE, 4, 1>(a, s);
+    else if (a.tokens <= 2) run_gemv<TYPE, 4, 2>(a, s);
+    else run_gemv<TYPE, 2, 4>(a, s);
+}
+
+__global__ void to_half_kernel(const float* x, int ldx, __half* out, int tokens, int cols) {
+    const long long total = (long long)tokens * cols;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i / cols, k = i % cols;
+        out[i] = __float2half_rn(x[t * ldx + k]);
+    }
+}
+
+}  // namespace
+
+void launch_gemv(const GemmArgs& a, cudaStream_t s) {
+    if (a.tokens <= 0) return;
+    if (a.epilogue == kSwiGLU && (a.w.rows % 2)) throw std::invalid_argument("SwiGLU needs paired rows");
+    switch (a.w.type) {
+        case kQ8_0: dispatch_tokens<kQ8_0>(a, s); break;
+        case kQ4_0: dispatch_tokens<kQ4_0>(a, s); break;
+        case kQ4_K: dispatch_tokens<kQ4_K>(a, s); break;
+        case kF16: dispatch_tokens<kF16>(a, s); break;
+        case kF32: dispatch_tokens<kF32>(a, s); break;
+        default: throw std::invalid_argument("unsupported projection type");
+    }
+}
+
+void launch_to_half(const float* x, int ldx, __half* out, int tokens, int cols, cudaStream_t s) {
+    const long long total = (long long)tokens * cols;
+    const int grid = int(std::min<long long>((total + 255) / 256, 148 * 16));
+    to_half_kernel<<<grid, 256, 0, s>>>(x, ldx, out, tokens, cols);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+void launch_dequantize(int type, const void* blocks, std::size_t nblocks, float* out, cudaStream_t s) {
+    std::size_t per = 0, bytes = 0;
+    if (!block_shape(type, per, bytes)) throw std::invalid_argument("unsupported quantized type");
+    const std::size_t total = nblocks * per;
+    if (!total) return;
+    const int grid = int(std::min<std::size_t>((total + 255) / 256, 148 * 32));
+    dequant_kernel<<<grid, 256, 0, s>>>(type, static_cast<const unsigned char*>(blocks), nblocks, out);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t* qs, std::uint8_t* meta,
+                   cudaStream_t s) {
+    if (type == kF32 || type == kF16) {
+        TVARA_CUDA(cudaMemcpyAsync(qs, gguf, std::size_t(rows) * qs_row_bytes(type, cols), cudaMemcpyDeviceToDevice, s));
+        return;
+    }
+    const int per = type == kQ4_K ? 256 : 32;
+    const std::size_t total = std::size_t(rows) * (cols / per);
+    const int grid = int(std::min<std::size_t>((total + 255) / 256, 148 * 32));
+    repack_kernel<<<grid, 256, 0, s>>>(type, static_cast<const unsigned char*>(gguf), rows, cols, qs, meta);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s) {
+    finite_kernel<<<148 * 8, 256, 0, s>>>(w, flag);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s) {
+    if (n <= 0) return;
+    embed_kernel<<<n, 256, 0, s>>>(emb, tokens, x, ldx);
+    TVARA_CUDA(cudaGetLastError());
+}
+
+}  // namespace tvara

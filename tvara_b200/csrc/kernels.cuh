@@ -1,0 +1,109 @@
+// Kernel launchers of the B200 decode/prefill engine (sm_100a).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.hpp"
+
+namespace tvara {
+
+// ---- epilogues of the projection kernels --------------------------------
+enum Epilogue : int {
+    kStore = 0,   // y[t][c] = acc
+    kAdd = 1,     // y[t][c] += acc            (residual add, o_proj / down_proj)
+    kSwiGLU = 2,  // rows (2i, 2i+1) = (gate_i, up_i): y[t][i] = silu(gate)*up
+};
+
+struct GemmArgs {
+    DeviceMatrix w;
+    const float* x = nullptr;   // [tokens][ldx] F32 activations
+    int ldx = 0;
+    const __half* xh = nullptr; // optional F16 copy of x for the tensor-core path
+    int tokens = 0;
+    float* y = nullptr;         // [tokens][ldy]
+    int ldy = 0;
+    int epilogue = kStore;
+};
+
+// y = epilogue(x . W^T): CUDA-core GEMV for small token counts.
+void launch_gemv(const GemmArgs& a, cudaStream_t s);
+// Tensor-core (tcgen05/TMEM) projection for larger token counts; falls
+// back to nothing -- callers pick it only where gemm_tc_supported() holds.
+bool gemm_tc_supported(const DeviceMatrix& w, int tokens);
+void launch_gemm_tc(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s);
+std::size_t gemm_tc_workspace(int max_tokens, int max_cols);
+// x [tokens][cols] F32 -> F16 copy (feeds the tensor-core path).
+void launch_to_half(const float* x, int ldx, __half* out, int tokens, int cols, cudaStream_t s);
+// Choose and run the projection (GEMV below the crossover, tensor cores above).
+void launch_projection(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s);
+
+// ---- block unpack / repack ----------------------------------------------
+// GGUF blocks of `type` -> F32, bit-exact with the reference's dequantisers.
+void launch_dequantize(int type, const void* blocks, std::size_t nblocks, float* out, cudaStream_t s);
+// GGUF rows [rows][row bytes] -> engine split layout (qs, meta).
+void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t* qs, std::uint8_t* meta,
+                   cudaStream_t s);
+// Sets *flag when any dequantised value of the matrix is not finite.
+void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s);
+
+// ---- elementwise ----------------------------------------------------------
+// x[t] = row tokens[t] of the embedding, dequantised.
+void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s);
+// out[i] = (x[rows[i]] * inv_rms) * w ; rows == nullptr means i.
+void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
+                    float* out, int ldo, cudaStream_t s);
+// (Combined with launch_rmsnorm) also emits an F16 copy for the tensor-core path.
+void launch_rmsnorm_h(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
+                      float* out, int ldo, __half* outh, cudaStream_t s);
+
+struct RopeArgs {
+    const float* qkv = nullptr;  // [T][ldqkv]: q (hq*d) | k (hkv*d) | v (hkv*d)
+    int ldqkv = 0;
+    float* q = nullptr;          // [T][hq*d] rotated queries
+    int tokens = 0, hq = 0, hkv = 0, dim = 0;
+    bool interleaved = false;
+    const float* cosines = nullptr;  // [context][dim/2]
+    const float* sines = nullptr;
+    const int* positions = nullptr;  // [T]
+    const int* slot_block = nullptr; // [T] physical block of the token's position
+    const int* slot_index = nullptr; // [T] slot within the block
+    void* kv = nullptr;              // pool base
+    int kv_f16 = 0;
+    long long block_stride = 0, layer_offset = 0, kind_stride = 0;  // elements
+    int tpb = 0;
+    int max_blocks = 0;
+    int* err = nullptr;
+};
+// Rotates q and k at each token's position and writes k, v into the pool.
+void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
+
+// g[i] = g[i] * (sigmoid(g[i]) * u[i]) for separate gate/up projections.
+void launch_swiglu(float* g, const float* u, long long n, cudaStream_t s);
+
+// ---- paged attention -------------------------------------------------------
+struct AttnArgs {
+    const float* q = nullptr;  // [T][hq*d]
+    float* out = nullptr;      // [T][hq*d]
+    const void* kv = nullptr;
+    int kv_f16 = 0;
+    int hq = 0, hkv = 0, dim = 0, tpb = 0;
+    long long block_stride = 0, layer_offset = 0, kind_stride = 0;  // elements
+    const int* tables = nullptr;  // concatenated physical block ids
+    const int4* work = nullptr;   // {token, table offset, pos begin, pos end}
+    const int* work_part = nullptr;  // partial slot per work item, -1 = whole range
+    int n_work = 0;
+    float* partial = nullptr;     // [n_parts][hq][dim+2]
+    const int4* combine = nullptr; // {token, first part, part count, 0}
+    int n_combine = 0;
+    int max_blocks = 0;
+    int* err = nullptr;
+};
+void launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// ---- output ---------------------------------------------------------------
+// argmax of each row (first index of the maximum; NaN counts as maximal).
+void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, cudaStream_t s);
+// Copies whole KV blocks (copy-on-write): pairs of (from, to) block ids.
+void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n, cudaStream_t s);
+
+}  // namespace tvara

@@ -1,0 +1,168 @@
+// Kernel-level C ABI (include/tvara_kernels.h): single hot-path kernels on
+// caller-owned device memory.
+#include "../../include/tvara_kernels.h"
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "attention_plan.hpp"
+#include "kernels.cuh"
+
+namespace tvara {
+std::string& last_error();
+}
+
+namespace {
+
+template <class F>
+int guarded(F&& body) {
+    tvara::last_error().clear();
+    try {
+        body();
+        return 0;
+    } catch (const std::exception& e) {
+        tvara::last_error() = e.what();
+        return -1;
+    }
+}
+
+std::size_t align256(std::size_t n) { return (n + 255) & ~std::size_t(255); }
+
+tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, std::size_t cols) {
+    std::size_t e = 0, w = 0;
+    if (!tvara::block_shape(type, e, w)) throw std::invalid_argument("unsupported quantized type");
+    if (!rows || !cols || cols % e || rows > 0x7fffffff || cols > 0x7fffffff)
+        throw std::invalid_argument("invalid quantized matrix dimensions");
+    if (type == tvara::kF32 && cols % 4) throw std::invalid_argument("F32 rows must be a multiple of 4 wide");
+    if (type == tvara::kF16 && cols % 8) throw std::invalid_argument("F16 rows must be a multiple of 8 wide");
+    tvara::DeviceMatrix m;
+    m.type = type;
+    m.rows = int(rows);
+    m.cols = int(cols);
+    m.qs_row = tvara::qs_row_bytes(type, cols);
+    m.meta_row = tvara::meta_row_bytes(type, cols);
+    m.qs = static_cast<const std::uint8_t*>(packed);
+    m.meta = m.qs + align256(m.qs_row * rows);
+    return m;
+}
+
+struct AttnLayout {
+    tvara::AttnPlan plan;
+    std::size_t off_tables = 0, off_work = 0, off_part = 0, off_comb = 0, off_partial = 0, off_err = 0, total = 0;
+};
+
+constexpr std::size_t kPartsCap = 16384;
+
+AttnLayout layout_for(const tvara_attention_args* a) {
+    if (!a || a->struct_size < sizeof(tvara_attention_args)) throw std::invalid_argument("invalid attention arguments");
+    if (!a->heads || !a->kv_heads || a->heads % a->kv_heads || !a->block_tokens || !a->layers || a->layer >= a->layers)
+        throw std::invalid_argument("invalid attention geometry");
+    AttnLayout L;
+    std::vector<int> vis(a->n_queries), off(a->n_queries);
+    for (std::size_t i = 0; i < a->n_queries; ++i) {
+        if (!a->visible[i]) throw std::invalid_argument("empty fused attention");
+        const std::size_t blocks = (a->visible[i] + a->block_tokens - 1) / a->block_tokens;
+        if (a->table_offset[i] + blocks > a->tables_len) throw std::invalid_argument("block table shorter than visible range");
+        vis[i] = int(a->visible[i]);
+        off[i] = int(a->table_offset[i]);
+    }
+    L.plan = tvara::plan_attention(vis, off, int(a->block_tokens), int(a->kv_heads), kPartsCap);
+    std::size_t at = 0;
+    L.off_tables = at;
+    at = align256(at + a->tables_len * 4);
+    L.off_work = at;
+    at = align256(at + L.plan.work.size() * 16);
+    L.off_part = at;
+    at = align256(at + L.plan.part.size() * 4);
+    L.off_comb = at;
+    at = align256(at + L.plan.comb.size() * 16);
+    L.off_partial = at;
+    at = align256(at + std::size_t(L.plan.parts) * a->heads * (a->head_dim + 2) * 4);
+    L.off_err = at;
+    L.total = align256(at + 4);
+    return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tvara_dequantize(int type, const void* blocks, size_t nblocks, float* out, void* stream) {
+    return guarded([&] { tvara::launch_dequantize(type, blocks, nblocks, out, static_cast<cudaStream_t>(stream)); });
+}
+
+size_t tvara_packed_bytes(int type, size_t rows, size_t cols) {
+    std::size_t e = 0, w = 0;
+    if (!tvara::block_shape(type, e, w) || !cols || cols % e) return 0;
+    return align256(tvara::qs_row_bytes(type, cols) * rows) + align256(tvara::meta_row_bytes(type, cols) * rows);
+}
+
+int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream) {
+    return guarded([&] {
+        auto m = packed_view(type, packed, rows, cols);
+        tvara::launch_repack(type, gguf_rows, int(rows), int(cols), const_cast<std::uint8_t*>(m.qs),
+                             const_cast<std::uint8_t*>(m.meta), static_cast<cudaStream_t>(stream));
+    });
+}
+
+int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, const float* x, size_t tokens,
+                       float* y, void* stream) {
+    return guarded([&] {
+        tvara::GemmArgs g;
+        g.w = packed_view(type, packed, rows, cols);
+        g.x = x;
+        g.ldx = int(cols);
+        g.tokens = int(tokens);
+        g.y = y;
+        g.ldy = int(rows);
+        g.epilogue = tvara::kStore;
+        tvara::launch_projection(g, nullptr, 0, static_cast<cudaStream_t>(stream));
+    });
+}
+
+size_t tvara_paged_attention_workspace(const tvara_attention_args* a) {
+    std::size_t n = 0;
+    if (guarded([&] { n = layout_for(a).total; })) return 0;
+    return n;
+}
+
+int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+    return guarded([&] {
+        auto L = layout_for(a);
+        if (!workspace || workspace_bytes < L.total) throw std::invalid_argument("attention workspace too small");
+        auto s = static_cast<cudaStream_t>(stream);
+        auto* base = static_cast<std::uint8_t*>(workspace);
+        std::vector<std::uint8_t> host(L.off_partial);
+        std::memcpy(host.data() + L.off_tables, a->tables, a->tables_len * 4);
+        std::memcpy(host.data() + L.off_work, L.plan.work.data(), L.plan.work.size() * 16);
+        std::memcpy(host.data() + L.off_part, L.plan.part.data(), L.plan.part.size() * 4);
+        std::memcpy(host.data() + L.off_comb, L.plan.comb.data(), L.plan.comb.size() * 16);
+        TVARA_CUDA(cudaMemcpyAsync(base, host.data(), host.size(), cudaMemcpyHostToDevice, s));
+        TVARA_CUDA(cudaMemsetAsync(base + L.off_err, 0, 4, s));
+        tvara::AttnArgs g;
+        g.q = a->q;
+        g.out = a->out;
+        g.kv = a->pool;
+        g.kv_f16 = a->kv_dtype == TVARA_KV_F16;
+        g.hq = int(a->heads);
+        g.hkv = int(a->kv_heads);
+        g.dim = int(a->head_dim);
+        g.tpb = int(a->block_tokens);
+        g.kind_stride = (long long)a->kv_heads * a->block_tokens * a->head_dim;
+        g.layer_offset = (long long)a->layer * 2 * g.kind_stride;
+        g.block_stride = (long long)a->layers * 2 * g.kind_stride;
+        g.tables = reinterpret_cast<const int*>(base + L.off_tables);
+        g.work = reinterpret_cast<const int4*>(base + L.off_work);
+        g.work_part = reinterpret_cast<const int*>(base + L.off_part);
+        g.n_work = int(L.plan.work.size());
+        g.partial = reinterpret_cast<float*>(base + L.off_partial);
+        g.combine = reinterpret_cast<const int4*>(base + L.off_comb);
+        g.n_combine = int(L.plan.comb.size());
+        g.max_blocks = int(a->max_blocks);
+        g.err = reinterpret_cast<int*>(base + L.off_err);
+        tvara::launch_attention(g, s);
+    });
+}
+
+}  // extern "C"

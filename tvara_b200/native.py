@@ -1,0 +1,346 @@
+"""Owned ctypes handle over the B200 engine, mirroring the reference's
+python/tvara/native.py:27-345 (same constructor, ``logits``, ``iter_tokens``,
+``generate``, ``metadata`` and error behaviour), plus the additive calls:
+``decode_batch`` (multi-token append with rollback), ``batch_step`` (one
+device step over a ragged batch of sequences), ``fork``, ``truncate``, KV
+inspection and the radix prefix cache.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import json
+import threading
+import weakref
+from pathlib import Path
+
+import numpy as np
+
+from . import load_library
+from ._bindings import OpenOptions, F32P, U32P, U64P, I32P
+
+KV_F32, KV_F16 = 0, 1
+STEP_ALL_LOGITS = 1
+
+
+def _ptr(a: np.ndarray, typ):
+    return a.ctypes.data_as(typ)
+
+
+class NativeModel:
+    def __init__(self, path, library=None, max_blocks=256, block_tokens=16, *, kv_dtype=None, device=None,
+                 max_step_tokens=None, tp_rank=0, tp_size=1, nccl_id: bytes | None = None):
+        self._lock = threading.RLock()
+        self._library = load_library(library)
+        lib = self._library
+        if (not isinstance(max_blocks, int) or not isinstance(block_tokens, int) or max_blocks <= 0
+                or block_tokens <= 0):
+            raise ValueError("Cache geometry must be positive integers")
+        encoded = str(Path(path).resolve()).encode("utf-8")
+        if kv_dtype is None and device is None and max_step_tokens is None and tp_size == 1:
+            self._handle = lib.tvara_model_open(encoded, max_blocks, block_tokens)
+        else:
+            opts = OpenOptions()
+            opts.struct_size = C.sizeof(OpenOptions)
+            opts.device = -1 if device is None else int(device)
+            opts.kv_dtype = {None: KV_F32, "f32": KV_F32, "f16": KV_F16, KV_F32: KV_F32, KV_F16: KV_F16}[kv_dtype]
+            opts.max_step_tokens = int(max_step_tokens or 0)
+            opts.tp_rank, opts.tp_size = int(tp_rank), int(tp_size)
+            self._nccl_id = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
+            opts.nccl_id = C.cast(self._nccl_id, C.c_void_p) if self._nccl_id is not None else None
+            self._handle = lib.tvara_model_open_ex(encoded, max_blocks, block_tokens, C.byref(opts))
+        if not self._handle:
+            self._raise_error()
+        self._finalizer = weakref.finalize(self, lib.tvara_model_close, self._handle)
+        self.vocab_size = int(lib.tvara_model_vocab_size(self._handle))
+        self.context_size = int(lib.tvara_model_context_size(self._handle))
+        self._tokenizer = None
+
+    # ------------------------------------------------------------- lifecycle
+    def _raise_error(self):
+        message = self._library.tvara_last_error()
+        raise RuntimeError(message.decode("utf-8", errors="replace") if message else "Native operation failed")
+
+    def _check_open(self):
+        if not self._handle:
+            raise RuntimeError("Model is closed")
+
+    def close(self):
+        with self._lock:
+            if self._handle:
+                self._finalizer()
+                self._handle = None
+
+    def __enter__(self):
+        self._check_open()
+        return self
+
+    def __exit__(self, *args):
+        self.close()
+
+    @property
+    def metadata(self):
+        with self._lock:
+            self._check_open()
+            raw = self._library.tvara_model_metadata(self._handle)
+            if not raw:
+                self._raise_error()
+            return json.loads(raw.decode("utf-8"))
+
+    # ------------------------------------------------------------- sequences
+    def _new_sequence(self):
+        with self._lock:
+            self._check_open()
+            seq = self._library.tvara_sequence_create(self._handle)
+            if not seq:
+                self._raise_error()
+            return seq
+
+    def _drop_sequence(self, sequence):
+        with self._lock:
+            if self._handle and self._library.tvara_sequence_drop(self._handle, sequence):
+                self._raise_error()
+
+    def logits(self, sequence, token):
+        if isinstance(token, (bool, np.bool_)) or not isinstance(token, (int, np.integer)) \
+                or not 0 <= token < self.vocab_size:
+            raise ValueError("Invalid token ID")
+        out = np.empty(self.vocab_size, dtype=np.float32)
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_decode(self._handle, sequence, int(token), _ptr(out, F32P), len(out)):
+                self._raise_error()
+        return out
+
+    def decode_batch(self, sequence, tokens) -> np.ndarray:
+        """tvara_sequence_decode_batch: every row's logits, rollback on failure."""
+        toks = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty((len(toks), self.vocab_size), dtype=np.float32)
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_decode_batch(self._handle, sequence, _ptr(toks, U32P), len(toks),
+                                                         _ptr(out, F32P), out.size):
+                self._raise_error()
+        return out
+
+    def truncate(self, sequence, length):
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_truncate(self._handle, sequence, int(length)):
+                self._raise_error()
+
+    def fork(self, sequence):
+        with self._lock:
+            self._check_open()
+            seq = self._library.tvara_sequence_fork(self._handle, sequence)
+            if not seq:
+                self._raise_error()
+            return seq
+
+    def sequence_length(self, sequence) -> int:
+        n = C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_length(self._handle, sequence, C.byref(n)):
+                self._raise_error()
+        return n.value
+
+    def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False):
+        """One device step: sequence i appends token_lists[i].  Returns
+        (logits [rows, vocab] or None, argmax [rows] or None) with one row per
+        sequence (its last token) or per token when all_logits."""
+        seqs = np.ascontiguousarray(sequences, dtype=np.uint64)
+        lens = np.array([len(t) for t in token_lists], dtype=np.uint32)
+        cu = np.zeros(len(seqs) + 1, dtype=np.uint32)
+        np.cumsum(lens, out=cu[1:])
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.uint32) for t in token_lists]))
+        rows = int(cu[-1]) if all_logits else len(seqs)
+        out = np.empty((rows, self.vocab_size), dtype=np.float32) if logits else None
+        am = np.empty(rows, dtype=np.uint32) if argmax else None
+        with self._lock:
+            self._check_open()
+            status = self._library.tvara_batch_step(
+                self._handle, len(seqs), _ptr(seqs, U64P), _ptr(cu, U32P), _ptr(toks, U32P),
+                STEP_ALL_LOGITS if all_logits else 0,
+                _ptr(out, F32P) if out is not None else None, out.size if out is not None else 0,
+                _ptr(am, U32P) if am is not None else None, len(am) if am is not None else 0)
+            if status:
+                self._raise_error()
+        return out, am
+
+    # ------------------------------------------------------- KV inspection
+    def kv_stats(self):
+        a, m = C.c_size_t(), C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_kv_stats(self._handle, C.byref(a), C.byref(m)):
+                self._raise_error()
+        return a.value, m.value
+
+    def kv_audit(self):
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_kv_audit(self._handle):
+                self._raise_error()
+
+    def sequence_blocks(self, sequence):
+        n = C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_blocks(self._handle, sequence, None, None, 0, C.byref(n)):
+                self._raise_error()
+            ids = np.empty(n.value, np.uint64)
+            gens = np.empty(n.value, np.uint64)
+            if self._library.tvara_sequence_blocks(self._handle, sequence, _ptr(ids, U64P), _ptr(gens, U64P),
+                                                   n.value, C.byref(n)):
+                self._raise_error()
+        return list(zip(ids.tolist(), gens.tolist()))
+
+    def kv_references(self, block_id) -> int:
+        r = C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_kv_references(self._handle, block_id, C.byref(r)):
+                self._raise_error()
+        return r.value
+
+    # --------------------------------------------------------- prefix cache
+    def prefix_insert(self, tokens, sequence) -> int:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        with self._lock:
+            self._check_open()
+            node = self._library.tvara_prefix_insert(self._handle, _ptr(t, I32P), len(t), sequence)
+            if not node:
+                self._raise_error()
+        return node
+
+    def prefix_reuse(self, tokens, partial=False):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        n = C.c_size_t()
+        with self._lock:
+            self._check_open()
+            seq = self._library.tvara_prefix_reuse(self._handle, _ptr(t, I32P), len(t), int(bool(partial)),
+                                                   C.byref(n))
+            if not seq:
+                self._raise_error()
+        return seq, n.value
+
+    def prefix_lookup(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        node, n = C.c_uint64(), C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_prefix_lookup(self._handle, _ptr(t, I32P), len(t), C.byref(node), C.byref(n)):
+                self._raise_error()
+        return node.value, n.value
+
+    def _prefix_call(self, name, node):
+        with self._lock:
+            self._check_open()
+            if getattr(self._library, name)(self._handle, node):
+                self._raise_error()
+
+    def prefix_pin(self, node):
+        self._prefix_call("tvara_prefix_pin", node)
+
+    def prefix_unpin(self, node):
+        self._prefix_call("tvara_prefix_unpin", node)
+
+    def prefix_touch(self, node):
+        self._prefix_call("tvara_prefix_touch", node)
+
+    def prefix_evict_one(self) -> bool:
+        with self._lock:
+            self._check_open()
+            r = self._library.tvara_prefix_evict_one(self._handle)
+            if r < 0:
+                self._raise_error()
+        return bool(r)
+
+    def prefix_size(self) -> int:
+        with self._lock:
+            self._check_open()
+            return int(self._library.tvara_prefix_size(self._handle))
+
+    # ------------------------------------------------------------ generation
+    def iter_tokens(self, prompt, max_new_tokens=16, temperature=0, seed=0, eos_id=None, top_p=1, top_k=0,
+                    min_p=0, repetition=1, frequency=0, presence=0, token_constraint=None):
+        """Host sampler over device logits, with the reference's parameter
+        checks and filter order (python/tvara/native.py:220-340)."""
+        prompt = list(prompt)
+        if not prompt or any(isinstance(t, (bool, np.bool_)) or not isinstance(t, (int, np.integer))
+                             or not 0 <= t < self.vocab_size for t in prompt):
+            raise ValueError("Invalid prompt token IDs")
+        if (isinstance(max_new_tokens, (bool, np.bool_)) or not isinstance(max_new_tokens, int)
+                or max_new_tokens < 0 or len(prompt) + max_new_tokens > self.context_size):
+            raise ValueError("Generation exceeds context limits")
+
+        def real(value):
+            if isinstance(value, (bool, np.bool_)) or not isinstance(value, (int, float, np.integer, np.floating)):
+                raise ValueError("Sampling parameters must be real scalars")
+            return float(value)
+
+        temperature, top_p, min_p, repetition, frequency, presence = (
+            real(v) for v in (temperature, top_p, min_p, repetition, frequency, presence))
+        if (not np.isfinite(temperature) or temperature < 0 or not np.isfinite(top_p) or not 0 < top_p <= 1
+                or not np.isfinite(min_p) or not 0 <= min_p <= 1):
+            raise ValueError("Invalid sampling parameters")
+        if (isinstance(top_k, (bool, np.bool_)) or not isinstance(top_k, int) or top_k < 0
+                or not np.isfinite(repetition) or repetition <= 0 or not np.isfinite(frequency)
+                or not np.isfinite(presence)):
+            raise ValueError("Invalid sampling filters or penalties")
+        if eos_id is not None and (not isinstance(eos_id, (int, np.integer)) or isinstance(eos_id, bool)
+                                   or not 0 <= eos_id < self.vocab_size):
+            raise ValueError("Invalid EOS ID")
+        if isinstance(seed, (bool, np.bool_)):
+            raise ValueError("Invalid random seed")
+        try:
+            rng = np.random.default_rng(seed)
+        except (ValueError, TypeError, OverflowError) as error:
+            raise ValueError("Invalid random seed") from error
+        sequence = self._new_sequence()
+        history = prompt.copy()
+        try:
+            # the prompt is one device step (all rows computed, last one kept)
+            logits = self.decode_batch(sequence, prompt)[-1]
+            for index in range(max_new_tokens):
+                logits = logits.astype(np.float64, copy=True)
+                if not np.isfinite(logits).all():
+                    raise ValueError("Nonfinite model logits")
+                counts = np.bincount(history, minlength=self.vocab_size)
+                seen = counts > 0
+                with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+                    logits[seen] = np.where(logits[seen] >= 0, logits[seen] / repetition, logits[seen] * repetition)
+                    logits -= counts * frequency + seen * presence
+                if not np.isfinite(logits).all():
+                    raise ValueError("Nonfinite adjusted sampling logits")
+                if token_constraint is not None:
+                    logits = token_constraint.mask_logits(logits)
+                if temperature == 0:
+                    token = int(logits.argmax())
+                else:
+                    values = (logits - float(logits.max())) / temperature
+                    p = np.exp(values)
+                    p /= p.sum()
+                    order = np.argsort(-p, kind="stable")
+                    if top_k:
+                        p[order[top_k:]] = 0
+                    p[p < p.max() * min_p] = 0
+                    p /= p.sum()
+                    cumulative = np.cumsum(p[order])
+                    p[order[np.r_[False, cumulative[:-1] >= top_p]]] = 0
+                    p /= p.sum()
+                    token = int(rng.choice(self.vocab_size, p=p))
+                if token_constraint is not None:
+                    token_constraint.accept(token)
+                history.append(token)
+                yield token
+                if token == eos_id:
+                    break
+                if index + 1 < max_new_tokens:
+                    logits = self.logits(sequence, token)
+        finally:
+            self._drop_sequence(sequence)
+
+    def generate(self, prompt, **options):
+        return list(self.iter_tokens(prompt, **options))
