@@ -123,6 +123,50 @@ TVARA_API int tvara_sequence_blocks(tvara_model* model, uint64_t sequence, uint6
 /* Reference count of pool block `id` (BlockPool::references_by_id). */
 TVARA_API int tvara_kv_references(tvara_model* model, size_t id, size_t* references);
 
+/* ---- additive: device access ------------------------------------------ */
+
+/* The cudaStream_t all of the handle's device work runs on (steps finish
+ * with this stream synchronised).  NULL on error. */
+TVARA_API void* tvara_model_stream(tvara_model* model);
+
+/* Device view of the paged KV pool, for KV import (e.g. K/V computed by a
+ * separate prefill service) and for benchmarks.  Element (block b, layer l,
+ * kind 0=K/1=V, KV head g, slot s, e) lives at
+ *   base + ((((b*layers + l)*2 + kind)*kv_heads + g)*block_tokens + s)*head_dim + e
+ * in elements of kv_dtype; kv_heads is this handle's share under tensor
+ * parallelism. */
+typedef struct tvara_kv_pool_info {
+    void* base;
+    size_t max_blocks;
+    size_t block_elements;
+    uint32_t kv_dtype;
+    uint32_t layers, kv_heads, head_dim, block_tokens;
+} tvara_kv_pool_info;
+TVARA_API int tvara_kv_pool(tvara_model* model, tvara_kv_pool_info* info);
+
+/* Appends `count` positions to a sequence's block table exactly as decoding
+ * would (block allocation, copy-on-write of a shared tail) without computing
+ * their K/V; those slots hold whatever the pool holds until written through
+ * tvara_kv_pool.  All-or-nothing.  0 / -1. */
+TVARA_API int tvara_sequence_reserve(tvara_model* model, uint64_t sequence, size_t count);
+
+/* ---- additive: measurement -------------------------------------------- */
+
+/* Device-time accounting per kernel class: while enabled, each step records
+ * CUDA events on the handle's stream around its launch groups.  Enabling
+ * resets the totals.  0 / -1. */
+TVARA_API int tvara_model_profile(tvara_model* model, int enable);
+/* Totals since enabling, in this class order: 0 attention, 1 projections
+ * (GEMV/GEMM), 2 final norm + LM head + argmax, 3 other elementwise
+ * (embedding, RMSNorm, RoPE/KV write, block copies), 4 collectives.  Writes
+ * up to capacity entries; returns the number of classes, -1 on error. */
+TVARA_API int tvara_model_profile_read(tvara_model* model, double* milliseconds, uint64_t* groups, size_t capacity);
+/* Kernel launches this library has issued since it was loaded. */
+TVARA_API uint64_t tvara_kernel_launches(void);
+/* Host->device and device->host bytes the last step on this handle copied
+ * (its packed batch description in, its logits/argmax out).  0 / -1. */
+TVARA_API int tvara_model_step_bytes(tvara_model* model, uint64_t* h2d, uint64_t* d2h);
+
 /* ---- additive: radix prefix cache (core/include/tvara/radix.hpp) ------ */
 
 /* RadixCache::insert + attach (radix.hpp:41-79): caches `sequence`'s KV

@@ -50,6 +50,13 @@ SIGNATURES = {
     "tvara_kv_audit": (C.c_int, [P]),
     "tvara_sequence_blocks": (C.c_int, [P, U64, U64P, U64P, SZ, SZP]),
     "tvara_kv_references": (C.c_int, [P, SZ, SZP]),
+    "tvara_model_profile": (C.c_int, [P, C.c_int]),
+    "tvara_model_profile_read": (C.c_int, [P, C.POINTER(C.c_double), U64P, SZ]),
+    "tvara_kernel_launches": (U64, []),
+    "tvara_model_step_bytes": (C.c_int, [P, U64P, U64P]),
+    "tvara_model_stream": (P, [P]),
+    "tvara_kv_pool": (C.c_int, [P, P]),
+    "tvara_sequence_reserve": (C.c_int, [P, U64, SZ]),
     "tvara_prefix_insert": (U64, [P, I32P, SZ, U64]),
     "tvara_prefix_reuse": (U64, [P, I32P, SZ, C.c_int, SZP]),
     "tvara_prefix_lookup": (C.c_int, [P, I32P, SZ, U64P, SZP]),

@@ -24,11 +24,18 @@ struct tvara_kv_book {
     explicit tvara_kv_book(tvara::CacheGeometry g) : book(g) {}
 };
 
+#include <atomic>
+
 namespace tvara {
 std::string& last_error() {
     thread_local std::string message;
     return message;
 }
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+void note_launches(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+unsigned long long launches() { return g_launches.load(std::memory_order_relaxed); }
 }  // namespace tvara
 
 // The calling thread's message (evaluated per use: the string is thread-local).
@@ -256,6 +263,73 @@ int tvara_kv_references(tvara_model* model, size_t id, size_t* references) {
         auto& e = engine_of(model);
         std::lock_guard lock(model->mutex);
         if (references) *references = e.book().pool().references_by_id(id);
+        return 0;
+    });
+}
+
+int tvara_model_profile(tvara_model* model, int enable) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.set_profiling(enable != 0);
+        return 0;
+    });
+}
+
+int tvara_model_profile_read(tvara_model* model, double* ms, uint64_t* groups, size_t capacity) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        double t[tvara::Engine::kProfClasses];
+        unsigned long long n[tvara::Engine::kProfClasses];
+        e.profile_read(t, n);
+        for (size_t i = 0; i < capacity && i < size_t(tvara::Engine::kProfClasses); ++i) {
+            if (ms) ms[i] = t[i];
+            if (groups) groups[i] = n[i];
+        }
+        return int(tvara::Engine::kProfClasses);
+    });
+}
+
+uint64_t tvara_kernel_launches(void) { return tvara::launches(); }
+
+int tvara_model_step_bytes(tvara_model* model, uint64_t* h2d, uint64_t* d2h) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        if (h2d) *h2d = e.last_h2d();
+        if (d2h) *d2h = e.last_d2h();
+        return 0;
+    });
+}
+
+void* tvara_model_stream(tvara_model* model) {
+    return guarded<void*>(nullptr, [&] { return static_cast<void*>(engine_of(model).stream()); });
+}
+
+int tvara_kv_pool(tvara_model* model, tvara_kv_pool_info* info) {
+    return guarded<int>(-1, [&] {
+        if (!info) throw std::invalid_argument("invalid output pointer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        const auto& g = e.book().geometry();
+        info->base = e.kv_pool();
+        info->max_blocks = g.max_blocks;
+        info->block_elements = size_t(e.block_elements());
+        info->kv_dtype = e.options().kv_f16 ? TVARA_KV_F16 : TVARA_KV_F32;
+        info->layers = uint32_t(g.layers);
+        info->kv_heads = uint32_t(e.local_kv_heads());
+        info->head_dim = uint32_t(g.head_dim);
+        info->block_tokens = uint32_t(g.tokens_per_block);
+        return 0;
+    });
+}
+
+int tvara_sequence_reserve(tvara_model* model, uint64_t sequence, size_t count) {
+    return guarded<int>(-1, [&] {
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.reserve(sequence, count);
         return 0;
     });
 }

@@ -62,7 +62,19 @@ public:
     using std::runtime_error::runtime_error;
 };
 
+// Kernel launches issued by this library since load (all handles, all
+// threads); every launch wrapper adds its launches.
+void note_launches(unsigned long long n = 1);
+unsigned long long launches();
+
 }  // namespace tvara
+
+// After a kernel launch: count it and surface launch errors.
+#define TVARA_LAUNCHED()                          \
+    do {                                          \
+        ::tvara::note_launches();                 \
+        TVARA_CUDA(cudaGetLastError());           \
+    } while (0)
 
 #define TVARA_CUDA(call)                                                                      \
     do {                                                                                      \

@@ -113,6 +113,7 @@ Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t bloc
 
 Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
+    for (auto e : events_) cudaEventDestroy(e);
     radix_.reset();
     coll_.reset();
     for (void* p : {static_cast<void*>(weights_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
@@ -363,6 +364,7 @@ void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint
         for (std::size_t i = 0; i < touched; ++i) book_->truncate(seqs[i], entry[i]);
         throw;
     }
+    acc_h2d_ = acc_d2h_ = 0;
     try {
         // ---- split into device sub-steps of at most tmax_ tokens
         std::size_t i = 0, j = 0;  // sequence, token offset within it
@@ -404,11 +406,85 @@ void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint
             }
             run(sub, logits, argmax, rows_total);
         }
+        last_h2d_ = acc_h2d_;
+        last_d2h_ = acc_d2h_;
     } catch (...) {
         cudaStreamSynchronize(stream_);
         for (std::size_t k = 0; k < n; ++k) book_->truncate(seqs[k], entry[k]);
         throw;
     }
+}
+
+template <class F>
+void Engine::timed(int cls, F&& launch) {
+    if (!profiling_) {
+        launch();
+        return;
+    }
+    if (2 * event_used_ + 2 > events_.size()) {
+        for (int i = 0; i < 64; ++i) {
+            cudaEvent_t e;
+            TVARA_CUDA(cudaEventCreate(&e));
+            events_.push_back(e);
+        }
+        event_class_.resize(events_.size() / 2);
+    }
+    TVARA_CUDA(cudaEventRecord(events_[2 * event_used_], stream_));
+    launch();
+    TVARA_CUDA(cudaEventRecord(events_[2 * event_used_ + 1], stream_));
+    event_class_[event_used_++] = cls;
+}
+
+void Engine::profile_collect() {
+    for (std::size_t i = 0; i < event_used_; ++i) {
+        float ms = 0.f;
+        TVARA_CUDA(cudaEventElapsedTime(&ms, events_[2 * i], events_[2 * i + 1]));
+        prof_ms_[event_class_[i]] += ms;
+        ++prof_n_[event_class_[i]];
+    }
+    event_used_ = 0;
+}
+
+void Engine::set_profiling(bool on) {
+    profiling_ = on;
+    for (int i = 0; i < kProfClasses; ++i) {
+        prof_ms_[i] = 0;
+        prof_n_[i] = 0;
+    }
+}
+
+void Engine::profile_read(double* ms, unsigned long long* groups) const {
+    for (int i = 0; i < kProfClasses; ++i) {
+        if (ms) ms[i] = prof_ms_[i];
+        if (groups) groups[i] = prof_n_[i];
+    }
+}
+
+void Engine::reserve(std::uint64_t seq, std::size_t count) {
+    const std::size_t entry = book_->sequence(seq).length;
+    if (count > cfg_.context - entry) throw std::invalid_argument("paged decode exceeds token/context limits");
+    std::vector<int2> copies;
+    auto copy_now = [&] {
+        if (copies.empty()) return;
+        int2* dev = nullptr;
+        TVARA_CUDA(cudaMalloc(&dev, copies.size() * sizeof(int2)));
+        TVARA_CUDA(cudaMemcpy(dev, copies.data(), copies.size() * sizeof(int2), cudaMemcpyHostToDevice));
+        launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), dev, int(copies.size()), stream_);
+        TVARA_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(dev);
+    };
+    try {
+        for (std::size_t i = 0; i < count; ++i) {
+            BlockCopy c{SIZE_MAX, SIZE_MAX};
+            book_->append(seq, &c);
+            if (c.from != SIZE_MAX) copies.push_back(make_int2(int(c.from), int(c.to)));
+        }
+    } catch (...) {
+        copy_now();
+        book_->truncate(seq, entry);
+        throw;
+    }
+    copy_now();
 }
 
 void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
@@ -458,20 +534,26 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     int2* d_copy = reinterpret_cast<int2*>(put(s.copies.data(), s.copies.size() * 2));
     int* d_rows = put(s.out_rows.data(), R);
     TVARA_CUDA(cudaMemcpyAsync(meta_dev_, meta_host_, at * 4, cudaMemcpyHostToDevice, stream_));
+    acc_h2d_ += at * 4;
 
     const std::size_t es = opt_.kv_f16 ? 2 : 4;
-    launch_block_copy(kv_, block_stride_ * es, d_copy, int(s.copies.size()), stream_);
-    launch_embed(embed_, d_tok, T, x_, D, stream_);
+    event_used_ = 0;
+    timed(kProfOther, [&] {
+        launch_block_copy(kv_, block_stride_ * es, d_copy, int(s.copies.size()), stream_);
+        launch_embed(embed_, d_tok, T, x_, D, stream_);
+    });
     for (int l = 0; l < layers_; ++l) {
         const auto& L = lw_[l];
-        launch_rmsnorm(x_, D, nullptr, T, D, L.attn_norm, cfg_.eps, xn_, D, stream_);
-        if (L.qkv.size() == 1) {
-            projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
-        } else {
-            projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
-            projection(L.qkv[1], xn_, D, T, qkv_ + hq_ * d, qkv_w_, kStore);
-            projection(L.qkv[2], xn_, D, T, qkv_ + (hq_ + hkv_) * d, qkv_w_, kStore);
-        }
+        timed(kProfOther, [&] { launch_rmsnorm(x_, D, nullptr, T, D, L.attn_norm, cfg_.eps, xn_, D, stream_); });
+        timed(kProfProjection, [&] {
+            if (L.qkv.size() == 1) {
+                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
+            } else {
+                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
+                projection(L.qkv[1], xn_, D, T, qkv_ + hq_ * d, qkv_w_, kStore);
+                projection(L.qkv[2], xn_, D, T, qkv_ + (hq_ + hkv_) * d, qkv_w_, kStore);
+            }
+        });
         RopeArgs ra;
         ra.qkv = qkv_;
         ra.ldqkv = qkv_w_;
@@ -494,7 +576,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         ra.tpb = tpb;
         ra.max_blocks = int(book_->geometry().max_blocks);
         ra.err = err_;
-        launch_rope_kv(ra, stream_);
+        timed(kProfOther, [&] { launch_rope_kv(ra, stream_); });
         AttnArgs aa;
         aa.q = q_;
         aa.out = att_;
@@ -516,30 +598,41 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         aa.n_combine = int(comb.size());
         aa.max_blocks = int(book_->geometry().max_blocks);
         aa.err = err_;
-        launch_attention(aa, stream_);
+        timed(kProfAttention, [&] { launch_attention(aa, stream_); });
         const bool lead = opt_.tp_rank == 0;
-        projection(L.o, att_, hq_ * d, T, x_, D, lead ? kAdd : kStore);
-        if (coll_) coll_->allreduce_sum(x_, std::size_t(T) * D, stream_);
-        launch_rmsnorm(x_, D, nullptr, T, D, L.ffn_norm, cfg_.eps, xn_, D, stream_);
-        if (L.gateup.size() == 1) {
-            projection(L.gateup[0], xn_, D, T, ff_, ffn_, kSwiGLU);
-        } else {
-            projection(L.gateup[0], xn_, D, T, ff_, ffn_, kStore);
-            projection(L.gateup[1], xn_, D, T, ffu_, ffn_, kStore);
-            launch_swiglu(ff_, ffu_, T * ffn_, stream_);
-        }
-        projection(L.down, ff_, ffn_, T, x_, D, lead ? kAdd : kStore);
-        if (coll_) coll_->allreduce_sum(x_, std::size_t(T) * D, stream_);
+        // Under tensor parallelism rank 0 adds its partial to the residual and
+        // the others store theirs, so the sum over ranks is x + sum(partials).
+        timed(kProfProjection, [&] { projection(L.o, att_, hq_ * d, T, x_, D, lead ? kAdd : kStore); });
+        if (coll_) timed(kProfCollective, [&] { coll_->allreduce_sum(x_, std::size_t(T) * D, stream_); });
+        timed(kProfOther, [&] { launch_rmsnorm(x_, D, nullptr, T, D, L.ffn_norm, cfg_.eps, xn_, D, stream_); });
+        timed(kProfProjection, [&] {
+            if (L.gateup.size() == 1) {
+                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kSwiGLU);
+            } else {
+                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kStore);
+                projection(L.gateup[1], xn_, D, T, ffu_, ffn_, kStore);
+                launch_swiglu(ff_, ffu_, T * ffn_, stream_);
+            }
+        });
+        timed(kProfProjection, [&] { projection(L.down, ff_, ffn_, T, x_, D, lead ? kAdd : kStore); });
+        if (coll_) timed(kProfCollective, [&] { coll_->allreduce_sum(x_, std::size_t(T) * D, stream_); });
     }
     if (R > 0) {
-        launch_rmsnorm(x_, D, d_rows, R, D, final_norm_, cfg_.eps, xn_, D, stream_);
-        projection(head_, xn_, D, R, logits_, vocab_, kStore);
-        if (argmax) launch_argmax(logits_, R, vocab_, argmax_, stream_);
+        timed(kProfHead, [&] {
+            launch_rmsnorm(x_, D, d_rows, R, D, final_norm_, cfg_.eps, xn_, D, stream_);
+            projection(head_, xn_, D, R, logits_, vocab_, kStore);
+            if (argmax) launch_argmax(logits_, R, vocab_, argmax_, stream_);
+        });
     }
     TVARA_CUDA(cudaMemcpyAsync(err_host_, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     // ---- results to the caller: contiguous destination runs, one copy each
+    acc_d2h_ += sizeof(int);
     std::vector<unsigned> am(argmax ? R : 0);
-    if (argmax && R) TVARA_CUDA(cudaMemcpyAsync(am.data(), argmax_, R * 4, cudaMemcpyDeviceToHost, stream_));
+    if (argmax && R) {
+        TVARA_CUDA(cudaMemcpyAsync(am.data(), argmax_, R * 4, cudaMemcpyDeviceToHost, stream_));
+        acc_d2h_ += std::uint64_t(R) * 4;
+    }
+    if (logits) acc_d2h_ += std::uint64_t(R) * vocab_ * 4;
     if (logits) {
         int k = 0;
         while (k < R) {
@@ -551,6 +644,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         }
     }
     TVARA_CUDA(cudaStreamSynchronize(stream_));
+    profile_collect();
     if (*err_host_) {
         const int code = *err_host_;
         TVARA_CUDA(cudaMemsetAsync(err_, 0, sizeof(int), stream_));

@@ -57,10 +57,35 @@ public:
     void step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
               std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax);
 
+    // Appends positions to a sequence's table without computing K/V.
+    void reserve(std::uint64_t seq, std::size_t count);
+    void* kv_pool() const { return kv_; }
+    long long block_elements() const { return block_stride_; }
+    int local_kv_heads() const { return hkv_; }
+
     int device() const { return device_; }
     cudaStream_t stream() const { return stream_; }
 
+    // Device time per kernel class, measured with CUDA events on the engine
+    // stream around each launch group while enabled (off by default).
+    enum ProfileClass { kProfAttention = 0, kProfProjection, kProfHead, kProfOther, kProfCollective, kProfClasses };
+    void set_profiling(bool on);
+    void profile_read(double* ms, unsigned long long* groups) const;
+    std::uint64_t last_h2d() const { return last_h2d_; }
+    std::uint64_t last_d2h() const { return last_d2h_; }
+
 private:
+    template <class F>
+    void timed(int cls, F&& launch);
+    void profile_collect();
+    bool profiling_ = false;
+    std::uint64_t last_h2d_ = 0, last_d2h_ = 0, acc_h2d_ = 0, acc_d2h_ = 0;
+    std::vector<cudaEvent_t> events_;
+    std::vector<int> event_class_;
+    std::size_t event_used_ = 0;
+    double prof_ms_[kProfClasses] = {};
+    unsigned long long prof_n_[kProfClasses] = {};
+
     struct Sub {  // one device launch sequence over <= max_step_tokens tokens
         std::vector<int> tok, pos, blk, slot;
         std::vector<int> seq_of;           // index into the sub-step's sequence list

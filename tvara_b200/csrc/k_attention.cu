@@ -255,10 +255,10 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_work <= 0) return;
     if (a.kv_f16) run_d<__half>(a, s);
     else run_d<float>(a, s);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
     if (a.n_combine > 0) {
         combine_kernel<<<dim3(a.n_combine, a.hq), 128, 0, s>>>(a);
-        TVARA_CUDA(cudaGetLastError());
+        TVARA_LAUNCHED();
     }
 }
 

@@ -167,39 +167,39 @@ void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, co
                     int ldo, cudaStream_t s) {
     if (n <= 0) return;
     rmsnorm_kernel<false><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, nullptr);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_rmsnorm_h(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
                       int ldo, __half* outh, cudaStream_t s) {
     if (n <= 0) return;
     rmsnorm_kernel<true><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, outh);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
     if (a.tokens <= 0) return;
     rope_kv_kernel<<<a.tokens, 256, 0, s>>>(a);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, cudaStream_t s) {
     if (rows <= 0) return;
     argmax_kernel<<<rows, 512, 0, s>>>(logits, vocab, out);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_swiglu(float* g, const float* u, long long n, cudaStream_t s) {
     if (n <= 0) return;
     swiglu_kernel<<<int(std::min<long long>((n + 255) / 256, 148 * 16)), 256, 0, s>>>(g, u, n);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n, cudaStream_t s) {
     if (n <= 0) return;
     if (block_bytes % 16) throw std::invalid_argument("KV block size must be a multiple of 16 bytes");
     block_copy_kernel<<<dim3(64, n), 256, 0, s>>>(static_cast<uint4*>(kv), block_bytes / 16, pairs);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 }  // namespace tvara

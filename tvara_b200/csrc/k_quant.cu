@@ -436,7 +436,7 @@ void run_gemv(const GemmArgs& a, cudaStream_t s) {
     const int rows_per_cta = kWarps * R;
     const int grid = (a.w.rows + rows_per_cta - 1) / rows_per_cta;
     gemv_kernel<TYPE, R, NT><<<grid, kWarps * 32, smem, s>>>(a, kc);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 template <int TYPE>
@@ -473,7 +473,7 @@ void launch_to_half(const float* x, int ldx, __half* out, int tokens, int cols, 
     const long long total = (long long)tokens * cols;
     const int grid = int(std::min<long long>((total + 255) / 256, 148 * 16));
     to_half_kernel<<<grid, 256, 0, s>>>(x, ldx, out, tokens, cols);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_dequantize(int type, const void* blocks, std::size_t nblocks, float* out, cudaStream_t s) {
@@ -483,7 +483,7 @@ void launch_dequantize(int type, const void* blocks, std::size_t nblocks, float*
     if (!total) return;
     const int grid = int(std::min<std::size_t>((total + 255) / 256, 148 * 32));
     dequant_kernel<<<grid, 256, 0, s>>>(type, static_cast<const unsigned char*>(blocks), nblocks, out);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t* qs, std::uint8_t* meta,
@@ -496,18 +496,18 @@ void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t*
     const std::size_t total = std::size_t(rows) * (cols / per);
     const int grid = int(std::min<std::size_t>((total + 255) / 256, 148 * 32));
     repack_kernel<<<grid, 256, 0, s>>>(type, static_cast<const unsigned char*>(gguf), rows, cols, qs, meta);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s) {
     finite_kernel<<<148 * 8, 256, 0, s>>>(w, flag);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s) {
     if (n <= 0) return;
     embed_kernel<<<n, 256, 0, s>>>(emb, tokens, x, ldx);
-    TVARA_CUDA(cudaGetLastError());
+    TVARA_LAUNCHED();
 }
 
 }  // namespace tvara

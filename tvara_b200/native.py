@@ -168,6 +168,39 @@ class NativeModel:
                 self._raise_error()
         return out, am
 
+    # -------------------------------------------------------- device access
+    @property
+    def stream(self) -> int:
+        """cudaStream_t (as an int) the handle's device work runs on."""
+        with self._lock:
+            self._check_open()
+            s = self._library.tvara_model_stream(self._handle)
+            if s is None:
+                self._raise_error()
+            return int(s)
+
+    def kv_pool(self) -> dict:
+        from ._bindings import C as _C
+
+        class Info(_C.Structure):
+            _fields_ = [("base", _C.c_void_p), ("max_blocks", _C.c_size_t), ("block_elements", _C.c_size_t),
+                        ("kv_dtype", _C.c_uint32), ("layers", _C.c_uint32), ("kv_heads", _C.c_uint32),
+                        ("head_dim", _C.c_uint32), ("block_tokens", _C.c_uint32)]
+
+        info = Info()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_kv_pool(self._handle, C.byref(info)):
+                self._raise_error()
+        return {f: getattr(info, f) for f, _ in Info._fields_}
+
+    def reserve(self, sequence, count):
+        """Append `count` positions without computing their K/V."""
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_sequence_reserve(self._handle, sequence, int(count)):
+                self._raise_error()
+
     # ------------------------------------------------------- KV inspection
     def kv_stats(self):
         a, m = C.c_size_t(), C.c_size_t()
