@@ -28,19 +28,24 @@ enum { TVARA_F32 = 0, TVARA_F16 = 1, TVARA_Q4_0 = 2, TVARA_Q8_0 = 8, TVARA_Q4_K 
 TVARA_API int tvara_dequantize(int type, const void* blocks, size_t nblocks, float* out, void* stream);
 
 /* Bytes of the engine's packed layout for a [rows][cols] matrix: the codes of
- * every row (16-byte aligned rows) followed, at a 256-byte aligned offset, by
- * the block headers. */
+ * every row (16-byte aligned rows), then the block headers, then one signed
+ * byte per row (the power-of-two scale of the tensor-core path), each part at
+ * a 256-byte aligned offset. */
 TVARA_API size_t tvara_packed_bytes(int type, size_t rows, size_t cols);
 /* GGUF rows (device) -> engine layout (device, tvara_packed_bytes long). */
 TVARA_API int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream);
 
+/* Device scratch tvara_quant_matmul needs for `tokens` rows of width `cols`
+ * (0 when the call runs on the CUDA-core path, at most 4 tokens). */
+TVARA_API size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens);
 /* Replaces quant::matvec_f32 over dequantised weights / Matrix::multiply and
  * prefill_reference (quant.hpp:163-196, prefill.hpp:12-18):
  * y[t][r] = sum_k W[r][k] * x[t][k] for t < tokens, W packed (device), x and y
- * F32 row-major (device).  Dequantisation happens in registers; F32
- * accumulation. */
+ * F32 row-major (device).  Up to 4 tokens: CUDA-core GEMV with the weights
+ * dequantised in registers.  More: tcgen05 tensor cores on an exact hi+lo
+ * FP16 split of both operands (F32 accumulation); needs `workspace`. */
 TVARA_API int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, const float* x,
-                                 size_t tokens, float* y, void* stream);
+                                 size_t tokens, float* y, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Paged GQA attention, replacing fused_paged_attention /
  * fused_prompt_attention (core/include/tvara/attention.hpp:57-89) for many

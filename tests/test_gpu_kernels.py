@@ -79,8 +79,10 @@ def packed(capi, kind, raw, rows, cols):
 def matmul(capi, kind, buf, rows, cols, x):
     torch = torch_dev()
     xd = dev(x.astype(np.float32))
-    y = torch.empty((x.shape[0], rows), dtype=torch.float32, device="cuda")
-    check(capi, capi.tvara_quant_matmul(kind, ptr(buf), rows, cols, ptr(xd), x.shape[0], ptr(y), None))
+    y = torch.full((x.shape[0], rows), float("nan"), dtype=torch.float32, device="cuda")
+    n = capi.tvara_quant_matmul_workspace(cols, x.shape[0])
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device="cuda")
+    check(capi, capi.tvara_quant_matmul(kind, ptr(buf), rows, cols, ptr(xd), x.shape[0], ptr(y), ptr(ws), n, None))
     sync()
     return y.cpu().numpy()
 
@@ -110,6 +112,20 @@ def test_quant_matmul_matches_oracle(capi, kind, tokens):
     assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6)
 
 
+@pytest.mark.parametrize("kind", TYPES)
+@pytest.mark.parametrize("tokens", [16, 33, 200, 256, 300, 512])
+def test_tensor_core_matmul_matches_oracle(capi, kind, tokens):
+    """tcgen05 path: partial weight-row tiles (rows % 128 != 0), partial and
+    multiple token tiles, split-K (few row tiles), every weight type."""
+    rng = np.random.default_rng(7 * tokens + kind)
+    rows, cols = 331, 1024
+    raw = make_weights(kind, rows, cols, rng)
+    x = (rng.standard_normal((tokens, cols)) * rng.uniform(0.01, 30, (tokens, 1))).astype(np.float32)
+    got = matmul(capi, kind, packed(capi, kind, raw, rows, cols), rows, cols, x)
+    ref, mag = oracle_matmul(kind, raw, rows, cols, x)
+    assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
+
+
 @pytest.mark.parametrize("kind", [gguf.Q4_K, gguf.Q8_0, gguf.Q4_0])
 def test_quant_matmul_standalone_config_shape(capi, kind):
     """BASELINE standalone config: 11008 x 4096, d/dmin ~ U(0.001, 0.05)."""
@@ -117,7 +133,7 @@ def test_quant_matmul_standalone_config_shape(capi, kind):
     rows, cols = 11008, 4096
     raw = np.frombuffer(gguf.random_blocks(kind, rows, cols, rng), np.uint8).copy()
     buf = packed(capi, kind, raw, rows, cols)
-    for tokens in (1, 8):
+    for tokens in (1, 8, 128, 512):
         x = rng.standard_normal((tokens, cols)).astype(np.float32)
         got = matmul(capi, kind, buf, rows, cols, x)
         sel = rng.choice(rows, 256, replace=False)

@@ -81,7 +81,8 @@ SIGNATURES = {
     "tvara_dequantize": (C.c_int, [C.c_int, P, SZ, P, P]),
     "tvara_packed_bytes": (SZ, [C.c_int, SZ, SZ]),
     "tvara_pack": (C.c_int, [C.c_int, P, SZ, SZ, P, P]),
-    "tvara_quant_matmul": (C.c_int, [C.c_int, P, SZ, SZ, P, SZ, P, P]),
+    "tvara_quant_matmul_workspace": (SZ, [SZ, SZ]),
+    "tvara_quant_matmul": (C.c_int, [C.c_int, P, SZ, SZ, P, SZ, P, P, SZ, P]),
     "tvara_paged_attention_workspace": (SZ, [P]),
     "tvara_paged_attention": (C.c_int, [P, P, SZ, P]),
 }

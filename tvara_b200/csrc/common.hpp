@@ -36,6 +36,10 @@ struct DeviceMatrix {
     const std::uint8_t* meta = nullptr;
     std::size_t qs_row = 0;    // bytes per row in qs
     std::size_t meta_row = 0;  // bytes per row in meta
+    // Per row, the power of two (2^shift) that brings the row's largest
+    // |value| into [2^14, 2^15): the tensor-core path scales by it before the
+    // exact hi+lo FP16 split.  Null until computed (then only GEMV is used).
+    const signed char* row_shift = nullptr;
 };
 
 inline std::size_t qs_row_bytes(int type, std::size_t cols) {

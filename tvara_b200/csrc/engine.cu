@@ -62,7 +62,7 @@ RawMatrix gather(const gguf::File& f, const std::vector<Segment>& segs, bool int
 }
 
 std::size_t matrix_bytes(int type, int rows, int cols) {
-    return align256(qs_row_bytes(type, cols) * rows) + align256(meta_row_bytes(type, cols) * rows);
+    return align256(qs_row_bytes(type, cols) * rows) + align256(meta_row_bytes(type, cols) * rows) + align256(rows);
 }
 
 }  // namespace
@@ -117,7 +117,7 @@ Engine::~Engine() {
     radix_.reset();
     coll_.reset();
     for (void* p : {static_cast<void*>(weights_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
-                    static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_)})
+                    static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_})
         if (p) cudaFree(p);
     if (meta_host_) cudaFreeHost(meta_host_);
     if (err_host_) cudaFreeHost(err_host_);
@@ -212,6 +212,10 @@ void Engine::load(const gguf::File& f) {
             launch_repack(raw.type, staging_dev, raw.rows, raw.cols, qs, meta, stream_);
             m.qs = qs;
             m.meta = meta;
+            auto* shifts = reinterpret_cast<signed char*>(cursor);
+            cursor += align256(m.rows);
+            launch_row_shift(m, shifts, stream_);
+            m.row_shift = shifts;
             launch_finite_check(m, flag, stream_);
             *pl.out = m;
             TVARA_CUDA(cudaStreamSynchronize(stream_));  // raw host buffer is released next iteration
@@ -297,6 +301,9 @@ void Engine::load(const gguf::File& f) {
     logits_ = take(T * vocab_);
     partial_ = take(partial_cap_ * hq_ * (d + 2));
     argmax_ = reinterpret_cast<unsigned*>(take(T));
+    const int max_k = std::max({D, hq_ * d, ffn_});
+    tc_ws_bytes_ = gemm_tc_workspace(int(T), max_k);
+    TVARA_CUDA(cudaMalloc(&tc_ws_, tc_ws_bytes_));
     TVARA_CUDA(cudaMalloc(&err_, sizeof(int)));
     TVARA_CUDA(cudaMemset(err_, 0, sizeof(int)));
     TVARA_CUDA(cudaHostAlloc(&err_host_, sizeof(int), cudaHostAllocDefault));
@@ -311,7 +318,8 @@ void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int toke
     a.y = y;
     a.ldy = ldy;
     a.epilogue = epi;
-    launch_projection(a, nullptr, 0, stream_);
+    a.err = err_;
+    launch_projection(a, tc_ws_, tc_ws_bytes_, stream_);
 }
 
 void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,

@@ -130,6 +130,8 @@ private:
           *ffu_ = nullptr, *logits_ = nullptr, *partial_ = nullptr, *xo_ = nullptr;
     unsigned* argmax_ = nullptr;
     int* err_ = nullptr;
+    void* tc_ws_ = nullptr;        // tensor-core projection: hi/lo FP16 activations + token scales
+    std::size_t tc_ws_bytes_ = 0;
     std::size_t partial_cap_ = 0;  // partial rows (part x hq)
     // per-step metadata (device + pinned host mirror)
     int* meta_dev_ = nullptr;

@@ -1,20 +1,501 @@
-// Projection dispatch: the CUDA-core GEMV streams weights once per group of
-// at most four tokens; larger token counts go to the tensor-core kernel when
-// it supports the matrix.
+// Projection for larger token counts on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in TMEM, activations fed by TMA).
+//
+// D[w_row][token] = sum_k W[w_row][k] * X[token][k] for a tile of 128 weight
+// rows (the MMA's M) and up to 256 tokens (N).  Quantised rows are
+// dequantised by four producer warps straight into the UMMA shared-memory
+// layout.  Precision: the reference multiplies F32 weights by F32 activations
+// (core/include/tvara/quant.hpp:163-169); a single FP16 rounding of either
+// operand costs ~5e-4 relative per product, which measurably exceeds the 2e-3
+// logit budget on deep models.  So both operands are split exactly into
+// hi + lo FP16 parts (after an exact power-of-two scaling that keeps them in
+// the normal FP16 range: per matrix for W, per token for X) and each K-step
+// issues three MMAs, hi*hi + hi*lo + lo*hi, accumulating in F32 -- products
+// carry ~2^-22 relative error.
+//
+// Warp roles (160 threads): warps 0-3 produce A (one weight row per thread)
+// and then run the epilogue (TMEM lane == weight row); warp 4 allocates TMEM
+// and one of its threads issues the MMAs.  X tiles arrive by TMA (no
+// multicast) on the same mbarrier the producers arrive on.  Every mbarrier
+// wait is bounded: on timeout the kernel records an error code, waits
+// (bounded) for its own TMA copies, frees TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "kernels.cuh"
 
 namespace tvara {
+namespace {
 
-bool gemm_tc_supported(const DeviceMatrix&, int) { return false; }
+constexpr int kBM = 128;          // weight rows per tile (MMA M)
+constexpr int kBK = 32;           // K per stage (one 64-byte swizzled row of FP16)
+constexpr int kStages = 4;
+constexpr int kMaxN = 256;        // tokens per tile (MMA N)
+constexpr int kThreads = 160;
+constexpr int kProducers = 128;
+constexpr unsigned kSpinLimit = 1u << 26;
+constexpr int kATile = kBM * kBK * 2;      // 8 KB per hi/lo A tile
+constexpr int kBTileMax = kMaxN * kBK * 2; // 16 KB per hi/lo B tile
 
-void launch_gemm_tc(const GemmArgs&, void*, std::size_t, cudaStream_t) {
-    throw std::logic_error("tensor-core projection not available for this matrix");
+struct TcArgs {
+    DeviceMatrix w;
+    const signed char* row_shift;  // weight row scaled by 2^row_shift before splitting
+    const int* x_shift;     // per token: X scaled by 2^x_shift
+    float* y;
+    int ldy;
+    int tokens;
+    int n_tile;             // tokens per tile (multiple of 16, <= 256)
+    int k_steps;            // kBK-steps per split
+    int epilogue;
+    int atomic;             // split-K: accumulate with atomics
+    unsigned idesc;         // tcgen05 instruction descriptor
+    int* err;
+};
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(std::uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(std::uint64_t* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false after the limit (or when another role gave up).
+__device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err,
+                                          int code) {
+    for (unsigned i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (i > 64) __nanosleep(64);
+    }
+    *abort_flag = 1;
+    atomicExch(err, code);
+    return false;
 }
 
-std::size_t gemm_tc_workspace(int, int) { return 0; }
+__device__ __forceinline__ std::uint64_t smem_desc(const void* tile) {
+    // K-major, 64-byte swizzle: 8-row atoms of 64-byte rows stacked every 512 B.
+    const std::uint64_t addr = smem_u32(tile);
+    return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
+}
+
+__device__ __forceinline__ void mma_f16(unsigned tmem_d, std::uint64_t a, std::uint64_t b, unsigned idesc, int acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, std::uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Byte offset of 16-byte chunk c (0..3) of row r in a [rows][64 B] tile with
+// the 64-byte swizzle (chunk index XOR bits 1-2 of the row).
+__device__ __forceinline__ int sw64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+
+__device__ __forceinline__ float h2f(unsigned short h) { return __half2float(__ushort_as_half(h)); }
+
+// The reference's F32 value of weight element (row, k0 + e), e < 32, for
+// one 32-element K-step; written into v[32].
+template <int TYPE>
+__device__ __forceinline__ void load_weights(const DeviceMatrix& w, long long row, int k0, float (&v)[32]) {
+    const unsigned char* qs = w.qs + row * w.qs_row;
+    const unsigned char* meta = w.meta + row * w.meta_row;
+    if constexpr (TYPE == kQ4_K || TYPE == kQ4_0) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
+        const unsigned ws[4] = {u.x, u.y, u.z, u.w};
+        float a, b;  // value = a*q - b
+        if constexpr (TYPE == kQ4_K) {
+            const uint4 m = __ldg(reinterpret_cast<const uint4*>(meta + (k0 / 256) * 16));
+            const float d = h2f((unsigned short)(m.x & 0xffff)), dmin = h2f((unsigned short)(m.x >> 16));
+            const int g = (k0 / 32) % 8;
+            const unsigned char* s = reinterpret_cast<const unsigned char*>(&m) + 4;
+            unsigned sc, mn;
+            if (g < 4) {
+                sc = s[g] & 63u;
+                mn = s[g + 4] & 63u;
+            } else {
+                sc = (s[g + 4] & 15u) | ((unsigned)(s[g - 4] >> 6) << 4);
+                mn = (s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
+            }
+            a = __fmul_rn(d, float(sc));
+            b = __fmul_rn(dmin, float(mn));
+        } else {
+            a = h2f(reinterpret_cast<const unsigned short*>(meta)[k0 / 32]);
+            b = __fmul_rn(a, 8.f);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const unsigned byte = (ws[i >> 2] >> (8 * (i & 3))) & 255u;
+            if constexpr (TYPE == kQ4_K) {
+                v[i] = __fsub_rn(__fmul_rn(a, float(byte & 15u)), b);
+                v[i + 16] = __fsub_rn(__fmul_rn(a, float(byte >> 4)), b);
+            } else {
+                v[i] = __fmul_rn(a, float(int(byte & 15u) - 8));
+                v[i + 16] = __fmul_rn(a, float(int(byte >> 4) - 8));
+            }
+        }
+    } else if constexpr (TYPE == kQ8_0) {
+        const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(qs + k0));
+        const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(qs + k0 + 16));
+        const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[k0 / 32]);
+        const unsigned ws[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(d, float((signed char)((ws[i >> 2] >> (8 * (i & 3))) & 255u)));
+    } else if constexpr (TYPE == kF16) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 2);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 u = __ldg(p + c);
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __half22float2(h[j]);
+                v[c * 8 + 2 * j] = f.x;
+                v[c * 8 + 2 * j + 1] = f.y;
+            }
+        }
+    } else {
+        const float4* p = reinterpret_cast<const float4*>(qs + std::size_t(k0) * 4);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 f = __ldg(p + c);
+            v[c * 4] = f.x;
+            v[c * 4 + 1] = f.y;
+            v[c * 4 + 2] = f.z;
+            v[c * 4 + 3] = f.w;
+        }
+    }
+}
+
+__device__ __forceinline__ float swiglu(float g, float up) {
+    const float small = expf(-fabsf(g));
+    const float sig = g >= 0.f ? 1.f / (1.f + small) : small / (1.f + small);
+    return __fmul_rn(g, __fmul_rn(sig, up));
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo, TcArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte aligned carve-up: per stage A_hi, A_lo (8 KB each), B_hi, B_lo
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int b_bytes = a.n_tile * kBK * 2;
+    const int stage_bytes = 2 * kATile + 2 * kBTileMax;
+    unsigned char* stages = base;
+    std::uint64_t* full_a = reinterpret_cast<std::uint64_t*>(base + kStages * stage_bytes);  // producers
+    std::uint64_t* full_b = full_a + kStages;  // TMA bytes of the X tiles
+    std::uint64_t* empty = full_b + kStages;   // MMA finished reading the stage
+    std::uint64_t* done = empty + kStages;     // accumulator complete
+    unsigned* tmem_slot = reinterpret_cast<unsigned*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * kBM;
+    const int tok0 = blockIdx.y * a.n_tile;
+    const int kstep0 = blockIdx.z * a.k_steps;
+    const unsigned tmem_cols = a.n_tile <= 32 ? 32 : a.n_tile <= 64 ? 64 : a.n_tile <= 128 ? 128 : 256;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full_a[s], kProducers);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp < 4) {
+        // ---------------- producers: A tiles (and thread 0: B tiles by TMA)
+        const int r = threadIdx.x;
+        const long long row = row0 + r;
+        const bool live = row < a.w.rows;
+        int last_ph[kStages];  // phase of the last TMA this thread issued per stage, -1 none
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) last_ph[s] = -1;
+        const int shift = live ? a.row_shift[row] : 0;
+        for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
+            const int s = ks % kStages;
+            const unsigned ph = (ks / kStages) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
+            unsigned char* st = stages + s * stage_bytes;
+            const int k0 = (kstep0 + ks) * kBK;
+            if (r == 0) {
+                mbar_expect_tx(&full_b[s], 2 * b_bytes);
+                tma_load_2d(st + 2 * kATile, &map_hi, k0, tok0, &full_b[s]);
+                tma_load_2d(st + 2 * kATile + kBTileMax, &map_lo, k0, tok0, &full_b[s]);
+                last_ph[s] = int(ph);
+            }
+            float v[32];
+            if (live) load_weights<TYPE>(a.w, row, k0, v);
+            else
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            unsigned char* ahi = st;
+            unsigned char* alo = st + kATile;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                __half hi[8], lo[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float x = ldexpf(v[c * 8 + j], shift);
+                    hi[j] = __float2half_rn(x);
+                    lo[j] = __float2half_rn(__fsub_rn(x, __half2float(hi[j])));
+                }
+                *reinterpret_cast<uint4*>(ahi + sw64(r, c)) = *reinterpret_cast<const uint4*>(hi);
+                *reinterpret_cast<uint4*>(alo + sw64(r, c)) = *reinterpret_cast<const uint4*>(lo);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&full_a[s]);
+        }
+        // ---------------- epilogue: TMEM lane r holds weight row row0 + r
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, a.err, 12) ? 1 : 0);
+        if (ok) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const float wscale = ldexpf(1.f, -shift);
+            for (int c0 = 0; c0 < a.n_tile; c0 += 32) {
+                unsigned u[32];
+                const unsigned taddr = tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c0;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                      "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                      "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                      "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                      "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = tok0 + c0 + j;
+                    if (c0 + j >= a.n_tile) break;
+                    float val = 0.f;
+                    if (t < a.tokens) val = __uint_as_float(u[j]) * wscale * ldexpf(1.f, -a.x_shift[t]);
+                    if (a.epilogue == kSwiGLU) {
+                        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+                        if (t < a.tokens && live && !(r & 1))
+                            a.y[(long long)t * a.ldy + row / 2] = swiglu(val, partner);
+                    } else if (t < a.tokens && live) {
+                        float* dst = a.y + (long long)t * a.ldy + row;
+                        if (a.atomic) atomicAdd(dst, val);
+                        else if (a.epilogue == kAdd) *dst += val;
+                        else *dst = val;
+                    }
+                }
+            }
+        }
+        // before leaving, every TMA copy this thread issued must have landed
+        // (normally long since consumed; after an abort, wait with a bound)
+        if (r == 0) {
+            for (int s = 0; s < kStages; ++s)
+                if (last_ph[s] >= 0)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full_b[s], unsigned(last_ph[s])); ++i) {
+                    }
+        }
+    } else if (lane == 0) {
+        // ---------------- MMA issuer
+        const int sub = kBK / 16;
+        for (int ks = 0; ks < a.k_steps; ++ks) {
+            const int s = ks % kStages;
+            const unsigned ph = (ks / kStages) & 1;
+            if (!mbar_wait(&full_b[s], ph, abort_flag, a.err, 13)) break;
+            if (!mbar_wait(&full_a[s], ph, abort_flag, a.err, 14)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            unsigned char* st = stages + s * stage_bytes;
+            const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+            const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
+#pragma unroll
+            for (int kk = 0; kk < sub; ++kk) {
+                const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;  // 16 K of FP16 = 32 B
+                mma_f16(tmem, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
+                mma_f16(tmem, ahi + adv, blo + adv, a.idesc, 1);
+                mma_f16(tmem, alo + adv, bhi + adv, a.idesc, 1);
+            }
+            mma_commit(&empty[s]);
+        }
+        mma_commit(done);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 4) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+    }
+}
+
+// X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
+// that puts max|x| in [2^14, 2^15).
+__global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half* lo, int* shift) {
+    const int t = blockIdx.x;
+    const float* row = x + (long long)t * ldx;
+    float m = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(row[k]));
+    __shared__ float sm[32];
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? sm[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) sm[0] = v;
+    }
+    __syncthreads();
+    int e = 0;
+    if (sm[0] > 0.f && isfinite(sm[0])) frexpf(sm[0], &e);
+    const int s = sm[0] > 0.f ? max(-120, min(120, 15 - e)) : 0;
+    if (threadIdx.x == 0) shift[t] = s;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = ldexpf(row[k], s);
+        const __half h = __float2half_rn(v);
+        hi[(long long)t * K + k] = h;
+        lo[(long long)t * K + k] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+CUtensorMap make_map(const __half* base, int K, int T, int n_tile) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(T)};
+    const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+    const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(n_tile)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+                                   box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+template <int TYPE>
+void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const TcArgs& a, dim3 grid, cudaStream_t s) {
+    const int smem = kStages * (2 * kATile + 2 * kBTileMax) + 1024 + 256;
+    static bool configured = false;
+    if (!configured) {
+        TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        configured = true;
+    }
+    tc_gemm_kernel<TYPE><<<grid, kThreads, smem, s>>>(hi, lo, a);
+    TVARA_LAUNCHED();
+}
+
+int g_tc_min_tokens = 5;  // below this the CUDA-core GEMV streams weights once per <=4 tokens
+
+}  // namespace
+
+bool gemm_tc_supported(const DeviceMatrix& w, int tokens) {
+    return tokens >= g_tc_min_tokens && w.cols % kBK == 0 && w.row_shift != nullptr;
+}
+
+std::size_t gemm_tc_workspace(int max_tokens, int max_cols) {
+    // hi + lo activations, per-token shifts (padded to 64), an error flag
+    return std::size_t(max_tokens) * max_cols * 2 * sizeof(__half) +
+           std::size_t((max_tokens + 63) / 64 * 64 + 64) * sizeof(int) + 1024;
+}
+
+void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_bytes, cudaStream_t s) {
+    const int T = g.tokens, K = g.w.cols;
+    if (!workspace || workspace_bytes < gemm_tc_workspace(T, K))
+        throw std::invalid_argument("tensor-core projection workspace too small");
+    auto* hi = static_cast<__half*>(workspace);
+    __half* lo = hi + std::size_t(T) * K;
+    int* shift = reinterpret_cast<int*>(lo + std::size_t(T) * K);
+    // callers without an error flag get one in the workspace (never null)
+    int* err = g.err ? g.err : shift + ((T + 63) / 64) * 64;
+    split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
+    TVARA_LAUNCHED();
+
+    int n_tile = T >= kMaxN ? kMaxN : ((T + 15) / 16) * 16;
+    const int token_tiles = (T + n_tile - 1) / n_tile;
+    const int row_tiles = (g.w.rows + kBM - 1) / kBM;
+    const int steps = K / kBK;
+    // split K until the grid covers the SMs (not for SwiGLU, which is nonlinear)
+    int splits = 1;
+    if (g.epilogue != kSwiGLU) {
+        while (row_tiles * token_tiles * splits < 148 && steps % (splits * 2) == 0 && steps / (splits * 2) >= 8)
+            splits *= 2;
+    }
+    TcArgs a;
+    a.w = g.w;
+    a.row_shift = g.w.row_shift;
+    a.x_shift = shift;
+    a.y = g.y;
+    a.ldy = g.ldy;
+    a.tokens = T;
+    a.n_tile = n_tile;
+    a.k_steps = steps / splits;
+    a.epilogue = g.epilogue;
+    a.atomic = splits > 1;
+    a.idesc = (1u << 4) | (unsigned(n_tile >> 3) << 17) | (unsigned(kBM >> 4) << 24);
+    a.err = err;
+    if (!g.err) TVARA_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+    if (splits > 1 && g.epilogue == kStore)
+        TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
+    const CUtensorMap mh = make_map(hi, K, T, n_tile), ml = make_map(lo, K, T, n_tile);
+    const dim3 grid(row_tiles, token_tiles, splits);
+    switch (g.w.type) {
+        case kQ4_K: run_tc<kQ4_K>(mh, ml, a, grid, s); break;
+        case kQ4_0: run_tc<kQ4_0>(mh, ml, a, grid, s); break;
+        case kQ8_0: run_tc<kQ8_0>(mh, ml, a, grid, s); break;
+        case kF16: run_tc<kF16>(mh, ml, a, grid, s); break;
+        case kF32: run_tc<kF32>(mh, ml, a, grid, s); break;
+        default: throw std::invalid_argument("unsupported projection type");
+    }
+}
+
+void set_tc_min_tokens(int n) { g_tc_min_tokens = n; }
 
 void launch_projection(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s) {
-    if (gemm_tc_supported(a.w, a.tokens)) launch_gemm_tc(a, workspace, workspace_bytes, s);
+    if (workspace && gemm_tc_supported(a.w, a.tokens)) launch_gemm_tc(a, workspace, workspace_bytes, s);
     else launch_gemv(a, s);
 }
 

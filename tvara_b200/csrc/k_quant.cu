@@ -207,6 +207,21 @@ __global__ void finite_kernel(DeviceMatrix w, int* flag) {
     }
 }
 
+// One warp per row: shift = 15 - e where max|w| = m * 2^e, m in [0.5, 1).
+__global__ void row_shift_kernel(DeviceMatrix w, signed char* out) {
+    const long long r = blockIdx.x * (long long)(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= w.rows) return;
+    float m = 0.f;
+    for (int k = lane; k < w.cols; k += 32) m = fmaxf(m, fabsf(element(w, r, k)));
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) {
+        int e = 0;
+        if (m > 0.f && isfinite(m)) frexpf(m, &e);
+        out[r] = (signed char)(m > 0.f ? max(-100, min(100, 15 - e)) : 0);
+    }
+}
+
 __global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx) {
     const int t = blockIdx.x;
     const long long r = tokens[t];
@@ -501,6 +516,12 @@ void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t*
 
 void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s) {
     finite_kernel<<<148 * 8, 256, 0, s>>>(w, flag);
+    TVARA_LAUNCHED();
+}
+
+void launch_row_shift(const DeviceMatrix& w, signed char* out, cudaStream_t s) {
+    if (w.rows <= 0) return;
+    row_shift_kernel<<<(w.rows + 7) / 8, 256, 0, s>>>(w, out);
     TVARA_LAUNCHED();
 }
 

@@ -23,6 +23,7 @@ struct GemmArgs {
     float* y = nullptr;         // [tokens][ldy]
     int ldy = 0;
     int epilogue = kStore;
+    int* err = nullptr;         // device error flag (tensor-core path)
 };
 
 // y = epilogue(x . W^T): CUDA-core GEMV for small token counts.
@@ -45,6 +46,10 @@ void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t*
                    cudaStream_t s);
 // Sets *flag when any dequantised value of the matrix is not finite.
 void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s);
+// Per-row power-of-two scale of the tensor-core split (DeviceMatrix::row_shift).
+void launch_row_shift(const DeviceMatrix& w, signed char* out, cudaStream_t s);
+// Minimum token count routed to the tensor-core projection.
+void set_tc_min_tokens(int n);
 
 // ---- elementwise ----------------------------------------------------------
 // x[t] = row tokens[t] of the embedding, dequantised.

@@ -44,6 +44,7 @@ tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, 
     m.meta_row = tvara::meta_row_bytes(type, cols);
     m.qs = static_cast<const std::uint8_t*>(packed);
     m.meta = m.qs + align256(m.qs_row * rows);
+    m.row_shift = reinterpret_cast<const signed char*>(m.meta + align256(m.meta_row * rows));
     return m;
 }
 
@@ -95,19 +96,26 @@ int tvara_dequantize(int type, const void* blocks, size_t nblocks, float* out, v
 size_t tvara_packed_bytes(int type, size_t rows, size_t cols) {
     std::size_t e = 0, w = 0;
     if (!tvara::block_shape(type, e, w) || !cols || cols % e) return 0;
-    return align256(tvara::qs_row_bytes(type, cols) * rows) + align256(tvara::meta_row_bytes(type, cols) * rows);
+    return align256(tvara::qs_row_bytes(type, cols) * rows) + align256(tvara::meta_row_bytes(type, cols) * rows) +
+           align256(rows);
 }
 
 int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream) {
     return guarded([&] {
         auto m = packed_view(type, packed, rows, cols);
+        auto s = static_cast<cudaStream_t>(stream);
         tvara::launch_repack(type, gguf_rows, int(rows), int(cols), const_cast<std::uint8_t*>(m.qs),
-                             const_cast<std::uint8_t*>(m.meta), static_cast<cudaStream_t>(stream));
+                             const_cast<std::uint8_t*>(m.meta), s);
+        tvara::launch_row_shift(m, const_cast<signed char*>(m.row_shift), s);
     });
 }
 
+size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens) {
+    return tokens <= 4 ? 0 : tvara::gemm_tc_workspace(int(tokens), int(cols));
+}
+
 int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, const float* x, size_t tokens,
-                       float* y, void* stream) {
+                       float* y, void* workspace, size_t workspace_bytes, void* stream) {
     return guarded([&] {
         tvara::GemmArgs g;
         g.w = packed_view(type, packed, rows, cols);
@@ -117,7 +125,9 @@ int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, c
         g.y = y;
         g.ldy = int(rows);
         g.epilogue = tvara::kStore;
-        tvara::launch_projection(g, nullptr, 0, static_cast<cudaStream_t>(stream));
+        if (tokens > 4 && workspace_bytes < tvara::gemm_tc_workspace(int(tokens), int(cols)))
+            throw std::invalid_argument("matmul workspace too small");
+        tvara::launch_projection(g, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
     });
 }
 
