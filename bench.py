@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="llama8b")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (same per-layer shapes; small cases for ncu captures)")
     ap.add_argument("--requests", type=int, default=512)
     ap.add_argument("--prefix", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0)
@@ -70,8 +72,17 @@ def parse():
 
 
 # ----------------------------------------------------------------- workload
+def model_config(args) -> dict:
+    from tvara_b200 import gguf
+    cfg = gguf.model_config(args.config)
+    if args.layers:
+        cfg["layers"] = args.layers
+    return cfg
+
+
 def model_path(args) -> Path:
-    return Path(args.model_dir) / f"{args.config}_s{args.seed}.gguf"
+    depth = f"_l{args.layers}" if args.layers else ""
+    return Path(args.model_dir) / f"{args.config}{depth}_s{args.seed}.gguf"
 
 
 def ensure_model(args, rank):
@@ -80,7 +91,7 @@ def ensure_model(args, rank):
     if rank == 0 and not path.exists():
         path.parent.mkdir(parents=True, exist_ok=True)
         tmp = path.with_suffix(".tmp")
-        gguf.make_llama(tmp, args.config, seed=args.seed, random_packed=args.config != "tiny")
+        gguf.make_llama(tmp, model_config(args), seed=args.seed, random_packed=args.config != "tiny")
         tmp.rename(path)
     return path
 
@@ -339,7 +350,7 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel class
     pk, pk_kind = peaks()
-    cfg = gguf.LLAMA_CONFIGS.get(args.config, {})
+    cfg = model_config(args)
     L, H, HKV, D = cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"]
     dh = D // H
     tp = world
@@ -381,7 +392,8 @@ def run_ours(args):
         "data": "synthetic",
         "config": {"workload": f"{args.config} ragged decode, {args.requests} requests, shared {args.prefix}-token "
                                "prefix + U(64,2048) suffix + U(0,out) generated, 1 token/request/step",
-                   "model": args.config, "global_batch": args.requests, "seq_len": float(np.mean(lens0)),
+                   "model": args.config + (f" ({args.layers} layers)" if args.layers else ""),
+                   "global_batch": args.requests, "seq_len": float(np.mean(lens0)),
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d.value) + caller_h2d,

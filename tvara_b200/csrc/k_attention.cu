@@ -204,6 +204,523 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined variant: each warp owns a ring of shared-memory stages; its lane 0
+// streams whole K and V chunks of the warp's KV blocks (one head's tpb x d run
+// is contiguous in the pool) with cp.async.bulk onto a per-stage mbarrier, so
+// several blocks per warp are in flight while the warp computes on one from
+// shared memory.  Same arithmetic as attn_kernel.
+constexpr int kRing = 2;                   // stages per warp
+constexpr unsigned kAttnSpin = 1u << 26;   // bounded waits
+
+__device__ __forceinline__ unsigned s_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, std::uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     s_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(s_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool bar_try(std::uint64_t* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(s_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+template <typename KV, int VEC>
+__device__ __forceinline__ void smem_vec(const KV* p, float (&out)[VEC]) {
+    if constexpr (sizeof(KV) == 4) {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(p + j);
+            out[j] = v.x;
+            out[j + 1] = v.y;
+            out[j + 2] = v.z;
+            out[j + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(p + j);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h[i]);
+                out[j + 2 * i] = f.x;
+                out[j + 2 * i + 1] = f.y;
+            }
+        }
+    }
+}
+
+template <int D, typename KV, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_pipe_kernel(AttnArgs a) {
+    constexpr int ES = sizeof(KV);
+    constexpr int LPS = (D * ES / 16) < 32 ? (D * ES / 16) : 32;
+    constexpr int VEC = D / LPS;
+    constexpr int SPL = 32 / LPS;
+    extern __shared__ __align__(128) unsigned char att_smem[];
+    const int tpb = a.tpb;
+    const int chunk = tpb * D * ES;  // bytes of one head's K (or V) run in a block
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(att_smem) + warp * kRing;
+    unsigned char* ring = att_smem + 128 + std::size_t(warp) * kRing * 2 * chunk;
+    __shared__ float s_acc[kAttnWarps][G][D];
+    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+
+    const int4 wk = a.work[blockIdx.x];
+    const int part = a.work_part[blockIdx.x];
+    const int t = wk.x, toff = wk.y, p0 = wk.z, p1 = wk.w;
+    const int h = blockIdx.y;
+    const int sub = lane % LPS, grp = lane / LPS;
+    const float scale = rsqrtf(float(D));
+    const KV* pool = static_cast<const KV*>(a.kv);
+    const int b0 = p0 / tpb, b1 = (p1 - 1) / tpb;
+    // this warp's blocks: b0 + warp + 4*i, i < nblk
+    const int nblk = b1 - b0 - warp >= 0 ? (b1 - b0 - warp) / kAttnWarps + 1 : 0;
+
+    if (lane == 0) {
+        for (int s = 0; s < kRing; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    auto issue = [&](int i) {  // lane 0: start block i of this warp into stage i % kRing
+        const int bi = b0 + warp + i * kAttnWarps;
+        int pb = a.tables[toff + bi];
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;  // read something in range; the step reports the error
+        }
+        const KV* kb = pool + (long long)pb * a.block_stride + a.layer_offset + (long long)h * tpb * D;
+        unsigned char* st = ring + std::size_t(i % kRing) * 2 * chunk;
+        std::uint64_t* bar = &bars[i % kRing];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(2 * chunk) : "memory");
+        bulk_g2s(st, kb, chunk, bar);
+        bulk_g2s(st + chunk, kb + a.kind_stride, chunk, bar);
+    };
+    if (lane == 0)
+        for (int i = 0; i < kRing && i < nblk; ++i) issue(i);
+
+    float q[G][VEC];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float* qp = a.q + (long long)t * a.hq * D + (h * G + g) * D + sub * VEC;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) q[g][j] = qp[j] * scale;
+    }
+    float acc[G][VEC], l[G], m[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        l[g] = 0.f;
+        m[g] = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[g][j] = 0.f;
+    }
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        const unsigned parity = (i / kRing) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[i % kRing], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const KV* ks = reinterpret_cast<const KV*>(ring + std::size_t(i % kRing) * 2 * chunk);
+        const KV* vs = ks + tpb * D;
+        const int s_hi = min(tpb, p1 - bi * tpb);
+        constexpr int NI = 8;  // slot passes per softmax rescale
+        for (int c0 = 0; c0 < s_hi; c0 += NI * SPL) {
+            float sc[NI][G], cmax[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) cmax[g] = -INFINITY;
+#pragma unroll
+            for (int it = 0; it < NI; ++it) {
+                const int s = c0 + it * SPL + grp;
+                const bool valid = s < s_hi;
+                float kv[VEC];
+                if (valid) smem_vec<KV, VEC>(ks + s * D + sub * VEC, kv);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float d = 0.f;
+                    if (valid) {
+#pragma unroll
+                        for (int j = 0; j < VEC; ++j) d = fmaf(q[g][j], kv[j], d);
+                    }
+#pragma unroll
+                    for (int o = LPS / 2; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                    sc[it][g] = valid ? d : -INFINITY;
+                    cmax[g] = fmaxf(cmax[g], sc[it][g]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+#pragma unroll
+                for (int o = LPS; o < 32; o <<= 1) cmax[g] = fmaxf(cmax[g], __shfl_xor_sync(0xffffffffu, cmax[g], o));
+                const float mn = fmaxf(m[g], cmax[g]);
+                const float alpha = m[g] == -INFINITY ? 0.f : __expf(m[g] - mn);
+                m[g] = mn;
+                l[g] *= alpha;
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) acc[g][j] *= alpha;
+#pragma unroll
+                for (int it = 0; it < NI; ++it) {
+                    sc[it][g] = sc[it][g] == -INFINITY ? 0.f : __expf(sc[it][g] - mn);
+                    l[g] += sc[it][g];
+                }
+            }
+#pragma unroll
+            for (int it = 0; it < NI; ++it) {
+                const int s = c0 + it * SPL + grp;
+                if (s < s_hi) {
+                    float kv[VEC];
+                    smem_vec<KV, VEC>(vs + s * D + sub * VEC, kv);
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int j = 0; j < VEC; ++j) acc[g][j] = fmaf(sc[it][g], kv[j], acc[g][j]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kRing < nblk) issue(i + kRing);
+    }
+    // every copy this warp started must land before the CTA exits
+    if (lane == 0 && failed) {
+        for (int i = 0; i < kRing && i < nblk; ++i)
+            for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[i], 0) && !bar_try(&bars[i], 1); ++spin) {
+            }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int o = LPS; o < 32; o <<= 1) {
+            l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], o);
+        }
+    }
+    if (lane < LPS) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) s_acc[warp][g][sub * VEC + j] = acc[g][j];
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            s_m[warp][g] = m[g];
+            s_l[warp][g] = l[g];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, e = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][g]);
+        float L = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (s_m[w][g] == -INFINITY) continue;
+            const float f = __expf(s_m[w][g] - M);
+            L = fmaf(s_l[w][g], f, L);
+            A = fmaf(s_acc[w][g][e], f, A);
+        }
+        const int head = h * G + g;
+        if (part < 0) {
+            a.out[(long long)t * a.hq * D + head * D + e] = A / L;
+        } else {
+            float* pp = a.partial + ((long long)part * a.hq + head) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+}
+
+// Packed F32x2 helpers (Blackwell fma.rn.f32x2).
+__device__ __forceinline__ unsigned long long pk(float x, float y) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ float2 upk(unsigned long long r) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// VEC consecutive elements of a K or V slot from shared memory as packed pairs.
+template <typename KV, int VEC>
+__device__ __forceinline__ void smem_pairs(const KV* p, unsigned long long (&out)[VEC / 2]) {
+    if constexpr (sizeof(KV) == 4) {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(p + j);
+            out[j / 2] = pk(v.x, v.y);
+            out[j / 2 + 1] = pk(v.z, v.w);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(p + j);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h[i]);
+                out[j / 2 + i] = pk(f.x, f.y);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Per-warp ring (as attn_pipe_kernel) with a transposing score reduction, for
+// G a power of two no larger than the lanes per slot: the G partial dots of a
+// lane are reduced across the slot's LPS lanes in log2(LPS) + G - 1 shuffles
+// (instead of G*log2(LPS)), after which each lane owns the score of one head
+// (its softmax state too, one exponential per lane); the probabilities are
+// broadcast back for the V pass.  Dots and the V accumulation use the packed
+// F32x2 FMA.
+template <int D, typename KV, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_xpose_kernel(AttnArgs a) {
+    constexpr int ES = sizeof(KV);
+    constexpr int LPS = (D * ES / 16) < 32 ? (D * ES / 16) : 32;
+    constexpr int VEC = D / LPS;
+    constexpr int SPL = 32 / LPS;
+    constexpr int NI = 8;
+    constexpr int HL = LPS / G;  // lanes holding one head's score within a slot group
+    static_assert((G & (G - 1)) == 0 && G <= LPS && VEC % 2 == 0, "transposing layout");
+    extern __shared__ __align__(128) unsigned char att_smem[];
+    const int tpb = a.tpb;
+    const int chunk = tpb * D * ES;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(att_smem) + warp * kRing;
+    unsigned char* ring = att_smem + 128 + std::size_t(warp) * kRing * 2 * chunk;
+    __shared__ float s_acc[kAttnWarps][G][D];
+    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+
+    const int4 wk = a.work[blockIdx.x];
+    const int part = a.work_part[blockIdx.x];
+    const int t = wk.x, toff = wk.y, p0 = wk.z, p1 = wk.w;
+    const int h = blockIdx.y;
+    const int sub = lane % LPS, grp = lane / LPS;
+    const int mine = sub / HL;  // the head whose score this lane ends up holding
+    const int gbase = lane - sub;
+    const KV* pool = static_cast<const KV*>(a.kv);
+    const int b0 = p0 / tpb, b1 = (p1 - 1) / tpb;
+    const int nblk = b1 - b0 - warp >= 0 ? (b1 - b0 - warp) / kAttnWarps + 1 : 0;
+
+    if (lane == 0) {
+        for (int s = 0; s < kRing; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    auto issue = [&](int i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        int pb = a.tables[toff + bi];
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;
+        }
+        const KV* kb = pool + (long long)pb * a.block_stride + a.layer_offset + (long long)h * tpb * D;
+        unsigned char* st = ring + std::size_t(i % kRing) * 2 * chunk;
+        std::uint64_t* bar = &bars[i % kRing];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(2 * chunk) : "memory");
+        bulk_g2s(st, kb, chunk, bar);
+        bulk_g2s(st + chunk, kb + a.kind_stride, chunk, bar);
+    };
+    if (lane == 0)
+        for (int i = 0; i < kRing && i < nblk; ++i) issue(i);
+
+    unsigned long long q2[G][VEC / 2], acc2[G][VEC / 2];
+    {
+        const float scale = rsqrtf(float(D));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float* qp = a.q + (long long)t * a.hq * D + (h * G + g) * D + sub * VEC;
+#pragma unroll
+            for (int j = 0; j < VEC / 2; ++j) {
+                q2[g][j] = pk(qp[2 * j] * scale, qp[2 * j + 1] * scale);
+                acc2[g][j] = 0ull;
+            }
+        }
+    }
+    float l = 0.f, m = -INFINITY;  // softmax state of head `mine`
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        const unsigned parity = (i / kRing) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[i % kRing], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const KV* ks = reinterpret_cast<const KV*>(ring + std::size_t(i % kRing) * 2 * chunk);
+        const KV* vs = ks + tpb * D;
+        const int s_hi = min(tpb, p1 - bi * tpb);
+        for (int c0 = 0; c0 < s_hi; c0 += NI * SPL) {
+            float sc[NI];
+            float cmax = -INFINITY;
+#pragma unroll
+            for (int it = 0; it < NI; ++it) {
+                const int s = c0 + it * SPL + grp;
+                const bool valid = s < s_hi;
+                float d[G];
+                {
+                    unsigned long long k2[VEC / 2];
+                    if (valid) smem_pairs<KV, VEC>(ks + s * D + sub * VEC, k2);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        unsigned long long d2 = 0ull;
+                        if (valid) {
+#pragma unroll
+                            for (int j = 0; j < VEC / 2; ++j) d2 = ffma2(q2[g][j], k2[j], d2);
+                        }
+                        const float2 f = upk(d2);
+                        d[g] = f.x + f.y;
+                    }
+                }
+                // transpose-reduce: halve the head set per exchange
+#pragma unroll
+                for (int n = G, o = LPS / 2; n > 1; n >>= 1, o >>= 1) {
+                    const bool upper = (lane & o) != 0;
+#pragma unroll
+                    for (int g = 0; g < n / 2; ++g) {
+                        const float send = upper ? d[g] : d[g + n / 2];
+                        const float keep = upper ? d[g + n / 2] : d[g];
+                        d[g] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                    }
+                }
+#pragma unroll
+                for (int o = HL / 2; o; o >>= 1) d[0] += __shfl_xor_sync(0xffffffffu, d[0], o);
+                sc[it] = valid ? d[0] : -INFINITY;
+                cmax = fmaxf(cmax, sc[it]);
+            }
+#pragma unroll
+            for (int o = LPS; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+            const float mn = fmaxf(m, cmax);
+            const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
+            m = mn;
+            l *= alpha;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float ag = __shfl_sync(0xffffffffu, alpha, gbase + g * HL);
+                const unsigned long long a2 = pk(ag, ag);
+#pragma unroll
+                for (int j = 0; j < VEC / 2; ++j) acc2[g][j] = ffma2(acc2[g][j], a2, 0ull);
+            }
+#pragma unroll
+            for (int it = 0; it < NI; ++it) {
+                const int s = c0 + it * SPL + grp;
+                const bool valid = s < s_hi;
+                const float p = valid ? __expf(sc[it] - mn) : 0.f;
+                l += p;
+                unsigned long long v2[VEC / 2];
+                if (valid) smem_pairs<KV, VEC>(vs + s * D + sub * VEC, v2);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float pg = __shfl_sync(0xffffffffu, p, gbase + g * HL);
+                    if (valid) {
+                        const unsigned long long p2 = pk(pg, pg);
+#pragma unroll
+                        for (int j = 0; j < VEC / 2; ++j) acc2[g][j] = ffma2(p2, v2[j], acc2[g][j]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kRing < nblk) issue(i + kRing);
+    }
+    if (lane == 0 && failed) {
+        for (int i = 0; i < kRing && i < nblk; ++i)
+            for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[i], 0) && !bar_try(&bars[i], 1); ++spin) {
+            }
+    }
+    // merge slot groups: acc for every head, l for this lane's head
+#pragma unroll
+    for (int o = LPS; o < 32; o <<= 1) {
+        l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < VEC / 2; ++j) {
+                const float2 f = upk(acc2[g][j]);
+                acc2[g][j] = pk(f.x + __shfl_xor_sync(0xffffffffu, f.x, o), f.y + __shfl_xor_sync(0xffffffffu, f.y, o));
+            }
+    }
+    if (lane < LPS) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < VEC / 2; ++j) {
+                const float2 f = upk(acc2[g][j]);
+                s_acc[warp][g][sub * VEC + 2 * j] = f.x;
+                s_acc[warp][g][sub * VEC + 2 * j + 1] = f.y;
+            }
+        if (sub % HL == 0) {
+            s_m[warp][mine] = m;
+            s_l[warp][mine] = l;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, e = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][g]);
+        float L = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (s_m[w][g] == -INFINITY) continue;
+            const float f = __expf(s_m[w][g] - M);
+            L = fmaf(s_l[w][g], f, L);
+            A = fmaf(s_acc[w][g][e], f, A);
+        }
+        const int head = h * G + g;
+        if (part < 0) {
+            a.out[(long long)t * a.hq * D + head * D + e] = A / L;
+        } else {
+            float* pp = a.partial + ((long long)part * a.hq + head) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+}
+
 // Merge split partials: out = sum_i A_i e^{M_i-M} / sum_i L_i e^{M_i-M}.
 __global__ void combine_kernel(AttnArgs a) {
     const int4 c = a.combine[blockIdx.x];
@@ -224,13 +741,52 @@ __global__ void combine_kernel(AttnArgs a) {
     }
 }
 
+template <int D, typename KV, int G>
+void run_pipe(const AttnArgs& a, dim3 grid, int smem, cudaStream_t s) {
+    static int configured = 0;
+    if (smem > configured) {
+        TVARA_CUDA(cudaFuncSetAttribute(attn_pipe_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        configured = smem;
+    }
+    attn_pipe_kernel<D, KV, G><<<grid, kAttnWarps * 32, smem, s>>>(a);
+}
+
+template <int D, typename KV, int G>
+void run_xpose(const AttnArgs& a, dim3 grid, int smem, cudaStream_t s) {
+    static int configured = 0;
+    if (smem > configured) {
+        TVARA_CUDA(cudaFuncSetAttribute(attn_xpose_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        configured = smem;
+    }
+    attn_xpose_kernel<D, KV, G><<<grid, kAttnWarps * 32, smem, s>>>(a);
+}
+
+template <int D, typename KV, int G>
+constexpr bool xpose_ok() {
+    constexpr int LPS = (D * int(sizeof(KV)) / 16) < 32 ? (D * int(sizeof(KV)) / 16) : 32;
+    return (G & (G - 1)) == 0 && G <= LPS && (D / LPS) % 2 == 0;
+}
+
 template <int D, typename KV>
 void run_g(const AttnArgs& a, cudaStream_t s) {
     const int g = a.hq / a.hkv;
     dim3 grid(a.n_work, a.hkv);
+    // Each warp stages its blocks' K/V runs in a two-deep shared-memory ring;
+    // blocks too large for that use the register-streaming kernel instead.
+    const long long chunk = (long long)a.tpb * D * sizeof(KV);
+    const long long smem = 128 + (long long)kAttnWarps * kRing * 2 * chunk;
+    const bool pipe = smem <= 110 * 1024;
     switch (g) {
-#define TV_G(N) \
-    case N: attn_kernel<D, KV, N><<<grid, kAttnWarps * 32, 0, s>>>(a); break;
+#define TV_G(N)                                                                  \
+    case N:                                                                      \
+        if (pipe && xpose_ok<D, KV, N>()) {                                      \
+            if constexpr (xpose_ok<D, KV, N>()) run_xpose<D, KV, N>(a, grid, int(smem), s); \
+        } else if (pipe) {                                                       \
+            run_pipe<D, KV, N>(a, grid, int(smem), s);                           \
+        } else {                                                                 \
+            attn_kernel<D, KV, N><<<grid, kAttnWarps * 32, 0, s>>>(a);           \
+        }                                                                        \
+        break;
         TV_G(1) TV_G(2) TV_G(3) TV_G(4) TV_G(5) TV_G(6) TV_G(7) TV_G(8)
 #undef TV_G
         default: throw std::invalid_argument("unsupported query/KV head ratio (1..8)");

@@ -9,16 +9,17 @@
 // operand costs ~5e-4 relative per product, which measurably exceeds the 2e-3
 // logit budget on deep models.  So both operands are split exactly into
 // hi + lo FP16 parts (after an exact power-of-two scaling that keeps them in
-// the normal FP16 range: per matrix for W, per token for X) and each K-step
-// issues three MMAs, hi*hi + hi*lo + lo*hi, accumulating in F32 -- products
-// carry ~2^-22 relative error.
+// the normal FP16 range: per weight row for W, per token for X) and each
+// K-step issues three MMAs, hi*hi + hi*lo + lo*hi, accumulating in F32 --
+// products carry ~2^-22 relative error.
 //
-// Warp roles (160 threads): warps 0-3 produce A (one weight row per thread)
-// and then run the epilogue (TMEM lane == weight row); warp 4 allocates TMEM
-// and one of its threads issues the MMAs.  X tiles arrive by TMA (no
-// multicast) on the same mbarrier the producers arrive on.  Every mbarrier
-// wait is bounded: on timeout the kernel records an error code, waits
-// (bounded) for its own TMA copies, frees TMEM and exits.
+// Warp roles (160 threads): warps 0-3 produce A (one weight row per thread,
+// with a register ring that keeps several K-steps of packed weights in
+// flight) and then run the epilogue (TMEM lane == weight row); warp 4
+// allocates TMEM and one of its threads issues the MMAs.  X tiles arrive by
+// TMA (no multicast).  Every mbarrier wait is bounded: on timeout the kernel
+// records an error code, waits (bounded) for its own TMA copies, frees TMEM
+// and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -41,7 +42,6 @@ constexpr int kBTileMax = kMaxN * kBK * 2; // 16 KB per hi/lo B tile
 
 struct TcArgs {
     DeviceMatrix w;
-    const signed char* row_shift;  // weight row scaled by 2^row_shift before splitting
     const int* x_shift;     // per token: X scaled by 2^x_shift
     float* y;
     int ldy;
@@ -116,77 +116,134 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 // the 64-byte swizzle (chunk index XOR bits 1-2 of the row).
 __device__ __forceinline__ int sw64(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 
-__device__ __forceinline__ float h2f(unsigned short h) { return __half2float(__ushort_as_half(h)); }
+// 2^e as a float for |e| <= 126 (exact; used to apply the power-of-two scales).
+__device__ __forceinline__ float pow2(int e) { return __uint_as_float(unsigned(127 + e) << 23); }
 
-// The reference's F32 value of weight element (row, k0 + e), e < 32, for
-// one 32-element K-step; written into v[32].
+// ---------------------------------------------------------------- producer
+// Packed weights of one row for one 32-element K-step, fetched ahead of use.
 template <int TYPE>
-__device__ __forceinline__ void load_weights(const DeviceMatrix& w, long long row, int k0, float (&v)[32]) {
+struct Raw;
+template <>
+struct Raw<kQ4_K> {
+    uint4 q, m;  // 16 nibble bytes; the block header {d, dmin, scales[12]}
+};
+template <>
+struct Raw<kQ4_0> {
+    uint4 q;
+    unsigned short d;
+};
+template <>
+struct Raw<kQ8_0> {
+    uint4 q0, q1;
+    unsigned short d;
+};
+template <>
+struct Raw<kF16> {
+    uint4 q[4];
+};
+template <>
+struct Raw<kF32> {
+    uint4 q[8];
+};
+template <int TYPE>
+struct Ring {  // K-steps of weights kept in flight per producer thread
+    static constexpr int kDepth = TYPE == kF32 ? 1 : (TYPE == kF16 ? 2 : 4);
+};
+
+template <int TYPE>
+__device__ __forceinline__ Raw<TYPE> fetch(const DeviceMatrix& w, long long row, int k0, bool live) {
+    Raw<TYPE> r{};
+    if (!live) return r;
     const unsigned char* qs = w.qs + row * w.qs_row;
     const unsigned char* meta = w.meta + row * w.meta_row;
+    if constexpr (TYPE == kQ4_K) {
+        r.q = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
+        r.m = __ldg(reinterpret_cast<const uint4*>(meta + (k0 / 256) * 16));
+    } else if constexpr (TYPE == kQ4_0) {
+        r.q = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
+        r.d = __ldg(reinterpret_cast<const unsigned short*>(meta) + k0 / 32);
+    } else if constexpr (TYPE == kQ8_0) {
+        r.q0 = __ldg(reinterpret_cast<const uint4*>(qs + k0));
+        r.q1 = __ldg(reinterpret_cast<const uint4*>(qs + k0 + 16));
+        r.d = __ldg(reinterpret_cast<const unsigned short*>(meta) + k0 / 32);
+    } else if constexpr (TYPE == kF16) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 2) + c);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 4) + c);
+    }
+    return r;
+}
+
+__device__ __forceinline__ float h2f(unsigned short h) { return __half2float(__ushort_as_half(h)); }
+
+// Byte k of w placed in the mantissa of 2^23: the float 2^23 + byte.
+__device__ __forceinline__ float magic_byte(unsigned w, int k) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | unsigned(k)));
+}
+
+// Weights of the step, times 2^shift (exact), into v[32].
+template <int TYPE>
+__device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale, float (&v)[32]) {
     if constexpr (TYPE == kQ4_K || TYPE == kQ4_0) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
-        const unsigned ws[4] = {u.x, u.y, u.z, u.w};
-        float a, b;  // value = a*q - b
+        float a, b;  // value = a*q - b, already scaled
         if constexpr (TYPE == kQ4_K) {
-            const uint4 m = __ldg(reinterpret_cast<const uint4*>(meta + (k0 / 256) * 16));
-            const float d = h2f((unsigned short)(m.x & 0xffff)), dmin = h2f((unsigned short)(m.x >> 16));
+            const float d = h2f((unsigned short)(r.m.x & 0xffff)), dmin = h2f((unsigned short)(r.m.x >> 16));
             const int g = (k0 / 32) % 8;
-            const unsigned char* s = reinterpret_cast<const unsigned char*>(&m) + 4;
+            const unsigned sw[3] = {r.m.y, r.m.z, r.m.w};
+            auto sbyte = [&](int j) { return (sw[j >> 2] >> (8 * (j & 3))) & 255u; };
             unsigned sc, mn;
             if (g < 4) {
-                sc = s[g] & 63u;
-                mn = s[g + 4] & 63u;
+                sc = sbyte(g) & 63u;
+                mn = sbyte(g + 4) & 63u;
             } else {
-                sc = (s[g + 4] & 15u) | ((unsigned)(s[g - 4] >> 6) << 4);
-                mn = (s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
+                sc = (sbyte(g + 4) & 15u) | ((sbyte(g - 4) >> 6) << 4);
+                mn = (sbyte(g + 4) >> 4) | ((sbyte(g) >> 6) << 4);
             }
-            a = __fmul_rn(d, float(sc));
-            b = __fmul_rn(dmin, float(mn));
+            a = d * float(sc) * scale;
+            b = dmin * float(mn) * scale;
         } else {
-            a = h2f(reinterpret_cast<const unsigned short*>(meta)[k0 / 32]);
-            b = __fmul_rn(a, 8.f);
+            a = h2f(r.d) * scale;
+            b = 8.f * a;
         }
+        const unsigned ws[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const unsigned byte = (ws[i >> 2] >> (8 * (i & 3))) & 255u;
-            if constexpr (TYPE == kQ4_K) {
-                v[i] = __fsub_rn(__fmul_rn(a, float(byte & 15u)), b);
-                v[i + 16] = __fsub_rn(__fmul_rn(a, float(byte >> 4)), b);
-            } else {
-                v[i] = __fmul_rn(a, float(int(byte & 15u) - 8));
-                v[i + 16] = __fmul_rn(a, float(int(byte >> 4) - 8));
+        for (int i = 0; i < 4; ++i) {
+            const unsigned lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[4 * i + k] = fmaf(a, magic_byte(lo, k) - 8388608.f, -b);
+                v[16 + 4 * i + k] = fmaf(a, magic_byte(hi, k) - 8388608.f, -b);
             }
         }
     } else if constexpr (TYPE == kQ8_0) {
-        const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(qs + k0));
-        const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(qs + k0 + 16));
-        const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[k0 / 32]);
-        const unsigned ws[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        const float d = h2f(r.d) * scale;
+        const unsigned ws[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(d, float((signed char)((ws[i >> 2] >> (8 * (i & 3))) & 255u)));
+        for (int i = 0; i < 8; ++i) {
+            const unsigned u = ws[i] ^ 0x80808080u;  // int8 -> biased byte
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[4 * i + k] = d * (magic_byte(u, k) - 8388736.f);
+        }
     } else if constexpr (TYPE == kF16) {
-        const uint4* p = reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 2);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const uint4 u = __ldg(p + c);
-            const __half2* h = reinterpret_cast<const __half2*>(&u);
+            const __half2* h = reinterpret_cast<const __half2*>(&r.q[c]);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float2 f = __half22float2(h[j]);
-                v[c * 8 + 2 * j] = f.x;
-                v[c * 8 + 2 * j + 1] = f.y;
+                v[c * 8 + 2 * j] = f.x * scale;
+                v[c * 8 + 2 * j + 1] = f.y * scale;
             }
         }
     } else {
-        const float4* p = reinterpret_cast<const float4*>(qs + std::size_t(k0) * 4);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const float4 f = __ldg(p + c);
-            v[c * 4] = f.x;
-            v[c * 4 + 1] = f.y;
-            v[c * 4 + 2] = f.z;
-            v[c * 4 + 3] = f.w;
+            v[c * 4] = __uint_as_float(r.q[c].x) * scale;
+            v[c * 4 + 1] = __uint_as_float(r.q[c].y) * scale;
+            v[c * 4 + 2] = __uint_as_float(r.q[c].z) * scale;
+            v[c * 4 + 3] = __uint_as_float(r.q[c].w) * scale;
         }
     }
 }
@@ -244,40 +301,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = threadIdx.x;
         const long long row = row0 + r;
         const bool live = row < a.w.rows;
+        const int shift = live ? a.w.row_shift[row] : 0;
+        const float scale = pow2(shift);
         int last_ph[kStages];  // phase of the last TMA this thread issued per stage, -1 none
 #pragma unroll
         for (int s = 0; s < kStages; ++s) last_ph[s] = -1;
-        const int shift = live ? a.row_shift[row] : 0;
+        constexpr int P = Ring<TYPE>::kDepth;
+        Raw<TYPE> ring[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j)
+            ring[j] = fetch<TYPE>(a.w, row, (kstep0 + j) * kBK, live && j < a.k_steps);
         for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
             const int s = ks % kStages;
             const unsigned ph = (ks / kStages) & 1;
+            const int k0 = (kstep0 + ks) * kBK;
+            const Raw<TYPE> cur = ring[0];
+#pragma unroll
+            for (int j = 0; j + 1 < P; ++j) ring[j] = ring[j + 1];
+            ring[P - 1] = fetch<TYPE>(a.w, row, k0 + P * kBK, live && ks + P < a.k_steps);
+            float v[32];
+            convert<TYPE>(cur, k0, scale, v);
             if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
             unsigned char* st = stages + s * stage_bytes;
-            const int k0 = (kstep0 + ks) * kBK;
             if (r == 0) {
                 mbar_expect_tx(&full_b[s], 2 * b_bytes);
                 tma_load_2d(st + 2 * kATile, &map_hi, k0, tok0, &full_b[s]);
                 tma_load_2d(st + 2 * kATile + kBTileMax, &map_lo, k0, tok0, &full_b[s]);
                 last_ph[s] = int(ph);
             }
-            float v[32];
-            if (live) load_weights<TYPE>(a.w, row, k0, v);
-            else
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = 0.f;
             unsigned char* ahi = st;
             unsigned char* alo = st + kATile;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                __half hi[8], lo[8];
+                uint4 hi, lo;
+                unsigned* hp = reinterpret_cast<unsigned*>(&hi);
+                unsigned* lp = reinterpret_cast<unsigned*>(&lo);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float x = ldexpf(v[c * 8 + j], shift);
-                    hi[j] = __float2half_rn(x);
-                    lo[j] = __float2half_rn(__fsub_rn(x, __half2float(hi[j])));
+                for (int j = 0; j < 4; ++j) {
+                    const float x0 = v[c * 8 + 2 * j], x1 = v[c * 8 + 2 * j + 1];
+                    const __half2 h = __floats2half2_rn(x0, x1);
+                    const float2 hf = __half22float2(h);
+                    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+                    hp[j] = *reinterpret_cast<const unsigned*>(&h);
+                    lp[j] = *reinterpret_cast<const unsigned*>(&l);
                 }
-                *reinterpret_cast<uint4*>(ahi + sw64(r, c)) = *reinterpret_cast<const uint4*>(hi);
-                *reinterpret_cast<uint4*>(alo + sw64(r, c)) = *reinterpret_cast<const uint4*>(lo);
+                *reinterpret_cast<uint4*>(ahi + sw64(r, c)) = hi;
+                *reinterpret_cast<uint4*>(alo + sw64(r, c)) = lo;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&full_a[s]);
@@ -286,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, a.err, 12) ? 1 : 0);
         if (ok) {
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const float wscale = ldexpf(1.f, -shift);
+            const float wscale = pow2(-shift);
             for (int c0 = 0; c0 < a.n_tile; c0 += 32) {
                 unsigned u[32];
                 const unsigned taddr = tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c0;
@@ -305,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int t = tok0 + c0 + j;
                     if (c0 + j >= a.n_tile) break;
                     float val = 0.f;
-                    if (t < a.tokens) val = __uint_as_float(u[j]) * wscale * ldexpf(1.f, -a.x_shift[t]);
+                    if (t < a.tokens) val = __uint_as_float(u[j]) * wscale * pow2(-a.x_shift[t]);
                     if (a.epilogue == kSwiGLU) {
                         const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
                         if (t < a.tokens && live && !(r & 1))
@@ -378,13 +447,14 @@ __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half*
     __syncthreads();
     int e = 0;
     if (sm[0] > 0.f && isfinite(sm[0])) frexpf(sm[0], &e);
-    const int s = sm[0] > 0.f ? max(-120, min(120, 15 - e)) : 0;
+    const int s = sm[0] > 0.f ? max(-100, min(100, 15 - e)) : 0;
     if (threadIdx.x == 0) shift[t] = s;
+    const float f = pow2(s);
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = ldexpf(row[k], s);
+        const float v = row[k] * f;
         const __half h = __float2half_rn(v);
         hi[(long long)t * K + k] = h;
-        lo[(long long)t * K + k] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+        lo[(long long)t * K + k] = __float2half_rn(v - __half2float(h));
     }
 }
 
@@ -466,7 +536,6 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     }
     TcArgs a;
     a.w = g.w;
-    a.row_shift = g.w.row_shift;
     a.x_shift = shift;
     a.y = g.y;
     a.ldy = g.ldy;
