@@ -61,6 +61,8 @@ def parse():
                     help="override the layer count (same per-layer shapes; small cases for ncu captures)")
     ap.add_argument("--requests", type=int, default=512)
     ap.add_argument("--prefix", type=int, default=1024)
+    ap.add_argument("--suffix", type=int, nargs=2, default=(64, 2048), metavar=("MIN", "MAX"),
+                    help="unique suffix length range per request")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -100,7 +102,7 @@ def workload(args, vocab):
     rng = np.random.default_rng(args.seed + 1)
     n = args.requests
     prefix = rng.integers(0, vocab, args.prefix)
-    suffix = rng.integers(64, 2049, n)
+    suffix = rng.integers(args.suffix[0], args.suffix[1] + 1, n)
     out_len = rng.integers(64, 513, n)
     done = (rng.random(n) * out_len).astype(np.int64)
     first = rng.integers(0, vocab, n)
@@ -391,7 +393,8 @@ def run_ours(args):
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (Q4_K/Q8_0 weights, f16 KV)",
         "data": "synthetic",
         "config": {"workload": f"{args.config} ragged decode, {args.requests} requests, shared {args.prefix}-token "
-                               "prefix + U(64,2048) suffix + U(0,out) generated, 1 token/request/step",
+                               f"prefix + U({args.suffix[0]},{args.suffix[1]}) suffix + U(0,out) generated, "
+                               "1 token/request/step",
                    "model": args.config + (f" ({args.layers} layers)" if args.layers else ""),
                    "global_batch": args.requests, "seq_len": float(np.mean(lens0)),
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,

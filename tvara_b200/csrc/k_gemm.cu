@@ -3,7 +3,7 @@
 //
 // D[w_row][token] = sum_k W[w_row][k] * X[token][k] for a tile of 128 weight
 // rows (the MMA's M) and up to 256 tokens (N).  Quantised rows are
-// dequantised by four producer warps straight into the UMMA shared-memory
+// dequantised by eight producer warps straight into the UMMA shared-memory
 // layout.  Precision: the reference multiplies F32 weights by F32 activations
 // (core/include/tvara/quant.hpp:163-169); a single FP16 rounding of either
 // operand costs ~5e-4 relative per product, which measurably exceeds the 2e-3
@@ -13,9 +13,11 @@
 // K-step issues three MMAs, hi*hi + hi*lo + lo*hi, accumulating in F32 --
 // products carry ~2^-22 relative error.
 //
-// Warp roles (160 threads): warps 0-3 produce A (one weight row per thread,
-// with a register ring that keeps several K-steps of packed weights in
-// flight) and then run the epilogue (TMEM lane == weight row); warp 4
+// Warp roles (288 threads): warps 0-7 produce A -- thread (r, h) converts
+// weight row r, K-half h of every step, keeping several steps of packed
+// weights in flight in a register ring; two producer warps per scheduler
+// hide each other's dependency stalls -- and then run the epilogue (TMEM
+// lane == weight row; warps w and w+4 split the token columns); warp 8
 // allocates TMEM and one of its threads issues the MMAs.  X tiles arrive by
 // TMA (no multicast).  Every mbarrier wait is bounded: on timeout the kernel
 // records an error code, waits (bounded) for its own TMA copies, frees TMEM
@@ -34,8 +36,10 @@ constexpr int kBM = 128;          // weight rows per tile (MMA M)
 constexpr int kBK = 32;           // K per stage (one 64-byte swizzled row of FP16)
 constexpr int kStages = 4;
 constexpr int kMaxN = 256;        // tokens per tile (MMA N)
-constexpr int kThreads = 160;
-constexpr int kProducers = 128;
+constexpr int kProducerWarps = 8;                // two per scheduler: (row, K-half) per thread
+constexpr int kProducers = kProducerWarps * 32;
+constexpr int kMmaWarp = kProducerWarps;
+constexpr int kThreads = kProducers + 32;
 constexpr unsigned kSpinLimit = 1u << 26;
 constexpr int kATile = kBM * kBK * 2;      // 8 KB per hi/lo A tile
 constexpr int kBTileMax = kMaxN * kBK * 2; // 16 KB per hi/lo B tile
@@ -120,58 +124,68 @@ __device__ __forceinline__ int sw64(int r, int c) { return r * 64 + ((c ^ ((r >>
 __device__ __forceinline__ float pow2(int e) { return __uint_as_float(unsigned(127 + e) << 23); }
 
 // ---------------------------------------------------------------- producer
-// Packed weights of one row for one 32-element K-step, fetched ahead of use.
+// Packed weights of one row for HALF of a 32-element K-step (hf = 0 or 1),
+// fetched ahead of use.  Q4 types: bytes hf*8..hf*8+7 of the 16-byte unit,
+// i.e. elements {hf*8..hf*8+7} (low nibbles) and {16+hf*8..} (high nibbles);
+// other types: elements hf*16..hf*16+15.
 template <int TYPE>
 struct Raw;
 template <>
 struct Raw<kQ4_K> {
-    uint4 q, m;  // 16 nibble bytes; the block header {d, dmin, scales[12]}
+    uint2 q;
+    uint4 m;  // the block header {d, dmin, scales[12]}
 };
 template <>
 struct Raw<kQ4_0> {
-    uint4 q;
+    uint2 q;
     unsigned short d;
 };
 template <>
 struct Raw<kQ8_0> {
-    uint4 q0, q1;
+    uint4 q;
     unsigned short d;
 };
 template <>
 struct Raw<kF16> {
-    uint4 q[4];
+    uint4 q[2];
 };
 template <>
 struct Raw<kF32> {
-    uint4 q[8];
+    uint4 q[4];
 };
 template <int TYPE>
 struct Ring {  // K-steps of weights kept in flight per producer thread
-    static constexpr int kDepth = TYPE == kF32 ? 1 : (TYPE == kF16 ? 2 : 4);
+    static constexpr int kDepth = TYPE == kF32 ? 2 : 4;
 };
+// 16-byte chunks (of the 64-byte swizzled row) holding v[0..7] and v[8..15]
+template <int TYPE>
+__device__ __forceinline__ int chunk_a(int hf) { return (TYPE == kQ4_K || TYPE == kQ4_0) ? hf : 2 * hf; }
+template <int TYPE>
+__device__ __forceinline__ int chunk_b(int hf) { return (TYPE == kQ4_K || TYPE == kQ4_0) ? 2 + hf : 2 * hf + 1; }
 
 template <int TYPE>
-__device__ __forceinline__ Raw<TYPE> fetch(const DeviceMatrix& w, long long row, int k0, bool live) {
+__device__ __forceinline__ Raw<TYPE> fetch(const DeviceMatrix& w, long long row, int k0, int hf, bool live) {
     Raw<TYPE> r{};
     if (!live) return r;
     const unsigned char* qs = w.qs + row * w.qs_row;
     const unsigned char* meta = w.meta + row * w.meta_row;
     if constexpr (TYPE == kQ4_K) {
-        r.q = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
+        r.q = __ldg(reinterpret_cast<const uint2*>(qs + (k0 / 32) * 16 + hf * 8));
         r.m = __ldg(reinterpret_cast<const uint4*>(meta + (k0 / 256) * 16));
     } else if constexpr (TYPE == kQ4_0) {
-        r.q = __ldg(reinterpret_cast<const uint4*>(qs + (k0 / 32) * 16));
+        r.q = __ldg(reinterpret_cast<const uint2*>(qs + (k0 / 32) * 16 + hf * 8));
         r.d = __ldg(reinterpret_cast<const unsigned short*>(meta) + k0 / 32);
     } else if constexpr (TYPE == kQ8_0) {
-        r.q0 = __ldg(reinterpret_cast<const uint4*>(qs + k0));
-        r.q1 = __ldg(reinterpret_cast<const uint4*>(qs + k0 + 16));
+        r.q = __ldg(reinterpret_cast<const uint4*>(qs + k0 + hf * 16));
         r.d = __ldg(reinterpret_cast<const unsigned short*>(meta) + k0 / 32);
     } else if constexpr (TYPE == kF16) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 2) + c);
+        for (int c = 0; c < 2; ++c)
+            r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0 + hf * 16) * 2) + c);
     } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0) * 4) + c);
+        for (int c = 0; c < 4; ++c)
+            r.q[c] = __ldg(reinterpret_cast<const uint4*>(qs + std::size_t(k0 + hf * 16) * 4) + c);
     }
     return r;
 }
@@ -183,9 +197,10 @@ __device__ __forceinline__ float magic_byte(unsigned w, int k) {
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | unsigned(k)));
 }
 
-// Weights of the step, times 2^shift (exact), into v[32].
+// The half-step's 16 weights, times 2^shift (exact), into v[16] in the order
+// of chunk_a (v[0..7]) then chunk_b (v[8..15]).
 template <int TYPE>
-__device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale, float (&v)[32]) {
+__device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale, float (&v)[16]) {
     if constexpr (TYPE == kQ4_K || TYPE == kQ4_0) {
         float a, b;  // value = a*q - b, already scaled
         if constexpr (TYPE == kQ4_K) {
@@ -201,34 +216,35 @@ __device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale,
                 sc = (sbyte(g + 4) & 15u) | ((sbyte(g - 4) >> 6) << 4);
                 mn = (sbyte(g + 4) >> 4) | ((sbyte(g) >> 6) << 4);
             }
-            a = d * float(sc) * scale;
-            b = dmin * float(mn) * scale;
+            // small integers to float through the 2^23 magic (no conversion unit)
+            a = d * (__uint_as_float(0x4B000000u | sc) - 8388608.f) * scale;
+            b = dmin * (__uint_as_float(0x4B000000u | mn) - 8388608.f) * scale;
         } else {
             a = h2f(r.d) * scale;
             b = 8.f * a;
         }
-        const unsigned ws[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+        const unsigned ws[2] = {r.q.x, r.q.y};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
             const unsigned lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 v[4 * i + k] = fmaf(a, magic_byte(lo, k) - 8388608.f, -b);
-                v[16 + 4 * i + k] = fmaf(a, magic_byte(hi, k) - 8388608.f, -b);
+                v[8 + 4 * i + k] = fmaf(a, magic_byte(hi, k) - 8388608.f, -b);
             }
         }
     } else if constexpr (TYPE == kQ8_0) {
         const float d = h2f(r.d) * scale;
-        const unsigned ws[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+        const unsigned ws[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
             const unsigned u = ws[i] ^ 0x80808080u;  // int8 -> biased byte
 #pragma unroll
             for (int k = 0; k < 4; ++k) v[4 * i + k] = d * (magic_byte(u, k) - 8388736.f);
         }
     } else if constexpr (TYPE == kF16) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
             const __half2* h = reinterpret_cast<const __half2*>(&r.q[c]);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -239,7 +255,7 @@ __device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale,
         }
     } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4; ++c) {
             v[c * 4] = __uint_as_float(r.q[c].x) * scale;
             v[c * 4 + 1] = __uint_as_float(r.q[c].y) * scale;
             v[c * 4 + 2] = __uint_as_float(r.q[c].z) * scale;
@@ -286,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 4) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -296,9 +312,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const unsigned tmem = *tmem_slot;
 
-    if (warp < 4) {
-        // ---------------- producers: A tiles (and thread 0: B tiles by TMA)
-        const int r = threadIdx.x;
+    if (warp < kProducerWarps) {
+        // ---------------- producers: A tiles (and thread 0: B tiles by TMA).
+        // Thread (r, hf): weight row r of the tile, K-half hf of each step.
+        const int r = threadIdx.x % kBM;
+        const int hf = threadIdx.x / kBM;
         const long long row = row0 + r;
         const bool live = row < a.w.rows;
         const int shift = live ? a.w.row_shift[row] : 0;
@@ -310,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         Raw<TYPE> ring[P];
 #pragma unroll
         for (int j = 0; j < P; ++j)
-            ring[j] = fetch<TYPE>(a.w, row, (kstep0 + j) * kBK, live && j < a.k_steps);
+            ring[j] = fetch<TYPE>(a.w, row, (kstep0 + j) * kBK, hf, live && j < a.k_steps);
         for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
             const int s = ks % kStages;
             const unsigned ph = (ks / kStages) & 1;
@@ -318,12 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Raw<TYPE> cur = ring[0];
 #pragma unroll
             for (int j = 0; j + 1 < P; ++j) ring[j] = ring[j + 1];
-            ring[P - 1] = fetch<TYPE>(a.w, row, k0 + P * kBK, live && ks + P < a.k_steps);
-            float v[32];
+            ring[P - 1] = fetch<TYPE>(a.w, row, k0 + P * kBK, hf, live && ks + P < a.k_steps);
+            float v[16];
             convert<TYPE>(cur, k0, scale, v);
             if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
             unsigned char* st = stages + s * stage_bytes;
-            if (r == 0) {
+            if (threadIdx.x == 0) {
                 mbar_expect_tx(&full_b[s], 2 * b_bytes);
                 tma_load_2d(st + 2 * kATile, &map_hi, k0, tok0, &full_b[s]);
                 tma_load_2d(st + 2 * kATile + kBTileMax, &map_lo, k0, tok0, &full_b[s]);
@@ -332,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char* ahi = st;
             unsigned char* alo = st + kATile;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint4 hi, lo;
                 unsigned* hp = reinterpret_cast<unsigned*>(&hi);
                 unsigned* lp = reinterpret_cast<unsigned*>(&lo);
@@ -340,25 +358,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 4; ++j) {
                     const float x0 = v[c * 8 + 2 * j], x1 = v[c * 8 + 2 * j + 1];
                     const __half2 h = __floats2half2_rn(x0, x1);
-                    const float2 hf = __half22float2(h);
-                    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+                    const float2 hf2 = __half22float2(h);
+                    const __half2 l = __floats2half2_rn(x0 - hf2.x, x1 - hf2.y);
                     hp[j] = *reinterpret_cast<const unsigned*>(&h);
                     lp[j] = *reinterpret_cast<const unsigned*>(&l);
                 }
-                *reinterpret_cast<uint4*>(ahi + sw64(r, c)) = hi;
-                *reinterpret_cast<uint4*>(alo + sw64(r, c)) = lo;
+                const int chunk = c == 0 ? chunk_a<TYPE>(hf) : chunk_b<TYPE>(hf);
+                *reinterpret_cast<uint4*>(ahi + sw64(r, chunk)) = hi;
+                *reinterpret_cast<uint4*>(alo + sw64(r, chunk)) = lo;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&full_a[s]);
         }
-        // ---------------- epilogue: TMEM lane r holds weight row row0 + r
+        // ---------------- epilogue: TMEM lane r holds weight row row0 + r;
+        // warps w and w+4 share lanes 32*(w%4).. and split the token columns
         const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, a.err, 12) ? 1 : 0);
         if (ok) {
             asm volatile("tcgen05.fence::after_thread_sync;");
             const float wscale = pow2(-shift);
-            for (int c0 = 0; c0 < a.n_tile; c0 += 32) {
+            for (int c0 = hf * 32; c0 < a.n_tile; c0 += 64) {
                 unsigned u[32];
-                const unsigned taddr = tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c0;
+                const unsigned taddr = tmem + ((unsigned)((warp % 4) * 32) << 16) + (unsigned)c0;
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -390,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // before leaving, every TMA copy this thread issued must have landed
         // (normally long since consumed; after an abort, wait with a bound)
-        if (r == 0) {
+        if (threadIdx.x == 0) {
             for (int s = 0; s < kStages; ++s)
                 if (last_ph[s] >= 0)
                     for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full_b[s], unsigned(last_ph[s])); ++i) {
@@ -421,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kMmaWarp) {
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
