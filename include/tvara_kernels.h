@@ -76,6 +76,22 @@ TVARA_API size_t tvara_paged_attention_workspace(const tvara_attention_args* arg
 TVARA_API int tvara_paged_attention(const tvara_attention_args* args, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* No counterpart in the reference (its attention runs on the CPU).  The same
+ * attention as tvara_paged_attention, with its scratch in a fixed area inside
+ * this library (tvara_paged_attention_noalloc_max() bytes per device, 16 MiB)
+ * instead of caller memory, for callers that cannot allocate device memory at
+ * the call: FFI hosts with no device allocator, code whose device memory
+ * belongs to another framework's allocator, code that must not pay
+ * cudaMalloc's device-wide synchronisation.  It allocates nothing.  Arguments
+ * needing more scratch than the maximum (tvara_paged_attention_workspace) are
+ * rejected with an error and nothing is launched.  The first call on a device,
+ * with that device current, resolves the scratch address; make it before any
+ * stream capture begins.  One scratch per device: calls overlapping on one
+ * device (other streams or threads) race and must be serialised by the
+ * caller. */
+TVARA_API size_t tvara_paged_attention_noalloc_max(void);
+TVARA_API int tvara_paged_attention_noalloc(const tvara_attention_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,8 @@ SIGNATURES = {
     "tvara_quant_matmul": (C.c_int, [C.c_int, P, SZ, SZ, P, SZ, P, P, SZ, P]),
     "tvara_paged_attention_workspace": (SZ, [P]),
     "tvara_paged_attention": (C.c_int, [P, P, SZ, P]),
+    "tvara_paged_attention_noalloc_max": (SZ, []),
+    "tvara_paged_attention_noalloc": (C.c_int, [P, P]),
 }
 
 
