@@ -83,10 +83,30 @@ typedef struct tvara_open_options {
 TVARA_API tvara_model* tvara_model_open_ex(const char* utf8_path, size_t max_blocks, size_t block_tokens,
                                            const tvara_open_options* options);
 
+/* The tensor-parallel shard a rank of tvara_model_open_ex holds (no
+ * reference counterpart: the reference engine is single-device).  Query
+ * heads, KV heads and FFN rows [begin, begin + count) of each layer; Q/K/V and
+ * gate/up are split by rows, o_proj and down_proj by the matching columns,
+ * and the partial outputs of o_proj / down_proj are summed over the group.
+ * Reads only the GGUF header (no GPU).  0, or -1 with the reason when the
+ * model cannot be split that way. */
+typedef struct tvara_tp_shard_info {
+    uint32_t struct_size;  /* sizeof(tvara_tp_shard_info) */
+    uint32_t head_dim;
+    uint32_t heads_begin, heads;
+    uint32_t kv_heads_begin, kv_heads;
+    uint32_t ffn_begin, ffn;
+} tvara_tp_shard_info;
+TVARA_API int tvara_tp_shard(const char* utf8_path, uint32_t tp_rank, uint32_t tp_size, tvara_tp_shard_info* out);
+
 /* ---- additive: ragged multi-sequence step ----------------------------- */
 
 enum {
-    TVARA_STEP_ALL_LOGITS = 1  /* one logits row per token instead of per sequence */
+    TVARA_STEP_ALL_LOGITS = 1,   /* one logits row per token instead of per sequence */
+    TVARA_STEP_FINITE_ARGMAX = 2 /* argmax is 0xFFFFFFFF for a row whose logits hold a NaN or an
+                                    infinity: the "Nonfinite model logits" check of
+                                    NativeSchedulerBackend.decode_batch (python/tvara/scheduler.py:205-206)
+                                    done on the device, without copying logits to the host */
 };
 
 /* One device step over a ragged batch: sequence i appends

@@ -1,0 +1,69 @@
+"""Tensor-parallel engine on two GPUs (skipped with fewer): one process per
+GPU opens its shard of the tiny model with an NCCL unique id, both ranks run
+the same prefill chunk, ragged batch step and decodes in the same order, and
+the logits must match the reference's F32 forward (the pinned oracle) within
+the logit tolerance on both ranks -- the allreduce leaves every rank with the
+same residual, so the ranks' logits are identical."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-3
+
+
+def _rank(rank, world, nccl_id, path, prompts, out):
+    import torch
+    from tvara_b200.native import NativeModel
+
+    torch.cuda.set_device(rank)
+    with NativeModel(path, max_blocks=64, block_tokens=16, device=rank, tp_rank=rank, tp_size=world,
+                     nccl_id=nccl_id) as m:
+        seqs = [m._new_sequence() for _ in prompts]
+        # one ragged step: every prompt but its last token, all rows
+        chunk, _ = m.batch_step(seqs, [p[:-1] for p in prompts], all_logits=True)
+        # then the last tokens one sequence at a time, through the reference ABI call
+        last = np.stack([m.logits(s, p[-1]) for s, p in zip(seqs, prompts)])
+        np.savez(out % rank, chunk=chunk, last=last)
+
+
+def _nccl_unique_id():
+    import torch  # noqa: F401  (loads the NCCL that torch ships)
+    lib = C.CDLL("libnccl.so.2")
+    buf = C.create_string_buffer(128)
+    assert lib.ncclGetUniqueId(buf) == 0
+    return buf.raw
+
+
+def test_tp2_matches_oracle(tiny_path, tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    from oracle.model import OracleModel
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (9, 3, 17)]
+    out = str(tmp_path / "rank%d.npz")
+    nccl_id = _nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, str(tiny_path), prompts, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    r0, r1 = np.load(out % 0), np.load(out % 1)
+    assert np.array_equal(r0["chunk"], r1["chunk"]) and np.array_equal(r0["last"], r1["last"])
+    oracle = OracleModel(tiny_path, max_positions=64)
+    refs = [oracle.forward(p) for p in prompts]
+    want_chunk = np.concatenate([r[:-1] for r in refs])
+    want_last = np.stack([r[-1] for r in refs])
+    assert np.abs(r0["chunk"] - want_chunk).max() <= ATOL
+    assert np.abs(r0["last"] - want_last).max() <= ATOL

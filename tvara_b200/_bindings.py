@@ -27,6 +27,12 @@ class OpenOptions(C.Structure):
     ]
 
 
+class TpShardInfo(C.Structure):
+    """include/tvara_capi.h tvara_tp_shard_info."""
+    _fields_ = [(name, C.c_uint32) for name in (
+        "struct_size", "head_dim", "heads_begin", "heads", "kv_heads_begin", "kv_heads", "ffn_begin", "ffn")]
+
+
 # name: (restype, argtypes)
 SIGNATURES = {
     # reference ABI (core/include/tvara/c_api.h:13-24)
@@ -43,6 +49,7 @@ SIGNATURES = {
     "tvara_sequence_truncate": (C.c_int, [P, U64, SZ]),
     # additive
     "tvara_model_open_ex": (P, [C.c_char_p, SZ, SZ, C.POINTER(OpenOptions)]),
+    "tvara_tp_shard": (C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.POINTER(TpShardInfo)]),
     "tvara_batch_step": (C.c_int, [P, SZ, U64P, U32P, U32P, C.c_uint32, F32P, SZ, U32P, SZ]),
     "tvara_sequence_fork": (U64, [P, U64]),
     "tvara_sequence_length": (C.c_int, [P, U64, SZP]),

@@ -13,6 +13,8 @@
 #include <string>
 
 #include "engine.hpp"
+#include "gguf.hpp"
+#include "tp_plan.hpp"
 
 struct tvara_model {
     std::unique_ptr<tvara::Engine> engine;
@@ -94,6 +96,25 @@ tvara_model* tvara_model_open(const char* path, size_t max_blocks, size_t block_
 tvara_model* tvara_model_open_ex(const char* path, size_t max_blocks, size_t block_tokens,
                                  const tvara_open_options* options) {
     return guarded<tvara_model*>(nullptr, [&] { return open_model(path, max_blocks, block_tokens, options); });
+}
+
+int tvara_tp_shard(const char* path, uint32_t tp_rank, uint32_t tp_size, tvara_tp_shard_info* out) {
+    return guarded<int>(-1, [&] {
+        if (!path || !*path) throw std::invalid_argument("empty model path");
+        if (!out || out->struct_size < sizeof(tvara_tp_shard_info)) throw std::invalid_argument("invalid shard output");
+        tvara::gguf::File f(path);
+        const auto cfg = tvara::gguf::llama_config(f.doc());
+        tvara::gguf::validate_llama_tensors(f.doc(), cfg);
+        const auto s = tvara::tp_shard(f, cfg, int(tp_rank), tp_size ? int(tp_size) : 1);
+        out->head_dim = uint32_t(s.head_dim);
+        out->heads_begin = uint32_t(s.heads_begin);
+        out->heads = uint32_t(s.heads);
+        out->kv_heads_begin = uint32_t(s.kv_heads_begin);
+        out->kv_heads = uint32_t(s.kv_heads);
+        out->ffn_begin = uint32_t(s.ffn_begin);
+        out->ffn = uint32_t(s.ffn);
+        return 0;
+    });
 }
 
 void tvara_model_close(tvara_model* model) {
@@ -190,7 +211,8 @@ int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t* sequences
                      size_t argmax_count) {
     return guarded<int>(-1, [&] {
         if (!model || !n_seq || !sequences || !cu_tokens || !tokens) throw std::invalid_argument("invalid batch buffers");
-        if (flags & ~uint32_t(TVARA_STEP_ALL_LOGITS)) throw std::invalid_argument("unknown step flags");
+        if (flags & ~uint32_t(TVARA_STEP_ALL_LOGITS | TVARA_STEP_FINITE_ARGMAX))
+            throw std::invalid_argument("unknown step flags");
         const size_t total = cu_tokens[n_seq];
         const bool all = flags & TVARA_STEP_ALL_LOGITS;
         const size_t rows = all ? total : n_seq;
@@ -200,7 +222,8 @@ int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t* sequences
         if (argmax && argmax_count != rows) throw std::invalid_argument("invalid argmax output buffer");
         auto& e = engine_of(model);
         std::lock_guard lock(model->mutex);
-        e.step({sequences, n_seq}, {cu_tokens, n_seq + 1}, {tokens, total}, all, logits, argmax);
+        e.step({sequences, n_seq}, {cu_tokens, n_seq + 1}, {tokens, total}, all, logits, argmax,
+               (flags & TVARA_STEP_FINITE_ARGMAX) != 0);
         return 0;
     });
 }

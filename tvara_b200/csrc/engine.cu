@@ -9,6 +9,7 @@
 
 #include "attention_plan.hpp"
 #include "collective.hpp"
+#include "tp_plan.hpp"
 
 namespace tvara {
 namespace {
@@ -76,18 +77,15 @@ Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t bloc
     gguf::validate_llama_tensors(f.doc(), cfg_);
     metadata_ = f.metadata_json();
     const int tp = std::max(1, opt.tp_size);
-    if (opt.tp_rank < 0 || opt.tp_rank >= tp) throw std::invalid_argument("invalid tensor-parallel rank");
-    if (cfg_.heads % tp || cfg_.kv_heads % tp || cfg_.ffn % tp)
-        throw std::invalid_argument("tensor-parallel size must divide the head counts and FFN width");
+    const TpShard shard = tp_shard(f, cfg_, opt.tp_rank, tp);
     hidden_ = int(cfg_.hidden);
     vocab_ = int(cfg_.vocab);
     layers_ = int(cfg_.layers);
-    dim_ = int(cfg_.head_dim());
-    hq_ = int(cfg_.heads) / tp;
-    hkv_ = int(cfg_.kv_heads) / tp;
-    ffn_ = int(cfg_.ffn) / tp;
+    dim_ = shard.head_dim;
+    hq_ = shard.heads;
+    hkv_ = shard.kv_heads;
+    ffn_ = shard.ffn;
     qkv_w_ = (hq_ + 2 * hkv_) * dim_;
-    if (hq_ / hkv_ > 8) throw std::invalid_argument("unsupported query/KV head ratio (1..8)");
     if (dim_ != 16 && dim_ != 32 && dim_ != 64 && dim_ != 128 && dim_ != 256)
         throw std::invalid_argument("unsupported head_dim (16, 32, 64, 128, 256)");
     tmax_ = std::max(1, opt.max_step_tokens);
@@ -323,7 +321,9 @@ void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int toke
 }
 
 void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
-                  std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax) {
+                  std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax,
+                  bool finite_argmax) {
+    finite_argmax_ = finite_argmax;
     const std::size_t n = seqs.size();
     if (!n || cu.size() != n + 1 || cu[0] != 0) throw std::invalid_argument("invalid batch layout");
     for (std::size_t i = 0; i < n; ++i)
@@ -629,7 +629,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         timed(kProfHead, [&] {
             launch_rmsnorm(x_, D, d_rows, R, D, final_norm_, cfg_.eps, xn_, D, stream_);
             projection(head_, xn_, D, R, logits_, vocab_, kStore);
-            if (argmax) launch_argmax(logits_, R, vocab_, argmax_, stream_);
+            if (argmax) launch_argmax(logits_, R, vocab_, argmax_, finite_argmax_, stream_);
         });
     }
     TVARA_CUDA(cudaMemcpyAsync(err_host_, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));

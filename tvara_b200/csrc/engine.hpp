@@ -53,9 +53,11 @@ public:
     const EngineOptions& options() const { return opt_; }
 
     // One ragged step; see tvara_batch_step.  Rows of logits / argmax are
-    // written to host memory (either may be null).
+    // written to host memory (either may be null).  finite_argmax marks rows
+    // whose logits are not all finite with argmax 0xFFFFFFFF.
     void step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
-              std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax);
+              std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax,
+              bool finite_argmax = false);
 
     // Appends positions to a sequence's table without computing K/V.
     void reserve(std::uint64_t seq, std::size_t count);
@@ -129,6 +131,7 @@ private:
     float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ff_ = nullptr,
           *ffu_ = nullptr, *logits_ = nullptr, *partial_ = nullptr, *xo_ = nullptr;
     unsigned* argmax_ = nullptr;
+    bool finite_argmax_ = false;
     int* err_ = nullptr;
     void* tc_ws_ = nullptr;        // tensor-core projection: hi/lo FP16 activations + token scales
     std::size_t tc_ws_bytes_ = 0;

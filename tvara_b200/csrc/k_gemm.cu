@@ -19,7 +19,7 @@
 // hide each other's dependency stalls -- and then run the epilogue (TMEM
 // lane == weight row; warps w and w+4 split the token columns); warp 8
 // allocates TMEM and one of its threads issues the MMAs.  X tiles arrive by
-// TMA (no multicast).  Every mbarrier wait is bounded: on timeout the kernel
+// per-CTA TMA loads of this GPU's own memory.  Every mbarrier wait is bounded: on timeout the kernel
 // records an error code, waits (bounded) for its own TMA copies, frees TMEM
 // and exits.
 #include <cuda.h>

@@ -91,13 +91,16 @@ __global__ void rope_kv_kernel(RopeArgs a) {
 }
 
 // First index of the maximum; NaN ranks above every number (numpy.argmax).
-__global__ void argmax_kernel(const float* logits, int vocab, unsigned* out) {
+// With finite_check, a row holding any NaN or infinity reports 0xFFFFFFFF.
+__global__ void argmax_kernel(const float* logits, int vocab, unsigned* out, int finite_check) {
     const float* row = logits + (long long)blockIdx.x * vocab;
     float best = -INFINITY;
     int idx = INT_MAX;
     bool nan = false;
+    bool bad = false;
     for (int k = threadIdx.x; k < vocab; k += blockDim.x) {
         const float v = row[k];
+        bad |= !isfinite(v);
         if (isnan(v)) {
             if (!nan || k < idx) {
                 nan = true;
@@ -111,6 +114,7 @@ __global__ void argmax_kernel(const float* logits, int vocab, unsigned* out) {
     __shared__ float sb[32];
     __shared__ int si[32];
     __shared__ int sn[32];
+    const int any_bad = __syncthreads_or(bad);
     for (int o = 16; o; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
@@ -140,7 +144,7 @@ __global__ void argmax_kernel(const float* logits, int vocab, unsigned* out) {
                 idx = si[j];
             }
         }
-        out[blockIdx.x] = unsigned(idx == INT_MAX ? 0 : idx);
+        out[blockIdx.x] = finite_check && any_bad ? 0xFFFFFFFFu : unsigned(idx == INT_MAX ? 0 : idx);
     }
 }
 
@@ -183,9 +187,9 @@ void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
     TVARA_LAUNCHED();
 }
 
-void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, cudaStream_t s) {
+void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, bool finite_check, cudaStream_t s) {
     if (rows <= 0) return;
-    argmax_kernel<<<rows, 512, 0, s>>>(logits, vocab, out);
+    argmax_kernel<<<rows, 512, 0, s>>>(logits, vocab, out, int(finite_check));
     TVARA_LAUNCHED();
 }
 

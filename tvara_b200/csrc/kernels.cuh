@@ -106,8 +106,9 @@ struct AttnArgs {
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 
 // ---- output ---------------------------------------------------------------
-// argmax of each row (first index of the maximum; NaN counts as maximal).
-void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, cudaStream_t s);
+// argmax of each row (first index of the maximum; NaN counts as maximal);
+// with finite_check, rows holding a NaN or infinity report 0xFFFFFFFF.
+void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, bool finite_check, cudaStream_t s);
 // Copies whole KV blocks (copy-on-write): pairs of (from, to) block ids.
 void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n, cudaStream_t s);
 

@@ -21,10 +21,24 @@ from ._bindings import OpenOptions, F32P, U32P, U64P, I32P
 
 KV_F32, KV_F16 = 0, 1
 STEP_ALL_LOGITS = 1
+STEP_FINITE_ARGMAX = 2
+ARGMAX_NONFINITE = 0xFFFFFFFF
 
 
 def _ptr(a: np.ndarray, typ):
     return a.ctypes.data_as(typ)
+
+
+def tp_shard(path, tp_rank: int, tp_size: int, library=None) -> dict:
+    """tvara_tp_shard: the query heads, KV heads and FFN rows a tensor-parallel
+    rank holds (reads the GGUF header only; no GPU needed)."""
+    from ._bindings import TpShardInfo
+    lib = load_library(library)
+    info = TpShardInfo()
+    info.struct_size = C.sizeof(TpShardInfo)
+    if lib.tvara_tp_shard(str(Path(path).resolve()).encode("utf-8"), int(tp_rank), int(tp_size), C.byref(info)):
+        raise RuntimeError(lib.tvara_last_error().decode("utf-8", "replace"))
+    return {name: int(getattr(info, name)) for name, _ in TpShardInfo._fields_ if name != "struct_size"}
 
 
 class NativeModel:
@@ -145,10 +159,12 @@ class NativeModel:
                 self._raise_error()
         return n.value
 
-    def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False):
+    def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False, finite_argmax=False):
         """One device step: sequence i appends token_lists[i].  Returns
         (logits [rows, vocab] or None, argmax [rows] or None) with one row per
-        sequence (its last token) or per token when all_logits."""
+        sequence (its last token) or per token when all_logits.  With
+        finite_argmax, a row whose logits hold a NaN or an infinity has
+        argmax ARGMAX_NONFINITE."""
         seqs = np.ascontiguousarray(sequences, dtype=np.uint64)
         lens = np.array([len(t) for t in token_lists], dtype=np.uint32)
         cu = np.zeros(len(seqs) + 1, dtype=np.uint32)
@@ -161,7 +177,7 @@ class NativeModel:
             self._check_open()
             status = self._library.tvara_batch_step(
                 self._handle, len(seqs), _ptr(seqs, U64P), _ptr(cu, U32P), _ptr(toks, U32P),
-                STEP_ALL_LOGITS if all_logits else 0,
+                (STEP_ALL_LOGITS if all_logits else 0) | (STEP_FINITE_ARGMAX if finite_argmax else 0),
                 _ptr(out, F32P) if out is not None else None, out.size if out is not None else 0,
                 _ptr(am, U32P) if am is not None else None, len(am) if am is not None else 0)
             if status:
