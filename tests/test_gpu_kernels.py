@@ -216,31 +216,59 @@ def attn_close(got, ref, tol=2e-5):
     return np.all(np.abs(got - ref) <= tol * (1 + np.abs(ref)))
 
 
+KV_DTYPES = {"f32": (np.float32, 0, 2e-5), "f16": (np.float16, 1, 5e-5)}
+
+
+@pytest.mark.parametrize("kv", ["f32", "f16"])
 @pytest.mark.parametrize("dim", [32, 64, 128])
 @pytest.mark.parametrize("length", [1, 15, 16, 17, 31, 32, 33])
-def test_attention_ragged_lengths_nan_poisoned(capi, dim, length):
+def test_attention_ragged_lengths_nan_poisoned(capi, dim, length, kv):
     """prefill_t174.cpp pattern: unused tail slots hold NaN, freed blocks hold
-    junk; neither may reach the output."""
+    junk; neither may reach the output.  F16 pools of head_dim 64/128 run the
+    tensor-core kernel, whose value MMA would turn 0 * NaN into NaN."""
+    dtype, code, tol = KV_DTYPES[kv]
     rng = np.random.default_rng(length * 7 + dim)
-    pool = Pool(1, 2, dim, 16, 8, rng=rng)
+    pool = Pool(1, 2, dim, 16, 8, dtype=dtype, rng=rng)
     junk = pool.sequence(48, scale=100.0)
     pool.free.extend(junk)  # dropped sequence: its blocks keep junk
     ids = pool.sequence(length)
     q = rng.standard_normal(4 * dim).astype(np.float32)
-    got = run_attention(capi, pool, 0, 4, q[None], ids, [0], [length])[0]
-    assert attn_close(got, oracle_attention(q, pool, ids, length, 0, 4))
+    got = run_attention(capi, pool, 0, 4, q[None], ids, [0], [length], kv_dtype=code)[0]
+    assert attn_close(got, oracle_attention(q, pool, ids, length, 0, 4), tol)
 
 
+@pytest.mark.parametrize("kv", ["f32", "f16"])
 @pytest.mark.parametrize("kv_heads", [1, 2, 4, 8])
-def test_attention_gqa_ratios(capi, kv_heads):
+def test_attention_gqa_ratios(capi, kv_heads, kv):
     """prefill_t172.cpp: query/KV head ratios 8/4/2/1."""
+    dtype, code, tol = KV_DTYPES[kv]
     rng = np.random.default_rng(kv_heads)
-    pool = Pool(2, kv_heads, 64, 16, 16, rng=rng)
+    pool = Pool(2, kv_heads, 64, 16, 16, dtype=dtype, rng=rng)
     ids = pool.sequence(67)
     q = rng.standard_normal(8 * 64).astype(np.float32)
     for layer in (0, 1):
-        got = run_attention(capi, pool, layer, 8, q[None], ids, [0], [67])[0]
-        assert attn_close(got, oracle_attention(q, pool, ids, 67, layer, 8))
+        got = run_attention(capi, pool, layer, 8, q[None], ids, [0], [67], kv_dtype=code)[0]
+        assert attn_close(got, oracle_attention(q, pool, ids, 67, layer, 8), tol)
+
+
+@pytest.mark.parametrize("scale", [1e-3, 1.0, 30.0])
+def test_attention_f16_tensor_core_scales_and_blocks(capi, scale):
+    """Tensor-core path across query magnitudes (the per-head power-of-two
+    scaling keeps tiny and large q exact), 32-slot blocks, head_dim 128, odd
+    GQA ratios (3, 6), many rows with split-KV."""
+    rng = np.random.default_rng(int(scale * 1000) + 5)
+    for heads, kv_heads, tpb in ((6, 2, 32), (9, 3, 16), (8, 1, 16)):
+        lens = [int(x) for x in rng.integers(1, 700, 12)] + [2049]
+        pool = Pool(1, kv_heads, 128, tpb, sum((n + tpb - 1) // tpb for n in lens) + 2, dtype=np.float16, rng=rng)
+        tables, offs = [], []
+        for n in lens:
+            offs.append(len(tables))
+            tables += pool.sequence(n, scale=0.7)
+        q = (scale * rng.standard_normal((len(lens), heads * 128))).astype(np.float32)
+        got = run_attention(capi, pool, 0, heads, q, tables, offs, lens, kv_dtype=1)
+        for i, n in enumerate(lens):
+            ref = oracle_attention(q[i], pool, tables[offs[i]:offs[i] + (n + tpb - 1) // tpb], n, 0, heads)
+            assert attn_close(got[i], ref, 5e-5), (heads, kv_heads, tpb, n)
 
 
 @pytest.mark.parametrize("kv", ["f32", "f16"])

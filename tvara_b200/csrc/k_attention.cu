@@ -16,8 +16,12 @@
 // of one token; long contexts are split over several items whose partial
 // (max, sum, weighted V) are merged by combine_kernel.
 #include <cfloat>
+#include <cstdint>
+#include <string>
+#include <type_traits>
 
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace tvara {
 namespace {
@@ -721,6 +725,286 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_xpose_kernel(AttnArgs
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core paged attention for F16 KV (head_dim 64 or 128, blocks of a
+// multiple of 16 slots).  CTA = (work item, KV head), four warps; each warp
+// streams its share of the blocks through a two-stage ring of TMA tensor
+// copies (one box per 64 elements of head_dim, 128-byte swizzle, so the
+// ldmatrix reads below are free of bank conflicts).  Per 16 positions a warp
+// computes S = Q K^T and O += P V with mma.m16n8k16 (F16 operands, F32
+// accumulation): the group's query heads are the M rows (G <= 8 of 16, the
+// other rows stay zero), positions the N dimension of S and the K dimension
+// of P V.  Q and P enter as exact hi + lo F16 pairs after a power-of-two
+// scaling (Q per head so that |q| < 2^15, P by 2^15), so every product keeps
+// about 22 significant bits: the F32 attention of the kernels above to
+// within rounding.
+constexpr int kMmaRing = 2;
+
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d += A b for one m16n8k16 tile whose A rows 8..15 are zero: a0 / a2 hold
+// row (lane / 4), columns 2(lane % 4) + {0, 1} and + {8, 9}.
+__device__ __forceinline__ void mma_rows8(float (&d)[4], unsigned a0, unsigned a2, unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+// x, y as packed F16 pairs hi + lo with hi + lo == (x, y) to ~22 bits.
+__device__ __forceinline__ void split_f16x2(float x, float y, unsigned& hi, unsigned& lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const unsigned*>(&h);
+    lo = *reinterpret_cast<const unsigned*>(&l);
+}
+// 2^e for |e| <= 126, exact.
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float(unsigned(127 + e) << 23); }
+
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                      AttnArgs a) {
+    constexpr int NB = D / 64;  // 128-byte boxes per slot row
+    constexpr int KS = D / 16;  // k-steps of S = Q K^T
+    constexpr int NT = D / 8;   // n-tiles of O
+    static_assert(D % 64 == 0 && KS % 2 == 0 && G >= 1 && G <= 8, "tensor-core attention shape");
+    extern __shared__ unsigned char att_raw[];
+    __shared__ std::uint64_t bars[kAttnWarps][kMmaRing];
+    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+    const int tpb = a.tpb;
+    const int box = tpb * 128;          // one box: tpb slots x 64 halves
+    const int half_stage = NB * box;    // K (or V) of one block
+    const int stage = 2 * half_stage;
+    unsigned char* smem = att_raw + ((1024u - (s_u32(att_raw) & 1023u)) & 1023u);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned char* ring = smem + std::size_t(warp) * kMmaRing * stage;
+    const unsigned ring_s = s_u32(ring);
+
+    const int4 wk = a.work[blockIdx.x];
+    const int part = a.work_part[blockIdx.x];
+    const int t = wk.x, toff = wk.y, p0 = wk.z, p1 = wk.w;
+    const int h = blockIdx.y;
+    const int b0 = p0 / tpb, b1 = (p1 - 1) / tpb;
+    const int nblk = b1 - b0 - warp >= 0 ? (b1 - b0 - warp) / kAttnWarps + 1 : 0;
+
+    if (lane == 0) {
+        for (int s = 0; s < kMmaRing; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[warp][s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    // tensor-map rows: [block][layer][K|V][kv head][slot] rows of D halves
+    const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
+    const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
+    auto issue = [&](int i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        int pb = a.tables[toff + bi];
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;
+        }
+        const int yk = int(pb * block_rows + head_row);
+        const int yv = int(yk + kind_rows);
+        const unsigned st = ring_s + unsigned((i % kMmaRing) * stage);
+        const unsigned bar = s_u32(&bars[warp][i % kMmaRing]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(stage) : "memory");
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            tma_load_2d(st + b * box, &kv_map, b * 64, yk, bar);
+            tma_load_2d(st + half_stage + b * box, &kv_map, b * 64, yv, bar);
+        }
+    };
+    if (lane == 0)
+        for (int i = 0; i < kMmaRing && i < nblk; ++i) issue(i);
+
+    // Q of head (lane / 4) as A fragments, scaled by 2^sh per head, hi + lo.
+    const int gq = lane >> 2, tq = lane & 3;
+    unsigned qh[KS][2], ql[KS][2];
+    float qinv;
+    {
+        const bool row = gq < G;
+        const float scale = rsqrtf(float(D));
+        const float* qp = a.q + (long long)t * a.hq * D + (h * G + (row ? gq : 0)) * D;
+        float v[KS][4];
+        float mx = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                v[kk][e] = row ? qp[16 * kk + 2 * tq + e] * scale : 0.f;
+                v[kk][2 + e] = row ? qp[16 * kk + 8 + 2 * tq + e] * scale : 0.f;
+                mx = fmaxf(mx, fmaxf(fabsf(v[kk][e]), fabsf(v[kk][2 + e])));
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        int e2 = 0;
+        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);  // mx < 2^e2
+        const int sh = max(-100, min(100, 15 - e2));
+        const float up = exp2i(sh);
+        qinv = exp2i(-sh);
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            split_f16x2(v[kk][0] * up, v[kk][1] * up, qh[kk][0], ql[kk][0]);
+            split_f16x2(v[kk][2] * up, v[kk][3] * up, qh[kk][1], ql[kk][1]);
+        }
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m = -INFINITY, l = 0.f;  // softmax state of head gq (shared by its four lanes)
+    const int lr = lane & 7, lm = lane >> 3;  // ldmatrix: row within an 8x8 matrix, matrix index
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        const unsigned parity = (i / kMmaRing) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[warp][i % kMmaRing], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const unsigned kst = ring_s + unsigned((i % kMmaRing) * stage);
+        const unsigned vst = kst + half_stage;
+        const int s_hi = min(tpb, p1 - bi * tpb);
+        if (s_hi % 16) {
+            // Slots past the visible end may hold anything (NaN included); P is
+            // zero there, but 0 * NaN is NaN, so clear those V rows.
+            unsigned char* vrows = ring + std::size_t(i % kMmaRing) * stage + half_stage;
+            const int rows = ((s_hi + 15) & ~15) - s_hi;
+            for (int idx = lane; idx < rows * NB * 8; idx += 32) {
+                const int r = s_hi + idx / (NB * 8), c = idx % (NB * 8);
+                *reinterpret_cast<uint4*>(vrows + (c >> 3) * box + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+        for (int sub = 0; sub < s_hi; sub += 16) {
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < KS; kk += 2) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int pos = sub + 8 * j + lr;
+                    const int c = 2 * kk + lm;
+                    unsigned f[4];
+                    ldsm_x4(kst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
+                    mma_rows8(s[j], qh[kk][0], qh[kk][1], f[0], f[1]);
+                    mma_rows8(s[j], ql[kk][0], ql[kk][1], f[0], f[1]);
+                    mma_rows8(s[j], qh[kk + 1][0], qh[kk + 1][1], f[2], f[3]);
+                    mma_rows8(s[j], ql[kk + 1][0], ql[kk + 1][1], f[2], f[3]);
+                }
+            }
+            float mloc = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    s[j][e] = sub + 8 * j + 2 * tq + e < s_hi ? s[j][e] * qinv : -INFINITY;
+                    mloc = fmaxf(mloc, s[j][e]);
+                }
+            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+            const float mn = fmaxf(m, mloc);
+            const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
+            m = mn;
+            float p[2][2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) p[j][e] = __expf(s[j][e] - mn);
+            l = fmaf(l, alpha, (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
+            if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    o[n][0] *= alpha;
+                    o[n][1] *= alpha;
+                }
+            }
+            unsigned ph0, pl0, ph2, pl2;
+            split_f16x2(p[0][0] * 32768.f, p[0][1] * 32768.f, ph0, pl0);
+            split_f16x2(p[1][0] * 32768.f, p[1][1] * 32768.f, ph2, pl2);
+#pragma unroll
+            for (int n = 0; n < NT; n += 2) {
+                const int pos = sub + lr + 8 * (lm & 1);
+                const int c = n + (lm >> 1);
+                unsigned f[4];
+                ldsm_x4_t(vst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
+                mma_rows8(o[n], ph0, ph2, f[0], f[1]);
+                mma_rows8(o[n], pl0, pl2, f[0], f[1]);
+                mma_rows8(o[n + 1], ph0, ph2, f[2], f[3]);
+                mma_rows8(o[n + 1], pl0, pl2, f[2], f[3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kMmaRing < nblk) issue(i + kMmaRing);
+    }
+    if (lane == 0 && failed) {
+        for (int i = 0; i < kMmaRing && i < nblk; ++i)
+            for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[warp][i], 0) && !bar_try(&bars[warp][i], 1);
+                 ++spin) {
+            }
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    __syncwarp();
+    // This warp's O (rows < G, scaled back by 2^-15) over its own first stage.
+    float* acc = reinterpret_cast<float*>(ring);
+    if (gq < G) {
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            acc[gq * D + 8 * n + 2 * tq] = o[n][0] * (1.f / 32768.f);
+            acc[gq * D + 8 * n + 2 * tq + 1] = o[n][1] * (1.f / 32768.f);
+        }
+        if (tq == 0) {
+            s_m[warp][gq] = m;
+            s_l[warp][gq] = l;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, e = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][g]);
+        float L = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (s_m[w][g] == -INFINITY) continue;
+            const float f = __expf(s_m[w][g] - M);
+            L = fmaf(s_l[w][g], f, L);
+            A = fmaf(reinterpret_cast<const float*>(smem + std::size_t(w) * kMmaRing * stage)[g * D + e], f, A);
+        }
+        const int head = h * G + g;
+        if (part < 0) {
+            a.out[(long long)t * a.hq * D + head * D + e] = A / L;
+        } else {
+            float* pp = a.partial + ((long long)part * a.hq + head) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+}
+
 // Merge split partials: out = sum_i A_i e^{M_i-M} / sum_i L_i e^{M_i-M}.
 __global__ void combine_kernel(AttnArgs a) {
     const int4 c = a.combine[blockIdx.x];
@@ -741,24 +1025,55 @@ __global__ void combine_kernel(AttnArgs a) {
     }
 }
 
+// The dynamic shared-memory limit is a per-device function attribute: set it
+// on every launch (a host-side call of about a microsecond).
 template <int D, typename KV, int G>
 void run_pipe(const AttnArgs& a, dim3 grid, int smem, cudaStream_t s) {
-    static int configured = 0;
-    if (smem > configured) {
-        TVARA_CUDA(cudaFuncSetAttribute(attn_pipe_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        configured = smem;
-    }
+    TVARA_CUDA(cudaFuncSetAttribute(attn_pipe_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attn_pipe_kernel<D, KV, G><<<grid, kAttnWarps * 32, smem, s>>>(a);
 }
 
 template <int D, typename KV, int G>
 void run_xpose(const AttnArgs& a, dim3 grid, int smem, cudaStream_t s) {
-    static int configured = 0;
-    if (smem > configured) {
-        TVARA_CUDA(cudaFuncSetAttribute(attn_xpose_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        configured = smem;
-    }
+    TVARA_CUDA(cudaFuncSetAttribute(attn_xpose_kernel<D, KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attn_xpose_kernel<D, KV, G><<<grid, kAttnWarps * 32, smem, s>>>(a);
+}
+
+// The F16 pool as a 2-D tensor of rows of D halves (one row = one slot of one
+// KV head of one layer of one block), read in boxes of 64 halves x tpb rows
+// with the 128-byte swizzle.
+CUtensorMap kv_map_f16(const AttnArgs& a, int D) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t((long long)a.max_blocks * (a.block_stride / D))};
+    const cuuint64_t strides[1] = {cuuint64_t(D) * 2};
+    const cuuint32_t box[2] = {64, cuuint32_t(a.tpb)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.kv), dims,
+                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+constexpr long long mma_smem_bytes(int D, int tpb) {
+    return 1024 + (long long)kAttnWarps * kMmaRing * 2 * (D / 64) * tpb * 128;
+}
+
+// Whether the tensor-core kernel takes these arguments: F16 pool, head_dim 64
+// or 128, blocks of a multiple of 16 slots, rows addressable by the map.
+bool mma_ok(const AttnArgs& a) {
+    if (!a.kv_f16 || (a.dim != 64 && a.dim != 128) || a.tpb % 16 || a.tpb > 256) return false;
+    if (reinterpret_cast<std::uintptr_t>(a.kv) % 16 || mma_smem_bytes(a.dim, a.tpb) > 200 * 1024) return false;
+    return (long long)a.max_blocks * (a.block_stride / a.dim) < (1ll << 31);
+}
+
+template <int D, int G>
+void run_mma(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+    const int smem = int(mma_smem_bytes(D, a.tpb));
+    TVARA_CUDA(cudaFuncSetAttribute(attn_mma_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const CUtensorMap map = kv_map_f16(a, D);
+    attn_mma_kernel<D, G><<<grid, kAttnWarps * 32, smem, s>>>(map, a);
 }
 
 template <int D, typename KV, int G>
@@ -776,10 +1091,14 @@ void run_g(const AttnArgs& a, cudaStream_t s) {
     const long long chunk = (long long)a.tpb * D * sizeof(KV);
     const long long smem = 128 + (long long)kAttnWarps * kRing * 2 * chunk;
     const bool pipe = smem <= 110 * 1024;
+    constexpr bool kMmaShape = std::is_same_v<KV, __half> && (D == 64 || D == 128);
+    const bool mma = kMmaShape && mma_ok(a);
     switch (g) {
 #define TV_G(N)                                                                  \
     case N:                                                                      \
-        if (pipe && xpose_ok<D, KV, N>()) {                                      \
+        if (mma) {                                                               \
+            if constexpr (kMmaShape) run_mma<D, N>(a, grid, s);                  \
+        } else if (pipe && xpose_ok<D, KV, N>()) {                               \
             if constexpr (xpose_ok<D, KV, N>()) run_xpose<D, KV, N>(a, grid, int(smem), s); \
         } else if (pipe) {                                                       \
             run_pipe<D, KV, N>(a, grid, int(smem), s);                           \

@@ -22,12 +22,10 @@
 // per-CTA TMA loads of this GPU's own memory.  Every mbarrier wait is bounded: on timeout the kernel
 // records an error code, waits (bounded) for its own TMA copies, frees TMEM
 // and exits.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <mutex>
 
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace tvara {
 namespace {
@@ -108,13 +106,6 @@ __device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, std::uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // Byte offset of 16-byte chunk c (0..3) of row r in a [rows][64 B] tile with
 // the 64-byte swizzle (chunk index XOR bits 1-2 of the row).
@@ -343,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char* st = stages + s * stage_bytes;
             if (threadIdx.x == 0) {
                 mbar_expect_tx(&full_b[s], 2 * b_bytes);
-                tma_load_2d(st + 2 * kATile, &map_hi, k0, tok0, &full_b[s]);
-                tma_load_2d(st + 2 * kATile + kBTileMax, &map_lo, k0, tok0, &full_b[s]);
+                tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, smem_u32(&full_b[s]));
+                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, smem_u32(&full_b[s]));
                 last_ph[s] = int(ph);
             }
             unsigned char* ahi = st;
@@ -479,27 +470,13 @@ __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half*
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
-    return fn;
-}
-
 CUtensorMap make_map(const __half* base, int K, int T, int n_tile) {
     CUtensorMap m;
     const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(T)};
     const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
     const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(n_tile)};
     const cuuint32_t elem[2] = {1, 1};
-    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
                                    box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
