@@ -731,13 +731,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_xpose_kernel(AttnArgs
 // streams its share of the blocks through a two-stage ring of TMA tensor
 // copies (one box per 64 elements of head_dim, 128-byte swizzle, so the
 // ldmatrix reads below are free of bank conflicts).  Per 16 positions a warp
-// computes S = Q K^T and O += P V with mma.m16n8k16 (F16 operands, F32
-// accumulation): the group's query heads are the M rows (G <= 8 of 16, the
-// other rows stay zero), positions the N dimension of S and the K dimension
-// of P V.  Q and P enter as exact hi + lo F16 pairs after a power-of-two
-// scaling (Q per head so that |q| < 2^15, P by 2^15), so every product keeps
-// about 22 significant bits: the F32 attention of the kernels above to
-// within rounding.
+// computes, with mma.m16n8k16 (F16 operands, F32 accumulation),
+//   S^T [16 positions x 8 heads] = K [16 x D] . Q^T [D x 8]   and
+//   O^T [D x 8 heads]           += V^T [D x 16] . P^T [16 x 8],
+// the group's G <= 8 query heads being the N columns; P^T reaches the B
+// operand layout by an in-register transpose (movmatrix) of the score tile.
+// Q and P enter as exact hi + lo F16 pairs after a power-of-two scaling (Q
+// per head so that |q| < 2^15, P by 2^15), so every product keeps about 22
+// significant bits: the F32 attention of the kernels above to within
+// rounding.
 constexpr int kMmaRing = 2;
 
 __device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&r)[4]) {
@@ -750,14 +752,19 @@ __device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned (&r)[4]) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
 }
-// d += A b for one m16n8k16 tile whose A rows 8..15 are zero: a0 / a2 hold
-// row (lane / 4), columns 2(lane % 4) + {0, 1} and + {8, 9}.
-__device__ __forceinline__ void mma_rows8(float (&d)[4], unsigned a0, unsigned a2, unsigned b0, unsigned b1) {
+// d += A b for one m16n8k16 tile (A row-major 16x16, b col-major 16x8).
+__device__ __forceinline__ void mma16816(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Transpose of an 8x8 matrix of 16-bit values held one pair per lane.
+__device__ __forceinline__ unsigned movmatrix_t(unsigned x) {
+    unsigned y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 // x, y as packed F16 pairs hi + lo with hi + lo == (x, y) to ~22 bits.
 __device__ __forceinline__ void split_f16x2(float x, float y, unsigned& hi, unsigned& lo) {
@@ -771,15 +778,14 @@ __device__ __forceinline__ void split_f16x2(float x, float y, unsigned& hi, unsi
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float(unsigned(127 + e) << 23); }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map,
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map,
                                                                       AttnArgs a) {
     constexpr int NB = D / 64;  // 128-byte boxes per slot row
-    constexpr int KS = D / 16;  // k-steps of S = Q K^T
-    constexpr int NT = D / 8;   // n-tiles of O
-    static_assert(D % 64 == 0 && KS % 2 == 0 && G >= 1 && G <= 8, "tensor-core attention shape");
+    constexpr int KS = D / 16;  // k-steps of S^T, and m-tiles of O^T
+    static_assert(D % 64 == 0 && G >= 1 && G <= 8, "tensor-core attention shape");
     extern __shared__ unsigned char att_raw[];
     __shared__ std::uint64_t bars[kAttnWarps][kMmaRing];
-    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+    __shared__ float s_m[kAttnWarps][8], s_l[kAttnWarps][8];
     const int tpb = a.tpb;
     const int box = tpb * 128;          // one box: tpb slots x 64 halves
     const int half_stage = NB * box;    // K (or V) of one block
@@ -827,10 +833,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __gr
     if (lane == 0)
         for (int i = 0; i < kMmaRing && i < nblk; ++i) issue(i);
 
-    // Q of head (lane / 4) as A fragments, scaled by 2^sh per head, hi + lo.
     const int gq = lane >> 2, tq = lane & 3;
+    // Q^T as B fragments: lane holds head gq, d 16kk + 2tq + {0, 1} (+8);
+    // scaled by 2^sh per head, hi + lo.
     unsigned qh[KS][2], ql[KS][2];
-    float qinv;
+    float qinv0, qinv1;  // 2^-sh of heads 2tq and 2tq + 1 (this lane's S columns)
     {
         const bool row = gq < G;
         const float scale = rsqrtf(float(D));
@@ -851,7 +858,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __gr
         if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);  // mx < 2^e2
         const int sh = max(-100, min(100, 15 - e2));
         const float up = exp2i(sh);
-        qinv = exp2i(-sh);
+        const float inv = exp2i(-sh);
+        qinv0 = __shfl_sync(0xffffffffu, inv, (2 * tq) * 4);
+        qinv1 = __shfl_sync(0xffffffffu, inv, (2 * tq + 1) * 4);
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
             split_f16x2(v[kk][0] * up, v[kk][1] * up, qh[kk][0], ql[kk][0]);
@@ -859,10 +868,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __gr
         }
     }
 
-    float o[NT][4];
+    float o[KS][4];  // O^T: d 16mt + gq (+8), heads 2tq, 2tq + 1
 #pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m = -INFINITY, l = 0.f;  // softmax state of head gq (shared by its four lanes)
+    for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2tq, 2tq + 1
     const int lr = lane & 7, lm = lane >> 3;  // ldmatrix: row within an 8x8 matrix, matrix index
     bool failed = false;
     for (int i = 0; i < nblk; ++i) {
@@ -896,60 +905,61 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __gr
             __syncwarp();
         }
         for (int sub = 0; sub < s_hi; sub += 16) {
-            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            // S^T: rows = positions sub + gq (+8), columns = heads 2tq, 2tq + 1
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int kk = 0; kk < KS; kk += 2) {
+            for (int kk = 0; kk < KS; ++kk) {
+                const int pos = sub + 8 * (lm & 1) + lr;
+                const int c = 2 * kk + (lm >> 1);
+                unsigned f[4];
+                ldsm_x4(kst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
+                mma16816(s, f, qh[kk][0], qh[kk][1]);
+                mma16816(s, f, ql[kk][0], ql[kk][1]);
+            }
+            const bool va = sub + gq < s_hi, vb = sub + gq + 8 < s_hi;
+            s[0] = va ? s[0] * qinv0 : -INFINITY;
+            s[1] = va ? s[1] * qinv1 : -INFINITY;
+            s[2] = vb ? s[2] * qinv0 : -INFINITY;
+            s[3] = vb ? s[3] * qinv1 : -INFINITY;
+            float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int pos = sub + 8 * j + lr;
-                    const int c = 2 * kk + lm;
-                    unsigned f[4];
-                    ldsm_x4(kst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
-                    mma_rows8(s[j], qh[kk][0], qh[kk][1], f[0], f[1]);
-                    mma_rows8(s[j], ql[kk][0], ql[kk][1], f[0], f[1]);
-                    mma_rows8(s[j], qh[kk + 1][0], qh[kk + 1][1], f[2], f[3]);
-                    mma_rows8(s[j], ql[kk + 1][0], ql[kk + 1][1], f[2], f[3]);
+            for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+            }
+            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+            const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
+            const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
+            m0 = n0;
+            m1 = n1;
+            const float pa0 = __expf(s[0] - n0), pa1 = __expf(s[1] - n1);
+            const float pb0 = __expf(s[2] - n0), pb1 = __expf(s[3] - n1);
+            l0 = fmaf(l0, al0, pa0 + pb0);
+            l1 = fmaf(l1, al1, pa1 + pb1);
+            if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    o[mt][0] *= al0;
+                    o[mt][1] *= al1;
+                    o[mt][2] *= al0;
+                    o[mt][3] *= al1;
                 }
             }
-            float mloc = -INFINITY;
+            // P^T (x 2^15) as the B operand: transpose the two 8x8 score tiles
+            unsigned ha, la, hb, lb;
+            split_f16x2(pa0 * 32768.f, pa1 * 32768.f, ha, la);
+            split_f16x2(pb0 * 32768.f, pb1 * 32768.f, hb, lb);
+            const unsigned bh0 = movmatrix_t(ha), bh1 = movmatrix_t(hb);
+            const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    s[j][e] = sub + 8 * j + 2 * tq + e < s_hi ? s[j][e] * qinv : -INFINITY;
-                    mloc = fmaxf(mloc, s[j][e]);
-                }
-            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-            const float mn = fmaxf(m, mloc);
-            const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-            m = mn;
-            float p[2][2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) p[j][e] = __expf(s[j][e] - mn);
-            l = fmaf(l, alpha, (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
-            if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-                for (int n = 0; n < NT; ++n) {
-                    o[n][0] *= alpha;
-                    o[n][1] *= alpha;
-                }
-            }
-            unsigned ph0, pl0, ph2, pl2;
-            split_f16x2(p[0][0] * 32768.f, p[0][1] * 32768.f, ph0, pl0);
-            split_f16x2(p[1][0] * 32768.f, p[1][1] * 32768.f, ph2, pl2);
-#pragma unroll
-            for (int n = 0; n < NT; n += 2) {
-                const int pos = sub + lr + 8 * (lm & 1);
-                const int c = n + (lm >> 1);
+            for (int mt = 0; mt < KS; ++mt) {
+                // V^T tile [d 16mt.., positions sub..]: matrices (pos +0/+8) x (d +0/+8)
+                const int pos = sub + 8 * (lm >> 1) + lr;
+                const int c = 2 * mt + (lm & 1);
                 unsigned f[4];
                 ldsm_x4_t(vst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
-                mma_rows8(o[n], ph0, ph2, f[0], f[1]);
-                mma_rows8(o[n], pl0, pl2, f[0], f[1]);
-                mma_rows8(o[n + 1], ph0, ph2, f[2], f[3]);
-                mma_rows8(o[n + 1], pl0, pl2, f[2], f[3]);
+                mma16816(o[mt], f, bh0, bh1);
+                mma16816(o[mt], f, bl0, bl1);
             }
         }
         __syncwarp();
@@ -961,21 +971,31 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_mma_kernel(const __gr
                  ++spin) {
             }
     }
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    __syncwarp();
-    // This warp's O (rows < G, scaled back by 2^-15) over its own first stage.
-    float* acc = reinterpret_cast<float*>(ring);
-    if (gq < G) {
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            acc[gq * D + 8 * n + 2 * tq] = o[n][0] * (1.f / 32768.f);
-            acc[gq * D + 8 * n + 2 * tq + 1] = o[n][1] * (1.f / 32768.f);
+    for (int o2 = 4; o2 < 32; o2 <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
+    }
+    __syncwarp();
+    // This warp's O (heads < G, scaled back by 2^-15) over its own first stage.
+    float* acc = reinterpret_cast<float*>(ring);
+    const int ha = 2 * tq, hb = 2 * tq + 1;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+        if (ha < G) {
+            acc[ha * D + 16 * mt + gq] = o[mt][0] * (1.f / 32768.f);
+            acc[ha * D + 16 * mt + gq + 8] = o[mt][2] * (1.f / 32768.f);
         }
-        if (tq == 0) {
-            s_m[warp][gq] = m;
-            s_l[warp][gq] = l;
+        if (hb < G) {
+            acc[hb * D + 16 * mt + gq] = o[mt][1] * (1.f / 32768.f);
+            acc[hb * D + 16 * mt + gq + 8] = o[mt][3] * (1.f / 32768.f);
         }
+    }
+    if (gq == 0) {
+        s_m[warp][ha] = m0;
+        s_l[warp][ha] = l0;
+        s_m[warp][hb] = m1;
+        s_l[warp][hb] = l1;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
