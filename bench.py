@@ -283,6 +283,7 @@ def run_ours(args):
     blocks = int(np.sum((args.prefix + unique + tpb - 1) // tpb - args.prefix // tpb)) + args.prefix // tpb + 64
     model = NativeModel(path, max_blocks=blocks, block_tokens=tpb, kv_dtype=args.kv, device=local,
                         max_step_tokens=max(2048, args.prefix), tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    wbytes = model.weight_bytes()
     fill_pool_random(model, args.seed + 2 + rank)
     seq0 = model._new_sequence()
     model.batch_step([seq0], [prefix.tolist()], logits=False)  # real prefill of the shared prefix
@@ -398,6 +399,8 @@ def run_ours(args):
                    "model": args.config + (f" ({args.layers} layers)" if args.layers else ""),
                    "global_batch": args.requests, "seq_len": float(np.mean(lens0)),
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,
+                   "weights_gb": {"packed": round(wbytes["packed"] / 1e9, 2),
+                                  "fp16_planes": round(wbytes["planes"] / 1e9, 2)},
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d.value) + caller_h2d,
                 "d2h_bytes_per_step": int(d2h.value),

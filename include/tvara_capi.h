@@ -77,9 +77,14 @@ typedef struct tvara_open_options {
     uint32_t tp_rank;          /* tensor-parallel rank of this handle */
     uint32_t tp_size;          /* tensor-parallel group size; 0 or 1 = no TP */
     const void* nccl_id;       /* 128-byte ncclUniqueId shared by the group (tp_size > 1) */
+    uint32_t weight_planes;    /* exact FP16 hi/lo copies of the projections for batches of >= 5
+                                  tokens (4 bytes per weight, like the reference's F32 expansion):
+                                  0 = when they fit beside the KV pool, 1 = always, 2 = never.
+                                  Callers built against the shorter struct get 0. */
 } tvara_open_options;
 
-/* tvara_model_open with options; NULL options equal tvara_model_open. */
+/* tvara_model_open with options; NULL options equal tvara_model_open.
+ * struct_size may be that of an earlier, shorter version of the struct. */
 TVARA_API tvara_model* tvara_model_open_ex(const char* utf8_path, size_t max_blocks, size_t block_tokens,
                                            const tvara_open_options* options);
 
@@ -98,6 +103,10 @@ typedef struct tvara_tp_shard_info {
     uint32_t ffn_begin, ffn;
 } tvara_tp_shard_info;
 TVARA_API int tvara_tp_shard(const char* utf8_path, uint32_t tp_rank, uint32_t tp_size, tvara_tp_shard_info* out);
+
+/* Device bytes of the packed weights and of the FP16 weight planes (0 when
+ * not built).  0 / -1. */
+TVARA_API int tvara_model_weight_bytes(tvara_model* model, size_t* packed, size_t* planes);
 
 /* ---- additive: ragged multi-sequence step ----------------------------- */
 

@@ -230,3 +230,28 @@ def test_small_step_budget_splits_long_prefill(tiny_path):
         s = m._new_sequence()
         got = m.decode_batch(s, toks)
     assert close(got, g["logits"])
+
+
+@pytest.mark.parametrize("name", ["tiny", "mixed"])
+def test_weight_planes_match_packed_path(tiny_path, model_dir, name):
+    """Tensor-core batches read exact FP16 hi/lo planes when they are built and
+    dequantise the packed rows otherwise: both stay within tolerance of the
+    reference, and of each other to F32 rounding."""
+    if name == "tiny":
+        path, golden = tiny_path, np.load(GOLDEN / "tiny_q8.npz")
+        toks = np.concatenate([golden["prompt"], golden["greedy"]]).tolist()
+        want = golden["logits"]
+    else:
+        from tests.golden.make_golden import MIXED
+        golden = np.load(GOLDEN / "tiny_mixed.npz")
+        path = make_model(model_dir, "mixed", gguf.model_config("tiny", **MIXED), seed=3)
+        toks, want = [int(t) for t in golden["tokens"]], golden["logits"]
+    got = {}
+    for planes in ("on", "off"):
+        with NativeModel(path, max_blocks=64, block_tokens=16, weight_planes=planes) as m:
+            sizes = m.weight_bytes()
+            assert (sizes["planes"] > 0) == (planes == "on") and sizes["packed"] > 0
+            s = m._new_sequence()
+            got[planes] = m.decode_batch(s, toks)
+        assert close(got[planes], want), (planes, np.abs(got[planes] - want).max())
+    assert np.abs(got["on"] - got["off"]).max() <= 1e-4

@@ -24,6 +24,7 @@ class OpenOptions(C.Structure):
         ("tp_rank", C.c_uint32),
         ("tp_size", C.c_uint32),
         ("nccl_id", C.c_void_p),
+        ("weight_planes", C.c_uint32),
     ]
 
 
@@ -49,6 +50,7 @@ SIGNATURES = {
     "tvara_sequence_truncate": (C.c_int, [P, U64, SZ]),
     # additive
     "tvara_model_open_ex": (P, [C.c_char_p, SZ, SZ, C.POINTER(OpenOptions)]),
+    "tvara_model_weight_bytes": (C.c_int, [P, SZP, SZP]),
     "tvara_tp_shard": (C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.POINTER(TpShardInfo)]),
     "tvara_batch_step": (C.c_int, [P, SZ, U64P, U32P, U32P, C.c_uint32, F32P, SZ, U32P, SZ]),
     "tvara_sequence_fork": (U64, [P, U64]),

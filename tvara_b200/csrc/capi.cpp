@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstddef>
 #include <cstring>
 #include <limits>
 #include <memory>
@@ -69,7 +70,9 @@ tvara_model* open_model(const char* path, size_t blocks, size_t tokens, const tv
     if (!path || !*path) throw std::invalid_argument("empty model path");
     tvara::EngineOptions opt;
     if (o) {
-        if (o->struct_size < sizeof(tvara_open_options)) throw std::invalid_argument("invalid open options size");
+        // the struct grows at its end; weight_planes is the first optional member
+        if (o->struct_size < offsetof(tvara_open_options, weight_planes))
+            throw std::invalid_argument("invalid open options size");
         opt.device = o->device;
         if (o->kv_dtype > TVARA_KV_F16) throw std::invalid_argument("invalid KV dtype");
         opt.kv_f16 = o->kv_dtype == TVARA_KV_F16;
@@ -79,6 +82,10 @@ tvara_model* open_model(const char* path, size_t blocks, size_t tokens, const tv
         if (o->nccl_id) {
             std::memcpy(opt.nccl_id.data(), o->nccl_id, opt.nccl_id.size());
             opt.has_nccl_id = true;
+        }
+        if (o->struct_size >= offsetof(tvara_open_options, weight_planes) + sizeof(uint32_t)) {
+            if (o->weight_planes > 2) throw std::invalid_argument("invalid weight planes option");
+            opt.weight_planes = int(o->weight_planes);
         }
     }
     auto m = std::make_unique<tvara_model>();
@@ -96,6 +103,15 @@ tvara_model* tvara_model_open(const char* path, size_t max_blocks, size_t block_
 tvara_model* tvara_model_open_ex(const char* path, size_t max_blocks, size_t block_tokens,
                                  const tvara_open_options* options) {
     return guarded<tvara_model*>(nullptr, [&] { return open_model(path, max_blocks, block_tokens, options); });
+}
+
+int tvara_model_weight_bytes(tvara_model* model, size_t* packed, size_t* planes) {
+    return guarded<int>(-1, [&] {
+        if (!model || !model->engine) throw std::invalid_argument("closed model");
+        if (packed) *packed = model->engine->weight_bytes();
+        if (planes) *planes = model->engine->plane_bytes();
+        return 0;
+    });
 }
 
 int tvara_tp_shard(const char* path, uint32_t tp_rank, uint32_t tp_size, tvara_tp_shard_info* out) {

@@ -40,6 +40,11 @@ struct DeviceMatrix {
     // |value| into [2^14, 2^15): the tensor-core path scales by it before the
     // exact hi+lo FP16 split.  Null until computed (then only GEMV is used).
     const signed char* row_shift = nullptr;
+    // Optional exact FP16 planes of the scaled values (value * 2^row_shift =
+    // hi + lo), [rows][cols] each: the tensor-core path then streams them by
+    // TMA instead of dequantising the packed rows.  Null when not built.
+    const std::uint16_t* plane_hi = nullptr;
+    const std::uint16_t* plane_lo = nullptr;
 };
 
 inline std::size_t qs_row_bytes(int type, std::size_t cols) {

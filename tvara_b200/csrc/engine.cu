@@ -103,7 +103,9 @@ Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t bloc
         load(f);
     } catch (...) {
         if (weights_) cudaFree(weights_);
+        if (planes_) cudaFree(planes_);
         weights_ = nullptr;
+        planes_ = nullptr;
         cudaStreamDestroy(stream_);
         throw;
     }
@@ -114,7 +116,7 @@ Engine::~Engine() {
     for (auto e : events_) cudaEventDestroy(e);
     radix_.reset();
     coll_.reset();
-    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
+    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
                     static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_})
         if (p) cudaFree(p);
     if (meta_host_) cudaFreeHost(meta_host_);
@@ -248,6 +250,45 @@ void Engine::load(const gguf::File& f) {
     }
     cudaFree(staging_dev);
     cudaFree(flag);
+
+    // ---- exact FP16 hi/lo planes of the projections for the tensor-core
+    // path (4 bytes per weight, the footprint of the reference's own F32
+    // expansion); batches of <= 4 tokens keep streaming the packed rows.
+    if (opt_.weight_planes != 2) {
+        std::vector<DeviceMatrix*> mats;
+        for (auto& L : lw_) {
+            for (auto& m : L.qkv) mats.push_back(&m);
+            mats.push_back(&L.o);
+            for (auto& m : L.gateup) mats.push_back(&m);
+            mats.push_back(&L.down);
+        }
+        mats.push_back(&head_);
+        std::size_t need = 0;
+        for (auto* m : mats)
+            if (m->cols % 32 == 0) need += std::size_t(m->rows) * m->cols * 4;
+        const std::size_t es = opt_.kv_f16 ? 2 : 4;
+        const std::size_t pool = std::size_t(layers_) * 2 * hkv_ * book_->geometry().tokens_per_block * d * es *
+                                 book_->geometry().max_blocks;
+        std::size_t free_b = 0, total_b = 0;
+        TVARA_CUDA(cudaMemGetInfo(&free_b, &total_b));
+        const std::size_t reserve = std::size_t(4) << 30;  // scratch, workspaces, other users
+        const bool fits = need + pool + reserve <= free_b;
+        if (opt_.weight_planes == 1 && !fits) throw std::runtime_error("weight planes do not fit in device memory");
+        if (fits && need) {
+            TVARA_CUDA(cudaMalloc(&planes_, need));
+            plane_bytes_ = need;
+            std::uint16_t* at = planes_;
+            for (auto* m : mats) {
+                if (m->cols % 32) continue;
+                const std::size_t n = std::size_t(m->rows) * m->cols;
+                launch_planes(*m, at, at + n, stream_);
+                m->plane_hi = at;
+                m->plane_lo = at + n;
+                at += 2 * n;
+            }
+            TVARA_CUDA(cudaStreamSynchronize(stream_));
+        }
+    }
 
     // ---- RoPE table with the reference's float expression (model.hpp:71-72)
     const std::size_t half = d / 2;

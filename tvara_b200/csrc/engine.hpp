@@ -26,6 +26,9 @@ struct EngineOptions {
     int tp_rank = 0, tp_size = 1;
     bool has_nccl_id = false;
     std::array<char, 128> nccl_id{};
+    // Exact FP16 hi/lo planes of the projections for the tensor-core path:
+    // 0 = when they fit beside the KV pool, 1 = always, 2 = never.
+    int weight_planes = 0;
 };
 
 class Collective;  // NCCL communicator of a tensor-parallel group (collective.cpp)
@@ -64,6 +67,10 @@ public:
     void* kv_pool() const { return kv_; }
     long long block_elements() const { return block_stride_; }
     int local_kv_heads() const { return hkv_; }
+
+    // Device bytes of the packed weights and of the FP16 planes (0 if none).
+    std::size_t weight_bytes() const { return weight_bytes_; }
+    std::size_t plane_bytes() const { return plane_bytes_; }
 
     int device() const { return device_; }
     cudaStream_t stream() const { return stream_; }
@@ -119,6 +126,8 @@ private:
     // device memory
     std::uint8_t* weights_ = nullptr;
     std::size_t weight_bytes_ = 0;
+    std::uint16_t* planes_ = nullptr;  // FP16 hi/lo planes of the projections (optional)
+    std::size_t plane_bytes_ = 0;
     DeviceMatrix embed_, head_;
     const float* final_norm_ = nullptr;
     std::vector<LayerWeights> lw_;

@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "kernels.cuh"
+#include "split.cuh"
 #include "tma.cuh"
 
 namespace tvara {
@@ -41,6 +42,7 @@ constexpr int kThreads = kProducers + 32;
 constexpr unsigned kSpinLimit = 1u << 26;
 constexpr int kATile = kBM * kBK * 2;      // 8 KB per hi/lo A tile
 constexpr int kBTileMax = kMaxN * kBK * 2; // 16 KB per hi/lo B tile
+constexpr int kPlanes = -1;                // template TYPE: A from prebuilt FP16 planes by TMA
 
 struct TcArgs {
     DeviceMatrix w;
@@ -76,13 +78,15 @@ __device__ __forceinline__ bool mbar_try(std::uint64_t* bar, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; false after the limit (or when another role gave up).
+// Bounded wait; false after the limit (or when another role gave up).  The
+// single MMA-issuing thread polls without sleeping (try_wait itself suspends
+// the thread for a while), the producer warps back off after a while.
 __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err,
-                                          int code) {
+                                          int code, bool backoff = true) {
     for (unsigned i = 0; i < kSpinLimit; ++i) {
         if (mbar_try(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (i > 64) __nanosleep(64);
+        if (backoff && i > 64) __nanosleep(64);
     }
     *abort_flag = 1;
     atomicExch(err, code);
@@ -113,6 +117,7 @@ __device__ __forceinline__ int sw64(int r, int c) { return r * 64 + ((c ^ ((r >>
 
 // 2^e as a float for |e| <= 126 (exact; used to apply the power-of-two scales).
 __device__ __forceinline__ float pow2(int e) { return __uint_as_float(unsigned(127 + e) << 23); }
+
 
 // ---------------------------------------------------------------- producer
 // Packed weights of one row for HALF of a 32-element K-step (hf = 0 or 1),
@@ -197,8 +202,11 @@ __device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale,
         if constexpr (TYPE == kQ4_K) {
             const float d = h2f((unsigned short)(r.m.x & 0xffff)), dmin = h2f((unsigned short)(r.m.x >> 16));
             const int g = (k0 / 32) % 8;
-            const unsigned sw[3] = {r.m.y, r.m.z, r.m.w};
-            auto sbyte = [&](int j) { return (sw[j >> 2] >> (8 * (j & 3))) & 255u; };
+            // byte j (0..11) of the packed scales, selected without an indexed array
+            auto sbyte = [&](int j) {
+                const unsigned word = j < 4 ? r.m.y : j < 8 ? r.m.z : r.m.w;
+                return (word >> (8 * (j & 3))) & 255u;
+            };
             unsigned sc, mn;
             if (g < 4) {
                 sc = sbyte(g) & 63u;
@@ -263,7 +271,8 @@ __device__ __forceinline__ float swiglu(float g, float up) {
 
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo, TcArgs a) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                   const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo, TcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned carve-up: per stage A_hi, A_lo (8 KB each), B_hi, B_lo
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
@@ -278,8 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = blockIdx.x * kBM;
-    const int tok0 = blockIdx.y * a.n_tile;
+    // token tiles of one row tile are neighbours in launch order (they share
+    // the weight rows in L2)
+    const int row0 = blockIdx.y * kBM;
+    const int tok0 = blockIdx.x * a.n_tile;
     const int kstep0 = blockIdx.z * a.k_steps;
     const unsigned tmem_cols = a.n_tile <= 32 ? 32 : a.n_tile <= 64 ? 64 : a.n_tile <= 128 ? 128 : 256;
 
@@ -312,54 +323,80 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool live = row < a.w.rows;
         const int shift = live ? a.w.row_shift[row] : 0;
         const float scale = pow2(shift);
-        int last_ph[kStages];  // phase of the last TMA this thread issued per stage, -1 none
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) last_ph[s] = -1;
-        constexpr int P = Ring<TYPE>::kDepth;
-        Raw<TYPE> ring[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j)
-            ring[j] = fetch<TYPE>(a.w, row, (kstep0 + j) * kBK, hf, live && j < a.k_steps);
-        for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
-            const int s = ks % kStages;
-            const unsigned ph = (ks / kStages) & 1;
-            const int k0 = (kstep0 + ks) * kBK;
-            const Raw<TYPE> cur = ring[0];
-#pragma unroll
-            for (int j = 0; j + 1 < P; ++j) ring[j] = ring[j + 1];
-            ring[P - 1] = fetch<TYPE>(a.w, row, k0 + P * kBK, hf, live && ks + P < a.k_steps);
-            float v[16];
-            convert<TYPE>(cur, k0, scale, v);
-            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
-            unsigned char* st = stages + s * stage_bytes;
+        // per stage: whether this thread issued a TMA there, and its phase
+        unsigned tma_issued = 0, tma_phase = 0;
+        if constexpr (TYPE == kPlanes) {
+            // A and B tiles both arrive by TMA, issued by one thread
             if (threadIdx.x == 0) {
-                mbar_expect_tx(&full_b[s], 2 * b_bytes);
-                tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, smem_u32(&full_b[s]));
-                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, smem_u32(&full_b[s]));
-                last_ph[s] = int(ph);
-            }
-            unsigned char* ahi = st;
-            unsigned char* alo = st + kATile;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint4 hi, lo;
-                unsigned* hp = reinterpret_cast<unsigned*>(&hi);
-                unsigned* lp = reinterpret_cast<unsigned*>(&lo);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float x0 = v[c * 8 + 2 * j], x1 = v[c * 8 + 2 * j + 1];
-                    const __half2 h = __floats2half2_rn(x0, x1);
-                    const float2 hf2 = __half22float2(h);
-                    const __half2 l = __floats2half2_rn(x0 - hf2.x, x1 - hf2.y);
-                    hp[j] = *reinterpret_cast<const unsigned*>(&h);
-                    lp[j] = *reinterpret_cast<const unsigned*>(&l);
+                for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
+                    const int s = ks % kStages;
+                    const unsigned ph = (ks / kStages) & 1;
+                    const int k0 = (kstep0 + ks) * kBK;
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
+                    unsigned char* st = stages + s * stage_bytes;
+                    const unsigned bar = smem_u32(&full_b[s]);
+                    mbar_expect_tx(&full_b[s], 2 * kATile + 2 * b_bytes);
+                    tma_load_2d(smem_u32(st), &map_ahi, k0, row0, bar);
+                    tma_load_2d(smem_u32(st + kATile), &map_alo, k0, row0, bar);
+                    tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, bar);
+                    tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, bar);
+                    tma_issued |= 1u << s;
+                    tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
                 }
-                const int chunk = c == 0 ? chunk_a<TYPE>(hf) : chunk_b<TYPE>(hf);
-                *reinterpret_cast<uint4*>(ahi + sw64(r, chunk)) = hi;
-                *reinterpret_cast<uint4*>(alo + sw64(r, chunk)) = lo;
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&full_a[s]);
+        } else {
+            constexpr int P = Ring<TYPE>::kDepth;
+            Raw<TYPE> ring[P];
+    #pragma unroll
+            for (int j = 0; j < P; ++j)
+                ring[j] = fetch<TYPE>(a.w, row, (kstep0 + j) * kBK, hf, live && j < a.k_steps);
+            // The K loop is unrolled by the ring depth so every ring slot is a
+            // fixed register set (no shifting).
+            bool stop = false;
+            for (int ks0 = 0; ks0 < a.k_steps && !stop; ks0 += P) {
+    #pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    const int ks = ks0 + j;
+                    if (ks >= a.k_steps || *abort_flag) {
+                        stop = true;
+                        break;
+                    }
+                    const int s = ks % kStages;
+                    const unsigned ph = (ks / kStages) & 1;
+                    const int k0 = (kstep0 + ks) * kBK;
+                    const Raw<TYPE> cur = ring[j];
+                    ring[j] = fetch<TYPE>(a.w, row, k0 + P * kBK, hf, live && ks + P < a.k_steps);
+                    float v[16];
+                    convert<TYPE>(cur, k0, scale, v);
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) {
+                        stop = true;
+                        break;
+                    }
+                    unsigned char* st = stages + s * stage_bytes;
+                    if (threadIdx.x == 0) {
+                        mbar_expect_tx(&full_b[s], 2 * b_bytes);
+                        tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, smem_u32(&full_b[s]));
+                        tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, smem_u32(&full_b[s]));
+                        tma_issued |= 1u << s;
+                        tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                    }
+                    unsigned char* ahi = st;
+                    unsigned char* alo = st + kATile;
+    #pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        uint4 hi, lo;
+                        unsigned* hp = reinterpret_cast<unsigned*>(&hi);
+                        unsigned* lp = reinterpret_cast<unsigned*>(&lo);
+    #pragma unroll
+                        for (int e = 0; e < 4; ++e) split_exact(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1], hp[e], lp[e]);
+                        const int chunk = c == 0 ? chunk_a<TYPE>(hf) : chunk_b<TYPE>(hf);
+                        *reinterpret_cast<uint4*>(ahi + sw64(r, chunk)) = hi;
+                        *reinterpret_cast<uint4*>(alo + sw64(r, chunk)) = lo;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(&full_a[s]);
+                }
+            }
         }
         // ---------------- epilogue: TMEM lane r holds weight row row0 + r;
         // warps w and w+4 share lanes 32*(w%4).. and split the token columns
@@ -403,8 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (normally long since consumed; after an abort, wait with a bound)
         if (threadIdx.x == 0) {
             for (int s = 0; s < kStages; ++s)
-                if (last_ph[s] >= 0)
-                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full_b[s], unsigned(last_ph[s])); ++i) {
+                if (tma_issued >> s & 1u)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full_b[s], (tma_phase >> s) & 1u); ++i) {
                     }
         }
     } else if (lane == 0) {
@@ -413,8 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < a.k_steps; ++ks) {
             const int s = ks % kStages;
             const unsigned ph = (ks / kStages) & 1;
-            if (!mbar_wait(&full_b[s], ph, abort_flag, a.err, 13)) break;
-            if (!mbar_wait(&full_a[s], ph, abort_flag, a.err, 14)) break;
+            if (!mbar_wait(&full_b[s], ph, abort_flag, a.err, 13, false)) break;
+            if (TYPE != kPlanes && !mbar_wait(&full_a[s], ph, abort_flag, a.err, 14, false)) break;
             asm volatile("tcgen05.fence::after_thread_sync;");
             unsigned char* st = stages + s * stage_bytes;
             const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
@@ -484,14 +521,12 @@ CUtensorMap make_map(const __half* base, int K, int T, int n_tile) {
 }
 
 template <int TYPE>
-void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const TcArgs& a, dim3 grid, cudaStream_t s) {
+void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const CUtensorMap& ahi, const CUtensorMap& alo,
+            const TcArgs& a, dim3 grid, cudaStream_t s) {
     const int smem = kStages * (2 * kATile + 2 * kBTileMax) + 1024 + 256;
-    static bool configured = false;
-    if (!configured) {
-        TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        configured = true;
-    }
-    tc_gemm_kernel<TYPE><<<grid, kThreads, smem, s>>>(hi, lo, a);
+    // a per-device attribute: set on every launch (about a microsecond)
+    TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    tc_gemm_kernel<TYPE><<<grid, kThreads, smem, s>>>(hi, lo, ahi, alo, a);
     TVARA_LAUNCHED();
 }
 
@@ -547,13 +582,19 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     if (splits > 1 && g.epilogue == kStore)
         TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
     const CUtensorMap mh = make_map(hi, K, T, n_tile), ml = make_map(lo, K, T, n_tile);
-    const dim3 grid(row_tiles, token_tiles, splits);
+    const dim3 grid(token_tiles, row_tiles, splits);
+    if (g.w.plane_hi && g.w.plane_lo) {
+        const CUtensorMap pa = make_map(reinterpret_cast<const __half*>(g.w.plane_hi), K, g.w.rows, kBM);
+        const CUtensorMap pb = make_map(reinterpret_cast<const __half*>(g.w.plane_lo), K, g.w.rows, kBM);
+        run_tc<kPlanes>(mh, ml, pa, pb, a, grid, s);
+        return;
+    }
     switch (g.w.type) {
-        case kQ4_K: run_tc<kQ4_K>(mh, ml, a, grid, s); break;
-        case kQ4_0: run_tc<kQ4_0>(mh, ml, a, grid, s); break;
-        case kQ8_0: run_tc<kQ8_0>(mh, ml, a, grid, s); break;
-        case kF16: run_tc<kF16>(mh, ml, a, grid, s); break;
-        case kF32: run_tc<kF32>(mh, ml, a, grid, s); break;
+        case kQ4_K: run_tc<kQ4_K>(mh, ml, mh, ml, a, grid, s); break;
+        case kQ4_0: run_tc<kQ4_0>(mh, ml, mh, ml, a, grid, s); break;
+        case kQ8_0: run_tc<kQ8_0>(mh, ml, mh, ml, a, grid, s); break;
+        case kF16: run_tc<kF16>(mh, ml, mh, ml, a, grid, s); break;
+        case kF32: run_tc<kF32>(mh, ml, mh, ml, a, grid, s); break;
         default: throw std::invalid_argument("unsupported projection type");
     }
 }

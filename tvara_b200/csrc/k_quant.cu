@@ -8,6 +8,7 @@
 #include <cstdint>
 
 #include "kernels.cuh"
+#include "split.cuh"
 
 namespace tvara {
 namespace {
@@ -219,6 +220,18 @@ __global__ void row_shift_kernel(DeviceMatrix w, signed char* out) {
         int e = 0;
         if (m > 0.f && isfinite(m)) frexpf(m, &e);
         out[r] = (signed char)(m > 0.f ? max(-100, min(100, 15 - e)) : 0);
+    }
+}
+
+// Exact FP16 planes of a matrix: element value (the reference's dequantised
+// F32) times 2^row_shift, split into hi + lo.
+__global__ void planes_kernel(DeviceMatrix w, unsigned* hi, unsigned* lo) {
+    const long long pairs = (long long)w.rows * w.cols / 2;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < pairs; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = 2 * i / w.cols;
+        const int k = int(2 * i % w.cols);
+        const float f = __uint_as_float(unsigned(127 + w.row_shift[r]) << 23);
+        split_exact(element(w, r, k) * f, element(w, r, k + 1) * f, hi[i], lo[i]);
     }
 }
 
@@ -511,6 +524,12 @@ void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t*
     const std::size_t total = std::size_t(rows) * (cols / per);
     const int grid = int(std::min<std::size_t>((total + 255) / 256, 148 * 32));
     repack_kernel<<<grid, 256, 0, s>>>(type, static_cast<const unsigned char*>(gguf), rows, cols, qs, meta);
+    TVARA_LAUNCHED();
+}
+
+void launch_planes(const DeviceMatrix& w, std::uint16_t* hi, std::uint16_t* lo, cudaStream_t s) {
+    if (!w.row_shift || w.cols % 2) throw std::invalid_argument("planes need row shifts and an even width");
+    planes_kernel<<<148 * 8, 256, 0, s>>>(w, reinterpret_cast<unsigned*>(hi), reinterpret_cast<unsigned*>(lo));
     TVARA_LAUNCHED();
 }
 

@@ -48,6 +48,9 @@ void launch_repack(int type, const void* gguf, int rows, int cols, std::uint8_t*
 void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s);
 // Per-row power-of-two scale of the tensor-core split (DeviceMatrix::row_shift).
 void launch_row_shift(const DeviceMatrix& w, signed char* out, cudaStream_t s);
+// Fills hi / lo ([rows][cols] FP16 each) with the exact split of every
+// value times 2^row_shift (the tensor-core planes of DeviceMatrix).
+void launch_planes(const DeviceMatrix& w, std::uint16_t* hi, std::uint16_t* lo, cudaStream_t s);
 // Minimum token count routed to the tensor-core projection.
 void set_tc_min_tokens(int n);
 

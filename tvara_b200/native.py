@@ -43,7 +43,7 @@ def tp_shard(path, tp_rank: int, tp_size: int, library=None) -> dict:
 
 class NativeModel:
     def __init__(self, path, library=None, max_blocks=256, block_tokens=16, *, kv_dtype=None, device=None,
-                 max_step_tokens=None, tp_rank=0, tp_size=1, nccl_id: bytes | None = None):
+                 max_step_tokens=None, tp_rank=0, tp_size=1, nccl_id: bytes | None = None, weight_planes=None):
         self._lock = threading.RLock()
         self._library = load_library(library)
         lib = self._library
@@ -51,7 +51,7 @@ class NativeModel:
                 or block_tokens <= 0):
             raise ValueError("Cache geometry must be positive integers")
         encoded = str(Path(path).resolve()).encode("utf-8")
-        if kv_dtype is None and device is None and max_step_tokens is None and tp_size == 1:
+        if kv_dtype is None and device is None and max_step_tokens is None and tp_size == 1 and weight_planes is None:
             self._handle = lib.tvara_model_open(encoded, max_blocks, block_tokens)
         else:
             opts = OpenOptions()
@@ -60,6 +60,7 @@ class NativeModel:
             opts.kv_dtype = {None: KV_F32, "f32": KV_F32, "f16": KV_F16, KV_F32: KV_F32, KV_F16: KV_F16}[kv_dtype]
             opts.max_step_tokens = int(max_step_tokens or 0)
             opts.tp_rank, opts.tp_size = int(tp_rank), int(tp_size)
+            opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2}[weight_planes]
             self._nccl_id = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
             opts.nccl_id = C.cast(self._nccl_id, C.c_void_p) if self._nccl_id is not None else None
             self._handle = lib.tvara_model_open_ex(encoded, max_blocks, block_tokens, C.byref(opts))
@@ -136,6 +137,15 @@ class NativeModel:
                                                          _ptr(out, F32P), out.size):
                 self._raise_error()
         return out
+
+    def weight_bytes(self) -> dict:
+        """Device bytes of the packed weights and of the FP16 weight planes."""
+        packed, planes = C.c_size_t(), C.c_size_t()
+        with self._lock:
+            self._check_open()
+            if self._library.tvara_model_weight_bytes(self._handle, C.byref(packed), C.byref(planes)):
+                self._raise_error()
+        return {"packed": packed.value, "planes": planes.value}
 
     def truncate(self, sequence, length):
         with self._lock:
