@@ -326,22 +326,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         // per stage: whether this thread issued a TMA there, and its phase
         unsigned tma_issued = 0, tma_phase = 0;
         if constexpr (TYPE == kPlanes) {
-            // A and B tiles both arrive by TMA, issued by one thread
-            if (threadIdx.x == 0) {
-                for (int ks = 0; ks < a.k_steps && !*abort_flag; ++ks) {
-                    const int s = ks % kStages;
-                    const unsigned ph = (ks / kStages) & 1;
-                    const int k0 = (kstep0 + ks) * kBK;
-                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11)) break;
-                    unsigned char* st = stages + s * stage_bytes;
-                    const unsigned bar = smem_u32(&full_b[s]);
-                    mbar_expect_tx(&full_b[s], 2 * kATile + 2 * b_bytes);
-                    tma_load_2d(smem_u32(st), &map_ahi, k0, row0, bar);
-                    tma_load_2d(smem_u32(st + kATile), &map_alo, k0, row0, bar);
-                    tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, bar);
-                    tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, bar);
-                    tma_issued |= 1u << s;
-                    tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+            // A and B tiles both arrive by TMA, issued by lane 0 of warp 0; the
+            // whole warp runs the loop so the issuing lane never shares its warp
+            // with lanes spinning elsewhere.
+            if (warp == 0) {
+                for (int ks = 0; ks < a.k_steps; ++ks) {
+                    int go = 1;
+                    if (lane == 0) {
+                        const int s = ks % kStages;
+                        const unsigned ph = (ks / kStages) & 1;
+                        const int k0 = (kstep0 + ks) * kBK;
+                        go = !*abort_flag && mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                        if (go) {
+                            unsigned char* st = stages + s * stage_bytes;
+                            const unsigned bar = smem_u32(&full_b[s]);
+                            mbar_expect_tx(&full_b[s], 2 * kATile + 2 * b_bytes);
+                            tma_load_2d(smem_u32(st), &map_ahi, k0, row0, bar);
+                            tma_load_2d(smem_u32(st + kATile), &map_alo, k0, row0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, bar);
+                            tma_issued |= 1u << s;
+                            tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, go, 0)) break;
                 }
             }
         } else {
@@ -532,6 +540,46 @@ void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const CUtensorMap& ahi
 
 int g_tc_min_tokens = 5;  // below this the CUDA-core GEMV streams weights once per <=4 tokens
 
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return n > 0 ? n : 148;
+}
+
+struct TilePlan {
+    int n_tile, token_tiles, splits;
+};
+
+// Token tile width and split-K count for a launch: one CTA per SM, so the
+// time is about (waves) x (per-tile time), and a partial last wave costs a
+// whole one.  Candidates: balanced token tiles (width a multiple of 16, at
+// most 256) and power-of-two K splits of at least 8 steps (none for SwiGLU,
+// which is nonlinear).  Per tile: K-steps x (width + a fixed per-step cost)
+// plus a fixed cost for the pipeline fill and the epilogue (which grows with
+// the width and, for split K, with the atomic accumulation).
+TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sms) {
+    TilePlan best{0, 0, 0};
+    double best_cost = 0;
+    for (int tt = (tokens + kMaxN - 1) / kMaxN; tt <= (tokens + 15) / 16 && tt <= 64; ++tt) {
+        const int width = (((tokens + tt - 1) / tt) + 15) / 16 * 16;
+        if (width > kMaxN) continue;
+        const int token_tiles = (tokens + width - 1) / width;
+        for (int sp = 1; sp <= 16; sp *= 2) {
+            if (sp > 1 && (!can_split || steps % sp || steps / sp < 8)) break;
+            const long long tiles = (long long)row_tiles * token_tiles * sp;
+            const long long waves = (tiles + sms - 1) / sms;
+            const double per_tile = double(steps / sp) * (width + 48) + 6.0 * width + 1500.0 + (sp > 1 ? 8.0 * width : 0.0);
+            const double cost = double(waves) * per_tile;
+            if (!best.n_tile || cost < best_cost) {
+                best = {width, token_tiles, sp};
+                best_cost = cost;
+            }
+        }
+    }
+    return best;
+}
+
 }  // namespace
 
 bool gemm_tc_supported(const DeviceMatrix& w, int tokens) {
@@ -556,16 +604,10 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
     TVARA_LAUNCHED();
 
-    int n_tile = T >= kMaxN ? kMaxN : ((T + 15) / 16) * 16;
-    const int token_tiles = (T + n_tile - 1) / n_tile;
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
-    // split K until the grid covers the SMs (not for SwiGLU, which is nonlinear)
-    int splits = 1;
-    if (g.epilogue != kSwiGLU) {
-        while (row_tiles * token_tiles * splits < 148 && steps % (splits * 2) == 0 && steps / (splits * 2) >= 8)
-            splits *= 2;
-    }
+    const TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
+    const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
     TcArgs a;
     a.w = g.w;
     a.x_shift = shift;
