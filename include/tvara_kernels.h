@@ -43,7 +43,8 @@ TVARA_API size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens);
  * y[t][r] = sum_k W[r][k] * x[t][k] for t < tokens, W packed (device), x and y
  * F32 row-major (device).  Up to 4 tokens: CUDA-core GEMV with the weights
  * dequantised in registers.  More: tcgen05 tensor cores on an exact hi+lo
- * FP16 split of both operands (F32 accumulation); needs `workspace`. */
+ * FP16 split of both operands (F32 accumulation); needs `workspace`, and x
+ * 16-byte aligned (cols is a multiple of 32 there). */
 TVARA_API int tvara_quant_matmul(int type, const void* packed, size_t rows, size_t cols, const float* x,
                                  size_t tokens, float* y, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -485,12 +485,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
-// that puts max|x| in [2^14, 2^15).
+// that puts max|x| in [2^14, 2^15), then the exact split (split.cuh).  One
+// block per token; float4 loads and 8-byte stores (K % 4 == 0, rows 16-byte
+// aligned, which the launcher checks).
 __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half* lo, int* shift) {
     const int t = blockIdx.x;
-    const float* row = x + (long long)t * ldx;
+    const float4* row = reinterpret_cast<const float4*>(x + (long long)t * ldx);
+    const int K4 = K / 4;
     float m = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(row[k]));
+    for (int k = threadIdx.x; k < K4; k += blockDim.x) {
+        const float4 v = row[k];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
     __shared__ float sm[32];
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
@@ -506,11 +512,15 @@ __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half*
     const int s = sm[0] > 0.f ? max(-100, min(100, 15 - e)) : 0;
     if (threadIdx.x == 0) shift[t] = s;
     const float f = pow2(s);
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = row[k] * f;
-        const __half h = __float2half_rn(v);
-        hi[(long long)t * K + k] = h;
-        lo[(long long)t * K + k] = __float2half_rn(v - __half2float(h));
+    uint2* hrow = reinterpret_cast<uint2*>(hi + (long long)t * K);
+    uint2* lrow = reinterpret_cast<uint2*>(lo + (long long)t * K);
+    for (int k = threadIdx.x; k < K4; k += blockDim.x) {
+        const float4 v = row[k];
+        uint2 h, l;
+        split_exact(v.x * f, v.y * f, h.x, l.x);
+        split_exact(v.z * f, v.w * f, h.y, l.y);
+        hrow[k] = h;
+        lrow[k] = l;
     }
 }
 
@@ -601,6 +611,8 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     int* shift = reinterpret_cast<int*>(lo + std::size_t(T) * K);
     // callers without an error flag get one in the workspace (never null)
     int* err = g.err ? g.err : shift + ((T + 63) / 64) * 64;
+    if (reinterpret_cast<std::uintptr_t>(g.x) % 16 || g.ldx % 4 || K % 4)
+        throw std::invalid_argument("tensor-core projection input must be 16-byte aligned rows");
     split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
     TVARA_LAUNCHED();
 
