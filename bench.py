@@ -17,9 +17,16 @@ values).  KV is F16.  N > 1 runs tensor parallel (NCCL allreduce after
 o_proj and down_proj) over the same 512 requests: strong scaling.
 
 Reported: value = decode tokens/s over the timed steps (device time on the
-engine stream, max over ranks), e2e = the same steps through the C ABI with
-full-vocabulary F32 logits copied to host memory every step, the dominant
-kernel's roofline, the reference CPU engine timed on this host, SM clocks.
+engine stream, max over ranks); e2e = wall-clock tokens/s of the same call a
+serving loop makes (tvara_batch_step with host token arrays in and the next
+tokens -- device argmax with the finiteness check -- back in host memory,
+exactly what tvara_b200.scheduler.BatchedSchedulerBackend issues), and
+e2e_full_logits = the same with every full-vocabulary F32 logit row copied to
+the host; the dominant kernel's roofline (DRAM traffic from the committed ncu
+captures) and the step roofline of the survey's convention (sum over kernels
+of max(bytes / HBM peak, flops / tensor peak), shared prefix counted per
+reader, over the measured step time); the reference CPU engine timed on this
+host; SM clocks.
 """
 
 from __future__ import annotations
@@ -40,6 +47,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM bytes (read + write) per launch from ncu captures of this workload
+# (profiles/attn_mma_llama8b_decode512.txt, profiles/tc_gemm_planes_llama8b_512tok.txt).
+NCU_TRAFFIC = {"attention": 2.63e9, "projections": 2.60e8}
 
 
 def peaks():
@@ -65,7 +76,7 @@ def parse():
                     help="unique suffix length range per request")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens the reference CPU engine decodes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model-dir", default=os.environ.get("TVARA_BENCH_DIR", "/tmp/tvara_bench"))
@@ -277,7 +288,7 @@ def run_ours(args):
     g = gguf.GGUFFile(path)
     vocab = len(g.metadata["tokenizer.ggml.tokens"])
     prefix, suffix, done, first = workload(args, vocab)
-    total_steps = args.warmup + args.steps + args.e2e_steps + 2
+    total_steps = args.warmup + 2 * args.steps + 2 * args.e2e_steps + 2
     tpb = 16
     unique = suffix + done + total_steps
     blocks = int(np.sum((args.prefix + unique + tpb - 1) // tpb - args.prefix // tpb)) + args.prefix // tpb + 64
@@ -296,12 +307,12 @@ def run_ours(args):
         seqs.append(s)
     model.prefix_pin(node)
     lens0 = np.array([model.sequence_length(s) for s in seqs])
-    tokens = [[int(t)] for t in first]
+    seqs = np.array(seqs, dtype=np.uint64)
+    tokens = np.asarray(first, dtype=np.uint32).copy()
 
     def step(logits=False):
-        out, am = model.batch_step(seqs, tokens, logits=logits, argmax=True)
-        for i, t in enumerate(am):
-            tokens[i][0] = int(t)
+        out, am = model.batch_step(seqs, tokens, logits=logits, argmax=True, finite_argmax=True)
+        tokens[:] = am
         return out
 
     for _ in range(args.warmup):
@@ -310,7 +321,6 @@ def run_ours(args):
     lib = model._library
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = Clocks(local)
-    model._library.tvara_model_profile(model._handle, 1)
     torch.cuda.synchronize()
     barrier()
     clocks.start()
@@ -325,9 +335,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     ms = start.elapsed_time(end)
-    prof_ms = (C.c_double * 5)()
-    prof_n = (C.c_uint64 * 5)()
-    lib.tvara_model_profile_read(model._handle, prof_ms, prof_n, 5)
+    # kernel-class breakdown: the same number of steps again, with CUDA events
+    # around each launch group (kept out of the timed region above)
+    lib.tvara_model_profile(model._handle, 1)
+    for _ in range(args.steps):
+        step()
+    prof_ms = (C.c_double * 6)()
+    prof_n = (C.c_uint64 * 6)()
+    lib.tvara_model_profile_read(model._handle, prof_ms, prof_n, 6)
     lib.tvara_model_profile(model._handle, 0)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -336,20 +351,29 @@ def run_ours(args):
     ms_per_step = ms / args.steps
     value = args.requests * args.steps / (ms / 1e3)
 
-    # ---- e2e: same call, full-vocab F32 logits to host every step
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        step(logits=True)
-    e2e_s = time.perf_counter() - t0
-    h2d, d2h = C.c_uint64(), C.c_uint64()
-    lib.tvara_model_step_bytes(model._handle, C.byref(h2d), C.byref(d2h))
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = args.requests * args.e2e_steps / e2e_s
-    caller_h2d = args.requests * (4 + 8) + (args.requests + 1) * 4
+    # ---- e2e: the same call from the host, wall clock (next tokens back; then full logits back)
+    caller_h2d = args.requests * (4 + 8) + (args.requests + 1) * 4  # tokens, sequence ids, cu_tokens
+
+    def e2e(logits):
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            step(logits=logits)
+        secs = time.perf_counter() - t0
+        h2d, d2h = C.c_uint64(), C.c_uint64()
+        lib.tvara_model_step_bytes(model._handle, C.byref(h2d), C.byref(d2h))
+        if world > 1:
+            t = torch.tensor([secs], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            secs = float(t.item())
+        return {"value": args.requests * args.e2e_steps / secs, "unit": "tok/s",
+                "h2d_bytes_per_step": int(h2d.value) + caller_h2d, "d2h_bytes_per_step": int(d2h.value)}
+
+    e2e_tokens = e2e(False)
+    e2e_tokens["note"] = ("tvara_batch_step: host token / sequence arrays in, next tokens (device argmax, "
+                          "finiteness checked) out -- the BatchedSchedulerBackend call")
+    e2e_logits = e2e(True)
+    e2e_logits["note"] = "same, plus every full-vocabulary F32 logit row copied to host memory"
 
     # ---- roofline of the dominant kernel class
     pk, pk_kind = peaks()
@@ -358,7 +382,7 @@ def run_ours(args):
     dh = D // H
     tp = world
     es = 2 if args.kv == "f16" else 4
-    mean_ctx = float(np.mean(lens0 + args.warmup + 1 + (args.steps - 1) / 2))
+    mean_ctx = float(np.mean(lens0 + args.warmup + args.steps + 1 + (args.steps - 1) / 2))  # profiled pass
     attn_bytes = args.requests * (mean_ctx * 2 * (HKV // tp) * dh * es + 2 * (H // tp) * dh * 4)
     attn_launches = int(prof_n[0])
     attn_ms = float(prof_ms[0])
@@ -375,17 +399,33 @@ def run_ours(args):
         "head": {"ms_per_step": prof_ms[2] / args.steps},
         "other": {"ms_per_step": prof_ms[3] / args.steps},
         "collective": {"ms_per_step": prof_ms[4] / args.steps},
+        "host_gap": {"ms_per_step": prof_ms[5] / args.steps,
+                     "note": "stream idle on the host between steps (previous results back -> next step's first copy)"},
     }
-    if attn_ms >= proj_ms:
-        ach = kernels["attention"]["achieved_gbs"]
-        roof = {"kernel": "paged attention (per layer launch)", "bound": "hbm", "achieved": ach,
-                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
-                "peak_source": pk_kind, "algorithmic_bytes_per_launch": attn_bytes}
-    else:
-        ach = kernels["projections"]["achieved_tflops"]
-        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
-        roof = {"kernel": "projections (all per step)", "bound": "tensor", "achieved": ach, "peak": peak,
-                "unit": "TFLOP/s", "frac": ach / peak, "traffic": None, "peak_source": pk_kind}
+    full = args.layers is None and tp == 1 and args.requests == 512
+    hbm, tensor = pk["hbm_gbs"], pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    ach = kernels["attention"]["achieved_gbs"]
+    roof_attn = {"kernel": "attn_mma_kernel (paged attention, one launch per layer)", "bound": "hbm",
+                 "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm if ach else None,
+                 "traffic": NCU_TRAFFIC["attention"] if full else None, "peak_source": pk_kind,
+                 "algorithmic_bytes_per_launch": attn_bytes,
+                 "note": "algorithmic bytes count the shared 1024-token prefix once per reader; DRAM traffic "
+                         "reads it once (L2 serves the rest), so frac can exceed 1"}
+    ach = kernels["projections"]["achieved_tflops"]
+    roof_proj = {"kernel": "tc_gemm_kernel (all projections of a step)", "bound": "tensor", "achieved": ach,
+                 "peak": tensor, "unit": "TFLOP/s", "frac": ach / tensor if ach else None,
+                 "traffic": NCU_TRAFFIC["projections"] if full else None, "peak_source": pk_kind,
+                 "algorithmic_flops_per_step": proj_flops_step, "tensor_work_multiplier": 3,
+                 "note": "useful flops 2*T*rows*cols; the exact hi/lo FP16 split issues 3 MMAs per product"}
+    roof = roof_attn if attn_ms >= proj_ms else roof_proj
+    # survey convention: sum over kernels of max(bytes/BW, flops/P) over the measured step time
+    head_bytes = cfg["vocab"] * D * 34 / 32
+    t_attn = L * max(attn_bytes / (hbm * 1e9), 4.0 * args.requests * mean_ctx * dh * (H // tp) / (tensor * 1e12))
+    weight_bytes = params * 0.5625 + head_bytes
+    t_proj = max(weight_bytes / (hbm * 1e9), (proj_flops_step + 2.0 * args.requests * cfg["vocab"] * D) / (tensor * 1e12))
+    t_roof_ms = (t_attn + t_proj) * 1e3
+    step_roof = {"t_roof_ms": t_roof_ms, "measured_ms": ms_per_step, "frac": t_roof_ms / ms_per_step,
+                 "convention": "sum over kernels of max(bytes/HBM, flops/tensor peak); shared prefix per reader"}
 
     cpu = reference_cpu(path, args.cpu_tokens, 1, cpu_job) if cpu_job else None
     line = {
@@ -402,10 +442,9 @@ def run_ours(args):
                    "weights_gb": {"packed": round(wbytes["packed"] / 1e9, 2),
                                   "fp16_planes": round(wbytes["planes"] / 1e9, 2)},
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d.value) + caller_h2d,
-                "d2h_bytes_per_step": int(d2h.value),
-                "note": "tvara_batch_step with host token/sequence arrays in and full-vocab F32 logits + argmax out"},
-        "roofline": roof, "kernels": kernels, "gpu_launches": int(launches), "clocks": clk,
+        "e2e": e2e_tokens, "e2e_full_logits": e2e_logits,
+        "roofline": roof, "rooflines": {"attention": roof_attn, "projections": roof_proj}, "step_roofline": step_roof,
+        "kernels": kernels, "gpu_launches": int(launches), "clocks": clk,
         "cpu_baseline": cpu,
     }
     if rank == 0:

@@ -187,8 +187,10 @@ TVARA_API int tvara_sequence_reserve(tvara_model* model, uint64_t sequence, size
 TVARA_API int tvara_model_profile(tvara_model* model, int enable);
 /* Totals since enabling, in this class order: 0 attention, 1 projections
  * (GEMV/GEMM), 2 final norm + LM head + argmax, 3 other elementwise
- * (embedding, RMSNorm, RoPE/KV write, block copies), 4 collectives.  Writes
- * up to capacity entries; returns the number of classes, -1 on error. */
+ * (embedding, RMSNorm, RoPE/KV write, block copies), 4 collectives, 5 host
+ * time with the stream idle between the end of one device step and the first
+ * work of the next (caller code included).  Writes up to capacity entries;
+ * returns the number of classes, -1 on error. */
 TVARA_API int tvara_model_profile_read(tvara_model* model, double* milliseconds, uint64_t* groups, size_t capacity);
 /* Kernel launches this library has issued since it was loaded. */
 TVARA_API uint64_t tvara_kernel_launches(void);

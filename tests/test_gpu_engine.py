@@ -255,3 +255,20 @@ def test_weight_planes_match_packed_path(tiny_path, model_dir, name):
             got[planes] = m.decode_batch(s, toks)
         assert close(got[planes], want), (planes, np.abs(got[planes] - want).max())
     assert np.abs(got["on"] - got["off"]).max() <= 1e-4
+
+
+def test_batch_step_decode_array_equals_lists(tiny_path):
+    """The 1-D decode form of batch_step (one token per sequence) is the same
+    call as the list form."""
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (5, 9, 2)]
+    outs = []
+    for form in ("lists", "array"):
+        with NativeModel(tiny_path, max_blocks=32, block_tokens=16) as m:
+            seqs = [m._new_sequence() for _ in prompts]
+            m.batch_step(seqs, prompts, logits=False)
+            toks = np.array([7, 8, 9], dtype=np.uint32)
+            arg = toks if form == "array" else [[int(t)] for t in toks]
+            logits, am = m.batch_step(np.array(seqs, dtype=np.uint64), arg, argmax=True)
+            outs.append((logits, am))
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])

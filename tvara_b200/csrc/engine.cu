@@ -496,6 +496,7 @@ void Engine::profile_collect() {
 
 void Engine::set_profiling(bool on) {
     profiling_ = on;
+    host_idle_valid_ = false;
     for (int i = 0; i < kProfClasses; ++i) {
         prof_ms_[i] = 0;
         prof_n_[i] = 0;
@@ -582,6 +583,11 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     int4* d_comb = reinterpret_cast<int4*>(put(comb.data(), comb.size() * 4));
     int2* d_copy = reinterpret_cast<int2*>(put(s.copies.data(), s.copies.size() * 2));
     int* d_rows = put(s.out_rows.data(), R);
+    if (profiling_ && host_idle_valid_) {
+        prof_ms_[kProfHost] +=
+            std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - host_idle_since_).count();
+        ++prof_n_[kProfHost];
+    }
     TVARA_CUDA(cudaMemcpyAsync(meta_dev_, meta_host_, at * 4, cudaMemcpyHostToDevice, stream_));
     acc_h2d_ += at * 4;
 
@@ -693,6 +699,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         }
     }
     TVARA_CUDA(cudaStreamSynchronize(stream_));
+    host_idle_since_ = std::chrono::steady_clock::now();
+    host_idle_valid_ = true;
     profile_collect();
     if (*err_host_) {
         const int code = *err_host_;

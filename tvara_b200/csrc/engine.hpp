@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <array>
+#include <chrono>
 #include <memory>
 #include <span>
 #include <string>
@@ -77,7 +78,17 @@ public:
 
     // Device time per kernel class, measured with CUDA events on the engine
     // stream around each launch group while enabled (off by default).
-    enum ProfileClass { kProfAttention = 0, kProfProjection, kProfHead, kProfOther, kProfCollective, kProfClasses };
+    // kProfHost: host time with the stream idle, from the end of one device
+    // step (its results back on the host) to the first work of the next one.
+    enum ProfileClass {
+        kProfAttention = 0,
+        kProfProjection,
+        kProfHead,
+        kProfOther,
+        kProfCollective,
+        kProfHost,
+        kProfClasses
+    };
     void set_profiling(bool on);
     void profile_read(double* ms, unsigned long long* groups) const;
     std::uint64_t last_h2d() const { return last_h2d_; }
@@ -88,6 +99,8 @@ private:
     void timed(int cls, F&& launch);
     void profile_collect();
     bool profiling_ = false;
+    bool host_idle_valid_ = false;
+    std::chrono::steady_clock::time_point host_idle_since_;
     std::uint64_t last_h2d_ = 0, last_d2h_ = 0, acc_h2d_ = 0, acc_d2h_ = 0;
     std::vector<cudaEvent_t> events_;
     std::vector<int> event_class_;

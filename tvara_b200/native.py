@@ -170,16 +170,24 @@ class NativeModel:
         return n.value
 
     def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False, finite_argmax=False):
-        """One device step: sequence i appends token_lists[i].  Returns
+        """One device step: sequence i appends token_lists[i] (or, given a 1-D
+        array, the single token token_lists[i]).  Returns
         (logits [rows, vocab] or None, argmax [rows] or None) with one row per
         sequence (its last token) or per token when all_logits.  With
         finite_argmax, a row whose logits hold a NaN or an infinity has
         argmax ARGMAX_NONFINITE."""
         seqs = np.ascontiguousarray(sequences, dtype=np.uint64)
-        lens = np.array([len(t) for t in token_lists], dtype=np.uint32)
-        cu = np.zeros(len(seqs) + 1, dtype=np.uint32)
-        np.cumsum(lens, out=cu[1:])
-        toks = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.uint32) for t in token_lists]))
+        if isinstance(token_lists, np.ndarray) and token_lists.ndim == 1:
+            # decode: one token per sequence
+            if len(token_lists) != len(seqs):
+                raise ValueError("one token per sequence expected")
+            toks = np.ascontiguousarray(token_lists, dtype=np.uint32)
+            cu = np.arange(len(seqs) + 1, dtype=np.uint32)
+        else:
+            lens = np.array([len(t) for t in token_lists], dtype=np.uint32)
+            cu = np.zeros(len(seqs) + 1, dtype=np.uint32)
+            np.cumsum(lens, out=cu[1:])
+            toks = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.uint32) for t in token_lists]))
         rows = int(cu[-1]) if all_logits else len(seqs)
         out = np.empty((rows, self.vocab_size), dtype=np.float32) if logits else None
         am = np.empty(rows, dtype=np.uint32) if argmax else None
