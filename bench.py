@@ -77,6 +77,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-standalone", action="store_true", help="skip the standalone GEMV / matmul figures")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens the reference CPU engine decodes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model-dir", default=os.environ.get("TVARA_BENCH_DIR", "/tmp/tvara_bench"))
@@ -249,6 +250,67 @@ def run_reference(args):
         line.update({"value": res["value"], "cpu_baseline": res,
                      "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
     print(json.dumps(line))
+
+
+def standalone_gemv(lib, hbm_gbs):
+    """Quantised GEMV (M = 1) and small-M matmul on the survey's standalone
+    shape, 11008 x 4096, through the kernel-level ABI: GB/s of packed weights
+    per launch over CUDA events.  Eight weight copies (> L2) are used in turn,
+    so every launch reads its weights from DRAM."""
+    import torch
+    from tvara_b200 import gguf
+    rows, cols, copies = 11008, 4096, 8
+    rng = np.random.default_rng(11)
+    out = {}
+    for name, kind in (("q4_k", gguf.Q4_K), ("q8_0", gguf.Q8_0), ("q4_0", gguf.Q4_0)):
+        nbytes = lib.tvara_packed_bytes(kind, rows, cols)
+        raw = torch.from_numpy(np.frombuffer(gguf.random_blocks(kind, rows, cols, rng), dtype=np.uint8).copy()).cuda()
+        mats = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        for m in mats:
+            assert lib.tvara_pack(kind, C.c_void_p(raw.data_ptr()), rows, cols, C.c_void_p(m.data_ptr()), None) == 0
+        weight_bytes = rows * cols // {gguf.Q4_K: 256, gguf.Q8_0: 32, gguf.Q4_0: 32}[kind] * \
+            {gguf.Q4_K: 144, gguf.Q8_0: 34, gguf.Q4_0: 18}[kind]
+        res = {}
+        for M in ((1, 8, 32, 128, 512) if kind == gguf.Q4_K else (1,)):
+            x = torch.randn(M, cols, device="cuda")
+            y = torch.empty(M, rows, device="cuda")
+            ws_n = lib.tvara_quant_matmul_workspace(cols, M)
+            ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device="cuda")
+
+            def call(m, stream):
+                assert lib.tvara_quant_matmul(kind, C.c_void_p(m.data_ptr()), rows, cols, C.c_void_p(x.data_ptr()),
+                                              M, C.c_void_p(y.data_ptr()), C.c_void_p(ws.data_ptr()), ws_n,
+                                              C.c_void_p(stream)) == 0
+            # the calls are captured in a CUDA graph and replayed, so the
+            # figure is device time, not the host cost of 64 ctypes calls
+            side = torch.cuda.Stream()
+            with torch.cuda.stream(side):
+                for m in mats:
+                    call(m, side.cuda_stream)
+            torch.cuda.synchronize()
+            reps = 64
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side, capture_error_mode="relaxed"):
+                for i in range(reps):
+                    call(mats[i % copies], side.cuda_stream)
+            graph.replay()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            graph.replay()
+            s1.record()
+            s1.synchronize()
+            us = s0.elapsed_time(s1) * 1e3 / reps
+            del graph
+            moved = weight_bytes + M * cols * 4 + M * rows * 4
+            res[f"m{M}"] = {"us": round(us, 2), "gbs": round(moved / us / 1e3, 1),
+                            "frac_hbm": round(moved / us / 1e3 / hbm_gbs, 3),
+                            "tflops": round(2.0 * M * rows * cols / us / 1e6, 2)}
+        out[name] = res
+    return {"shape": f"{rows}x{cols}", "weights": "seeded random packed blocks, 8 copies used in turn (> L2)",
+            "note": "kernel-level ABI, 64 calls replayed from a CUDA graph (device time); M <= 4 CUDA-core GEMV, "
+                    "M >= 5 tensor cores on the packed (producer) path incl. the activation split",
+            **out}
 
 
 def run_ours(args):
@@ -427,6 +489,7 @@ def run_ours(args):
     step_roof = {"t_roof_ms": t_roof_ms, "measured_ms": ms_per_step, "frac": t_roof_ms / ms_per_step,
                  "convention": "sum over kernels of max(bytes/HBM, flops/tensor peak); shared prefix per reader"}
 
+    gemv = standalone_gemv(lib, hbm) if rank == 0 and world == 1 and not args.no_standalone else None
     cpu = reference_cpu(path, args.cpu_tokens, 1, cpu_job) if cpu_job else None
     line = {
         "metric": "ragged-batch decode tok/s (8B-shape Q4_K)", "value": value, "unit": "tok/s", "n_gpus": world,
@@ -444,7 +507,7 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},
         "e2e": e2e_tokens, "e2e_full_logits": e2e_logits,
         "roofline": roof, "rooflines": {"attention": roof_attn, "projections": roof_proj}, "step_roofline": step_roof,
-        "kernels": kernels, "gpu_launches": int(launches), "clocks": clk,
+        "kernels": kernels, "standalone_kernels": gemv, "gpu_launches": int(launches), "clocks": clk,
         "cpu_baseline": cpu,
     }
     if rank == 0:
