@@ -13,11 +13,11 @@
 namespace tvara {
 namespace {
 
-constexpr int kWarps = 8;  // warps per CTA of the GEMV
+constexpr int kWarps = 4;  // warps per CTA of the GEMV (small CTAs: the whole grid is resident at once)
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
@@ -59,19 +59,15 @@ __device__ __forceinline__ void q4k_scale_min(const unsigned char* s, int g, uns
     }
 }
 // Same decode from the 12 scale bytes held in three words.
+// Branch-free (g differs between the lanes of a warp): with k = g & 3 and
+// the k-th bytes y, z, w of the three scale words, sub-blocks 0-3 take
+// (y & 63, z & 63) and 4-7 take (w & 15 | (y >> 6) << 4, w >> 4 | (z >> 6) << 4).
 __device__ __forceinline__ void q4k_scale_min_w(unsigned w0, unsigned w1, unsigned w2, int g, float& sc, float& m) {
-    auto byte = [&](int j) -> unsigned {
-        const unsigned w = j < 4 ? w0 : (j < 8 ? w1 : w2);
-        return (w >> (8 * (j & 3))) & 255u;
-    };
-    unsigned s, mm;
-    if (g < 4) {
-        s = byte(g) & 63u;
-        mm = byte(g + 4) & 63u;
-    } else {
-        s = (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
-        mm = (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
-    }
+    const unsigned sh = 8u * unsigned(g & 3);
+    const unsigned y = (w0 >> sh) & 255u, z = (w1 >> sh) & 255u, w = (w2 >> sh) & 255u;
+    const bool low = g < 4;
+    const unsigned s = low ? (y & 63u) : ((w & 15u) | ((y >> 6) << 4));
+    const unsigned mm = low ? (z & 63u) : ((w >> 4) | ((z >> 6) << 4));
     sc = float(s);
     m = float(mm);
 }
@@ -345,6 +341,76 @@ __device__ __forceinline__ float unit_dot(uint4 w, const float* xs, float s, int
     }
 }
 
+// The unit u of R rows against one token's x: each float4 of x is read from
+// shared memory once and used for all R rows (the x traffic per weight byte
+// falls by R).  Same arithmetic per row as unit_dot.
+template <int TYPE, int R>
+__device__ __forceinline__ void rows_unit_dot(const uint4 (&wv)[R], const float* xs, float s, int u,
+                                              const unsigned char* const (&meta)[R], float (&acc)[R]) {
+    if constexpr (TYPE == kQ4_0 || TYPE == kQ4_K) {
+        float a0[R], a1[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) a0[r] = a1[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 xl = *reinterpret_cast<const float4*>(xs + 4 * i);
+            const float4 xh = *reinterpret_cast<const float4*>(xs + 16 + 4 * i);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned w = i == 0 ? wv[r].x : i == 1 ? wv[r].y : i == 2 ? wv[r].z : wv[r].w;
+                const unsigned lo = ((w << 3) & 0x78787878u) | 0x80808080u;
+                const unsigned hi = ((w >> 1) & 0x78787878u) | 0x80808080u;
+                a0[r] = fmaf(nib(lo, 0), xl.x, a0[r]);
+                a1[r] = fmaf(nib(lo, 1), xl.y, a1[r]);
+                a0[r] = fmaf(nib(lo, 2), xl.z, a0[r]);
+                a1[r] = fmaf(nib(lo, 3), xl.w, a1[r]);
+                a0[r] = fmaf(nib(hi, 0), xh.x, a0[r]);
+                a1[r] = fmaf(nib(hi, 1), xh.y, a1[r]);
+                a0[r] = fmaf(nib(hi, 2), xh.z, a0[r]);
+                a1[r] = fmaf(nib(hi, 3), xh.w, a1[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float A = a0[r] + a1[r];
+            if constexpr (TYPE == kQ4_0) {
+                const float d = h2f(reinterpret_cast<const unsigned short*>(meta[r])[u]);
+                acc[r] += d * fmaf(16.f, A, -24.f * s);
+            } else {
+                const uint4 m = __ldg(reinterpret_cast<const uint4*>(meta[r]) + (u >> 3));
+                const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xffff)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
+                float sc, mn;
+                q4k_scale_min_w(m.y, m.z, m.w, u & 7, sc, mn);
+                const float ds = 16.f * d * sc;
+                acc[r] += fmaf(ds, A, -fmaf(dmin, mn, ds) * s);
+            }
+        }
+    } else if constexpr (TYPE == kQ8_0) {
+        float a0[R], a1[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) a0[r] = a1[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 xv = *reinterpret_cast<const float4*>(xs + 4 * i);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned w = (i == 0 ? wv[r].x : i == 1 ? wv[r].y : i == 2 ? wv[r].z : wv[r].w) ^ 0x80808080u;
+                a0[r] = fmaf(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u)) - 8388736.f, xv.x, a0[r]);
+                a1[r] = fmaf(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4551u)) - 8388736.f, xv.y, a1[r]);
+                a0[r] = fmaf(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4552u)) - 8388736.f, xv.z, a0[r]);
+                a1[r] = fmaf(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4553u)) - 8388736.f, xv.w, a1[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            acc[r] += h2f(reinterpret_cast<const unsigned short*>(meta[r])[u >> 1]) * (a0[r] + a1[r]);
+    } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] += unit_dot<TYPE>(wv[r], xs, s, u, meta[r]);
+    }
+}
+
 // The reference SwiGLU (model.hpp:120-124): gate * (sigmoid(gate) * up).
 __device__ __forceinline__ float swiglu(float g, float up) {
     const float small = expf(-fabsf(g));
@@ -402,17 +468,21 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemmArgs a, int kc) {
                         const int row = min(row0 + r, a.w.rows - 1);
                         wv[r] = ld_stream(a.w.qs + (long long)row * a.w.qs_row + (long long)(ubase + u) * 16);
                     }
+                    const unsigned char* metas[R];
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        metas[r] = a.w.meta + (long long)min(row0 + r, a.w.rows - 1) * a.w.meta_row;
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
                         if (t < nt) {
                             const float* xp = xs + t * kcp + xpad(u * E);
                             const float sv = (TYPE == kQ4_0 || TYPE == kQ4_K) ? s32[t * (kc / 32) + u] : 0.f;
+                            float col[R];
 #pragma unroll
-                            for (int r = 0; r < R; ++r) {
-                                const int row = min(row0 + r, a.w.rows - 1);
-                                const unsigned char* meta = a.w.meta + (long long)row * a.w.meta_row;
-                                acc[r][t] += unit_dot<TYPE>(wv[r], xp, sv, ubase + u, meta);
-                            }
+                            for (int r = 0; r < R; ++r) col[r] = acc[r][t];
+                            rows_unit_dot<TYPE, R>(wv, xp, sv, ubase + u, metas, col);
+#pragma unroll
+                            for (int r = 0; r < R; ++r) acc[r][t] = col[r];
                         }
                     }
                 }
@@ -451,6 +521,201 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemmArgs a, int kc) {
     }
 }
 
+// One token (decode): no shared-memory staging, so no barrier delays the
+// first weight loads.  Warp = kRows1 rows; lane l takes units l, l+32, ... of
+// them, prefetching the next unit's loads while it computes the current one.
+// The unit's x is read float4 by float4 through L1 (each load serves all the
+// warp's rows) and, for the 4-bit types, summed on the way.  Few live
+// registers (row addresses from one base, x never held whole), so many warps
+// stay resident to hide the load latency.
+constexpr int kRows1 = 4;
+
+// Packed F32x2 arithmetic (Blackwell fma.rn.f32x2 / add.rn.f32x2): two
+// weights per instruction, each half rounded exactly as the scalar op.
+__device__ __forceinline__ unsigned long long f2pk(float x, float y) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ float f2sum(unsigned long long r) {
+    float x, y;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(r));
+    return x + y;
+}
+__device__ __forceinline__ unsigned long long f2fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// x of unit u staged transposed in shared memory: float4 #i of unit u at
+// xt[i * units + u], so the lanes of a warp (consecutive units) read
+// consecutive 16-byte words.  S[u] = sum of the unit's x (4-bit types).
+template <int TYPE>
+__device__ __forceinline__ void rows_unit_dot_t(const uint4 (&wv)[kRows1], const float4* xt, int units, float S,
+                                                int u, const unsigned char* meta0, std::size_t meta_row,
+                                                float (&acc)[kRows1]) {
+    constexpr int R = kRows1;
+    if constexpr (TYPE == kQ4_0 || TYPE == kQ4_K) {
+        unsigned long long a2[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) a2[r] = 0ull;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 xl = xt[i * units + u];
+            const float4 xh = xt[(4 + i) * units + u];
+            const unsigned long long l01 = f2pk(xl.x, xl.y), l23 = f2pk(xl.z, xl.w);
+            const unsigned long long h01 = f2pk(xh.x, xh.y), h23 = f2pk(xh.z, xh.w);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned w = i == 0 ? wv[r].x : i == 1 ? wv[r].y : i == 2 ? wv[r].z : wv[r].w;
+                const unsigned lo = ((w << 3) & 0x78787878u) | 0x80808080u;
+                const unsigned hi = ((w >> 1) & 0x78787878u) | 0x80808080u;
+                a2[r] = f2fma(f2pk(nib(lo, 0), nib(lo, 1)), l01, a2[r]);
+                a2[r] = f2fma(f2pk(nib(lo, 2), nib(lo, 3)), l23, a2[r]);
+                a2[r] = f2fma(f2pk(nib(hi, 0), nib(hi, 1)), h01, a2[r]);
+                a2[r] = f2fma(f2pk(nib(hi, 2), nib(hi, 3)), h23, a2[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const unsigned char* meta = meta0 + r * meta_row;
+            const float A = f2sum(a2[r]);
+            if constexpr (TYPE == kQ4_0) {
+                const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[u]);
+                acc[r] += d * fmaf(16.f, A, -24.f * S);
+            } else {
+                const uint4 m = __ldg(reinterpret_cast<const uint4*>(meta) + (u >> 3));
+                const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xffff)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
+                float sc, mn;
+                q4k_scale_min_w(m.y, m.z, m.w, u & 7, sc, mn);
+                const float ds = 16.f * d * sc;
+                acc[r] += fmaf(ds, A, -fmaf(dmin, mn, ds) * S);
+            }
+        }
+    } else if constexpr (TYPE == kQ8_0) {
+        unsigned long long a2[R];
+        const unsigned long long bias = f2pk(-8388736.f, -8388736.f);  // -(2^23 + 128)
+#pragma unroll
+        for (int r = 0; r < R; ++r) a2[r] = 0ull;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 xv = xt[i * units + u];
+            const unsigned long long x01 = f2pk(xv.x, xv.y), x23 = f2pk(xv.z, xv.w);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned w = (i == 0 ? wv[r].x : i == 1 ? wv[r].y : i == 2 ? wv[r].z : wv[r].w) ^ 0x80808080u;
+                const unsigned long long q01 = f2add(f2pk(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u)),
+                                                          __uint_as_float(__byte_perm(w, 0x4Bu, 0x4551u))), bias);
+                const unsigned long long q23 = f2add(f2pk(__uint_as_float(__byte_perm(w, 0x4Bu, 0x4552u)),
+                                                          __uint_as_float(__byte_perm(w, 0x4Bu, 0x4553u))), bias);
+                a2[r] = f2fma(q01, x01, a2[r]);
+                a2[r] = f2fma(q23, x23, a2[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            acc[r] += h2f(reinterpret_cast<const unsigned short*>(meta0 + r * meta_row)[u >> 1]) * f2sum(a2[r]);
+    } else {
+        alignas(16) float xv[Unit<TYPE>::kElems];
+#pragma unroll
+        for (int j = 0; j < Unit<TYPE>::kElems / 4; ++j) {
+            const float4 v = xt[j * units + u];
+            xv[4 * j] = v.x;
+            xv[4 * j + 1] = v.y;
+            xv[4 * j + 2] = v.z;
+            xv[4 * j + 3] = v.w;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] += unit_dot<TYPE>(wv[r], xv, 0.f, u, meta0 + r * meta_row);
+    }
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
+    constexpr int R = kRows1, E = Unit<TYPE>::kElems, F4 = E / 4;
+    extern __shared__ float4 gemv_xt[];  // [F4][units] transposed x, then S[units]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int units = a.w.cols / E;
+    const int row0 = (blockIdx.x * kWarps + warp) * R;
+    const bool active = row0 < a.w.rows;
+    // The last group starts R rows before the end instead of reading past it
+    // (it recomputes rows of the previous group and stores only its own).
+    // The launcher sends matrices of fewer than R rows elsewhere.
+    const int base_row = min(row0, a.w.rows - R);
+    const int shift_rows = row0 - base_row;
+    const unsigned char* q0 = a.w.qs + (long long)base_row * a.w.qs_row;
+    const unsigned char* m0 = a.w.meta + (long long)base_row * a.w.meta_row;
+    constexpr int kAhead = 2;  // units of weight loads in flight per lane
+    uint4 ring[kAhead][R];
+    // weight loads first: they are in flight while x is staged
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j) {
+        const int u = lane + 32 * j;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            ring[j][r] = active && u < units ? ld_stream(q0 + r * a.w.qs_row + (long long)u * 16) : make_uint4(0, 0, 0, 0);
+    }
+    float* S = reinterpret_cast<float*>(gemv_xt + F4 * units);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < F4; ++j) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(a.x + (long long)u * E) + j);
+            gemv_xt[j * units + u] = v;
+            sum += (v.x + v.y) + (v.z + v.w);
+        }
+        S[u] = sum;
+    }
+    __syncthreads();
+    if (!active) return;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int u0 = lane; u0 < units; u0 += 32 * kAhead) {
+#pragma unroll
+        for (int j = 0; j < kAhead; ++j) {
+            const int u = u0 + 32 * j;
+            if (u >= units) break;
+            uint4 cur[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) cur[r] = ring[j][r];
+            const int un = u + 32 * kAhead;
+            if (un < units) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) ring[j][r] = ld_stream(q0 + r * a.w.qs_row + (long long)un * 16);
+            }
+            rows_unit_dot_t<TYPE>(cur, gemv_xt, units, S[u], u, m0, a.w.meta_row, acc);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    if (lane == 0) {
+        // results for rows base_row + r; this group owns rows row0.. (r >= shift_rows)
+        if (a.epilogue == kSwiGLU) {
+#pragma unroll
+            for (int r = 0; r + 1 < R; r += 2)
+                if (r >= shift_rows && base_row + r + 1 < a.w.rows)
+                    a.y[(base_row + r) / 2] = swiglu(acc[r], acc[r + 1]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (r < shift_rows || base_row + r >= a.w.rows) continue;
+                if (a.epilogue == kAdd) a.y[base_row + r] += acc[r];
+                else a.y[base_row + r] = acc[r];
+            }
+        }
+    }
+}
+
 template <int TYPE, int R, int NT>
 void run_gemv(const GemmArgs& a, cudaStream_t s) {
     constexpr int E = Unit<TYPE>::kElems;
@@ -469,9 +734,20 @@ void run_gemv(const GemmArgs& a, cudaStream_t s) {
 
 template <int TYPE>
 void dispatch_tokens(const GemmArgs& a, cudaStream_t s) {
-    if (a.tokens <= 1) run_gemv<TYPE, 4, 1>(a, s);
-    else if (a.tokens <= 2) run_gemv<TYPE, 4, 2>(a, s);
-    else run_gemv<TYPE, 2, 4>(a, s);
+    const std::size_t smem1 = std::size_t(a.w.cols) * 4 + std::size_t(a.w.cols / Unit<TYPE>::kElems) * 4;
+    if (a.tokens <= 1 && (reinterpret_cast<std::uintptr_t>(a.x) & 15) == 0 && a.w.rows >= kRows1 &&
+        smem1 <= 100 * 1024) {
+        const int rows_per_cta = kWarps * kRows1;
+        TVARA_CUDA(cudaFuncSetAttribute(gemv1_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
+        gemv1_kernel<TYPE><<<(a.w.rows + rows_per_cta - 1) / rows_per_cta, kWarps * 32, smem1, s>>>(a);
+        TVARA_LAUNCHED();
+    } else if (a.tokens <= 1) {
+        run_gemv<TYPE, 8, 1>(a, s);  // unaligned activations or < 4 rows: staged through shared memory
+    } else if (a.tokens <= 2) {
+        run_gemv<TYPE, 4, 2>(a, s);
+    } else {
+        run_gemv<TYPE, 4, 4>(a, s);
+    }
 }
 
 __global__ void to_half_kernel(const float* x, int ldx, __half* out, int tokens, int cols) {
