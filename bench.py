@@ -249,7 +249,7 @@ def run_reference(args):
     else:
         line.update({"value": res["value"], "cpu_baseline": res,
                      "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
-    print(json.dumps(line))
+    emit(line)
 
 
 def standalone_gemv(lib, hbm_gbs):
@@ -511,16 +511,33 @@ def run_ours(args):
         "cpu_baseline": cpu,
     }
     if rank == 0:
-        print(json.dumps(line))
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
 
+_RESULT = None  # the original stdout, kept for the one result line
+
+
+def emit(line: dict) -> None:
+    """Writes the result JSON line to the process's original stdout."""
+    out = _RESULT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _RESULT
     args = parse()
     if args.cpu_worker:
         cpu_worker(args.cpu_worker)
         return
+    # Libraries (NCCL's version banner, warnings) may print to stdout; the
+    # contract is ONE JSON line there, so fd 1 is pointed at stderr and the
+    # result goes to a duplicate of the original stdout.
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:

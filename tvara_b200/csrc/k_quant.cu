@@ -662,6 +662,13 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
         for (int r = 0; r < R; ++r)
             ring[j][r] = active && u < units ? ld_stream(q0 + r * a.w.qs_row + (long long)u * 16) : make_uint4(0, 0, 0, 0);
     }
+    // Programmatic dependent launch: the weights above do not depend on the
+    // previous kernel, x does.  Let the next kernel start its own prefetch
+    // (it launches once every CTA of this grid has reached this point), then
+    // wait for the previous kernel's results before reading x.  Both are
+    // no-ops for an ordinary launch.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float* S = reinterpret_cast<float*>(gemv_xt + F4 * units);
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
         float sum = 0.f;
@@ -683,15 +690,13 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
         for (int j = 0; j < kAhead; ++j) {
             const int u = u0 + 32 * j;
             if (u >= units) break;
-            uint4 cur[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) cur[r] = ring[j][r];
+            // compute from the slot, then refill it (the other slots stay in flight)
+            rows_unit_dot_t<TYPE>(ring[j], gemv_xt, units, S[u], u, m0, a.w.meta_row, acc);
             const int un = u + 32 * kAhead;
             if (un < units) {
 #pragma unroll
                 for (int r = 0; r < R; ++r) ring[j][r] = ld_stream(q0 + r * a.w.qs_row + (long long)un * 16);
             }
-            rows_unit_dot_t<TYPE>(cur, gemv_xt, units, S[u], u, m0, a.w.meta_row, acc);
         }
     }
 #pragma unroll
@@ -739,7 +744,17 @@ void dispatch_tokens(const GemmArgs& a, cudaStream_t s) {
         smem1 <= 100 * 1024) {
         const int rows_per_cta = kWarps * kRows1;
         TVARA_CUDA(cudaFuncSetAttribute(gemv1_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
-        gemv1_kernel<TYPE><<<(a.w.rows + rows_per_cta - 1) / rows_per_cta, kWarps * 32, smem1, s>>>(a);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((a.w.rows + rows_per_cta - 1) / rows_per_cta);
+        cfg.blockDim = dim3(kWarps * 32);
+        cfg.dynamicSmemBytes = smem1;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        TVARA_CUDA(cudaLaunchKernelEx(&cfg, gemv1_kernel<TYPE>, a));
         TVARA_LAUNCHED();
     } else if (a.tokens <= 1) {
         run_gemv<TYPE, 8, 1>(a, s);  // unaligned activations or < 4 rows: staged through shared memory
