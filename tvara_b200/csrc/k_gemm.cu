@@ -484,6 +484,205 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant for prebuilt weight planes: one CTA per SM walks the
+// tiles b, b + G, b + 2G, ... (token tiles of a row tile adjacent).  Warp 9
+// issues the TMA loads of A (planes) and B (activations) through one stage
+// ring that runs on across tile boundaries, warp 8 issues the MMAs into one
+// of two TMEM accumulators (2 x 256 columns), and warps 0-7 run the epilogue
+// of tile i while the MMAs of tile i+1 proceed -- the epilogue and the
+// pipeline fill of each tile are hidden.
+constexpr int kPersistThreads = 320;
+constexpr int kEpilogueWarps = 8;
+constexpr int kMmaWarpP = 8;
+constexpr int kTmaWarpP = 9;
+
+struct TileSpace {
+    int token_tiles, row_tiles, splits, n_tiles;
+};
+
+__device__ __forceinline__ void tile_coords(const TileSpace& ts, int t, int n_tile, int k_steps, int& row0, int& tok0,
+                                            int& kstep0) {
+    const int tt = t % ts.token_tiles;
+    const int rest = t / ts.token_tiles;
+    row0 = (rest % ts.row_tiles) * kBM;
+    tok0 = tt * n_tile;
+    kstep0 = (rest / ts.row_tiles) * k_steps;
+}
+
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                           const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                           TcArgs a, TileSpace ts) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int b_bytes = a.n_tile * kBK * 2;
+    const int stage_bytes = 2 * kATile + 2 * kBTileMax;
+    unsigned char* stages = base;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(base + kStages * stage_bytes);  // TMA bytes landed
+    std::uint64_t* empty = full + kStages;       // MMA finished reading the stage
+    std::uint64_t* acc_full = empty + kStages;   // [2] accumulator ready for the epilogue
+    std::uint64_t* acc_empty = acc_full + 2;     // [2] epilogue finished reading it
+    unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kEpilogueWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarpP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp == kTmaWarpP) {
+        // ---------------- TMA producer (lane 0 issues; the warp stays converged)
+        unsigned tma_issued = 0, tma_phase = 0;
+        int q = 0;  // K-steps issued by this CTA (stage ring position)
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            for (int ks = 0; ks < a.k_steps; ++ks, ++q) {
+                int ok = 1;
+                if (lane == 0) {
+                    const int s = q % kStages;
+                    const unsigned ph = (q / kStages) & 1;
+                    const int k0 = (kstep0 + ks) * kBK;
+                    ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                    if (ok) {
+                        unsigned char* st = stages + s * stage_bytes;
+                        const unsigned bar = smem_u32(&full[s]);
+                        mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
+                        tma_load_2d(smem_u32(st), &map_ahi, k0, row0, bar);
+                        tma_load_2d(smem_u32(st + kATile), &map_alo, k0, row0, bar);
+                        tma_load_2d(smem_u32(st + 2 * kATile), &map_hi, k0, tok0, bar);
+                        tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_lo, k0, tok0, bar);
+                        tma_issued |= 1u << s;
+                        tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    go = false;
+                    break;
+                }
+            }
+        }
+        // every copy issued must have landed before the CTA leaves
+        if (lane == 0)
+            for (int s = 0; s < kStages; ++s)
+                if (tma_issued >> s & 1u)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full[s], (tma_phase >> s) & 1u); ++i) {
+                    }
+    } else if (warp == kMmaWarpP) {
+        // ---------------- MMA issuer (lane 0)
+        if (lane == 0) {
+            int q = 0, i = 0;
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x, ++i) {
+                const int b = i & 1;
+                if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, abort_flag, a.err, 15, false)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const unsigned acc = tmem + unsigned(b * 256);
+                for (int ks = 0; ks < a.k_steps; ++ks, ++q) {
+                    const int s = q % kStages;
+                    const unsigned ph = (q / kStages) & 1;
+                    if (!mbar_wait(&full[s], ph, abort_flag, a.err, 13, false)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    unsigned char* st = stages + s * stage_bytes;
+                    const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+                    const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;  // 16 K of FP16 = 32 B
+                        mma_f16(acc, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
+                        mma_f16(acc, ahi + adv, blo + adv, a.idesc, 1);
+                        mma_f16(acc, alo + adv, bhi + adv, a.idesc, 1);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (go) mma_commit(&acc_full[b]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 0-7): TMEM lane r = weight row row0 + r;
+        // warps w and w+4 share lanes 32*(w%4).. and split the token columns
+        const int r = threadIdx.x % kBM;
+        const int hf = threadIdx.x / kBM;
+        int i = 0;
+        for (int t = blockIdx.x; t < ts.n_tiles; t += gridDim.x, ++i) {
+            const int b = i & 1;
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (i >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const long long row = row0 + r;
+            const bool live = row < a.w.rows;
+            const float wscale = pow2(live ? -a.w.row_shift[row] : 0);
+            for (int c0 = hf * 32; c0 < a.n_tile; c0 += 64) {
+                unsigned u[32];
+                const unsigned taddr = tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + c0);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                      "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                      "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                      "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                      "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int tk = tok0 + c0 + j;
+                    if (c0 + j >= a.n_tile) break;
+                    float val = 0.f;
+                    if (tk < a.tokens) val = __uint_as_float(u[j]) * wscale * pow2(-a.x_shift[tk]);
+                    if (a.epilogue == kSwiGLU) {
+                        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+                        if (tk < a.tokens && live && !(r & 1))
+                            a.y[(long long)tk * a.ldy + row / 2] = swiglu(val, partner);
+                    } else if (tk < a.tokens && live) {
+                        float* dst = a.y + (long long)tk * a.ldy + row;
+                        if (a.atomic) atomicAdd(dst, val);
+                        else if (a.epilogue == kAdd) *dst += val;
+                        else *dst = val;
+                    }
+                }
+            }
+            // this warp is done with the accumulator: release it to the MMA warp
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == kMmaWarpP) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
 // that puts max|x| in [2^14, 2^15), then the exact split (split.cuh).  One
 // block per token; float4 loads and 8-byte stores (K % 4 == 0, rows 16-byte
@@ -549,6 +748,7 @@ void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const CUtensorMap& ahi
 }
 
 int g_tc_min_tokens = 5;  // below this the CUDA-core GEMV streams weights once per <=4 tokens
+bool g_tc_persistent = true;  // plane path: persistent kernel (else one CTA per tile)
 
 int sm_count() {
     int dev = 0, n = 0;
@@ -640,7 +840,15 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     if (g.w.plane_hi && g.w.plane_lo) {
         const CUtensorMap pa = make_map(reinterpret_cast<const __half*>(g.w.plane_hi), K, g.w.rows, kBM);
         const CUtensorMap pb = make_map(reinterpret_cast<const __half*>(g.w.plane_lo), K, g.w.rows, kBM);
-        run_tc<kPlanes>(mh, ml, pa, pb, a, grid, s);
+        if (g_tc_persistent) {
+            TileSpace ts{token_tiles, row_tiles, splits, token_tiles * row_tiles * splits};
+            const int smem = kStages * (2 * kATile + 2 * kBTileMax) + 1024 + 256;
+            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            tc_gemm_persist_kernel<<<std::min(ts.n_tiles, sm_count()), kPersistThreads, smem, s>>>(mh, ml, pa, pb, a, ts);
+            TVARA_LAUNCHED();
+        } else {
+            run_tc<kPlanes>(mh, ml, pa, pb, a, grid, s);
+        }
         return;
     }
     switch (g.w.type) {

@@ -690,13 +690,17 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
         for (int j = 0; j < kAhead; ++j) {
             const int u = u0 + 32 * j;
             if (u >= units) break;
-            // compute from the slot, then refill it (the other slots stay in flight)
-            rows_unit_dot_t<TYPE>(ring[j], gemv_xt, units, S[u], u, m0, a.w.meta_row, acc);
+            // refill the slot before computing on its old contents, so the
+            // next load is in flight during this unit's arithmetic
+            uint4 cur[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) cur[r] = ring[j][r];
             const int un = u + 32 * kAhead;
             if (un < units) {
 #pragma unroll
                 for (int r = 0; r < R; ++r) ring[j][r] = ld_stream(q0 + r * a.w.qs_row + (long long)un * 16);
             }
+            rows_unit_dot_t<TYPE>(cur, gemv_xt, units, S[u], u, m0, a.w.meta_row, acc);
         }
     }
 #pragma unroll
