@@ -348,9 +348,11 @@ void Engine::load(const gguf::File& f) {
     TVARA_CUDA(cudaHostAlloc(&err_host_, sizeof(int), cudaHostAllocDefault));
 }
 
-void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi) {
+void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi,
+                        bool presplit) {
     GemmArgs a;
     a.w = w;
+    a.presplit = presplit;
     a.x = x;
     a.ldx = ldx;
     a.tokens = tokens;
@@ -597,16 +599,30 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         launch_block_copy(kv_, block_stride_ * es, d_copy, int(s.copies.size()), stream_);
         launch_embed(embed_, d_tok, T, x_, D, stream_);
     });
+    // RMSNorm whose every consumer takes the tensor-core path also writes
+    // their split input (one kernel instead of a norm and a split per
+    // projection); the F32 output is written in every case.
+    auto norm = [&](const float* w, const int* rows, int n, const std::vector<const DeviceMatrix*>& consumers) {
+        bool tc = tc_ws_ != nullptr;
+        for (const auto* m : consumers) tc = tc && gemm_tc_supported(*m, n);
+        if (tc) launch_rmsnorm_split(x_, D, rows, n, D, w, cfg_.eps, xn_, D, tc_ws_, tc_ws_bytes_, stream_);
+        else launch_rmsnorm(x_, D, rows, n, D, w, cfg_.eps, xn_, D, stream_);
+        return tc;
+    };
     for (int l = 0; l < layers_; ++l) {
         const auto& L = lw_[l];
-        timed(kProfOther, [&] { launch_rmsnorm(x_, D, nullptr, T, D, L.attn_norm, cfg_.eps, xn_, D, stream_); });
+        std::vector<const DeviceMatrix*> qkv_in, gu_in;
+        for (const auto& m : L.qkv) qkv_in.push_back(&m);
+        for (const auto& m : L.gateup) gu_in.push_back(&m);
+        bool split = false;
+        timed(kProfOther, [&] { split = norm(L.attn_norm, nullptr, T, qkv_in); });
         timed(kProfProjection, [&] {
             if (L.qkv.size() == 1) {
-                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
+                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore, split);
             } else {
-                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore);
-                projection(L.qkv[1], xn_, D, T, qkv_ + hq_ * d, qkv_w_, kStore);
-                projection(L.qkv[2], xn_, D, T, qkv_ + (hq_ + hkv_) * d, qkv_w_, kStore);
+                projection(L.qkv[0], xn_, D, T, qkv_, qkv_w_, kStore, split);
+                projection(L.qkv[1], xn_, D, T, qkv_ + hq_ * d, qkv_w_, kStore, split);
+                projection(L.qkv[2], xn_, D, T, qkv_ + (hq_ + hkv_) * d, qkv_w_, kStore, split);
             }
         });
         RopeArgs ra;
@@ -659,13 +675,13 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         // the others store theirs, so the sum over ranks is x + sum(partials).
         timed(kProfProjection, [&] { projection(L.o, att_, hq_ * d, T, x_, D, lead ? kAdd : kStore); });
         if (coll_) timed(kProfCollective, [&] { coll_->allreduce_sum(x_, std::size_t(T) * D, stream_); });
-        timed(kProfOther, [&] { launch_rmsnorm(x_, D, nullptr, T, D, L.ffn_norm, cfg_.eps, xn_, D, stream_); });
+        timed(kProfOther, [&] { split = norm(L.ffn_norm, nullptr, T, gu_in); });
         timed(kProfProjection, [&] {
             if (L.gateup.size() == 1) {
-                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kSwiGLU);
+                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kSwiGLU, split);
             } else {
-                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kStore);
-                projection(L.gateup[1], xn_, D, T, ffu_, ffn_, kStore);
+                projection(L.gateup[0], xn_, D, T, ff_, ffn_, kStore, split);
+                projection(L.gateup[1], xn_, D, T, ffu_, ffn_, kStore, split);
                 launch_swiglu(ff_, ffu_, T * ffn_, stream_);
             }
         });
@@ -674,8 +690,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     }
     if (R > 0) {
         timed(kProfHead, [&] {
-            launch_rmsnorm(x_, D, d_rows, R, D, final_norm_, cfg_.eps, xn_, D, stream_);
-            projection(head_, xn_, D, R, logits_, vocab_, kStore);
+            const bool hsplit = norm(final_norm_, d_rows, R, {&head_});
+            projection(head_, xn_, D, R, logits_, vocab_, kStore, hsplit);
             if (argmax) launch_argmax(logits_, R, vocab_, argmax_, finite_argmax_, stream_);
         });
     }

@@ -121,7 +121,9 @@ private:
     DeviceMatrix upload_matrix(const gguf::File& f, const std::string& name, int row0, int rows, int col0, int cols,
                                std::uint8_t*& cursor);
     void run(Sub& sub, float* logits, std::uint32_t* argmax, std::size_t vocab_rows_total);
-    void projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi);
+    // presplit: the tensor-core input is already in the workspace (launch_rmsnorm_split)
+    void projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi,
+                    bool presplit = false);
 
     gguf::LlamaConfig cfg_;
     EngineOptions opt_;

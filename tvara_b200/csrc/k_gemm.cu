@@ -802,19 +802,30 @@ std::size_t gemm_tc_workspace(int max_tokens, int max_cols) {
            std::size_t((max_tokens + 63) / 64 * 64 + 64) * sizeof(int) + 1024;
 }
 
+void gemm_tc_split_buffers(void* workspace, std::size_t workspace_bytes, int tokens, int cols, __half*& hi,
+                           __half*& lo, int*& shift) {
+    if (!workspace || workspace_bytes < gemm_tc_workspace(tokens, cols))
+        throw std::invalid_argument("tensor-core projection workspace too small");
+    hi = static_cast<__half*>(workspace);
+    lo = hi + std::size_t(tokens) * cols;
+    shift = reinterpret_cast<int*>(lo + std::size_t(tokens) * cols);
+}
+
 void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_bytes, cudaStream_t s) {
     const int T = g.tokens, K = g.w.cols;
     if (!workspace || workspace_bytes < gemm_tc_workspace(T, K))
         throw std::invalid_argument("tensor-core projection workspace too small");
-    auto* hi = static_cast<__half*>(workspace);
-    __half* lo = hi + std::size_t(T) * K;
-    int* shift = reinterpret_cast<int*>(lo + std::size_t(T) * K);
+    __half *hi = nullptr, *lo = nullptr;
+    int* shift = nullptr;
+    gemm_tc_split_buffers(workspace, workspace_bytes, T, K, hi, lo, shift);
     // callers without an error flag get one in the workspace (never null)
     int* err = g.err ? g.err : shift + ((T + 63) / 64) * 64;
-    if (reinterpret_cast<std::uintptr_t>(g.x) % 16 || g.ldx % 4 || K % 4)
-        throw std::invalid_argument("tensor-core projection input must be 16-byte aligned rows");
-    split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
-    TVARA_LAUNCHED();
+    if (!g.presplit) {
+        if (reinterpret_cast<std::uintptr_t>(g.x) % 16 || g.ldx % 4 || K % 4)
+            throw std::invalid_argument("tensor-core projection input must be 16-byte aligned rows");
+        split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
+        TVARA_LAUNCHED();
+    }
 
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;

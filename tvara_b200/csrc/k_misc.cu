@@ -1,40 +1,85 @@
 // RMSNorm, RoPE + paged-KV write, argmax and block copies.
 #include <cfloat>
 
+#include <cstdint>
+#include <stdexcept>
+
 #include "kernels.cuh"
+#include "split.cuh"
 
 namespace tvara {
 namespace {
 
 // RMSNorm of core/include/tvara/model.hpp:57-65: sum of squares in double,
 // inverse = float(1/sqrt(sum/n + eps)), out = (x*inverse)*w rounded twice.
-template <bool HALF>
-__global__ void rmsnorm_kernel(const float* x, int ldx, const int* rows, int dim, const float* w, float eps,
-                               float* out, int ldo, __half* outh) {
+// One CTA (256 threads) per row;
+// the row is loaded once as float4 and kept in registers (V per thread) for
+// the output pass.  With SPLIT the normalised row is also written as the
+// exact hi/lo FP16 split with its per-row power-of-two scale (max |v| in
+// [2^14, 2^15)) -- the tensor-core projection's input format.
+template <int V, bool SPLIT>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ldx, const int* rows, int dim, const float* w,
+                                                      float eps, float* out, int ldo, __half* hi, __half* lo,
+                                                      int* shift) {
     const int i = blockIdx.x;
     const long long r = rows ? rows[i] : i;
-    const float* xr = x + r * ldx;
+    const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
+    const int n4 = dim / 4;
+    float4 v[V];
     double s = 0.0;
-    for (int k = threadIdx.x; k < dim; k += blockDim.x) {
-        const double v = xr[k];
-        s += v * v;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int k = threadIdx.x + j * 256;
+        v[j] = k < n4 ? xr[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += double(v[j].x) * v[j].x + double(v[j].y) * v[j].y + double(v[j].z) * v[j].z + double(v[j].w) * v[j].w;
     }
-    __shared__ double part[32];
+    __shared__ double part[8];
+    __shared__ float pmax[8];
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        double v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0;
-        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) part[0] = v;
+    double tot = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += part[k];
+    const float inv = float(1.0 / sqrt(tot / double(dim) + double(eps)));
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int k = threadIdx.x + j * 256;
+        if (k < n4) {
+            const float4 g = w4[k];
+            v[j] = make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), g.x), __fmul_rn(__fmul_rn(v[j].y, inv), g.y),
+                               __fmul_rn(__fmul_rn(v[j].z, inv), g.z), __fmul_rn(__fmul_rn(v[j].w, inv), g.w));
+            if (out) reinterpret_cast<float4*>(out + (long long)i * ldo)[k] = v[j];
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+        }
     }
-    __syncthreads();
-    const float inv = float(1.0 / sqrt(part[0] / double(dim) + double(eps)));
-    float* o = out + (long long)i * ldo;
-    for (int k = threadIdx.x; k < dim; k += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(xr[k], inv), w[k]);
-        o[k] = v;
-        if (HALF) outh[(long long)i * dim + k] = __float2half_rn(v);
+    if constexpr (SPLIT) {
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0) pmax[threadIdx.x >> 5] = m;
+        __syncthreads();
+        float mx = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx = fmaxf(mx, pmax[k]);
+        int e = 0;
+        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);
+        const int sh = mx > 0.f ? max(-100, min(100, 15 - e)) : 0;
+        if (threadIdx.x == 0) shift[i] = sh;
+        const float f = __uint_as_float(unsigned(127 + sh) << 23);
+        uint2* hrow = reinterpret_cast<uint2*>(hi + (long long)i * dim);
+        uint2* lrow = reinterpret_cast<uint2*>(lo + (long long)i * dim);
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int k = threadIdx.x + j * 256;
+            if (k < n4) {
+                uint2 h, l;
+                split_exact(v[j].x * f, v[j].y * f, h.x, l.x);
+                split_exact(v[j].z * f, v[j].w * f, h.y, l.y);
+                hrow[k] = h;
+                lrow[k] = l;
+            }
+        }
     }
 }
 
@@ -167,18 +212,40 @@ __global__ void block_copy_kernel(uint4* kv, long long block_vec, const int2* pa
 
 }  // namespace
 
-void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
-                    int ldo, cudaStream_t s) {
+namespace {
+template <bool SPLIT>
+void run_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
+                 int ldo, __half* hi, __half* lo, int* shift, cudaStream_t s) {
     if (n <= 0) return;
-    rmsnorm_kernel<false><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, nullptr);
+    if (dim % 4 || (reinterpret_cast<std::uintptr_t>(x) & 15) || ldx % 4 || (out && ((reinterpret_cast<std::uintptr_t>(out) & 15) || ldo % 4)))
+        throw std::invalid_argument("RMSNorm rows must be 16-byte aligned");
+    const int v = (dim / 4 + 255) / 256;
+    switch (v) {
+        case 1: rmsnorm_kernel<1, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 2: rmsnorm_kernel<2, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 3:
+        case 4: rmsnorm_kernel<4, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 5:
+        case 6:
+        case 7:
+        case 8: rmsnorm_kernel<8, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        default: throw std::invalid_argument("RMSNorm width above 8192");
+    }
     TVARA_LAUNCHED();
 }
+}  // namespace
 
-void launch_rmsnorm_h(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
-                      int ldo, __half* outh, cudaStream_t s) {
-    if (n <= 0) return;
-    rmsnorm_kernel<true><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, outh);
-    TVARA_LAUNCHED();
+void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
+                    int ldo, cudaStream_t s) {
+    run_rmsnorm<false>(x, ldx, rows, n, dim, w, eps, out, ldo, nullptr, nullptr, nullptr, s);
+}
+
+void launch_rmsnorm_split(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
+                          float* out, int ldo, void* tc_workspace, std::size_t tc_workspace_bytes, cudaStream_t s) {
+    __half *hi = nullptr, *lo = nullptr;
+    int* shift = nullptr;
+    gemm_tc_split_buffers(tc_workspace, tc_workspace_bytes, n, dim, hi, lo, shift);
+    run_rmsnorm<true>(x, ldx, rows, n, dim, w, eps, out, ldo, hi, lo, shift, s);
 }
 
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {

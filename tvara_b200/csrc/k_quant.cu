@@ -769,14 +769,6 @@ void dispatch_tokens(const GemmArgs& a, cudaStream_t s) {
     }
 }
 
-__global__ void to_half_kernel(const float* x, int ldx, __half* out, int tokens, int cols) {
-    const long long total = (long long)tokens * cols;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const long long t = i / cols, k = i % cols;
-        out[i] = __float2half_rn(x[t * ldx + k]);
-    }
-}
-
 }  // namespace
 
 void launch_gemv(const GemmArgs& a, cudaStream_t s) {
@@ -790,13 +782,6 @@ void launch_gemv(const GemmArgs& a, cudaStream_t s) {
         case kF32: dispatch_tokens<kF32>(a, s); break;
         default: throw std::invalid_argument("unsupported projection type");
     }
-}
-
-void launch_to_half(const float* x, int ldx, __half* out, int tokens, int cols, cudaStream_t s) {
-    const long long total = (long long)tokens * cols;
-    const int grid = int(std::min<long long>((total + 255) / 256, 148 * 16));
-    to_half_kernel<<<grid, 256, 0, s>>>(x, ldx, out, tokens, cols);
-    TVARA_LAUNCHED();
 }
 
 void launch_dequantize(int type, const void* blocks, std::size_t nblocks, float* out, cudaStream_t s) {

@@ -18,7 +18,7 @@ struct GemmArgs {
     DeviceMatrix w;
     const float* x = nullptr;   // [tokens][ldx] F32 activations
     int ldx = 0;
-    const __half* xh = nullptr; // optional F16 copy of x for the tensor-core path
+    bool presplit = false;      // tensor-core path: x already split into the workspace (launch_rmsnorm_split)
     int tokens = 0;
     float* y = nullptr;         // [tokens][ldy]
     int ldy = 0;
@@ -33,8 +33,10 @@ void launch_gemv(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const DeviceMatrix& w, int tokens);
 void launch_gemm_tc(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s);
 std::size_t gemm_tc_workspace(int max_tokens, int max_cols);
-// x [tokens][cols] F32 -> F16 copy (feeds the tensor-core path).
-void launch_to_half(const float* x, int ldx, __half* out, int tokens, int cols, cudaStream_t s);
+// Where the tensor-core path keeps the split activations of `tokens` rows of
+// width `cols` in its workspace (hi, lo FP16 [tokens][cols], per-row shift).
+void gemm_tc_split_buffers(void* workspace, std::size_t workspace_bytes, int tokens, int cols, __half*& hi,
+                           __half*& lo, int*& shift);
 // Choose and run the projection (GEMV below the crossover, tensor cores above).
 void launch_projection(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s);
 
@@ -60,9 +62,11 @@ void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, i
 // out[i] = (x[rows[i]] * inv_rms) * w ; rows == nullptr means i.
 void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
                     float* out, int ldo, cudaStream_t s);
-// (Combined with launch_rmsnorm) also emits an F16 copy for the tensor-core path.
-void launch_rmsnorm_h(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
-                      float* out, int ldo, __half* outh, cudaStream_t s);
+// launch_rmsnorm that also writes the output's exact hi/lo split into the
+// tensor-core workspace (then a projection with presplit skips its split);
+// out may be null.
+void launch_rmsnorm_split(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
+                          float* out, int ldo, void* tc_workspace, std::size_t tc_workspace_bytes, cudaStream_t s);
 
 struct RopeArgs {
     const float* qkv = nullptr;  // [T][ldqkv]: q (hq*d) | k (hkv*d) | v (hkv*d)
