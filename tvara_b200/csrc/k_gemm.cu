@@ -2,9 +2,10 @@
 // (tcgen05.mma, accumulators in TMEM, activations fed by TMA).
 //
 // D[w_row][token] = sum_k W[w_row][k] * X[token][k] for a tile of 128 weight
-// rows (the MMA's M) and up to 256 tokens (N).  Quantised rows are
-// dequantised by eight producer warps straight into the UMMA shared-memory
-// layout.  Precision: the reference multiplies F32 weights by F32 activations
+// rows (the MMA's M) and up to 256 tokens (N).  The weight operand comes from
+// exact FP16 planes built at load, or from packed rows dequantised by
+// producer warps into the UMMA shared-memory layout.
+// Precision: the reference multiplies F32 weights by F32 activations
 // (core/include/tvara/quant.hpp:163-169); a single FP16 rounding of either
 // operand costs ~5e-4 relative per product, which measurably exceeds the 2e-3
 // logit budget on deep models.  So both operands are split exactly into
@@ -13,15 +14,20 @@
 // K-step issues three MMAs, hi*hi + hi*lo + lo*hi, accumulating in F32 --
 // products carry ~2^-22 relative error.
 //
-// Warp roles (288 threads): warps 0-7 produce A -- thread (r, h) converts
-// weight row r, K-half h of every step, keeping several steps of packed
-// weights in flight in a register ring; two producer warps per scheduler
-// hide each other's dependency stalls -- and then run the epilogue (TMEM
-// lane == weight row; warps w and w+4 split the token columns); warp 8
-// allocates TMEM and one of its threads issues the MMAs.  X tiles arrive by
-// per-CTA TMA loads of this GPU's own memory.  Every mbarrier wait is bounded: on timeout the kernel
-// records an error code, waits (bounded) for its own TMA copies, frees TMEM
-// and exits.
+// Two kernels share the tile, the stage layout and the epilogue:
+// * tc_gemm_persist_kernel (weights with prebuilt FP16 planes, the engine's
+//   batched path): persistent, warp-specialised -- a TMA warp streams A
+//   (planes) and B (split activations) through the stage ring across tile
+//   boundaries, an MMA warp accumulates into one of two TMEM buffers, eight
+//   epilogue warps drain the other;
+// * tc_gemm_kernel (packed weights, the kernel-level ABI): one CTA per tile;
+//   warps 0-7 produce A -- thread (r, h) converts weight row r, K-half h of
+//   every step from a register ring of packed blocks -- then run the
+//   epilogue; warp 8 allocates TMEM and issues the MMAs.
+// Epilogue: TMEM lane == weight row; warps w and w+4 split the token columns.
+// All TMA loads are per-CTA loads of this GPU's own memory.  Every mbarrier
+// wait is bounded: on timeout the kernel records an error code, waits
+// (bounded) for its own TMA copies, frees TMEM and exits.
 #include <mutex>
 
 #include "kernels.cuh"
