@@ -159,6 +159,30 @@ def test_ragged_batch_step_matches_oracle(tiny, oracle_tiny):
     tiny.kv_audit()
 
 
+@pytest.mark.parametrize("types", [dict(default=gguf.Q4_K, ffn_down=gguf.Q4_K, output=gguf.Q8_0),
+                                   dict(default=gguf.Q4_0, ffn_down=gguf.Q8_0, output=gguf.Q4_0)],
+                         ids=["q4k", "q40_q80"])
+def test_wide_decode_matches_oracle(model_dir, types):
+    """Single-token decode steps of a model wide enough (hidden 1024, ffn
+    2816) for the streamed GEMV: every projection -- QKV, O with the residual
+    add, gate/up with SwiGLU, down, the LM head -- runs at one token."""
+    from oracle.model import OracleModel
+    cfg = gguf.model_config("tiny", hidden=1024, heads=8, kv_heads=2, ffn=2816, layers=2, tied=False,
+                            types=dict(types, embd=gguf.Q8_0))
+    path = make_model(model_dir, "wide_" + "_".join(str(v) for v in types.values()), cfg, seed=5)
+    ref = OracleModel(path, max_positions=64)
+    state = ref.new_state()
+    rng = np.random.default_rng(4)
+    with NativeModel(path, max_blocks=8, block_tokens=16) as m:
+        seq = m._new_sequence()
+        tok = int(rng.integers(0, 512))
+        for _ in range(5):
+            logits, am = m.batch_step([seq], [[tok]], argmax=True)
+            want = ref.decode(state, tok)
+            assert close(logits[0], want)
+            tok = int(am[0])
+
+
 def test_fork_copy_on_write(tiny, oracle_tiny):
     """kv.hpp fork + copy-on-write of a shared partial tail block: both
     branches keep their own continuation."""

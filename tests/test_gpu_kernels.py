@@ -88,10 +88,14 @@ def matmul(capi, kind, buf, rows, cols, x):
 
 
 def oracle_matmul(kind, raw, rows, cols, x):
+    """Reference product and the error scale of the single-token integer
+    path: sum |x||w| (float rounding) plus sum_j |w_j| 2^-22 max|x| over
+    x_j's 32-element block (its fixed-point rounding of x)."""
     from oracle.oracle import dequantize
     w = dequantize(kind, raw, rows * cols).reshape(rows, cols).astype(np.float64)
     x64 = x.astype(np.float64)
-    return (x64 @ w.T), np.abs(x64) @ np.abs(w.T)
+    blk = np.repeat(np.abs(x64).reshape(x.shape[0], -1, 32).max(axis=2), 32, axis=1)
+    return (x64 @ w.T), np.abs(x64) @ np.abs(w.T) + (blk @ np.abs(w.T)) * 2.0 ** -22 / 2e-5
 
 
 def make_weights(kind, rows, cols, rng):
@@ -110,6 +114,22 @@ def test_quant_matmul_matches_oracle(capi, kind, tokens):
     got = matmul(capi, kind, packed(capi, kind, raw, rows, cols), rows, cols, x)
     ref, mag = oracle_matmul(kind, raw, rows, cols, x)
     assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6)
+
+
+@pytest.mark.parametrize("kind", [gguf.Q4_K, gguf.Q8_0, gguf.Q4_0])
+@pytest.mark.parametrize("rows,cols", [(1, 4096), (203, 1024), (33, 2816), (77, 14336)])
+def test_streamed_gemv_matches_oracle(capi, kind, rows, cols):
+    """Single-token GEMV on the streamed path (K a multiple of 256): one row,
+    a partial last row group, a K tail chunk shorter than the stage (2816 =
+    11 x 256) and a wide K; activations spanning 1e-3..30 per element with a
+    few large outliers, which the per-unit fixed-point scale must absorb."""
+    rng = np.random.default_rng(rows * 7 + cols + kind)
+    raw = make_weights(kind, rows, cols, rng)
+    x = (rng.standard_normal((1, cols)) * rng.uniform(1e-3, 30, (1, cols))).astype(np.float32)
+    x[0, rng.choice(cols, 4, replace=False)] = [1e3, -2e3, 5e-4, 0.0]
+    got = matmul(capi, kind, packed(capi, kind, raw, rows, cols), rows, cols, x)
+    ref, mag = oracle_matmul(kind, raw, rows, cols, x)
+    assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
 
 
 @pytest.mark.parametrize("kind", TYPES)

@@ -637,6 +637,163 @@ __device__ __forceinline__ void rows_unit_dot_t(const uint4 (&wv)[kRows1], const
     }
 }
 
+// Integer path of the quantised formats (streamed GEMV).  Each unit of the
+// token's x is held as 22-bit fixed point against the unit's own max:
+// x_int = rint(x * 2^sh) with max |x| * 2^sh in [2^21, 2^22), so each x is
+// rounded by at most 2^-22 of its unit's max |x| (the reference's own
+// quantised dot products, quant.hpp:87-161, round x to 8 bits per block).  Its two's-complement bytes are the digits, x_int = b0 + 256 b1 +
+// 65536 b2 with b0, b1 unsigned and b2 = x_int >> 16 signed (|b2| <= 64), so
+// no carries need fixing.  Digit words hold one byte position of four
+// consecutive elements: d[k][w] = digit k of elements 16w..16w+15.  The codes
+// of a weight word (four int8, or eight nibbles as two masked words) meet the
+// digit words in dp4a, three per four codes; the partial sums stay below
+// 2^20, so (S0 + 256 S1 + 65536 S2) * 2^-sh is sum(q * x) to float rounding,
+// and the block scale is applied once per unit.  A lane keeps the digits of
+// the units it works on in registers for the whole launch.
+__device__ __forceinline__ float small_int_to_float(int v) {  // exact for |v| < 2^22
+    return __int_as_float(v + 0x4B400000) - 12582912.f;
+}
+__device__ __forceinline__ int dp4a_uu(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+template <int TYPE>
+struct XUnit {
+    static constexpr int kW4 = Unit<TYPE>::kElems / 16;
+    uint4 d[3][kW4];  // digit words (see above)
+    float S;          // sum of the unit's x
+    float inv;        // 2^-sh
+};
+
+// One unit of x in the form above.  A unit whose max |x| is inf or NaN gets
+// inv = NaN, so its products come out NaN.
+template <int TYPE>
+__device__ __forceinline__ void load_xunit(const float* x, int u, XUnit<TYPE>& xu) {
+    constexpr int E = Unit<TYPE>::kElems, F4 = E / 4, W4 = E / 16;
+    float4 v[F4];
+    float sum = 0.f, mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < F4; ++j) {
+        v[j] = __ldg(reinterpret_cast<const float4*>(x + (long long)u * E) + j);
+        sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    }
+    // mx = m * 2^e with m in [0.5, 1); zero and subnormal units take the clamp
+    const int e = int((__float_as_uint(mx) >> 23) & 255u) - 126;
+    const int sh = min(126, 22 - e);  // e <= 128: 2^sh and 2^-sh stay normal
+    const bool fin = mx <= 3.4028235e38f;  // false for inf and NaN
+    const float up = fin ? __uint_as_float(unsigned(127 + sh) << 23) : 0.f;
+    xu.S = sum;
+    xu.inv = fin ? __uint_as_float(unsigned(127 - sh) << 23) : mx - mx;
+#pragma unroll
+    for (int w = 0; w < W4; ++w) {
+        unsigned b[3][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 f = v[w * 4 + q];
+            // round to nearest integer through the 1.5 * 2^23 magic (|x * 2^sh| <= 2^22)
+            const unsigned i0 = __float_as_uint(fmaf(f.x, up, 12582912.f)) - 0x4B400000u;
+            const unsigned i1 = __float_as_uint(fmaf(f.y, up, 12582912.f)) - 0x4B400000u;
+            const unsigned i2 = __float_as_uint(fmaf(f.z, up, 12582912.f)) - 0x4B400000u;
+            const unsigned i3 = __float_as_uint(fmaf(f.w, up, 12582912.f)) - 0x4B400000u;
+            const unsigned lo01 = __byte_perm(i0, i1, 0x5140);  // i0.b0 i1.b0 i0.b1 i1.b1
+            const unsigned lo23 = __byte_perm(i2, i3, 0x5140);
+            const unsigned hi01 = __byte_perm(i0, i1, 0x0062);  // i0.b2 i1.b2 . .
+            const unsigned hi23 = __byte_perm(i2, i3, 0x0062);
+            b[0][q] = __byte_perm(lo01, lo23, 0x5410);
+            b[1][q] = __byte_perm(lo01, lo23, 0x7632);
+            b[2][q] = __byte_perm(hi01, hi23, 0x5410);
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) xu.d[k][w] = make_uint4(b[k][0], b[k][1], b[k][2], b[k][3]);
+    }
+}
+
+// Q4_K scale and min of sub-block g from the three scale words, with the
+// shifts and masks fixed per lane (a lane always sees the same g).
+struct Q4kSel {
+    unsigned sh, sh2, ma, mb;
+    bool hi;
+    __device__ __forceinline__ explicit Q4kSel(int g) {
+        hi = g >= 4;
+        sh = 8u * unsigned(g & 3);
+        sh2 = sh + 2u;
+        ma = hi ? 15u : 63u;
+        mb = hi ? 0x30u : 0u;
+    }
+    // sub-blocks 0-3: (y & 63, z & 63); 4-7: (w & 15 | (y >> 6) << 4, w >> 4 | (z >> 6) << 4)
+    __device__ __forceinline__ void decode(unsigned y, unsigned z, unsigned w, float& sc, float& mn) const {
+        const unsigned a = ((hi ? w : y) >> sh) & ma;
+        const unsigned b = ((hi ? (w >> 4) : z) >> sh) & ma;
+        sc = __uint_as_float(a | ((y >> sh2) & mb) | 0x4B000000u) - 8388608.f;
+        mn = __uint_as_float(b | ((z >> sh2) & mb) | 0x4B000000u) - 8388608.f;
+    }
+};
+
+// acc[r] += row r's unit (codes wv[r], block headers at meta0 + r * meta_row,
+// unit mu of them) . x unit xu.
+template <int TYPE>
+__device__ __forceinline__ void rows_unit_dot_x(const uint4 (&wv)[kRows1], const XUnit<TYPE>& xu,
+                                                const unsigned char* meta0, int meta_row, int mu, const Q4kSel& sel,
+                                                float (&acc)[kRows1]) {
+    auto word = [](const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; };
+#pragma unroll
+    for (int r = 0; r < kRows1; ++r) {
+        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const unsigned w = word(wv[r], i);
+            if constexpr (TYPE == kQ8_0) {
+                // elements 4i..4i+3: digit word i of the unit's 16
+                s0 = dp4a_su(w, word(xu.d[0][0], i), s0);
+                s1 = dp4a_su(w, word(xu.d[1][0], i), s1);
+                s2 = dp4a_ss(w, word(xu.d[2][0], i), s2);
+            } else {
+                // low nibbles: elements 4i..4i+3 (digit word i of 0..15);
+                // high nibbles: elements 16+4i.. (digit word i of 16..31)
+                const unsigned lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                s0 = dp4a_uu(lo, word(xu.d[0][0], i), dp4a_uu(hi, word(xu.d[0][1], i), s0));
+                s1 = dp4a_uu(lo, word(xu.d[1][0], i), dp4a_uu(hi, word(xu.d[1][1], i), s1));
+                s2 = dp4a_us(lo, word(xu.d[2][0], i), dp4a_us(hi, word(xu.d[2][1], i), s2));
+            }
+        }
+        // sum(q * x) = (S0 + 256 (S1 + 256 S2)) * 2^-sh (S1 + 256 S2 < 2^26: one
+        // rounding in its conversion, S0 converts exactly)
+        const float A = fmaf(256.f, float(s1 + 256 * s2), small_int_to_float(s0)) * xu.inv;
+        const unsigned char* meta = meta0 + r * meta_row;
+        if constexpr (TYPE == kQ8_0) {
+            acc[r] = fmaf(h2f(reinterpret_cast<const unsigned short*>(meta)[mu >> 1]), A, acc[r]);
+        } else if constexpr (TYPE == kQ4_0) {
+            const float d = h2f(reinterpret_cast<const unsigned short*>(meta)[mu]);
+            acc[r] = fmaf(d, fmaf(-8.f, xu.S, A), acc[r]);
+        } else {
+            const uint4 m = reinterpret_cast<const uint4*>(meta)[mu >> 3];
+            const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xffff)));
+            const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
+            float sc, mn;
+            sel.decode(m.y, m.z, m.w, sc, mn);
+            acc[r] = fmaf(d * sc, A, fmaf(-dmin * mn, xu.S, acc[r]));
+        }
+    }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
     constexpr int R = kRows1, E = Unit<TYPE>::kElems, F4 = E / 4;
@@ -725,6 +882,201 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
     }
 }
 
+// ------------------------------------------------------------ streamed GEMV
+// Single-token projection of a quantised matrix with the weights streamed
+// through shared memory.  A copy warp moves each stage -- the codes and block
+// headers of RG rows over KCU units of K -- with cp.async.bulk (one copy per
+// row and array) onto the stage's mbarrier, kStreamStages stages ahead,
+// starting before the wait on the previous kernel since the weights do not
+// depend on it.  Eight consumer warps compute from shared memory: a lane owns
+// one unit position of the stage for a set of four rows, so it sees the same
+// CH units of x (one per K chunk) in every row group and keeps their digits
+// in registers for the whole launch.  RG = 1024 / KCU rows per stage (16 KB
+// of codes); the grid is persistent and takes row groups in turn.  Every wait
+// is bounded; on a timeout the kernel records an error, stops issuing copies,
+// keeps its barriers in step, waits (bounded) for the copies it issued and
+// exits.
+constexpr int kStreamWarps = 8;                          // consumer warps
+constexpr int kStreamThreads = (kStreamWarps + 1) * 32;  // + the copy warp
+constexpr int kStreamSlots = kStreamWarps * 32;          // (unit, 4-row set) slots per stage
+constexpr int kStreamStages = 4;
+constexpr int kStreamQs = kStreamSlots * 4 * 16;         // 16 KB of codes per stage
+constexpr int kStreamMeta = kStreamSlots * 4 * 2;        // block headers: <= 2 bytes per unit
+constexpr unsigned kStreamSpin = 1u << 24;
+
+__device__ int g_gemv_stream_err;  // error word when the caller passed none
+
+struct StreamShape {
+    int kcu;     // units per row per stage: a power of two in [32, 256]
+    int rg;      // rows per group (1024 / kcu)
+    int chunks;  // stages per row group
+    int groups;  // row groups
+};
+
+__device__ __forceinline__ unsigned sh_addr(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void sb_init(std::uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sh_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void sb_arrive(std::uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sh_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void sb_expect(std::uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sh_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool sb_try(std::uint64_t* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(sh_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void sb_copy(void* dst, const void* src, unsigned bytes, std::uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sh_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(sh_addr(bar))
+                 : "memory");
+}
+// Bounded wait: false on timeout (the error code is recorded and the abort
+// flag set) or, when abort_flag is given, once another warp has given up.
+__device__ __forceinline__ bool sb_wait(std::uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err,
+                                        int code) {
+    for (unsigned i = 0; i < kStreamSpin; ++i) {
+        if (sb_try(bar, parity)) return true;
+        if (abort_flag && *abort_flag) return false;
+        if (i > 16) __nanosleep(64);
+    }
+    if (abort_flag) *abort_flag = 1;
+    atomicExch(err, code);
+    return false;
+}
+
+template <int TYPE, int CH>
+__global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs a, StreamShape sp) {
+    constexpr int E = Unit<TYPE>::kElems;
+    constexpr int MPU = TYPE == kQ8_0 ? 1 : 2;  // block-header bytes per unit
+    // [stages][16 KB] codes, then [stages][2 KB] headers
+    extern __shared__ __align__(16) unsigned char stream_smem[];
+    unsigned char* st_qs = stream_smem;
+    unsigned char* st_meta = stream_smem + kStreamStages * kStreamQs;
+    __shared__ std::uint64_t full[kStreamStages], empty[kStreamStages];
+    __shared__ float red[2][kStreamWarps][4];
+    __shared__ int abort_word;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = a.w.cols / E;
+    int* err = a.err ? a.err : &g_gemv_stream_err;
+    volatile int* abort_flag = &abort_word;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStreamStages; ++i) {
+            sb_init(&full[i], 1);
+            sb_init(&empty[i], kStreamWarps);
+        }
+        abort_word = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == kStreamWarps) {  // copy warp
+        int it = 0;
+        for (int g = blockIdx.x; g < sp.groups; g += gridDim.x) {
+            const int row0 = g * sp.rg;
+            const int nr = min(sp.rg, a.w.rows - row0);
+            bool ok = true;
+            for (int c = 0; c < sp.chunks; ++c) {
+                const int st = it % kStreamStages;
+                const unsigned ph = (unsigned(it) / kStreamStages) & 1u;
+                int go = lane == 0 ? int(sb_wait(&empty[st], ph ^ 1u, abort_flag, err, 21)) : 0;
+                go = __shfl_sync(0xffffffffu, go, 0);
+                if (!go) {
+                    ok = false;
+                    break;
+                }
+                const int cu = min(sp.kcu, units - c * sp.kcu);
+                if (lane == 0) sb_expect(&full[st], unsigned(nr * cu * (16 + MPU)));
+                __syncwarp();
+                if (lane < nr) {
+                    const long long row = row0 + lane;
+                    sb_copy(st_qs + st * kStreamQs + lane * sp.kcu * 16,
+                            a.w.qs + row * (long long)a.w.qs_row + (long long)c * sp.kcu * 16, unsigned(cu * 16),
+                            &full[st]);
+                    sb_copy(st_meta + st * kStreamMeta + lane * sp.kcu * MPU,
+                            a.w.meta + row * (long long)a.w.meta_row + (long long)c * sp.kcu * MPU, unsigned(cu * MPU),
+                            &full[st]);
+                }
+                ++it;
+            }
+            if (!ok) break;
+        }
+        // the copies issued land before the CTA exits (bounded, even after an abort)
+        if (lane == 0)
+            for (int j = max(0, it - kStreamStages); j < it; ++j)
+                sb_wait(&full[j % kStreamStages], (unsigned(j) / kStreamStages) & 1u, nullptr, err, 22);
+        return;
+    }
+
+    // consumer warps: x depends on the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int ul = threadIdx.x & (sp.kcu - 1);  // unit within the stage
+    const int rs = threadIdx.x / sp.kcu;        // 4-row set within the group (one per warp or warp range)
+    const int wpr = sp.kcu / 32;                // warps per 4-row set
+    XUnit<TYPE> xu[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+        if (c * sp.kcu + ul < units) load_xunit<TYPE>(a.x, c * sp.kcu + ul, xu[c]);
+    const Q4kSel sel(ul & 7);  // stage offsets are multiples of 8 units
+    int it = 0, gi = 0;
+    for (int g = blockIdx.x; g < sp.groups; g += gridDim.x, ++gi) {
+        float acc[kRows1] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < CH; ++c, ++it) {
+            const int st = it % kStreamStages;
+            const unsigned ph = (unsigned(it) / kStreamStages) & 1u;
+            // after an abort the warps keep the same steps (no early exit) so
+            // every barrier below is still reached by all of them
+            if (!*abort_flag) sb_wait(&full[st], ph, abort_flag, err, 23);
+            if (c * sp.kcu + ul < units) {
+                const unsigned char* q = st_qs + st * kStreamQs + (rs * 4 * sp.kcu + ul) * 16;
+                uint4 wv[kRows1];
+#pragma unroll
+                for (int r = 0; r < kRows1; ++r) wv[r] = *reinterpret_cast<const uint4*>(q + r * sp.kcu * 16);
+                rows_unit_dot_x<TYPE>(wv, xu[c], st_meta + st * kStreamMeta + rs * 4 * sp.kcu * MPU, sp.kcu * MPU,
+                                      ul, sel, acc);
+            }
+            __syncwarp();
+            if (lane == 0) sb_arrive(&empty[st]);
+        }
+#pragma unroll
+        for (int r = 0; r < kRows1; ++r)
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < kRows1; ++r) red[gi & 1][warp][r] = acc[r];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kStreamSlots) : "memory");
+        if (warp == 0) {
+            // lane = row within the group; red is double-buffered by group, so
+            // the next group's partial sums do not overwrite these
+            float v = 0.f;
+            if (lane < sp.rg)
+                for (int w = 0; w < wpr; ++w) v += red[gi & 1][(lane >> 2) * wpr + w][lane & 3];
+            const float partner = __shfl_down_sync(0xffffffffu, v, 1);
+            const int row = g * sp.rg + lane;
+            if (lane < sp.rg && row < a.w.rows) {
+                if (a.epilogue == kSwiGLU) {
+                    if (!(lane & 1)) a.y[row / 2] = swiglu(v, partner);
+                } else if (a.epilogue == kAdd) {
+                    a.y[row] += v;
+                } else {
+                    a.y[row] = v;
+                }
+            }
+        }
+    }
+}
+
 template <int TYPE, int R, int NT>
 void run_gemv(const GemmArgs& a, cudaStream_t s) {
     constexpr int E = Unit<TYPE>::kElems;
@@ -741,9 +1093,76 @@ void run_gemv(const GemmArgs& a, cudaStream_t s) {
     TVARA_LAUNCHED();
 }
 
+int gemv_sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+    if (dev < 64 && cached[dev]) return cached[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev < 64) cached[dev] = n;
+    return n;
+}
+
+template <int TYPE, int CH>
+bool launch_gemv_stream_ch(const GemmArgs& a, const StreamShape& sp, cudaStream_t s) {
+    auto kernel = gemv_stream_kernel<TYPE, CH>;
+    constexpr int smem = kStreamStages * (kStreamQs + kStreamMeta);
+    // a per-device attribute: set on every launch
+    TVARA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    static const int per_sm = [&] {  // resident CTAs per SM (the same on every B200)
+        int n = 0;
+        TVARA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kStreamThreads, smem));
+        return n > 0 ? n : 1;
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(sp.groups, gemv_sm_count() * per_sm));
+    cfg.blockDim = dim3(kStreamThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TVARA_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, sp));
+    TVARA_LAUNCHED();
+    return true;
+}
+
+// Streamed single-token GEMV for the integer formats when the rows allow
+// 16-byte bulk copies of whole units and headers (K a multiple of 256, at
+// least 32 units per row); false when the caller should use another kernel.
+template <int TYPE>
+bool launch_gemv_stream(const GemmArgs& a, cudaStream_t s) {
+    constexpr int E = Unit<TYPE>::kElems;
+    const int units = a.w.cols / E;
+    if (a.tokens != 1 || a.w.cols % 256 || units < 32 || a.w.rows < 1) return false;
+    if ((reinterpret_cast<std::uintptr_t>(a.x) | reinterpret_cast<std::uintptr_t>(a.w.qs) |
+         reinterpret_cast<std::uintptr_t>(a.w.meta) | a.w.qs_row | a.w.meta_row) & 15)
+        return false;
+    StreamShape sp;
+    sp.kcu = 32;
+    while (sp.kcu < 256 && sp.kcu * 2 <= units) sp.kcu *= 2;
+    sp.rg = 1024 / sp.kcu;
+    sp.chunks = (units + sp.kcu - 1) / sp.kcu;
+    sp.groups = (a.w.rows + sp.rg - 1) / sp.rg;
+    // x units held per lane: up to 2 (4-bit formats) or 4 (Q8_0) chunks of K
+    switch (sp.chunks) {
+        case 1: return launch_gemv_stream_ch<TYPE, 1>(a, sp, s);
+        case 2: return launch_gemv_stream_ch<TYPE, 2>(a, sp, s);
+        case 3: return TYPE == kQ8_0 && launch_gemv_stream_ch<TYPE, TYPE == kQ8_0 ? 3 : 1>(a, sp, s);
+        case 4: return TYPE == kQ8_0 && launch_gemv_stream_ch<TYPE, TYPE == kQ8_0 ? 4 : 1>(a, sp, s);
+    }
+    return false;
+}
+
 template <int TYPE>
 void dispatch_tokens(const GemmArgs& a, cudaStream_t s) {
     const std::size_t smem1 = std::size_t(a.w.cols) * 4 + std::size_t(a.w.cols / Unit<TYPE>::kElems) * 4;
+    if constexpr (TYPE == kQ4_0 || TYPE == kQ4_K || TYPE == kQ8_0) {
+        if (launch_gemv_stream<TYPE>(a, s)) return;
+    }
     if (a.tokens <= 1 && (reinterpret_cast<std::uintptr_t>(a.x) & 15) == 0 && a.w.rows >= kRows1 &&
         smem1 <= 100 * 1024) {
         const int rows_per_cta = kWarps * kRows1;
