@@ -78,6 +78,8 @@ def parse():
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-standalone", action="store_true", help="skip the standalone GEMV / matmul figures")
+    ap.add_argument("--standalone-only", action="store_true",
+                    help="only the standalone GEMV / matmul figures (one JSON line; used for kernel profiles)")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens the reference CPU engine decodes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model-dir", default=os.environ.get("TVARA_BENCH_DIR", "/tmp/tvara_bench"))
@@ -538,7 +540,10 @@ def main():
     sys.stdout.flush()
     _RESULT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
-    if args.impl == "reference":
+    if args.standalone_only:
+        from tvara_b200 import load_library
+        emit({"standalone_kernels": standalone_gemv(load_library(), peaks()[0]["hbm_gbs"])})
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -133,6 +133,45 @@ TVARA_API int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t*
                                const uint32_t* cu_tokens, const uint32_t* tokens, uint32_t flags, float* logits,
                                size_t count, uint32_t* argmax, size_t argmax_count);
 
+/* Device-side logit post-processing of a step (the sampler of
+ * python/tvara/native.py:301-336 up to its random draw; SURVEY's "next"
+ * row for cutting the full-vocabulary copy).  Per sequence, in float64 with
+ * the reference's numpy operations: repetition / frequency / presence
+ * penalties from the tokens already in the sequence (this step's included),
+ * then the token mask (token_masks.py:228-241: disallowed -> -inf).
+ * Arrays are indexed by the step's sequence order; NULL parameters take the
+ * neutral values 1, 0, 0 and NULL `allowed` allows every token. */
+typedef struct tvara_sampling {
+    size_t struct_size;          /* sizeof(tvara_sampling) */
+    const double* repetition;    /* [n_seq] > 0, or NULL */
+    const double* frequency;     /* [n_seq], or NULL */
+    const double* presence;      /* [n_seq], or NULL */
+    const uint32_t* allowed;     /* [n_seq][ceil(vocab/32)] bit t%32 of word t/32, or NULL */
+    uint32_t top_k;              /* candidates returned per sequence, 0..64 */
+} tvara_sampling;
+
+enum {
+    TVARA_SAMPLE_NONFINITE_LOGITS = 1,   /* "Nonfinite model logits" (native.py:304-305) */
+    TVARA_SAMPLE_NONFINITE_ADJUSTED = 2, /* "Nonfinite adjusted sampling logits" (native.py:312-313) */
+    TVARA_SAMPLE_NONE_ALLOWED = 4        /* "No grammar-valid tokens remain" (token_masks.py:237-238) */
+};
+
+/* tvara_batch_step (one row per sequence) followed by the post-processing
+ * above on the device.  Outputs (host, any may be NULL):
+ *   logits     F32 [n_seq][vocab] (count = n_seq*vocab) the rows before
+ *              post-processing, as tvara_batch_step returns them
+ *   argmax     [n_seq] first index of the maximum of the adjusted, masked
+ *              logits (np.argmax)
+ *   status     [n_seq] TVARA_SAMPLE_* bits of the reference's checks
+ *   top_values [n_seq][top_k] the top_k largest adjusted, masked logits,
+ *              value descending, ties by index
+ *   top_ids    [n_seq][top_k] their token ids
+ * Histories are limited to 16384 tokens.  0 / -1 (all-or-nothing). */
+TVARA_API int tvara_batch_sample(tvara_model* model, size_t n_seq, const uint64_t* sequences,
+                                 const uint32_t* cu_tokens, const uint32_t* tokens, const tvara_sampling* sampling,
+                                 float* logits, size_t count, uint32_t* argmax, int32_t* status,
+                                 double* top_values, uint32_t* top_ids);
+
 /* ---- additive: sequence management (core/include/tvara/kv.hpp) -------- */
 
 /* PagedCache::fork (kv.hpp:123-129): a new sequence sharing every block;

@@ -35,6 +35,24 @@ TVARA_API size_t tvara_packed_bytes(int type, size_t rows, size_t cols);
 /* GGUF rows (device) -> engine layout (device, tvara_packed_bytes long). */
 TVARA_API int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream);
 
+/* Logit post-processing on the device (the sampler of
+ * python/tvara/native.py:301-336 up to its random draw, for many rows):
+ * logits F32 [rows][vocab] (device); the token history of row r is
+ * history[history_offsets[r] .. history_offsets[r+1]) (history device,
+ * offsets host, at most 16384 tokens a row); per-row repetition / frequency /
+ * presence (host, NULL = 1, 0, 0); allowed (device [rows][ceil(vocab/32)]
+ * bitmask, NULL = all).  Outputs on the device: argmax [rows] of the
+ * adjusted, masked float64 logits, status [rows] (bit 1: non-finite model
+ * logits, 2: non-finite adjusted logits, 4: no allowed token), and the
+ * top_k (<= 64) largest values with their ids [rows][top_k] (value
+ * descending, ties by index).  `workspace` of tvara_sample_workspace bytes. */
+TVARA_API size_t tvara_sample_workspace(size_t rows, size_t max_history);
+TVARA_API int tvara_sample_logits(const float* logits, size_t rows, size_t vocab, const int32_t* history,
+                                  const uint64_t* history_offsets, const double* repetition, const double* frequency,
+                                  const double* presence, const uint32_t* allowed, uint32_t top_k, uint32_t* argmax,
+                                  int32_t* status, double* top_values, uint32_t* top_ids, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* Device scratch tvara_quant_matmul needs for `tokens` rows of width `cols`
  * (0 when the call runs on the CUDA-core path, at most 4 tokens). */
 TVARA_API size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens);

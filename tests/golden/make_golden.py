@@ -17,6 +17,13 @@ its seed, so only the reference's outputs are stored:
 * dequant.npz     -- random GGUF blocks of each type (including fp16 scale
                      bit patterns that are subnormal, inf and NaN) and the
                      reference's dequantised floats.
+* sampling.npz    -- tokens from the reference's own NativeModel.iter_tokens
+                     (python/tvara/native.py, over its C++ library in
+                     oracle/_ref) on the tiny model: greedy with repetition /
+                     frequency / presence penalties and an even-token
+                     constraint, and seeded temperature / top-k / min-p /
+                     top-p sampling with penalties.  Only this file:
+                     ``python tests/golden/make_golden.py sampling``.
 """
 
 from __future__ import annotations
@@ -33,6 +40,7 @@ sys.path.insert(0, str(ROOT))
 from tvara_b200 import gguf  # noqa: E402
 from oracle import oracle as O  # noqa: E402
 from oracle.model import RefEngine  # noqa: E402
+from tests.golden.sampling_cases import SAMPLING_CASES, EvenTokens  # noqa: E402
 
 TINY_PROMPT_SEED = 1
 MIXED = dict(rope="interleaved", types=dict(attn_q=gguf.Q4_K, attn_k=gguf.Q4_0, attn_v=gguf.F16,
@@ -68,8 +76,30 @@ def random_blocks(rng, kind, n):
     return raw
 
 
+def sampling_golden(tiny_path):
+    import os
+    sys.path.insert(0, "/root/reference/python")
+    from tvara.native import NativeModel as RefNativeModel
+    lib = ROOT / "oracle" / "_ref" / "libtvara_capi.so"
+    os.environ["TVARA_LIBRARY"] = str(lib)
+    prompt = [int(t) for t in tiny_prompt()[:24]]
+    out = {"prompt": np.array(prompt)}
+    with RefNativeModel(str(tiny_path), library=str(lib)) as model:
+        for name, case in SAMPLING_CASES.items():
+            kw = dict(case)
+            constraint = EvenTokens(model.vocab_size) if kw.pop("constraint", False) else None
+            toks = list(model.iter_tokens(prompt, max_new_tokens=32, token_constraint=constraint, **kw))
+            out[name] = np.array(toks)
+    np.savez_compressed(HERE / "sampling.npz", **out)
+
+
 def main():
     import tempfile
+    if sys.argv[1:] == ["sampling"]:
+        tmp = Path(tempfile.mkdtemp())
+        sampling_golden(gguf.make_llama(tmp / "tiny.gguf", "tiny", seed=0))
+        print("wrote sampling.npz")
+        return
     tmp = Path(tempfile.mkdtemp())
     tiny = gguf.make_llama(tmp / "tiny.gguf", "tiny", seed=0)
     ref = RefEngine(tiny)
@@ -95,6 +125,7 @@ def main():
         out[f"raw_{kind}"] = raw.reshape(-1)
         out[f"out_{kind}"] = vals.view(np.uint32)
     np.savez_compressed(HERE / "dequant.npz", **out)
+    sampling_golden(tiny)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

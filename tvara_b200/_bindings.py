@@ -35,6 +35,20 @@ class TpShardInfo(C.Structure):
 
 
 # name: (restype, argtypes)
+class Sampling(C.Structure):
+    """tvara_sampling: device-side logit post-processing of tvara_batch_sample."""
+    _fields_ = [
+        ("struct_size", C.c_size_t),
+        ("repetition", C.POINTER(C.c_double)),
+        ("frequency", C.POINTER(C.c_double)),
+        ("presence", C.POINTER(C.c_double)),
+        ("allowed", C.POINTER(C.c_uint32)),
+        ("top_k", C.c_uint32),
+    ]
+
+
+F64P = C.POINTER(C.c_double)
+
 SIGNATURES = {
     # reference ABI (core/include/tvara/c_api.h:13-24)
     "tvara_model_open": (P, [C.c_char_p, SZ, SZ]),
@@ -53,6 +67,8 @@ SIGNATURES = {
     "tvara_model_weight_bytes": (C.c_int, [P, SZP, SZP]),
     "tvara_tp_shard": (C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.POINTER(TpShardInfo)]),
     "tvara_batch_step": (C.c_int, [P, SZ, U64P, U32P, U32P, C.c_uint32, F32P, SZ, U32P, SZ]),
+    "tvara_batch_sample": (C.c_int, [P, SZ, U64P, U32P, U32P, C.POINTER(Sampling), F32P, SZ, U32P, I32P, F64P,
+                                     U32P]),
     "tvara_sequence_fork": (U64, [P, U64]),
     "tvara_sequence_length": (C.c_int, [P, U64, SZP]),
     "tvara_kv_stats": (C.c_int, [P, SZP, SZP]),
@@ -90,6 +106,9 @@ SIGNATURES = {
     "tvara_dequantize": (C.c_int, [C.c_int, P, SZ, P, P]),
     "tvara_packed_bytes": (SZ, [C.c_int, SZ, SZ]),
     "tvara_pack": (C.c_int, [C.c_int, P, SZ, SZ, P, P]),
+    "tvara_sample_workspace": (SZ, [SZ, SZ]),
+    "tvara_sample_logits": (C.c_int, [P, SZ, SZ, P, U64P, F64P, F64P, F64P, P, C.c_uint32, P, P, P, P, P, SZ,
+                                      P]),
     "tvara_quant_matmul_workspace": (SZ, [SZ, SZ]),
     "tvara_quant_matmul": (C.c_int, [C.c_int, P, SZ, SZ, P, SZ, P, P, SZ, P]),
     "tvara_paged_attention_workspace": (SZ, [P]),

@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstddef>
 #include <cstring>
 #include <limits>
@@ -240,6 +241,43 @@ int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t* sequences
         std::lock_guard lock(model->mutex);
         e.step({sequences, n_seq}, {cu_tokens, n_seq + 1}, {tokens, total}, all, logits, argmax,
                (flags & TVARA_STEP_FINITE_ARGMAX) != 0);
+        return 0;
+    });
+}
+
+int tvara_batch_sample(tvara_model* model, size_t n_seq, const uint64_t* sequences, const uint32_t* cu_tokens,
+                       const uint32_t* tokens, const tvara_sampling* sampling, float* logits, size_t count,
+                       uint32_t* argmax, int32_t* status, double* top_values, uint32_t* top_ids) {
+    return guarded<int>(-1, [&] {
+        if (!model || !n_seq || !sequences || !cu_tokens || !tokens) throw std::invalid_argument("invalid batch buffers");
+        if (!sampling || sampling->struct_size < sizeof(tvara_sampling))
+            throw std::invalid_argument("invalid sampling arguments");
+        if (sampling->top_k > tvara::kSampleMaxK) throw std::invalid_argument("top-k candidates must be between 0 and 64");
+        if (sampling->top_k && (!top_values || !top_ids)) throw std::invalid_argument("invalid top-k output buffers");
+        for (size_t i = 0; i < n_seq; ++i) {
+            const double r = sampling->repetition ? sampling->repetition[i] : 1.0;
+            const double f = sampling->frequency ? sampling->frequency[i] : 0.0;
+            const double p = sampling->presence ? sampling->presence[i] : 0.0;
+            if (!std::isfinite(r) || r <= 0 || !std::isfinite(f) || !std::isfinite(p))
+                throw std::invalid_argument("Invalid sampling filters or penalties");
+        }
+        const size_t total = cu_tokens[n_seq];
+        if (logits && (n_seq > std::numeric_limits<size_t>::max() / model->engine->config().vocab ||
+                       count != n_seq * model->engine->config().vocab))
+            throw std::invalid_argument("invalid logit output buffer");
+        tvara::SampleSpec spec;
+        spec.repetition = sampling->repetition;
+        spec.frequency = sampling->frequency;
+        spec.presence = sampling->presence;
+        spec.allowed = sampling->allowed;
+        spec.top_k = int(sampling->top_k);
+        spec.argmax = argmax;
+        spec.status = status;
+        spec.top_values = top_values;
+        spec.top_ids = top_ids;
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        e.step({sequences, n_seq}, {cu_tokens, n_seq + 1}, {tokens, total}, false, logits, nullptr, false, &spec);
         return 0;
     });
 }

@@ -116,8 +116,8 @@ Engine::~Engine() {
     for (auto e : events_) cudaEventDestroy(e);
     radix_.reset();
     coll_.reset();
-    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_,
-                    static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_})
+    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_, static_cast<void*>(token_ids_),
+                    static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_, sample_buf_})
         if (p) cudaFree(p);
     if (meta_host_) cudaFreeHost(meta_host_);
     if (err_host_) cudaFreeHost(err_host_);
@@ -315,6 +315,7 @@ void Engine::load(const gguf::File& f) {
     TVARA_CUDA(cudaMemGetInfo(&free_b, &total_b));
     if (pool_bytes > free_b) throw std::runtime_error("KV pool does not fit in device memory");
     TVARA_CUDA(cudaMalloc(&kv_, pool_bytes));
+    TVARA_CUDA(cudaMalloc(&token_ids_, g.max_blocks * g.tokens_per_block * sizeof(int)));
 
     // ---- scratch for tmax_ tokens (one allocation)
     const std::size_t T = tmax_;
@@ -365,9 +366,13 @@ void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int toke
 
 void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
                   std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax,
-                  bool finite_argmax) {
+                  bool finite_argmax, const SampleSpec* sample) {
     finite_argmax_ = finite_argmax;
+    sample_ = sample;
     const std::size_t n = seqs.size();
+    if (sample && all_logits) throw std::invalid_argument("device sampling takes one row per sequence");
+    if (sample && (sample->top_k < 0 || sample->top_k > kSampleMaxK || std::size_t(sample->top_k) > cfg_.vocab))
+        throw std::invalid_argument("top-k candidates must be between 0 and 64");
     if (!n || cu.size() != n + 1 || cu[0] != 0) throw std::invalid_argument("invalid batch layout");
     for (std::size_t i = 0; i < n; ++i)
         if (cu[i + 1] <= cu[i]) throw std::invalid_argument("invalid batch layout");
@@ -381,6 +386,8 @@ void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint
         entry[i] = book_->sequence(seqs[i]).length;
         const std::size_t count = cu[i + 1] - cu[i];
         if (entry[i] + count > cfg_.context) throw std::invalid_argument("paged decode exceeds token/context limits");
+        if (sample && entry[i] + count > kSampleHistoryMax)
+            throw std::invalid_argument("device sampling holds at most 16384 tokens of history");
         for (std::size_t j = cu[i]; j < cu[i + 1]; ++j)
             if (tokens[j] >= cfg_.vocab) throw std::invalid_argument("paged decode exceeds token/context limits");
     }
@@ -407,7 +414,7 @@ void Engine::step(std::span<const std::uint64_t> seqs, std::span<const std::uint
             int2* dev = nullptr;
             if (cudaMalloc(&dev, copies.size() * sizeof(int2)) == cudaSuccess) {
                 cudaMemcpy(dev, copies.data(), copies.size() * sizeof(int2), cudaMemcpyHostToDevice);
-                launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), dev, int(copies.size()), stream_);
+                copy_blocks(dev, int(copies.size()));
                 cudaStreamSynchronize(stream_);
                 cudaFree(dev);
             }
@@ -512,6 +519,11 @@ void Engine::profile_read(double* ms, unsigned long long* groups) const {
     }
 }
 
+void Engine::copy_blocks(const int2* pairs, int n) {
+    launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), pairs, n, stream_);
+    launch_id_copy(token_ids_, int(book_->geometry().tokens_per_block), pairs, n, stream_);
+}
+
 void Engine::reserve(std::uint64_t seq, std::size_t count) {
     const std::size_t entry = book_->sequence(seq).length;
     if (count > cfg_.context - entry) throw std::invalid_argument("paged decode exceeds token/context limits");
@@ -521,7 +533,7 @@ void Engine::reserve(std::uint64_t seq, std::size_t count) {
         int2* dev = nullptr;
         TVARA_CUDA(cudaMalloc(&dev, copies.size() * sizeof(int2)));
         TVARA_CUDA(cudaMemcpy(dev, copies.data(), copies.size() * sizeof(int2), cudaMemcpyHostToDevice));
-        launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), dev, int(copies.size()), stream_);
+        copy_blocks(dev, int(copies.size()));
         TVARA_CUDA(cudaStreamSynchronize(stream_));
         cudaFree(dev);
     };
@@ -537,6 +549,15 @@ void Engine::reserve(std::uint64_t seq, std::size_t count) {
         throw;
     }
     copy_now();
+    // reserved positions hold no token: id -1 (the sampler's history skips them)
+    const auto& t = book_->sequence(seq);
+    const std::size_t tpb = book_->geometry().tokens_per_block;
+    for (std::size_t p = entry; p < entry + count;) {
+        const std::size_t b = p / tpb, end = std::min(entry + count, (b + 1) * tpb);
+        TVARA_CUDA(cudaMemsetAsync(token_ids_ + t.blocks[b].id * tpb + p % tpb, 0xFF, (end - p) * sizeof(int), stream_));
+        p = end;
+    }
+    TVARA_CUDA(cudaStreamSynchronize(stream_));
 }
 
 void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
@@ -555,8 +576,40 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     auto& wpart = plan.part;
     // ---- pack metadata into one pinned buffer and upload
     const int R = int(s.out_rows.size());
+    // device sampler inputs per output row k (sequence s.out_dest[k])
+    const SampleSpec* sp = sample_;
+    const int words = int((vocab_ + 31) / 32);
+    std::vector<int> smp_hlen, smp_toff;
+    std::vector<double> smp_par;
+    int hist_cap = 1;
+    if (sp && R > 0) {
+        smp_hlen.resize(R);
+        smp_toff.resize(R);
+        smp_par.resize(std::size_t(R) * 3);
+        for (int k = 0; k < R; ++k) {
+            const int o = s.out_rows[k];
+            const auto i = s.out_dest[k];
+            smp_hlen[k] = s.pos[o] + 1;
+            smp_toff[k] = s.table_off[s.seq_of[o]];
+            smp_par[3 * k] = sp->repetition ? sp->repetition[i] : 1.0;
+            smp_par[3 * k + 1] = sp->frequency ? sp->frequency[i] : 0.0;
+            smp_par[3 * k + 2] = sp->presence ? sp->presence[i] : 0.0;
+            while (hist_cap < smp_hlen[k]) hist_cap <<= 1;
+        }
+        const int K = sp->top_k;
+        const std::size_t bytes = std::size_t(R) * (4 + std::size_t(K) * 12) + std::size_t(R) * hist_cap * 8 + 256;
+        if (bytes > sample_cap_) {
+            TVARA_CUDA(cudaStreamSynchronize(stream_));
+            if (sample_buf_) cudaFree(sample_buf_);
+            sample_buf_ = nullptr;
+            sample_cap_ = 0;
+            TVARA_CUDA(cudaMalloc(&sample_buf_, bytes * 2));
+            sample_cap_ = bytes * 2;
+        }
+    }
     const std::size_t need = std::size_t(T) * 4 + s.tables.size() + work.size() * 5 + comb.size() * 4 +
-                             s.copies.size() * 2 + R + 64;
+                             s.copies.size() * 2 + R + 64 +
+                             (sp ? std::size_t(R) * (8 + (sp->allowed ? words : 0)) + 16 : 0);
     if (need > meta_cap_) {
         TVARA_CUDA(cudaStreamSynchronize(stream_));
         if (meta_dev_) cudaFree(meta_dev_);
@@ -585,6 +638,22 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     int4* d_comb = reinterpret_cast<int4*>(put(comb.data(), comb.size() * 4));
     int2* d_copy = reinterpret_cast<int2*>(put(s.copies.data(), s.copies.size() * 2));
     int* d_rows = put(s.out_rows.data(), R);
+    int *d_hlen = nullptr, *d_toff = nullptr;
+    const double* d_par = nullptr;
+    const unsigned* d_allow = nullptr;
+    if (sp && R > 0) {
+        d_hlen = put(smp_hlen.data(), R);
+        d_toff = put(smp_toff.data(), R);
+        d_par = reinterpret_cast<const double*>(put(smp_par.data(), std::size_t(R) * 6));
+        if (sp->allowed) {
+            at = (at + 3) & ~std::size_t(3);
+            for (int k = 0; k < R; ++k)
+                std::memcpy(meta_host_ + at + std::size_t(k) * words, sp->allowed + std::size_t(s.out_dest[k]) * words,
+                            std::size_t(words) * 4);
+            d_allow = reinterpret_cast<const unsigned*>(meta_dev_ + at);
+            at += std::size_t(R) * words;
+        }
+    }
     if (profiling_ && host_idle_valid_) {
         prof_ms_[kProfHost] +=
             std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - host_idle_since_).count();
@@ -593,11 +662,11 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     TVARA_CUDA(cudaMemcpyAsync(meta_dev_, meta_host_, at * 4, cudaMemcpyHostToDevice, stream_));
     acc_h2d_ += at * 4;
 
-    const std::size_t es = opt_.kv_f16 ? 2 : 4;
     event_used_ = 0;
     timed(kProfOther, [&] {
-        launch_block_copy(kv_, block_stride_ * es, d_copy, int(s.copies.size()), stream_);
-        launch_embed(embed_, d_tok, T, x_, D, stream_);
+        copy_blocks(d_copy, int(s.copies.size()));
+        launch_embed(embed_, d_tok, T, x_, D, stream_, token_ids_, d_blk, d_slot,
+                     int(book_->geometry().tokens_per_block));
     });
     // RMSNorm whose every consumer takes the tensor-core path also writes
     // their split input (one kernel instead of a norm and a split per
@@ -693,15 +762,58 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
             const bool hsplit = norm(final_norm_, d_rows, R, {&head_});
             projection(head_, xn_, D, R, logits_, vocab_, kStore, hsplit);
             if (argmax) launch_argmax(logits_, R, vocab_, argmax_, finite_argmax_, stream_);
+            if (sp) {
+                SampleJob job;
+                job.logits = logits_;
+                job.ld = vocab_;
+                job.rows = R;
+                job.vocab = vocab_;
+                job.ids = token_ids_;
+                job.tables = d_tables;
+                job.toff = d_toff;
+                job.tpb = int(book_->geometry().tokens_per_block);
+                job.hlen = d_hlen;
+                job.hist_cap = hist_cap;
+                job.params = d_par;
+                job.allowed = d_allow;
+                job.words = words;
+                job.top_k = sp->top_k;
+                auto* b = static_cast<unsigned char*>(sample_buf_);
+                job.pen = reinterpret_cast<double*>(b);
+                job.pen_stride = hist_cap;
+                b += std::size_t(R) * hist_cap * 8;
+                job.top_val = reinterpret_cast<double*>(b);
+                b += std::size_t(R) * sp->top_k * 8;
+                job.status = reinterpret_cast<int*>(b);
+                b += std::size_t(R) * 4;
+                job.top_id = reinterpret_cast<unsigned*>(b);
+                job.argmax = argmax_;
+                launch_sample(job, stream_);
+            }
         });
     }
     TVARA_CUDA(cudaMemcpyAsync(err_host_, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     // ---- results to the caller: contiguous destination runs, one copy each
     acc_d2h_ += sizeof(int);
-    std::vector<unsigned> am(argmax ? R : 0);
-    if (argmax && R) {
+    std::vector<unsigned> am(argmax || sp ? R : 0);
+    if ((argmax || sp) && R) {
         TVARA_CUDA(cudaMemcpyAsync(am.data(), argmax_, R * 4, cudaMemcpyDeviceToHost, stream_));
         acc_d2h_ += std::uint64_t(R) * 4;
+    }
+    const int K = sp ? sp->top_k : 0;
+    std::vector<int> st(sp ? R : 0);
+    std::vector<double> tv(std::size_t(R) * K);
+    std::vector<unsigned> ti(std::size_t(R) * K);
+    if (sp && R) {
+        const auto* b = static_cast<const unsigned char*>(sample_buf_) + std::size_t(R) * hist_cap * 8;
+        if (K) {
+            TVARA_CUDA(cudaMemcpyAsync(tv.data(), b, tv.size() * 8, cudaMemcpyDeviceToHost, stream_));
+            TVARA_CUDA(cudaMemcpyAsync(ti.data(), b + std::size_t(R) * K * 8 + std::size_t(R) * 4, ti.size() * 4,
+                                       cudaMemcpyDeviceToHost, stream_));
+        }
+        TVARA_CUDA(cudaMemcpyAsync(st.data(), b + std::size_t(R) * K * 8, std::size_t(R) * 4, cudaMemcpyDeviceToHost,
+                                   stream_));
+        acc_d2h_ += std::uint64_t(R) * (4 + std::uint64_t(K) * 12);
     }
     if (logits) acc_d2h_ += std::uint64_t(R) * vocab_ * 4;
     if (logits) {
@@ -725,6 +837,16 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     }
     if (argmax)
         for (int k = 0; k < R; ++k) argmax[s.out_dest[k]] = am[k];
+    if (sp)
+        for (int k = 0; k < R; ++k) {
+            const auto i = s.out_dest[k];
+            if (sp->argmax) sp->argmax[i] = am[k];
+            if (sp->status) sp->status[i] = st[k];
+            for (int c = 0; c < K; ++c) {
+                if (sp->top_values) sp->top_values[i * K + c] = tv[std::size_t(k) * K + c];
+                if (sp->top_ids) sp->top_ids[i * K + c] = ti[std::size_t(k) * K + c];
+            }
+        }
 }
 
 }  // namespace tvara

@@ -34,6 +34,21 @@ struct EngineOptions {
 
 class Collective;  // NCCL communicator of a tensor-parallel group (collective.cpp)
 
+// Device-side logit post-processing of a step's rows (k_sample.cu); all
+// arrays are host memory indexed by the step's sequence order.
+struct SampleSpec {
+    const double* repetition = nullptr;   // null: 1
+    const double* frequency = nullptr;    // null: 0
+    const double* presence = nullptr;     // null: 0
+    const std::uint32_t* allowed = nullptr;  // [n][ceil(vocab / 32)] or null
+    int top_k = 0;
+    std::uint32_t* argmax = nullptr;      // [n]
+    std::int32_t* status = nullptr;       // [n]
+    double* top_values = nullptr;         // [n][top_k]
+    std::uint32_t* top_ids = nullptr;     // [n][top_k]
+};
+constexpr std::size_t kSampleHistoryMax = 16384;  // tokens of history the device sampler holds per row
+
 struct LayerWeights {
     const float* attn_norm = nullptr;
     const float* ffn_norm = nullptr;
@@ -61,7 +76,7 @@ public:
     // whose logits are not all finite with argmax 0xFFFFFFFF.
     void step(std::span<const std::uint64_t> seqs, std::span<const std::uint32_t> cu,
               std::span<const std::uint32_t> tokens, bool all_logits, float* logits, std::uint32_t* argmax,
-              bool finite_argmax = false);
+              bool finite_argmax = false, const SampleSpec* sample = nullptr);
 
     // Appends positions to a sequence's table without computing K/V.
     void reserve(std::uint64_t seq, std::size_t count);
@@ -150,12 +165,20 @@ private:
     float* rope_sin_ = nullptr;
     void* kv_ = nullptr;
     long long block_stride_ = 0, layer_stride_ = 0, kind_stride_ = 0;
+    // Token id of every KV slot, [block][slot]: the history the device-side
+    // sampler reads through a sequence's block table.
+    int* token_ids_ = nullptr;
+    // Copies blocks (KV payload and token ids) on the engine stream.
+    void copy_blocks(const int2* pairs, int n);
 
     int tmax_ = 0;
     float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ff_ = nullptr,
           *ffu_ = nullptr, *logits_ = nullptr, *partial_ = nullptr, *xo_ = nullptr;
     unsigned* argmax_ = nullptr;
     bool finite_argmax_ = false;
+    const SampleSpec* sample_ = nullptr;  // during a sampling step
+    void* sample_buf_ = nullptr;          // status, top-k and penalty scratch of the sampler
+    std::size_t sample_cap_ = 0;
     int* err_ = nullptr;
     void* tc_ws_ = nullptr;        // tensor-core projection: hi/lo FP16 activations + token scales
     std::size_t tc_ws_bytes_ = 0;

@@ -202,6 +202,13 @@ __global__ void swiglu_kernel(float* g, const float* u, long long n) {
     }
 }
 
+// Token ids of copied blocks (any block size).
+__global__ void id_copy_kernel(int* ids, int per_block, const int2* pairs) {
+    const int2 p = pairs[blockIdx.x];
+    for (int i = threadIdx.x; i < per_block; i += blockDim.x)
+        ids[(long long)p.y * per_block + i] = ids[(long long)p.x * per_block + i];
+}
+
 __global__ void block_copy_kernel(uint4* kv, long long block_vec, const int2* pairs) {
     const int2 p = pairs[blockIdx.y];
     const uint4* src = kv + (long long)p.x * block_vec;
@@ -270,6 +277,12 @@ void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n
     if (n <= 0) return;
     if (block_bytes % 16) throw std::invalid_argument("KV block size must be a multiple of 16 bytes");
     block_copy_kernel<<<dim3(64, n), 256, 0, s>>>(static_cast<uint4*>(kv), block_bytes / 16, pairs);
+    TVARA_LAUNCHED();
+}
+
+void launch_id_copy(int* ids, int per_block, const int2* pairs, int n, cudaStream_t s) {
+    if (n <= 0) return;
+    id_copy_kernel<<<n, 128, 0, s>>>(ids, per_block, pairs);
     TVARA_LAUNCHED();
 }
 

@@ -231,9 +231,11 @@ __global__ void planes_kernel(DeviceMatrix w, unsigned* hi, unsigned* lo) {
     }
 }
 
-__global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx) {
+__global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx, int* ids, const int* blk,
+                             const int* slot, int tpb) {
     const int t = blockIdx.x;
     const long long r = tokens[t];
+    if (ids && threadIdx.x == 0) ids[(long long)blk[t] * tpb + slot[t]] = int(r);
     for (int k = threadIdx.x; k < w.cols; k += blockDim.x) x[(long long)t * ldx + k] = element(w, r, k);
 }
 
@@ -1243,9 +1245,10 @@ void launch_row_shift(const DeviceMatrix& w, signed char* out, cudaStream_t s) {
     TVARA_LAUNCHED();
 }
 
-void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s) {
+void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s, int* ids,
+                  const int* blk, const int* slot, int tpb) {
     if (n <= 0) return;
-    embed_kernel<<<n, 256, 0, s>>>(emb, tokens, x, ldx);
+    embed_kernel<<<n, 256, 0, s>>>(emb, tokens, x, ldx, ids, blk, slot, tpb);
     TVARA_LAUNCHED();
 }
 

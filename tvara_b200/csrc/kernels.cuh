@@ -58,7 +58,9 @@ void set_tc_min_tokens(int n);
 
 // ---- elementwise ----------------------------------------------------------
 // x[t] = row tokens[t] of the embedding, dequantised.
-void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s);
+// ids (optional): token id plane of the KV pool, ids[blk[t] * tpb + slot[t]] = tokens[t]
+void launch_embed(const DeviceMatrix& emb, const int* tokens, int n, float* x, int ldx, cudaStream_t s,
+                  int* ids = nullptr, const int* blk = nullptr, const int* slot = nullptr, int tpb = 0);
 // out[i] = (x[rows[i]] * inv_rms) * w ; rows == nullptr means i.
 void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
                     float* out, int ldo, cudaStream_t s);
@@ -118,5 +120,39 @@ void launch_attention(const AttnArgs& a, cudaStream_t s);
 void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, bool finite_check, cudaStream_t s);
 // Copies whole KV blocks (copy-on-write): pairs of (from, to) block ids.
 void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n, cudaStream_t s);
+// The same pairs over the token id plane ([block][per_block] ints).
+void launch_id_copy(int* ids, int per_block, const int2* pairs, int n, cudaStream_t s);
+
+// Device-side logit post-processing (k_sample.cu): penalties from each row's
+// token history, the token mask, finiteness checks, argmax and top-k.
+constexpr int kSampleMaxK = 64;
+enum { kSampleNonfiniteLogits = 1, kSampleNonfiniteAdjusted = 2, kSampleNoneAllowed = 4 };
+struct SampleJob {
+    const float* logits = nullptr;  // row r at logits + r * ld
+    long long ld = 0;
+    int rows = 0, vocab = 0;
+    // history of row r: flat hist[hoff[r] ..), or through the KV pool's token
+    // ids: ids[tables[toff[r] + i / tpb] * tpb + i % tpb]; hlen[r] tokens
+    const int* hist = nullptr;
+    const long long* hoff = nullptr;
+    const int* ids = nullptr;
+    const int* tables = nullptr;
+    const int* toff = nullptr;
+    int tpb = 1;
+    const int* hlen = nullptr;
+    int hist_cap = 1;                  // power of two >= every hlen
+    const double* params = nullptr;    // [rows][3]: repetition, frequency, presence
+    const unsigned* allowed = nullptr; // [rows][words] bitmask or null
+    int words = 0;
+    int top_k = 0;
+    double* pen = nullptr;             // scratch [rows][pen_stride >= hist_cap]
+    long long pen_stride = 0;
+    unsigned* argmax = nullptr;        // [rows]
+    int* status = nullptr;             // [rows] kSample* bits
+    double* top_val = nullptr;         // [rows][top_k]
+    unsigned* top_id = nullptr;        // [rows][top_k]
+};
+std::size_t sample_smem_bytes(int vocab, int hist_cap);
+void launch_sample(const SampleJob& j, cudaStream_t s);
 
 }  // namespace tvara

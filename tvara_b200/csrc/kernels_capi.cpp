@@ -3,6 +3,8 @@
 #include "../../include/tvara_kernels.h"
 
 #include <cstring>
+#include <algorithm>
+#include <cmath>
 #include <string>
 #include <vector>
 
@@ -107,6 +109,85 @@ int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* 
         tvara::launch_repack(type, gguf_rows, int(rows), int(cols), const_cast<std::uint8_t*>(m.qs),
                              const_cast<std::uint8_t*>(m.meta), s);
         tvara::launch_row_shift(m, const_cast<signed char*>(m.row_shift), s);
+    });
+}
+
+namespace {
+std::size_t pow2_at_least(std::size_t n) {
+    std::size_t p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+}  // namespace
+
+size_t tvara_sample_workspace(size_t rows, size_t max_history) {
+    if (!rows || max_history > 16384) return 0;
+    return rows * (8 + 4 + 24) + rows * pow2_at_least(std::max<std::size_t>(max_history, 1)) * 8 + 256;
+}
+
+int tvara_sample_logits(const float* logits, size_t rows, size_t vocab, const int32_t* history,
+                        const uint64_t* history_offsets, const double* repetition, const double* frequency,
+                        const double* presence, const uint32_t* allowed, uint32_t top_k, uint32_t* argmax,
+                        int32_t* status, double* top_values, uint32_t* top_ids, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    return guarded([&] {
+        if (!logits || !rows || !vocab || vocab > 0x7fffffff || rows > 0x7fffffff || !history_offsets || !argmax ||
+            !status || !workspace)
+            throw std::invalid_argument("invalid sampling arguments");
+        if (top_k > 64 || top_k > vocab) throw std::invalid_argument("top-k candidates must be between 0 and 64");
+        if (top_k && (!top_values || !top_ids)) throw std::invalid_argument("invalid top-k output buffers");
+        std::vector<long long> hoff(rows);
+        std::vector<int> hlen(rows);
+        std::vector<double> par(rows * 3);
+        std::size_t longest = 0;
+        for (std::size_t r = 0; r < rows; ++r) {
+            if (history_offsets[r + 1] < history_offsets[r]) throw std::invalid_argument("invalid history offsets");
+            const std::size_t n = history_offsets[r + 1] - history_offsets[r];
+            if (n > 16384) throw std::invalid_argument("device sampling holds at most 16384 tokens of history");
+            if (n && !history) throw std::invalid_argument("invalid sampling arguments");
+            hoff[r] = (long long)history_offsets[r];
+            hlen[r] = int(n);
+            longest = std::max(longest, n);
+            par[3 * r] = repetition ? repetition[r] : 1.0;
+            par[3 * r + 1] = frequency ? frequency[r] : 0.0;
+            par[3 * r + 2] = presence ? presence[r] : 0.0;
+            if (!std::isfinite(par[3 * r]) || par[3 * r] <= 0 || !std::isfinite(par[3 * r + 1]) ||
+                !std::isfinite(par[3 * r + 2]))
+                throw std::invalid_argument("Invalid sampling filters or penalties");
+        }
+        if (workspace_bytes < tvara_sample_workspace(rows, longest))
+            throw std::invalid_argument("sampling workspace too small");
+        const std::size_t cap = pow2_at_least(std::max<std::size_t>(longest, 1));
+        auto* base = static_cast<unsigned char*>(workspace);
+        auto s = static_cast<cudaStream_t>(stream);
+        // [pen rows x cap doubles][params rows x 3 doubles][hoff rows][hlen rows]
+        double* pen = reinterpret_cast<double*>(base);
+        double* d_par = pen + rows * cap;
+        long long* d_hoff = reinterpret_cast<long long*>(d_par + rows * 3);
+        int* d_hlen = reinterpret_cast<int*>(d_hoff + rows);
+        TVARA_CUDA(cudaMemcpyAsync(d_par, par.data(), par.size() * 8, cudaMemcpyHostToDevice, s));
+        TVARA_CUDA(cudaMemcpyAsync(d_hoff, hoff.data(), hoff.size() * 8, cudaMemcpyHostToDevice, s));
+        TVARA_CUDA(cudaMemcpyAsync(d_hlen, hlen.data(), hlen.size() * 4, cudaMemcpyHostToDevice, s));
+        tvara::SampleJob j;
+        j.logits = logits;
+        j.ld = (long long)vocab;
+        j.rows = int(rows);
+        j.vocab = int(vocab);
+        j.hist = history;
+        j.hoff = d_hoff;
+        j.hlen = d_hlen;
+        j.hist_cap = int(cap);
+        j.params = d_par;
+        j.allowed = allowed;
+        j.words = int((vocab + 31) / 32);
+        j.top_k = int(top_k);
+        j.pen = pen;
+        j.pen_stride = (long long)cap;
+        j.argmax = argmax;
+        j.status = status;
+        j.top_val = top_values;
+        j.top_id = top_ids;
+        tvara::launch_sample(j, s);
     });
 }
 

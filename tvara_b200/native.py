@@ -17,12 +17,19 @@ from pathlib import Path
 import numpy as np
 
 from . import load_library
-from ._bindings import OpenOptions, F32P, U32P, U64P, I32P
+from ._bindings import OpenOptions, Sampling, F32P, F64P, U32P, U64P, I32P
 
 KV_F32, KV_F16 = 0, 1
 STEP_ALL_LOGITS = 1
 STEP_FINITE_ARGMAX = 2
 ARGMAX_NONFINITE = 0xFFFFFFFF
+SAMPLE_NONFINITE_LOGITS = 1
+SAMPLE_NONFINITE_ADJUSTED = 2
+SAMPLE_NONE_ALLOWED = 4
+SAMPLE_MAX_K = 64
+# Extra device candidates beyond top_k, so that tokens whose probabilities
+# tie after rounding at the top_k boundary are still seen by the host.
+SAMPLE_MARGIN = 16
 
 
 def _ptr(a: np.ndarray, typ):
@@ -169,13 +176,8 @@ class NativeModel:
                 self._raise_error()
         return n.value
 
-    def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False, finite_argmax=False):
-        """One device step: sequence i appends token_lists[i] (or, given a 1-D
-        array, the single token token_lists[i]).  Returns
-        (logits [rows, vocab] or None, argmax [rows] or None) with one row per
-        sequence (its last token) or per token when all_logits.  With
-        finite_argmax, a row whose logits hold a NaN or an infinity has
-        argmax ARGMAX_NONFINITE."""
+    @staticmethod
+    def _pack(sequences, token_lists):
         seqs = np.ascontiguousarray(sequences, dtype=np.uint64)
         if isinstance(token_lists, np.ndarray) and token_lists.ndim == 1:
             # decode: one token per sequence
@@ -188,6 +190,63 @@ class NativeModel:
             cu = np.zeros(len(seqs) + 1, dtype=np.uint32)
             np.cumsum(lens, out=cu[1:])
             toks = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.uint32) for t in token_lists]))
+        return seqs, cu, toks
+
+    def batch_sample(self, sequences, token_lists, repetition=None, frequency=None, presence=None, allowed=None,
+                     top_k=0, logits=False):
+        """A step (one row per sequence) followed by the sampler's logit
+        post-processing on the device (tvara_batch_sample): penalties from
+        each sequence's tokens, the allowed-token mask ([n, vocab] bool or
+        None), argmax and the top_k largest adjusted values.  Returns a dict
+        of numpy arrays: argmax [n], status [n] (SAMPLE_* bits), top_values
+        [n, top_k] float64, top_ids [n, top_k] and, with logits, the rows
+        before post-processing [n, vocab] F32."""
+        seqs, cu, toks = self._pack(sequences, token_lists)
+        n = len(seqs)
+
+        def per_row(v):
+            if v is None:
+                return None
+            a = np.broadcast_to(np.asarray(v, dtype=np.float64), (n,))
+            return np.ascontiguousarray(a)
+
+        rep, fre, pre = per_row(repetition), per_row(frequency), per_row(presence)
+        words = None
+        if allowed is not None:
+            mask = np.asarray(allowed, dtype=bool).reshape(n, self.vocab_size)
+            words = np.packbits(mask, axis=1, bitorder="little")
+            pad = (-words.shape[1]) % 4
+            words = np.ascontiguousarray(np.pad(words, ((0, 0), (0, pad)))).view(np.uint32)
+        args = Sampling()
+        args.struct_size = C.sizeof(Sampling)
+        args.repetition = _ptr(rep, F64P) if rep is not None else None
+        args.frequency = _ptr(fre, F64P) if fre is not None else None
+        args.presence = _ptr(pre, F64P) if pre is not None else None
+        args.allowed = _ptr(words, U32P) if words is not None else None
+        args.top_k = int(top_k)
+        am = np.empty(n, dtype=np.uint32)
+        st = np.empty(n, dtype=np.int32)
+        tv = np.empty((n, top_k), dtype=np.float64)
+        ti = np.empty((n, top_k), dtype=np.uint32)
+        lg = np.empty((n, self.vocab_size), dtype=np.float32) if logits else None
+        with self._lock:
+            self._check_open()
+            status = self._library.tvara_batch_sample(
+                self._handle, n, _ptr(seqs, U64P), _ptr(cu, U32P), _ptr(toks, U32P), C.byref(args),
+                _ptr(lg, F32P) if lg is not None else None, lg.size if lg is not None else 0,
+                _ptr(am, U32P), _ptr(st, I32P), _ptr(tv, F64P) if top_k else None, _ptr(ti, U32P) if top_k else None)
+            if status:
+                self._raise_error()
+        return {"argmax": am, "status": st, "top_values": tv, "top_ids": ti, "logits": lg}
+
+    def batch_step(self, sequences, token_lists, all_logits=False, logits=True, argmax=False, finite_argmax=False):
+        """One device step: sequence i appends token_lists[i] (or, given a 1-D
+        array, the single token token_lists[i]).  Returns
+        (logits [rows, vocab] or None, argmax [rows] or None) with one row per
+        sequence (its last token) or per token when all_logits.  With
+        finite_argmax, a row whose logits hold a NaN or an infinity has
+        argmax ARGMAX_NONFINITE."""
+        seqs, cu, toks = self._pack(sequences, token_lists)
         rows = int(cu[-1]) if all_logits else len(seqs)
         out = np.empty((rows, self.vocab_size), dtype=np.float32) if logits else None
         am = np.empty(rows, dtype=np.uint32) if argmax else None
@@ -331,9 +390,18 @@ class NativeModel:
 
     # ------------------------------------------------------------ generation
     def iter_tokens(self, prompt, max_new_tokens=16, temperature=0, seed=0, eos_id=None, top_p=1, top_k=0,
-                    min_p=0, repetition=1, frequency=0, presence=0, token_constraint=None):
-        """Host sampler over device logits, with the reference's parameter
-        checks and filter order (python/tvara/native.py:220-340)."""
+                    min_p=0, repetition=1, frequency=0, presence=0, token_constraint=None, device_sampling=True):
+        """The reference's sampler (python/tvara/native.py:220-340): same
+        parameter checks, penalties, mask and filter order.  With
+        device_sampling, the penalties, the mask, the checks and either the
+        argmax (temperature 0: bit-identical to the host path) or the top
+        candidates (1 <= top_k <= 48) are computed on the device and only
+        those cross to the host; the random draw stays numpy's.  On the
+        candidate path the probabilities are normalised over the candidates
+        instead of the whole vocabulary, which changes them by rounding only:
+        the drawn token can differ only if the uniform draw falls within that
+        rounding of a boundary of the cumulative distribution.  Other
+        settings copy full logits and sample on the host."""
         prompt = list(prompt)
         if not prompt or any(isinstance(t, (bool, np.bool_)) or not isinstance(t, (int, np.integer))
                              or not 0 <= t < self.vocab_size for t in prompt):
@@ -365,6 +433,11 @@ class NativeModel:
             rng = np.random.default_rng(seed)
         except (ValueError, TypeError, OverflowError) as error:
             raise ValueError("Invalid random seed") from error
+        on_device = device_sampling and (temperature == 0 or 1 <= top_k <= SAMPLE_MAX_K - SAMPLE_MARGIN)
+        if on_device:
+            yield from self._iter_tokens_device(prompt, max_new_tokens, temperature, rng, eos_id, top_p, top_k,
+                                                min_p, repetition, frequency, presence, token_constraint)
+            return
         sequence = self._new_sequence()
         history = prompt.copy()
         try:
@@ -406,6 +479,62 @@ class NativeModel:
                     break
                 if index + 1 < max_new_tokens:
                     logits = self.logits(sequence, token)
+        finally:
+            self._drop_sequence(sequence)
+
+    def _iter_tokens_device(self, prompt, max_new_tokens, temperature, rng, eos_id, top_p, top_k, min_p, repetition,
+                            frequency, presence, token_constraint):
+        k = 0 if temperature == 0 else top_k + SAMPLE_MARGIN
+        sequence = self._new_sequence()
+        try:
+            feed = prompt
+            for index in range(max_new_tokens):
+                allowed, mask_error = None, None
+                if token_constraint is not None:
+                    # the constraint's own mask (-inf outside its tokens); its error is
+                    # raised after the logit checks, in the reference's order
+                    try:
+                        allowed = np.isfinite(token_constraint.mask_logits(np.zeros(self.vocab_size)))[None, :]
+                    except ValueError as error:
+                        mask_error = error
+                out = self.batch_sample([sequence], [feed], repetition, frequency, presence, allowed, k)
+                status = int(out["status"][0])
+                if status & SAMPLE_NONFINITE_LOGITS:
+                    raise ValueError("Nonfinite model logits")
+                if status & SAMPLE_NONFINITE_ADJUSTED:
+                    raise ValueError("Nonfinite adjusted sampling logits")
+                if mask_error is not None:
+                    raise mask_error
+                if status & SAMPLE_NONE_ALLOWED:
+                    raise ValueError("No grammar-valid tokens remain")
+                if temperature == 0:
+                    token = int(out["argmax"][0])
+                else:
+                    # the reference's filters on the candidates, held in token order
+                    ids = out["top_ids"][0].astype(np.int64)
+                    vals = out["top_values"][0]
+                    order_ids = np.argsort(ids, kind="stable")
+                    ids, vals = ids[order_ids], vals[order_ids]
+                    p = np.exp((vals - float(vals.max())) / temperature)
+                    p /= p.sum()
+                    order = np.argsort(-p, kind="stable")
+                    p[order[top_k:]] = 0
+                    p[p < p.max() * min_p] = 0
+                    p /= p.sum()
+                    cumulative = np.cumsum(p[order])
+                    p[order[np.r_[False, cumulative[:-1] >= top_p]]] = 0
+                    p /= p.sum()
+                    full = np.zeros(self.vocab_size)
+                    full[ids] = p
+                    token = int(rng.choice(self.vocab_size, p=full))
+                if token_constraint is not None:
+                    token_constraint.accept(token)
+                yield token
+                if token == eos_id:
+                    break
+                feed = [token]
+                if index + 1 == max_new_tokens:
+                    break
         finally:
             self._drop_sequence(sequence)
 
