@@ -78,6 +78,8 @@ def parse():
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-standalone", action="store_true", help="skip the standalone GEMV / matmul figures")
+    ap.add_argument("--planes", choices=["auto", "hilo", "off"], default="auto",
+                    help="tensor-core weight form: auto (Q4_K plane of sc*q, other types hi/lo), hilo, off")
     ap.add_argument("--standalone-only", action="store_true",
                     help="only the standalone GEMV / matmul figures (one JSON line; used for kernel profiles)")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens the reference CPU engine decodes")
@@ -357,7 +359,8 @@ def run_ours(args):
     unique = suffix + done + total_steps
     blocks = int(np.sum((args.prefix + unique + tpb - 1) // tpb - args.prefix // tpb)) + args.prefix // tpb + 64
     model = NativeModel(path, max_blocks=blocks, block_tokens=tpb, kv_dtype=args.kv, device=local,
-                        max_step_tokens=max(2048, args.prefix), tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+                        max_step_tokens=max(2048, args.prefix), tp_rank=rank, tp_size=world, nccl_id=nccl_id,
+                        weight_planes=None if args.planes == "auto" else args.planes)
     wbytes = model.weight_bytes()
     fill_pool_random(model, args.seed + 2 + rank)
     seq0 = model._new_sequence()
@@ -505,7 +508,11 @@ def run_ours(args):
                    "global_batch": args.requests, "seq_len": float(np.mean(lens0)),
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,
                    "weights_gb": {"packed": round(wbytes["packed"] / 1e9, 2),
-                                  "fp16_planes": round(wbytes["planes"] / 1e9, 2)},
+                                  "tensor_core_forms": round(wbytes["planes"] / 1e9, 2)},
+                   "tensor_core_weight_form": {"auto": "Q4_K: FP16 plane of sc*q + block scales + minima "
+                                                       "(2 MMAs per K-step); other types: exact hi/lo FP16 planes",
+                                               "hilo": "exact hi/lo FP16 planes (3 MMAs per K-step)",
+                                               "off": "packed rows dequantised by producer warps"}[args.planes],
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},
         "e2e": e2e_tokens, "e2e_full_logits": e2e_logits,
         "roofline": roof, "rooflines": {"attention": roof_attn, "projections": roof_proj}, "step_roofline": step_roof,

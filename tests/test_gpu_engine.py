@@ -281,6 +281,31 @@ def test_weight_planes_match_packed_path(tiny_path, model_dir, name):
     assert np.abs(got["on"] - got["off"]).max() <= 1e-4
 
 
+@pytest.mark.parametrize("split_k", [False, True])
+def test_wide_q4k_prefill_matches_oracle(model_dir, split_k):
+    """Multi-token steps of a Q4_K model wide enough (K >= 1024, a multiple of
+    256) for the two-MMA tensor-core form (FP16 plane of sc*q, block scales,
+    min term): every position's logits within tolerance of the oracle, for the
+    planes and for the packed path, and the two within 1e-4.  A short step
+    budget splits the prompt across device steps; a single 48-token step uses
+    split K on the narrow projections."""
+    from oracle.model import OracleModel
+    cfg = gguf.model_config("tiny", hidden=1024, heads=8, kv_heads=2, ffn=2816, layers=2, tied=False,
+                            types=dict(default=gguf.Q4_K, ffn_down=gguf.Q4_K, output=gguf.Q8_0, embd=gguf.Q8_0))
+    path = make_model(model_dir, "wide_q4k_prefill", cfg, seed=6)
+    toks = np.random.default_rng(9).integers(0, 512, 48).tolist()
+    want = OracleModel(path, max_positions=64).forward(toks)
+    got = {}
+    for planes in ("on", "off"):
+        with NativeModel(path, max_blocks=8, block_tokens=16, weight_planes=planes,
+                         max_step_tokens=None if split_k else 20) as m:
+            assert (m.weight_bytes()["planes"] > 0) == (planes == "on")
+            s = m._new_sequence()
+            got[planes] = m.decode_batch(s, toks)
+        assert close(got[planes], want), (planes, np.abs(got[planes] - want).max())
+    assert np.abs(got["on"] - got["off"]).max() <= 1e-4
+
+
 def test_batch_step_decode_array_equals_lists(tiny_path):
     """The 1-D decode form of batch_step (one token per sequence) is the same
     call as the list form."""

@@ -45,6 +45,16 @@ struct DeviceMatrix {
     // TMA instead of dequantising the packed rows.  Null when not built.
     const std::uint16_t* plane_hi = nullptr;
     const std::uint16_t* plane_lo = nullptr;
+    // Optional Q4_K tensor-core form (instead of the planes above): a Q4_K
+    // value is d*sc*q - dmin*m per 32-element sub-block, and sc*q is an
+    // integer below 1024, exact in FP16.  qplane [rows][cols] FP16 holds sc*q;
+    // qscale [rows][cols/256] the block scales d; qmin_hi / qmin_lo
+    // [rows][cols/32] FP16 the exact split of dmin*m * 2^qmin_shift[row].
+    const std::uint16_t* qplane = nullptr;
+    const float* qscale = nullptr;
+    const std::uint16_t* qmin_hi = nullptr;
+    const std::uint16_t* qmin_lo = nullptr;
+    const signed char* qmin_shift = nullptr;
 };
 
 inline std::size_t qs_row_bytes(int type, std::size_t cols) {

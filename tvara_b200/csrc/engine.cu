@@ -251,8 +251,10 @@ void Engine::load(const gguf::File& f) {
     cudaFree(staging_dev);
     cudaFree(flag);
 
-    // ---- exact FP16 hi/lo planes of the projections for the tensor-core
-    // path (4 bytes per weight, the footprint of the reference's own F32
+    // ---- tensor-core forms of the projections: Q4_K rows as an FP16 plane
+    // of sc*q with block scales and the min term (2 bytes per weight, two
+    // MMAs per K-step), other types as exact FP16 hi/lo planes of their
+    // values (4 bytes per weight, the footprint of the reference's own F32
     // expansion); batches of <= 4 tokens keep streaming the packed rows.
     if (opt_.weight_planes != 2) {
         std::vector<DeviceMatrix*> mats;
@@ -263,9 +265,15 @@ void Engine::load(const gguf::File& f) {
             mats.push_back(&L.down);
         }
         mats.push_back(&head_);
+        auto q4k_form = [&](const DeviceMatrix* m) {
+            return opt_.weight_planes != 3 && m->type == kQ4_K && m->cols % 256 == 0 && m->cols >= 1024;
+        };
+        auto form_bytes = [&](const DeviceMatrix* m) -> std::size_t {
+            if (q4k_form(m)) return (q4k_planes_bytes(m->rows, m->cols) + 255) & ~std::size_t(255);
+            return m->cols % 32 == 0 ? std::size_t(m->rows) * m->cols * 4 : 0;
+        };
         std::size_t need = 0;
-        for (auto* m : mats)
-            if (m->cols % 32 == 0) need += std::size_t(m->rows) * m->cols * 4;
+        for (auto* m : mats) need += form_bytes(m);
         const std::size_t es = opt_.kv_f16 ? 2 : 4;
         const std::size_t pool = std::size_t(layers_) * 2 * hkv_ * book_->geometry().tokens_per_block * d * es *
                                  book_->geometry().max_blocks;
@@ -277,14 +285,20 @@ void Engine::load(const gguf::File& f) {
         if (fits && need) {
             TVARA_CUDA(cudaMalloc(&planes_, need));
             plane_bytes_ = need;
-            std::uint16_t* at = planes_;
+            auto* at = reinterpret_cast<unsigned char*>(planes_);
             for (auto* m : mats) {
-                if (m->cols % 32) continue;
-                const std::size_t n = std::size_t(m->rows) * m->cols;
-                launch_planes(*m, at, at + n, stream_);
-                m->plane_hi = at;
-                m->plane_lo = at + n;
-                at += 2 * n;
+                const std::size_t bytes = form_bytes(m);
+                if (!bytes) continue;
+                if (q4k_form(m)) {
+                    launch_q4k_planes(*m, at, stream_);
+                } else {
+                    const std::size_t n = std::size_t(m->rows) * m->cols;
+                    auto* p = reinterpret_cast<std::uint16_t*>(at);
+                    launch_planes(*m, p, p + n, stream_);
+                    m->plane_hi = p;
+                    m->plane_lo = p + n;
+                }
+                at += bytes;
             }
             TVARA_CUDA(cudaStreamSynchronize(stream_));
         }

@@ -28,7 +28,8 @@ struct EngineOptions {
     bool has_nccl_id = false;
     std::array<char, 128> nccl_id{};
     // Exact FP16 hi/lo planes of the projections for the tensor-core path:
-    // 0 = when they fit beside the KV pool, 1 = always, 2 = never.
+    // 0 = when they fit beside the KV pool, 1 = always, 2 = never, 3 = the
+    // hi/lo planes for every type (no Q4_K form), when they fit.
     int weight_planes = 0;
 };
 

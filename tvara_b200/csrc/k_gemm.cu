@@ -269,6 +269,21 @@ __device__ __forceinline__ void convert(const Raw<TYPE>& r, int k0, float scale,
     }
 }
 
+// a / b for b in [1, 2] without the IEEE division's out-of-line path: the
+// approximate quotient corrected once by the exact residual (within about
+// half an ulp of the correctly rounded quotient).
+__device__ __forceinline__ float div_12(float a, float b) {
+    const float q = __fdividef(a, b);
+    return __fmaf_rn(__fmaf_rn(-q, b, a), __fdividef(1.f, b), q);
+}
+// swiglu with div_12 (the epilogue of the Q4_K kernel, where the division's
+// call and spills stalled the MMAs)
+__device__ __forceinline__ float swiglu_12(float g, float up) {
+    const float small = expf(-fabsf(g));
+    const float sig = g >= 0.f ? div_12(1.f, 1.f + small) : div_12(small, 1.f + small);
+    return __fmul_rn(g, __fmul_rn(sig, up));
+}
+
 __device__ __forceinline__ float swiglu(float g, float up) {
     const float small = expf(-fabsf(g));
     const float sig = g >= 0.f ? 1.f / (1.f + small) : small / (1.f + small);
@@ -689,11 +704,280 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Q4_K weights with two MMAs per K-step instead of three (DeviceMatrix::
+// qplane).  A Q4_K value is d*sc*q - dmin*m per 32-element sub-block
+// (quant.hpp:70-84); sc*q is an integer below 1024, exact in FP16, so the A
+// operand is one plane and only the activations are split: P*x_hi + P*x_lo.
+// The block scale d changes every 256 elements, so each block's MMAs go to
+// one of two 256-column TMEM accumulators and the epilogue warps add
+// d[row][block] * accumulator into registers while the MMAs fill the other.
+// The min term -sum over sub-blocks of dmin*m * sum(x) is one more block at
+// the end of a tile (its first K split only): the exact hi/lo split of
+// dmin*m * 2^qmin_shift[row] against the hi/lo split of the sub-block sums
+// of x / 32, three MMAs per step over cols/32 columns, scaled back by
+// -32 * 2^-qmin_shift[row].  Roles as in the persistent plane kernel: warp 9
+// issues the TMA loads through one stage ring, warp 8 the MMAs, warps 0-7
+// hold a row and 128 token columns each.
+struct Q4kArgs {
+    TcArgs t;        // k_steps = 8 * blocks (K-steps per split)
+    int blocks;      // 256-element blocks per split
+    int min_steps;   // 32-column steps of the min term
+};
+
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                       const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_mhi,
+                       const __grid_constant__ CUtensorMap map_mlo, const __grid_constant__ CUtensorMap map_shi,
+                       const __grid_constant__ CUtensorMap map_slo, Q4kArgs q, TileSpace ts) {
+    const TcArgs& a = q.t;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int b_bytes = a.n_tile * kBK * 2;
+    const int stage_bytes = 2 * kATile + 2 * kBTileMax;
+    unsigned char* stages = base;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(base + kStages * stage_bytes);
+    std::uint64_t* empty = full + kStages;
+    std::uint64_t* acc_full = empty + kStages;   // [2] block accumulator ready
+    std::uint64_t* acc_empty = acc_full + 2;     // [2] epilogue done with it
+    unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = a.w.cols / 256;  // blocks per row
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kEpilogueWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarpP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp == kTmaWarpP) {
+        unsigned tma_issued = 0, tma_phase = 0;
+        int qq = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+            for (int ks = 0; ks < steps; ++ks, ++qq) {
+                int ok = 1;
+                if (lane == 0) {
+                    const int s = qq % kStages;
+                    const unsigned ph = (qq / kStages) & 1;
+                    ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                    if (ok) {
+                        unsigned char* st = stages + s * stage_bytes;
+                        const unsigned bar = smem_u32(&full[s]);
+                        if (ks < a.k_steps) {
+                            const int k0 = (kstep0 + ks) * kBK;
+                            mbar_expect_tx(&full[s], kATile + 2 * b_bytes);
+                            tma_load_2d(smem_u32(st), &map_q, k0, row0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
+                        } else {
+                            const int c0 = (ks - a.k_steps) * kBK;
+                            mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
+                            tma_load_2d(smem_u32(st), &map_mhi, c0, row0, bar);
+                            tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
+                        }
+                        tma_issued |= 1u << s;
+                        tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    go = false;
+                    break;
+                }
+            }
+        }
+        if (lane == 0)
+            for (int s = 0; s < kStages; ++s)
+                if (tma_issued >> s & 1u)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full[s], (tma_phase >> s) & 1u); ++i) {
+                    }
+    } else if (warp == kMmaWarpP) {
+        if (lane == 0) {
+            int qq = 0, gb = 0;
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+                const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+                for (int j = 0; j < nb && go; ++j, ++gb) {
+                    const int b = gb & 1;
+                    if (!mbar_wait(&acc_empty[b], ((gb >> 1) & 1) ^ 1, abort_flag, a.err, 15, false)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const unsigned acc = tmem + unsigned(b * 256);
+                    const bool minterm = j == q.blocks;
+                    const int n_steps = minterm ? q.min_steps : 256 / kBK;
+                    for (int ks = 0; ks < n_steps; ++ks, ++qq) {
+                        const int s = qq % kStages;
+                        const unsigned ph = (qq / kStages) & 1;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, 13, false)) {
+                            go = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;");
+                        unsigned char* st = stages + s * stage_bytes;
+                        const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+                        const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                            mma_f16(acc, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
+                            mma_f16(acc, ahi + adv, blo + adv, a.idesc, 1);
+                            if (minterm) mma_f16(acc, alo + adv, bhi + adv, a.idesc, 1);
+                        }
+                        mma_commit(&empty[s]);
+                    }
+                    if (go) mma_commit(&acc_full[b]);
+                }
+            }
+        }
+    } else {
+        // epilogue: TMEM lane r = weight row row0 + r; warps w and w+4 share
+        // lanes 32*(w%4).. and take token columns [0, 128) and [128, 256)
+        const int r = threadIdx.x % kBM;
+        const int hf = threadIdx.x / kBM;
+        int gb = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+            const long long row = row0 + r;
+            const bool live = row < a.w.rows;
+            float acc[128];
+#pragma unroll
+            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+            // block scales are loaded one block ahead of their accumulator
+            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
+            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
+            float next = live && q.blocks > 0 ? qs_row[0] : 0.f;
+            for (int j = 0; j < nb; ++j, ++gb) {
+                const int b = gb & 1;
+                const float scale = !live ? 0.f : j < q.blocks ? next : min_scale;
+                if (live && j + 1 < q.blocks) next = qs_row[j + 1];
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
+                    go = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
+                    unsigned u[32];
+                    const unsigned taddr =
+                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                        : "r"(taddr));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+            }
+            if (!go) break;
+            // store, 32 token columns at a time (a runtime loop over one
+            // compact body: a fully unrolled 128-column store ran from a cold
+            // instruction cache): lane l loads token l's shift (broadcast by
+            // shuffles); the residual add is a reduction at L2 (one thread per
+            // element, so one IEEE addition as y += val)
+            for (int c = 0; c < 4; ++c) {
+                const int col0 = hf * 128 + c * 32;
+                if (col0 >= a.n_tile) break;  // warp-uniform
+                float v[32];
+                switch (c) {
+#define TVARA_TAKE(C)                                        \
+    case C:                                                  \
+        _Pragma("unroll") for (int jj = 0; jj < 32; ++jj) v[jj] = acc[C * 32 + jj]; \
+        break;
+                    TVARA_TAKE(0)
+                    TVARA_TAKE(1)
+                    TVARA_TAKE(2)
+                    TVARA_TAKE(3)
+#undef TVARA_TAKE
+                }
+                const int tl = tok0 + col0 + lane;
+                const float inv_l = tl < a.tokens ? pow2(-a.x_shift[tl]) : 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] *= __shfl_sync(0xffffffffu, inv_l, jj);
+                const int ncol = min(32, min(a.n_tile - col0, a.tokens - (tok0 + col0)));
+                if (a.epilogue == kSwiGLU) {
+                    // rows (2i, 2i+1) are (gate_i, up_i) in adjacent lanes: per
+                    // column pair the lanes swap values, the even lane finishes
+                    // the even column and the odd lane the odd one (compile-time
+                    // indices keep v in registers: a runtime index put it in local
+                    // memory, which thrashed the small L1 beside the stages)
+                    const bool odd = r & 1;
+                    float* dst = a.y + (long long)(tok0 + col0 + odd) * a.ldy + row / 2;
+#pragma unroll
+                    for (int pr = 0; pr < 16; ++pr) {
+                        const float pe = __shfl_xor_sync(0xffffffffu, v[2 * pr], 1);
+                        const float po = __shfl_xor_sync(0xffffffffu, v[2 * pr + 1], 1);
+                        if (live && 2 * pr + odd < ncol) {
+                            const float g = odd ? po : v[2 * pr];
+                            const float u = odd ? v[2 * pr + 1] : pe;
+                            dst[(long long)(2 * pr) * a.ldy] = swiglu_12(g, u);
+                        }
+                    }
+                } else if (live) {
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {
+                        if (jj >= ncol) break;
+                        float* dst = a.y + (long long)(tok0 + col0 + jj) * a.ldy + row;
+                        if (a.atomic || a.epilogue == kAdd) atomicAdd(dst, v[jj]);
+                        else *dst = v[jj];
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == kMmaWarpP) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
 // that puts max|x| in [2^14, 2^15), then the exact split (split.cuh).  One
 // block per token; float4 loads and 8-byte stores (K % 4 == 0, rows 16-byte
 // aligned, which the launcher checks).
-__global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half* lo, int* shift) {
+__global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half* lo, int* shift, __half* shi,
+                             __half* slo) {
     const int t = blockIdx.x;
     const float4* row = reinterpret_cast<const float4*>(x + (long long)t * ldx);
     const int K4 = K / 4;
@@ -719,13 +1003,19 @@ __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half*
     const float f = pow2(s);
     uint2* hrow = reinterpret_cast<uint2*>(hi + (long long)t * K);
     uint2* lrow = reinterpret_cast<uint2*>(lo + (long long)t * K);
-    for (int k = threadIdx.x; k < K4; k += blockDim.x) {
-        const float4 v = row[k];
-        uint2 h, l;
-        split_exact(v.x * f, v.y * f, h.x, l.x);
-        split_exact(v.z * f, v.w * f, h.y, l.y);
-        hrow[k] = h;
-        lrow[k] = l;
+    const bool sums = K % 32 == 0;  // the Q4_K min term's sub-block sums
+    const float f32 = pow2(s - 5);
+    for (int k0 = 0; k0 < K4; k0 += blockDim.x) {  // uniform trip count (shuffles)
+        const int k = k0 + threadIdx.x;
+        const float4 v = k < K4 ? row[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < K4) {
+            uint2 h, l;
+            split_exact(v.x * f, v.y * f, h.x, l.x);
+            split_exact(v.z * f, v.w * f, h.y, l.y);
+            hrow[k] = h;
+            lrow[k] = l;
+        }
+        if (sums) subblock_sum_split(v, k, k < K4, f32, shi + (long long)t * (K / 32), slo + (long long)t * (K / 32));
     }
 }
 
@@ -803,39 +1093,48 @@ bool gemm_tc_supported(const DeviceMatrix& w, int tokens) {
 }
 
 std::size_t gemm_tc_workspace(int max_tokens, int max_cols) {
-    // hi + lo activations, per-token shifts (padded to 64), an error flag
+    // hi + lo activations, per-token shifts (padded to 64), an error flag,
+    // hi + lo sub-block sums (the Q4_K min term)
     return std::size_t(max_tokens) * max_cols * 2 * sizeof(__half) +
-           std::size_t((max_tokens + 63) / 64 * 64 + 64) * sizeof(int) + 1024;
+           std::size_t((max_tokens + 63) / 64 * 64 + 64) * sizeof(int) +
+           std::size_t(max_tokens) * (max_cols / 32) * 2 * sizeof(__half) + 2048;
 }
 
 void gemm_tc_split_buffers(void* workspace, std::size_t workspace_bytes, int tokens, int cols, __half*& hi,
-                           __half*& lo, int*& shift) {
+                           __half*& lo, int*& shift, __half** shi, __half** slo) {
     if (!workspace || workspace_bytes < gemm_tc_workspace(tokens, cols))
         throw std::invalid_argument("tensor-core projection workspace too small");
     hi = static_cast<__half*>(workspace);
     lo = hi + std::size_t(tokens) * cols;
     shift = reinterpret_cast<int*>(lo + std::size_t(tokens) * cols);
+    // after the shifts and the workspace's error slot
+    auto* s0 = reinterpret_cast<__half*>(
+        (reinterpret_cast<std::uintptr_t>(shift + ((tokens + 63) / 64) * 64 + 64) + 255) & ~std::uintptr_t(255));
+    if (shi) *shi = s0;
+    if (slo) *slo = s0 + std::size_t(tokens) * (cols / 32);
 }
 
 void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_bytes, cudaStream_t s) {
     const int T = g.tokens, K = g.w.cols;
     if (!workspace || workspace_bytes < gemm_tc_workspace(T, K))
         throw std::invalid_argument("tensor-core projection workspace too small");
-    __half *hi = nullptr, *lo = nullptr;
+    __half *hi = nullptr, *lo = nullptr, *shi = nullptr, *slo = nullptr;
     int* shift = nullptr;
-    gemm_tc_split_buffers(workspace, workspace_bytes, T, K, hi, lo, shift);
+    gemm_tc_split_buffers(workspace, workspace_bytes, T, K, hi, lo, shift, &shi, &slo);
     // callers without an error flag get one in the workspace (never null)
     int* err = g.err ? g.err : shift + ((T + 63) / 64) * 64;
     if (!g.presplit) {
         if (reinterpret_cast<std::uintptr_t>(g.x) % 16 || g.ldx % 4 || K % 4)
             throw std::invalid_argument("tensor-core projection input must be 16-byte aligned rows");
-        split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift);
+        split_kernel<<<T, 256, 0, s>>>(g.x, g.ldx, K, hi, lo, shift, shi, slo);
         TVARA_LAUNCHED();
     }
 
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
-    const TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
+    TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
+    if (g.w.qplane)  // whole 256-element blocks per split
+        while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
     const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
     TcArgs a;
     a.w = g.w;
@@ -854,6 +1153,26 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
     const CUtensorMap mh = make_map(hi, K, T, n_tile), ml = make_map(lo, K, T, n_tile);
     const dim3 grid(token_tiles, row_tiles, splits);
+    if (g.w.qplane) {
+        // Q4_K two-MMA kernel: splits whole 256-element blocks; y was zeroed above for split K
+        if (steps % (8 * splits)) throw std::logic_error("Q4_K split does not divide the blocks");
+        const int units = K / 32;  // sub-block sums written with the split
+        const CUtensorMap mq = make_map(reinterpret_cast<const __half*>(g.w.qplane), K, g.w.rows, kBM);
+        const CUtensorMap mmh = make_map(reinterpret_cast<const __half*>(g.w.qmin_hi), units, g.w.rows, kBM);
+        const CUtensorMap mml = make_map(reinterpret_cast<const __half*>(g.w.qmin_lo), units, g.w.rows, kBM);
+        const CUtensorMap msh = make_map(shi, units, T, n_tile), msl = make_map(slo, units, T, n_tile);
+        Q4kArgs qa;
+        qa.t = a;
+        qa.blocks = a.k_steps / 8;
+        qa.min_steps = (units + kBK - 1) / kBK;
+        TileSpace ts{token_tiles, row_tiles, splits, token_tiles * row_tiles * splits};
+        const int smem = kStages * (2 * kATile + 2 * kBTileMax) + 1024 + 256;
+        TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        tc_gemm_q4k_kernel<<<std::min(ts.n_tiles, sm_count()), kPersistThreads, smem, s>>>(mh, ml, mq, mmh, mml, msh,
+                                                                                              msl, qa, ts);
+        TVARA_LAUNCHED();
+        return;
+    }
     if (g.w.plane_hi && g.w.plane_lo) {
         const CUtensorMap pa = make_map(reinterpret_cast<const __half*>(g.w.plane_hi), K, g.w.rows, kBM);
         const CUtensorMap pb = make_map(reinterpret_cast<const __half*>(g.w.plane_lo), K, g.w.rows, kBM);

@@ -20,7 +20,7 @@ namespace {
 template <int V, bool SPLIT>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ldx, const int* rows, int dim, const float* w,
                                                       float eps, float* out, int ldo, __half* hi, __half* lo,
-                                                      int* shift) {
+                                                      int* shift, __half* shi, __half* slo) {
     const int i = blockIdx.x;
     const long long r = rows ? rows[i] : i;
     const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ldx, c
         const float f = __uint_as_float(unsigned(127 + sh) << 23);
         uint2* hrow = reinterpret_cast<uint2*>(hi + (long long)i * dim);
         uint2* lrow = reinterpret_cast<uint2*>(lo + (long long)i * dim);
+        const float f32 = __uint_as_float(unsigned(127 + sh - 5) << 23);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             const int k = threadIdx.x + j * 256;
@@ -79,6 +80,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ldx, c
                 hrow[k] = h;
                 lrow[k] = l;
             }
+            // the Q4_K min term's sub-block sums (v[j] is zero past the row)
+            if (dim % 32 == 0)
+                subblock_sum_split(v[j], k, k < n4, f32, shi + (long long)i * (dim / 32), slo + (long long)i * (dim / 32));
         }
     }
 }
@@ -222,20 +226,20 @@ __global__ void block_copy_kernel(uint4* kv, long long block_vec, const int2* pa
 namespace {
 template <bool SPLIT>
 void run_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
-                 int ldo, __half* hi, __half* lo, int* shift, cudaStream_t s) {
+                 int ldo, __half* hi, __half* lo, int* shift, __half* shi, __half* slo, cudaStream_t s) {
     if (n <= 0) return;
     if (dim % 4 || (reinterpret_cast<std::uintptr_t>(x) & 15) || ldx % 4 || (out && ((reinterpret_cast<std::uintptr_t>(out) & 15) || ldo % 4)))
         throw std::invalid_argument("RMSNorm rows must be 16-byte aligned");
     const int v = (dim / 4 + 255) / 256;
     switch (v) {
-        case 1: rmsnorm_kernel<1, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
-        case 2: rmsnorm_kernel<2, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 1: rmsnorm_kernel<1, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift, shi, slo); break;
+        case 2: rmsnorm_kernel<2, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift, shi, slo); break;
         case 3:
-        case 4: rmsnorm_kernel<4, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 4: rmsnorm_kernel<4, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift, shi, slo); break;
         case 5:
         case 6:
         case 7:
-        case 8: rmsnorm_kernel<8, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift); break;
+        case 8: rmsnorm_kernel<8, SPLIT><<<n, 256, 0, s>>>(x, ldx, rows, dim, w, eps, out, ldo, hi, lo, shift, shi, slo); break;
         default: throw std::invalid_argument("RMSNorm width above 8192");
     }
     TVARA_LAUNCHED();
@@ -244,15 +248,15 @@ void run_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const
 
 void launch_rmsnorm(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps, float* out,
                     int ldo, cudaStream_t s) {
-    run_rmsnorm<false>(x, ldx, rows, n, dim, w, eps, out, ldo, nullptr, nullptr, nullptr, s);
+    run_rmsnorm<false>(x, ldx, rows, n, dim, w, eps, out, ldo, nullptr, nullptr, nullptr, nullptr, nullptr, s);
 }
 
 void launch_rmsnorm_split(const float* x, int ldx, const int* rows, int n, int dim, const float* w, float eps,
                           float* out, int ldo, void* tc_workspace, std::size_t tc_workspace_bytes, cudaStream_t s) {
-    __half *hi = nullptr, *lo = nullptr;
+    __half *hi = nullptr, *lo = nullptr, *shi = nullptr, *slo = nullptr;
     int* shift = nullptr;
-    gemm_tc_split_buffers(tc_workspace, tc_workspace_bytes, n, dim, hi, lo, shift);
-    run_rmsnorm<true>(x, ldx, rows, n, dim, w, eps, out, ldo, hi, lo, shift, s);
+    gemm_tc_split_buffers(tc_workspace, tc_workspace_bytes, n, dim, hi, lo, shift, &shi, &slo);
+    run_rmsnorm<true>(x, ldx, rows, n, dim, w, eps, out, ldo, hi, lo, shift, shi, slo, s);
 }
 
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {

@@ -231,6 +231,57 @@ __global__ void planes_kernel(DeviceMatrix w, unsigned* hi, unsigned* lo) {
     }
 }
 
+// Q4_K tensor-core form (DeviceMatrix::qplane ...) from the packed rows.
+// Per row, the power of two that brings max |dmin * m| into [2^14, 2^15)
+// (0 for a row without minima), so the split of dmin * m is exact.
+__global__ void q4k_min_shift_kernel(DeviceMatrix w, signed char* out) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= w.rows) return;
+    const unsigned char* meta = w.meta + (long long)r * w.meta_row;
+    float mx = 0.f;
+    for (int u = lane; u < w.cols / 32; u += 32) {
+        const unsigned char* blk = meta + (u >> 3) * 16;
+        unsigned sc, m;
+        q4k_scale_min(blk + 4, u & 7, sc, m);
+        mx = fmaxf(mx, fabsf(h2f((unsigned short)(blk[2] | (blk[3] << 8))) * float(m)));
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) {
+        int e = 0;
+        if (mx > 0.f) frexpf(mx, &e);
+        out[r] = (signed char)(mx > 0.f ? 15 - e : 0);
+    }
+}
+
+// qplane (pairs of sc*q), qscale (d per block), qmin_hi / qmin_lo (split of
+// dmin * m * 2^shift per sub-block); one thread per pair of elements.
+__global__ void q4k_planes_kernel(DeviceMatrix w, unsigned* qplane, float* qscale, unsigned short* min_hi,
+                                  unsigned short* min_lo, const signed char* shift) {
+    const long long pairs = (long long)w.rows * w.cols / 2;
+    const int units = w.cols / 32;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < pairs; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = 2 * i / w.cols;
+        const int k = int(2 * i % w.cols);
+        const int u = k >> 5, j = k & 31;
+        const unsigned char* blk = w.meta + r * (long long)w.meta_row + (k >> 8) * 16;
+        unsigned sc, m;
+        q4k_scale_min(blk + 4, u & 7, sc, m);
+        const unsigned char* q = w.qs + r * (long long)w.qs_row + u * 16 + (j & 15);
+        const unsigned q0 = j < 16 ? (q[0] & 15u) : (q[0] >> 4);
+        const unsigned q1 = j < 16 ? (q[1] & 15u) : (q[1] >> 4);
+        const __half2 p = __floats2half2_rn(float(sc * q0), float(sc * q1));  // integers < 1024: exact
+        qplane[i] = *reinterpret_cast<const unsigned*>(&p);
+        if (j == 0) {
+            const float f = __uint_as_float(unsigned(127 + shift[r]) << 23);
+            unsigned hi, lo;
+            split_exact(h2f((unsigned short)(blk[2] | (blk[3] << 8))) * float(m) * f, 0.f, hi, lo);
+            min_hi[r * units + u] = (unsigned short)(hi & 0xffffu);
+            min_lo[r * units + u] = (unsigned short)(lo & 0xffffu);
+        }
+        if ((k & 255) == 0) qscale[r * (w.cols / 256) + (k >> 8)] = h2f((unsigned short)(blk[0] | (blk[1] << 8)));
+    }
+}
+
 __global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx, int* ids, const int* blk,
                              const int* slot, int tpb) {
     const int t = blockIdx.x;
@@ -1232,6 +1283,35 @@ void launch_planes(const DeviceMatrix& w, std::uint16_t* hi, std::uint16_t* lo, 
     if (!w.row_shift || w.cols % 2) throw std::invalid_argument("planes need row shifts and an even width");
     planes_kernel<<<148 * 8, 256, 0, s>>>(w, reinterpret_cast<unsigned*>(hi), reinterpret_cast<unsigned*>(lo));
     TVARA_LAUNCHED();
+}
+
+std::size_t q4k_planes_bytes(int rows, int cols) {
+    return std::size_t(rows) * cols * 2 + std::size_t(rows) * (cols / 32) * 4 + std::size_t(rows) * (cols / 256) * 4 +
+           std::size_t(rows) + 5 * 256;
+}
+
+void launch_q4k_planes(DeviceMatrix& w, void* storage, cudaStream_t s) {
+    if (w.type != kQ4_K || w.cols % 256) throw std::invalid_argument("Q4_K planes need Q4_K rows");
+    auto* at = static_cast<unsigned char*>(storage);
+    auto take = [&](std::size_t bytes) {
+        unsigned char* p = at;
+        at += (bytes + 255) & ~std::size_t(255);
+        return p;
+    };
+    auto* qplane = reinterpret_cast<std::uint16_t*>(take(std::size_t(w.rows) * w.cols * 2));
+    auto* min_hi = reinterpret_cast<std::uint16_t*>(take(std::size_t(w.rows) * (w.cols / 32) * 2));
+    auto* min_lo = reinterpret_cast<std::uint16_t*>(take(std::size_t(w.rows) * (w.cols / 32) * 2));
+    auto* qscale = reinterpret_cast<float*>(take(std::size_t(w.rows) * (w.cols / 256) * 4));
+    auto* shift = reinterpret_cast<signed char*>(take(std::size_t(w.rows)));
+    q4k_min_shift_kernel<<<(w.rows + 7) / 8, 256, 0, s>>>(w, shift);
+    TVARA_LAUNCHED();
+    q4k_planes_kernel<<<148 * 8, 256, 0, s>>>(w, reinterpret_cast<unsigned*>(qplane), qscale, min_hi, min_lo, shift);
+    TVARA_LAUNCHED();
+    w.qplane = qplane;
+    w.qscale = qscale;
+    w.qmin_hi = min_hi;
+    w.qmin_lo = min_lo;
+    w.qmin_shift = shift;
 }
 
 void launch_finite_check(const DeviceMatrix& w, int* flag, cudaStream_t s) {

@@ -35,8 +35,10 @@ void launch_gemm_tc(const GemmArgs& a, void* workspace, std::size_t workspace_by
 std::size_t gemm_tc_workspace(int max_tokens, int max_cols);
 // Where the tensor-core path keeps the split activations of `tokens` rows of
 // width `cols` in its workspace (hi, lo FP16 [tokens][cols], per-row shift).
+// (hi, lo [tokens][cols], shift [tokens], and the sub-block sums shi, slo
+// [tokens][cols / 32] of the Q4_K min term, written when cols % 32 == 0)
 void gemm_tc_split_buffers(void* workspace, std::size_t workspace_bytes, int tokens, int cols, __half*& hi,
-                           __half*& lo, int*& shift);
+                           __half*& lo, int*& shift, __half** shi = nullptr, __half** slo = nullptr);
 // Choose and run the projection (GEMV below the crossover, tensor cores above).
 void launch_projection(const GemmArgs& a, void* workspace, std::size_t workspace_bytes, cudaStream_t s);
 
@@ -53,6 +55,10 @@ void launch_row_shift(const DeviceMatrix& w, signed char* out, cudaStream_t s);
 // Fills hi / lo ([rows][cols] FP16 each) with the exact split of every
 // value times 2^row_shift (the tensor-core planes of DeviceMatrix).
 void launch_planes(const DeviceMatrix& w, std::uint16_t* hi, std::uint16_t* lo, cudaStream_t s);
+// Q4_K tensor-core form (DeviceMatrix::qplane ...) in `storage` of
+// q4k_planes_bytes; sets the matrix's pointers.
+std::size_t q4k_planes_bytes(int rows, int cols);
+void launch_q4k_planes(DeviceMatrix& w, void* storage, cudaStream_t s);
 // Minimum token count routed to the tensor-core projection.
 void set_tc_min_tokens(int n);
 

@@ -21,4 +21,22 @@ __device__ __forceinline__ void split_exact(float x0, float x1, unsigned& hi, un
     lo = *reinterpret_cast<const unsigned*>(&l);
 }
 
+// The Q4_K min term's B operand, written by the kernels that split a token's
+// activations: when lanes 8m..8m+7 hold the eight float4s of one 32-element
+// sub-block (float4 k at lane k % 32), the sub-block sum scaled by
+// 2^(shift - 5) (below 2^15 since every |x * 2^shift| is) is split exactly
+// into shi / slo [unit].  Every lane of the warp calls it (shuffles).
+__device__ __forceinline__ void subblock_sum_split(float4 v, int k, bool valid, float f32, __half* shi, __half* slo) {
+    float sum = valid ? (v.x + v.y) + (v.z + v.w) : 0.f;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (valid && (k & 7) == 0) {
+        unsigned hi, lo;
+        split_exact(sum * f32, 0.f, hi, lo);
+        shi[k >> 3] = __ushort_as_half((unsigned short)(hi & 0xffffu));
+        slo[k >> 3] = __ushort_as_half((unsigned short)(lo & 0xffffu));
+    }
+}
+
 }  // namespace tvara

@@ -67,7 +67,7 @@ class NativeModel:
             opts.kv_dtype = {None: KV_F32, "f32": KV_F32, "f16": KV_F16, KV_F32: KV_F32, KV_F16: KV_F16}[kv_dtype]
             opts.max_step_tokens = int(max_step_tokens or 0)
             opts.tp_rank, opts.tp_size = int(tp_rank), int(tp_size)
-            opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2}[weight_planes]
+            opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2, "hilo": 3}[weight_planes]
             self._nccl_id = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
             opts.nccl_id = C.cast(self._nccl_id, C.c_void_p) if self._nccl_id is not None else None
             self._handle = lib.tvara_model_open_ex(encoded, max_blocks, block_tokens, C.byref(opts))
