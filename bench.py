@@ -75,7 +75,7 @@ def parse():
     ap.add_argument("--suffix", type=int, nargs=2, default=(64, 2048), metavar=("MIN", "MAX"),
                     help="unique suffix length range per request")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--kv", choices=["f16", "f32", "i8"], default="f16")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-standalone", action="store_true", help="skip the standalone GEMV / matmul figures")
     ap.add_argument("--planes", choices=["auto", "hilo", "off"], default="auto",
@@ -136,12 +136,20 @@ def fill_pool_random(model, seed):
     import torch
     info = model.kv_pool()
     n = info["max_blocks"] * info["block_elements"]
-    t = torch.as_tensor(DeviceView(info["base"], n, "<f2" if info["kv_dtype"] == 1 else "<f4"), device="cuda")
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     chunk = 1 << 28
-    for i in range(0, n, chunk):
-        t[i:i + chunk].normal_(0.0, 1.0, generator=g)
+    if info["kv_dtype"] == 2:  # int8 codes and one F32 scale per row of head_dim
+        t = torch.as_tensor(DeviceView(info["base"], n, "|i1"), device="cuda")
+        for i in range(0, n, chunk):
+            t[i:i + chunk].random_(-127, 128, generator=g)
+        rows = n // info["head_dim"]
+        sc = torch.as_tensor(DeviceView(info["scales"], rows, "<f4"), device="cuda")
+        sc.uniform_(0.005, 0.02, generator=g)
+    else:
+        t = torch.as_tensor(DeviceView(info["base"], n, "<f2" if info["kv_dtype"] == 1 else "<f4"), device="cuda")
+        for i in range(0, n, chunk):
+            t[i:i + chunk].normal_(0.0, 1.0, generator=g)
     torch.cuda.synchronize()
 
 
@@ -448,9 +456,10 @@ def run_ours(args):
     L, H, HKV, D = cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["hidden"]
     dh = D // H
     tp = world
-    es = 2 if args.kv == "f16" else 4
+    es = {"f16": 2, "f32": 4, "i8": 1}[args.kv]
     mean_ctx = float(np.mean(lens0 + args.warmup + args.steps + 1 + (args.steps - 1) / 2))  # profiled pass
-    attn_bytes = args.requests * (mean_ctx * 2 * (HKV // tp) * dh * es + 2 * (H // tp) * dh * 4)
+    row_scale = 4 if args.kv == "i8" else 0  # int8 pools: one F32 scale per K/V row
+    attn_bytes = args.requests * (mean_ctx * 2 * (HKV // tp) * (dh * es + row_scale) + 2 * (H // tp) * dh * 4)
     attn_launches = int(prof_n[0])
     attn_ms = float(prof_ms[0])
     proj_launches = int(prof_n[1])

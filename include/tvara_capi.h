@@ -67,12 +67,15 @@ TVARA_API int tvara_sequence_truncate(tvara_model* model, uint64_t sequence, siz
 
 /* ---- additive: open options ------------------------------------------- */
 
-enum { TVARA_KV_F32 = 0, TVARA_KV_F16 = 1 };
+/* TVARA_KV_I8: the reference's experimental per token-head int8 KV
+ * (python/tvara/quantized_kv.py): int8 codes plus one F32 scale per
+ * (token, KV head) row; lossy against the F32 KV of the served path. */
+enum { TVARA_KV_F32 = 0, TVARA_KV_F16 = 1, TVARA_KV_I8 = 2 };
 
 typedef struct tvara_open_options {
     uint32_t struct_size;      /* sizeof(tvara_open_options) */
     int32_t device;            /* CUDA ordinal; -1 keeps the current device */
-    uint32_t kv_dtype;         /* TVARA_KV_F32 (reference numerics) or TVARA_KV_F16 */
+    uint32_t kv_dtype;         /* TVARA_KV_F32 (reference numerics), TVARA_KV_F16 or TVARA_KV_I8 */
     uint32_t max_step_tokens;  /* tokens per device step (scratch sizing); 0 = 2048 */
     uint32_t tp_rank;          /* tensor-parallel rank of this handle */
     uint32_t tp_size;          /* tensor-parallel group size; 0 or 1 = no TP */
@@ -215,6 +218,11 @@ typedef struct tvara_kv_pool_info {
     uint32_t layers, kv_heads, head_dim, block_tokens;
 } tvara_kv_pool_info;
 TVARA_API int tvara_kv_pool(tvara_model* model, tvara_kv_pool_info* info);
+/* TVARA_KV_I8 pools: the device array of row scales, one F32 per (block,
+ * layer, kind, KV head, slot) row -- the row of element offset o is o /
+ * head_dim; a row decodes as code * scale.  *scales is NULL for other
+ * dtypes.  0 / -1. */
+TVARA_API int tvara_kv_pool_scales(tvara_model* model, float** scales);
 
 /* Appends `count` positions to a sequence's block table exactly as decoding
  * would (block allocation, copy-on-write of a shared tail) without computing

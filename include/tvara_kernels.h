@@ -53,6 +53,12 @@ TVARA_API int tvara_sample_logits(const float* logits, size_t rows, size_t vocab
                                   int32_t* status, double* top_values, uint32_t* top_ids, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* The int8 KV encode of TVARA_KV_I8 pools (python/tvara/quantized_kv.py:
+ * 21-30, QuantizedKV.encode): rows F32 [n][dim] (device) -> codes int8
+ * [n][dim] and scales F32 [n] (device).  A non-finite row fails with
+ * "Nonfinite KV input" (the call synchronises the stream to report it). */
+TVARA_API int tvara_kv_quantize(const float* rows, size_t n, size_t dim, int8_t* codes, float* scales, void* stream);
+
 /* Device scratch tvara_quant_matmul needs for `tokens` rows of width `cols`
  * (0 when the call runs on the CUDA-core path, at most 4 tokens). */
 TVARA_API size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens);
@@ -75,7 +81,7 @@ TVARA_API int tvara_quant_matmul(int type, const void* packed, size_t rows, size
  *   ((((b*layers + l)*2 + kind)*kv_heads + g)*block_tokens + s)*head_dim + e. */
 typedef struct tvara_attention_args {
     uint32_t struct_size;       /* sizeof(tvara_attention_args) */
-    uint32_t kv_dtype;          /* TVARA_KV_F32 or TVARA_KV_F16 */
+    uint32_t kv_dtype;          /* TVARA_KV_F32, TVARA_KV_F16 or TVARA_KV_I8 (needs kv_scales) */
     uint32_t heads, kv_heads, head_dim, block_tokens;
     uint32_t layers, layer;
     size_t max_blocks;
@@ -87,6 +93,9 @@ typedef struct tvara_attention_args {
     size_t tables_len;
     const uint32_t* table_offset; /* host [n_queries] */
     const uint32_t* visible;      /* host [n_queries], each >= 1 */
+    /* TVARA_KV_I8: device F32 scale of each pool row (element offset / head_dim);
+     * callers of the shorter struct (struct_size up to `visible`) get F32/F16 only */
+    const float* kv_scales;
 } tvara_attention_args;
 
 /* Device scratch (bytes) tvara_paged_attention needs for these arguments. */

@@ -30,7 +30,10 @@ from tvara_b200.gguf import GGUFFile
 
 
 class OracleModel:
-    def __init__(self, path, max_positions: int | None = None):
+    def __init__(self, path, max_positions: int | None = None, kv_quant: bool = False):
+        # kv_quant: K and V rows pass through the int8 format of TVARA_KV_I8
+        # pools (oracle/kvquant.py) before they are attended, as they are stored
+        self.kv_quant = kv_quant
         f = GGUFFile(path)
         md = f.metadata
         self.vocab = len(md["tokenizer.ggml.tokens"])
@@ -133,6 +136,10 @@ class OracleModel:
             q = self.rotary(self.matvec(b["attn_q"], xn), self.heads, pos)
             k = self.rotary(self.matvec(b["attn_k"], xn), self.kv_heads, pos)
             v = self.matvec(b["attn_v"], xn)
+            if self.kv_quant:
+                from oracle import kvquant
+                k = kvquant.roundtrip(k.reshape(self.kv_heads, self.dim)).reshape(-1)
+                v = kvquant.roundtrip(v.reshape(self.kv_heads, self.dim)).reshape(-1)
             keys = np.array(state["k"][i] + [k], np.float32)
             values = np.array(state["v"][i] + [v], np.float32)
             att = self.attention(q, keys, values)

@@ -24,6 +24,10 @@ its seed, so only the reference's outputs are stored:
                      constraint, and seeded temperature / top-k / min-p /
                      top-p sampling with penalties.  Only this file:
                      ``python tests/golden/make_golden.py sampling``.
+* quantized_kv.npz -- rows (zero, subnormal, tiny, large, exact .5 ties,
+                     random) and the codes and scales of the reference's own
+                     QuantizedKV.encode (python/tvara/quantized_kv.py).  Only
+                     this file: ``python tests/golden/make_golden.py kv``.
 """
 
 from __future__ import annotations
@@ -93,8 +97,30 @@ def sampling_golden(tiny_path):
     np.savez_compressed(HERE / "sampling.npz", **out)
 
 
+def quantized_kv_golden():
+    sys.path.insert(0, "/root/reference/python")
+    from tvara.quantized_kv import QuantizedKV
+    rng = np.random.default_rng(4242)
+    d = 64
+    rows = [np.zeros(d, np.float32), np.full(d, 1e-44, np.float32), np.full(d, 1e-30, np.float32),
+            (rng.standard_normal(d) * 3e38 / 4).astype(np.float32)]
+    tie = np.zeros(d, np.float32)
+    tie[0] = 127.0
+    tie[1:] = np.arange(1, d, dtype=np.float32) + 0.5  # exact halves after dividing by a scale of 1
+    rows.append(tie)
+    rows += [(rng.standard_normal(d) * s).astype(np.float32) for s in (1e-3, 1.0, 30.0)]
+    rows += [(rng.standard_normal(d) * rng.uniform(0.01, 10)).astype(np.float32) for _ in range(24)]
+    rows = np.stack(rows)
+    codes, scales = QuantizedKV.encode(rows)
+    np.savez_compressed(HERE / "quantized_kv.npz", rows=rows, codes=codes, scales=scales)
+
+
 def main():
     import tempfile
+    if sys.argv[1:] == ["kv"]:
+        quantized_kv_golden()
+        print("wrote quantized_kv.npz")
+        return
     if sys.argv[1:] == ["sampling"]:
         tmp = Path(tempfile.mkdtemp())
         sampling_golden(gguf.make_llama(tmp / "tiny.gguf", "tiny", seed=0))
@@ -126,6 +152,7 @@ def main():
         out[f"out_{kind}"] = vals.view(np.uint32)
     np.savez_compressed(HERE / "dequant.npz", **out)
     sampling_golden(tiny)
+    quantized_kv_golden()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -69,6 +69,7 @@ SIGNATURES = {
     "tvara_batch_step": (C.c_int, [P, SZ, U64P, U32P, U32P, C.c_uint32, F32P, SZ, U32P, SZ]),
     "tvara_batch_sample": (C.c_int, [P, SZ, U64P, U32P, U32P, C.POINTER(Sampling), F32P, SZ, U32P, I32P, F64P,
                                      U32P]),
+    "tvara_kv_pool_scales": (C.c_int, [P, C.POINTER(C.c_void_p)]),
     "tvara_sequence_fork": (U64, [P, U64]),
     "tvara_sequence_length": (C.c_int, [P, U64, SZP]),
     "tvara_kv_stats": (C.c_int, [P, SZP, SZP]),
@@ -106,6 +107,7 @@ SIGNATURES = {
     "tvara_dequantize": (C.c_int, [C.c_int, P, SZ, P, P]),
     "tvara_packed_bytes": (SZ, [C.c_int, SZ, SZ]),
     "tvara_pack": (C.c_int, [C.c_int, P, SZ, SZ, P, P]),
+    "tvara_kv_quantize": (C.c_int, [P, SZ, SZ, P, P, P]),
     "tvara_sample_workspace": (SZ, [SZ, SZ]),
     "tvara_sample_logits": (C.c_int, [P, SZ, SZ, P, U64P, F64P, F64P, F64P, P, C.c_uint32, P, P, P, P, P, SZ,
                                       P]),
@@ -138,6 +140,7 @@ class AttentionArgs(C.Structure):
         ("tables_len", C.c_size_t),
         ("table_offset", C.c_void_p),
         ("visible", C.c_void_p),
+        ("kv_scales", C.c_void_p),
     ]
 
 

@@ -75,8 +75,9 @@ tvara_model* open_model(const char* path, size_t blocks, size_t tokens, const tv
         if (o->struct_size < offsetof(tvara_open_options, weight_planes))
             throw std::invalid_argument("invalid open options size");
         opt.device = o->device;
-        if (o->kv_dtype > TVARA_KV_F16) throw std::invalid_argument("invalid KV dtype");
+        if (o->kv_dtype > TVARA_KV_I8) throw std::invalid_argument("invalid KV dtype");
         opt.kv_f16 = o->kv_dtype == TVARA_KV_F16;
+        opt.kv_i8 = o->kv_dtype == TVARA_KV_I8;
         if (o->max_step_tokens) opt.max_step_tokens = int(o->max_step_tokens);
         opt.tp_rank = int(o->tp_rank);
         opt.tp_size = o->tp_size ? int(o->tp_size) : 1;
@@ -393,11 +394,21 @@ int tvara_kv_pool(tvara_model* model, tvara_kv_pool_info* info) {
         info->base = e.kv_pool();
         info->max_blocks = g.max_blocks;
         info->block_elements = size_t(e.block_elements());
-        info->kv_dtype = e.options().kv_f16 ? TVARA_KV_F16 : TVARA_KV_F32;
+        info->kv_dtype = e.options().kv_i8 ? TVARA_KV_I8 : e.options().kv_f16 ? TVARA_KV_F16 : TVARA_KV_F32;
         info->layers = uint32_t(g.layers);
         info->kv_heads = uint32_t(e.local_kv_heads());
         info->head_dim = uint32_t(g.head_dim);
         info->block_tokens = uint32_t(g.tokens_per_block);
+        return 0;
+    });
+}
+
+int tvara_kv_pool_scales(tvara_model* model, float** scales) {
+    return guarded<int>(-1, [&] {
+        if (!scales) throw std::invalid_argument("invalid output pointer");
+        auto& e = engine_of(model);
+        std::lock_guard lock(model->mutex);
+        *scales = e.kv_scales();
         return 0;
     });
 }

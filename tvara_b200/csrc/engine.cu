@@ -116,7 +116,7 @@ Engine::~Engine() {
     for (auto e : events_) cudaEventDestroy(e);
     radix_.reset();
     coll_.reset();
-    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_, static_cast<void*>(token_ids_),
+    for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_, static_cast<void*>(token_ids_), static_cast<void*>(kv_scales_),
                     static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_, sample_buf_})
         if (p) cudaFree(p);
     if (meta_host_) cudaFreeHost(meta_host_);
@@ -274,7 +274,7 @@ void Engine::load(const gguf::File& f) {
         };
         std::size_t need = 0;
         for (auto* m : mats) need += form_bytes(m);
-        const std::size_t es = opt_.kv_f16 ? 2 : 4;
+        const std::size_t es = opt_.kv_elem_bytes();
         const std::size_t pool = std::size_t(layers_) * 2 * hkv_ * book_->geometry().tokens_per_block * d * es *
                                  book_->geometry().max_blocks;
         std::size_t free_b = 0, total_b = 0;
@@ -320,7 +320,7 @@ void Engine::load(const gguf::File& f) {
 
     // ---- KV pool: [block][layer][K|V][kv head][slot][d]
     const auto& g = book_->geometry();
-    const std::size_t es = opt_.kv_f16 ? 2 : 4;
+    const std::size_t es = opt_.kv_elem_bytes();
     kind_stride_ = (long long)hkv_ * g.tokens_per_block * d;
     layer_stride_ = 2 * kind_stride_;
     block_stride_ = (long long)layers_ * layer_stride_;
@@ -330,6 +330,7 @@ void Engine::load(const gguf::File& f) {
     if (pool_bytes > free_b) throw std::runtime_error("KV pool does not fit in device memory");
     TVARA_CUDA(cudaMalloc(&kv_, pool_bytes));
     TVARA_CUDA(cudaMalloc(&token_ids_, g.max_blocks * g.tokens_per_block * sizeof(int)));
+    if (opt_.kv_i8) TVARA_CUDA(cudaMalloc(&kv_scales_, std::size_t(block_stride_ / d) * g.max_blocks * sizeof(float)));
 
     // ---- scratch for tmax_ tokens (one allocation)
     const std::size_t T = tmax_;
@@ -534,7 +535,8 @@ void Engine::profile_read(double* ms, unsigned long long* groups) const {
 }
 
 void Engine::copy_blocks(const int2* pairs, int n) {
-    launch_block_copy(kv_, block_stride_ * (opt_.kv_f16 ? 2 : 4), pairs, n, stream_);
+    launch_block_copy(kv_, block_stride_ * (long long)opt_.kv_elem_bytes(), pairs, n, stream_);
+    if (kv_scales_) launch_id_copy(reinterpret_cast<int*>(kv_scales_), int(block_stride_ / cfg_.head_dim()), pairs, n, stream_);
     launch_id_copy(token_ids_, int(book_->geometry().tokens_per_block), pairs, n, stream_);
 }
 
@@ -724,6 +726,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         ra.slot_index = d_slot;
         ra.kv = kv_;
         ra.kv_f16 = opt_.kv_f16;
+        ra.kv_i8 = opt_.kv_i8;
+        ra.kv_scales = kv_scales_;
         ra.block_stride = block_stride_;
         ra.layer_offset = (long long)l * layer_stride_;
         ra.kind_stride = kind_stride_;
@@ -736,6 +740,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         aa.out = att_;
         aa.kv = kv_;
         aa.kv_f16 = opt_.kv_f16;
+        aa.kv_i8 = opt_.kv_i8;
+        aa.kv_scales = kv_scales_;
         aa.hq = hq_;
         aa.hkv = hkv_;
         aa.dim = d;
@@ -847,6 +853,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     if (*err_host_) {
         const int code = *err_host_;
         TVARA_CUDA(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
+        if (code == 3) throw std::invalid_argument("Nonfinite KV input");
         throw std::runtime_error("device bounds check failed (code " + std::to_string(code) + ")");
     }
     if (argmax)

@@ -23,6 +23,8 @@ namespace tvara {
 struct EngineOptions {
     int device = -1;
     bool kv_f16 = false;
+    bool kv_i8 = false;  // int8 per token-head with F32 scales (quantized_kv.py)
+    std::size_t kv_elem_bytes() const { return kv_i8 ? 1 : kv_f16 ? 2 : 4; }
     int max_step_tokens = 2048;
     int tp_rank = 0, tp_size = 1;
     bool has_nccl_id = false;
@@ -82,6 +84,7 @@ public:
     // Appends positions to a sequence's table without computing K/V.
     void reserve(std::uint64_t seq, std::size_t count);
     void* kv_pool() const { return kv_; }
+    float* kv_scales() const { return kv_scales_; }
     long long block_elements() const { return block_stride_; }
     int local_kv_heads() const { return hkv_; }
 
@@ -169,6 +172,7 @@ private:
     // Token id of every KV slot, [block][slot]: the history the device-side
     // sampler reads through a sequence's block table.
     int* token_ids_ = nullptr;
+    float* kv_scales_ = nullptr;  // int8 pools: one F32 scale per (block, layer, kind, head, slot) row
     // Copies blocks (KV payload and token ids) on the engine stream.
     void copy_blocks(const int2* pairs, int n);
 

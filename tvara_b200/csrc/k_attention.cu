@@ -39,6 +39,15 @@ __device__ __forceinline__ void load_vec(const KV* p, bool ok, float (&out)[VEC]
             out[j + 2] = v.z;
             out[j + 3] = v.w;
         }
+    } else if constexpr (sizeof(KV) == 1) {
+        // int8 rows: the caller multiplies by the row's scale
+#pragma unroll
+        for (int j = 0; j < VEC; j += 16) {
+            uint4 v = ok ? __ldg(reinterpret_cast<const uint4*>(p + j)) : make_uint4(0, 0, 0, 0);
+            const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 16; ++i) out[j + i] = float(int((signed char)((w[i >> 2] >> (8 * (i & 3))) & 255u)));
+        }
     } else {
 #pragma unroll
         for (int j = 0; j < VEC; j += 8) {
@@ -108,6 +117,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs a) {
                 const int s = c0 + it * SPL + grp;
                 valid[it] = s < s_hi;
                 load_vec<KV, VEC>(kb + (long long)s * D + sub * VEC, valid[it], kv[it]);
+                if constexpr (sizeof(KV) == 1) {
+                    // decoded value = code * scale (quantized_kv.py:49-54), one F32 product
+                    const float sc = valid[it] ? a.kv_scales[(kb - pool) / D + s] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < VEC; ++j) kv[it][j] = __fmul_rn(kv[it][j], sc);
+                }
             }
             float sc[NIT][G];
             float cmax[G];
@@ -146,6 +161,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs a) {
             for (int it = 0; it < NIT; ++it) {
                 const int s = c0 + it * SPL + grp;
                 load_vec<KV, VEC>(vb + (long long)s * D + sub * VEC, valid[it], kv[it]);
+                if constexpr (sizeof(KV) == 1) {
+                    const float sc = valid[it] ? a.kv_scales[(vb - pool) / D + s] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < VEC; ++j) kv[it][j] = __fmul_rn(kv[it][j], sc);
+                }
             }
 #pragma unroll
             for (int it = 0; it < NIT; ++it)
@@ -1132,6 +1152,22 @@ void run_g(const AttnArgs& a, cudaStream_t s) {
     }
 }
 
+// int8 pools: the register-streaming kernel (one 16-byte load per lane and
+// slot, decoded with the slot's scale).
+template <int D>
+void run_g_i8(const AttnArgs& a, cudaStream_t s) {
+    dim3 grid(a.n_work, a.hkv);
+    switch (a.hq / a.hkv) {
+#define TV_G(N)                                                                        \
+    case N:                                                                            \
+        attn_kernel<D, signed char, N><<<grid, kAttnWarps * 32, 0, s>>>(a);            \
+        break;
+        TV_G(1) TV_G(2) TV_G(3) TV_G(4) TV_G(5) TV_G(6) TV_G(7) TV_G(8)
+#undef TV_G
+        default: throw std::invalid_argument("unsupported query/KV head ratio (1..8)");
+    }
+}
+
 template <typename KV>
 void run_d(const AttnArgs& a, cudaStream_t s) {
     switch (a.dim) {
@@ -1148,8 +1184,21 @@ void run_d(const AttnArgs& a, cudaStream_t s) {
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_work <= 0) return;
-    if (a.kv_f16) run_d<__half>(a, s);
-    else run_d<float>(a, s);
+    if (a.kv_i8) {
+        if (!a.kv_scales) throw std::invalid_argument("int8 KV needs its scales");
+        switch (a.dim) {
+            case 16: run_g_i8<16>(a, s); break;
+            case 32: run_g_i8<32>(a, s); break;
+            case 64: run_g_i8<64>(a, s); break;
+            case 128: run_g_i8<128>(a, s); break;
+            case 256: run_g_i8<256>(a, s); break;
+            default: throw std::invalid_argument("unsupported head_dim (16, 32, 64, 128, 256)");
+        }
+    } else if (a.kv_f16) {
+        run_d<__half>(a, s);
+    } else {
+        run_d<float>(a, s);
+    }
     TVARA_LAUNCHED();
     if (a.n_combine > 0) {
         combine_kernel<<<dim3(a.n_combine, a.hq), 128, 0, s>>>(a);

@@ -87,11 +87,39 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ldx, c
     }
 }
 
+// One warp: the reference's int8 encode of a row of d floats
+// (python/tvara/quantized_kv.py:21-30): scale = max|x| / 127 (1 for a zero
+// row, the smallest positive float if that underflows), codes rint(x / scale)
+// clipped to [-127, 127]; a non-finite row records error 3.
+__device__ void encode_row_i8(const float* src, int d, signed char* dst, float* scale_out, int* err) {
+    const int lane = threadIdx.x & 31;
+    float mx = 0.f;
+    int bad = 0;
+    for (int i = lane; i < d; i += 32) {
+        bad |= !isfinite(src[i]);
+        mx = fmaxf(mx, fabsf(src[i]));
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    bad = __any_sync(0xffffffffu, bad);
+    if (bad && lane == 0) atomicExch(err, 3);  // "Nonfinite KV input"
+    float scale = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
+    if (scale == 0.f) scale = __int_as_float(1);
+    for (int i = lane; i < d; i += 32)
+        dst[i] = (signed char)int(fminf(fmaxf(rintf(__fdiv_rn(src[i], scale)), -127.f), 127.f));
+    if (lane == 0) *scale_out = scale;
+}
+
+__global__ void kv_quantize_kernel(const float* rows, int n, int d, signed char* codes, float* scales, int* err) {
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r < n) encode_row_i8(rows + (long long)r * d, d, codes + (long long)r * d, scales + r, err);
+}
+
 // RoPE of model.hpp:67-76 with the cos/sin table the host built from the
 // reference's own float expression; pairs are (i, i+d/2) for the split layout
 // and (2i, 2i+1) interleaved.  The rotation keeps the reference's two
 // roundings per term (no contraction).  One CTA per token.
 __global__ void rope_kv_kernel(RopeArgs a) {
+    extern __shared__ float rkv[];  // int8 pools: the token's rotated K rows, then its V rows
     const int t = blockIdx.x;
     const int d = a.dim, half = d / 2;
     const long long pos = a.positions[t];
@@ -118,7 +146,10 @@ __global__ void rope_kv_kernel(RopeArgs a) {
             q[ib] = rb;
         } else if (ok) {
             const long long off = base + ((long long)h * a.tpb + slot) * d;
-            if (a.kv_f16) {
+            if (a.kv_i8) {
+                rkv[h * d + ia] = ra;
+                rkv[h * d + ib] = rb;
+            } else if (a.kv_f16) {
                 __half* kv = static_cast<__half*>(a.kv);
                 kv[off + ia] = __float2half_rn(ra);
                 kv[off + ib] = __float2half_rn(rb);
@@ -129,13 +160,22 @@ __global__ void rope_kv_kernel(RopeArgs a) {
             }
         }
     }
-    if (!ok) return;
+    if (!ok) return;  // uniform over the block
     const float* v = row + (a.hq + a.hkv) * d;
     for (int e = threadIdx.x; e < a.hkv * d; e += blockDim.x) {
         const int h = e / d, i = e % d;
         const long long off = base + a.kind_stride + ((long long)h * a.tpb + slot) * d + i;
-        if (a.kv_f16) static_cast<__half*>(a.kv)[off] = __float2half_rn(v[e]);
+        if (a.kv_i8) rkv[a.hkv * d + e] = v[e];
+        else if (a.kv_f16) static_cast<__half*>(a.kv)[off] = __float2half_rn(v[e]);
         else static_cast<float*>(a.kv)[off] = v[e];
+    }
+    if (!a.kv_i8) return;
+    // int8 rows, one warp per (kind, head)
+    __syncthreads();
+    for (int r = threadIdx.x >> 5; r < 2 * a.hkv; r += blockDim.x >> 5) {
+        const int kind = r < a.hkv ? 0 : 1, h = r % a.hkv;
+        const long long off = base + kind * a.kind_stride + ((long long)h * a.tpb + slot) * d;
+        encode_row_i8(rkv + r * d, d, static_cast<signed char*>(a.kv) + off, a.kv_scales + off / d, a.err);
     }
 }
 
@@ -259,9 +299,21 @@ void launch_rmsnorm_split(const float* x, int ldx, const int* rows, int n, int d
     run_rmsnorm<true>(x, ldx, rows, n, dim, w, eps, out, ldo, hi, lo, shift, shi, slo, s);
 }
 
+void launch_kv_quantize(const float* rows, int n, int d, signed char* codes, float* scales, int* err, cudaStream_t s) {
+    if (n <= 0) return;
+    kv_quantize_kernel<<<(n + 7) / 8, 256, 0, s>>>(rows, n, d, codes, scales, err);
+    TVARA_LAUNCHED();
+}
+
+std::size_t rope_kv_smem(const RopeArgs& a) {
+    return a.kv_i8 ? std::size_t(2) * a.hkv * a.dim * sizeof(float) : 0;
+}
+
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
     if (a.tokens <= 0) return;
-    rope_kv_kernel<<<a.tokens, 256, 0, s>>>(a);
+    if (a.kv_i8 && (!a.kv_scales || rope_kv_smem(a) > 48 * 1024))
+        throw std::invalid_argument("int8 KV: scales missing or KV heads x head_dim above 6144");
+    rope_kv_kernel<<<a.tokens, 256, rope_kv_smem(a), s>>>(a);
     TVARA_LAUNCHED();
 }
 

@@ -89,12 +89,22 @@ struct RopeArgs {
     const int* slot_index = nullptr; // [T] slot within the block
     void* kv = nullptr;              // pool base
     int kv_f16 = 0;
+    int kv_i8 = 0;                   // int8 per token-head with F32 scales (kv_scales)
+    float* kv_scales = nullptr;      // [element offset of a row / dim] for kv_i8
     long long block_stride = 0, layer_offset = 0, kind_stride = 0;  // elements
     int tpb = 0;
     int max_blocks = 0;
     int* err = nullptr;
 };
 // Rotates q and k at each token's position and writes k, v into the pool.
+// int8 pools: each (token, KV head) row is stored as the reference's
+// quantized_kv encode (python/tvara/quantized_kv.py:21-30): scale = max|x| /
+// 127 (1 for a zero row, the smallest subnormal if that underflows),
+// values rint(x / scale) clipped to [-127, 127]; a non-finite row sets the
+// error flag (3).  Dynamic shared memory: rope_kv_smem bytes.
+std::size_t rope_kv_smem(const RopeArgs& a);
+// The same encode on n rows of d floats (codes [n][d], scales [n]).
+void launch_kv_quantize(const float* rows, int n, int d, signed char* codes, float* scales, int* err, cudaStream_t s);
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
 
 // g[i] = g[i] * (sigmoid(g[i]) * u[i]) for separate gate/up projections.
@@ -106,6 +116,8 @@ struct AttnArgs {
     float* out = nullptr;      // [T][hq*d]
     const void* kv = nullptr;
     int kv_f16 = 0;
+    int kv_i8 = 0;                    // int8 rows with F32 scales
+    const float* kv_scales = nullptr; // row r (element offset / dim) scale
     int hq = 0, hkv = 0, dim = 0, tpb = 0;
     long long block_stride = 0, layer_offset = 0, kind_stride = 0;  // elements
     const int* tables = nullptr;  // concatenated physical block ids

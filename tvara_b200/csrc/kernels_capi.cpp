@@ -2,6 +2,7 @@
 // caller-owned device memory.
 #include "../../include/tvara_kernels.h"
 
+#include <cstddef>
 #include <cstring>
 #include <algorithm>
 #include <cmath>
@@ -58,7 +59,13 @@ struct AttnLayout {
 constexpr std::size_t kPartsCap = 16384;
 
 AttnLayout layout_for(const tvara_attention_args* a) {
-    if (!a || a->struct_size < sizeof(tvara_attention_args)) throw std::invalid_argument("invalid attention arguments");
+    // kv_scales was appended: the shorter struct stays valid for F32 / F16 pools
+    if (!a || a->struct_size < offsetof(tvara_attention_args, kv_scales))
+        throw std::invalid_argument("invalid attention arguments");
+    if (a->kv_dtype > TVARA_KV_I8 ||
+        (a->kv_dtype == TVARA_KV_I8 &&
+         (a->struct_size < offsetof(tvara_attention_args, kv_scales) + sizeof(a->kv_scales) || !a->kv_scales)))
+        throw std::invalid_argument("invalid KV dtype or missing int8 scales");
     if (!a->heads || !a->kv_heads || a->heads % a->kv_heads || !a->block_tokens || !a->layers || a->layer >= a->layers)
         throw std::invalid_argument("invalid attention geometry");
     AttnLayout L;
@@ -191,6 +198,23 @@ int tvara_sample_logits(const float* logits, size_t rows, size_t vocab, const in
     });
 }
 
+int tvara_kv_quantize(const float* rows, size_t n, size_t dim, int8_t* codes, float* scales, void* stream) {
+    return guarded([&] {
+        if (!rows || !codes || !scales || !n || !dim || n > 0x7fffffff || dim > 0x7fffffff)
+            throw std::invalid_argument("invalid KV quantize arguments");
+        auto s = static_cast<cudaStream_t>(stream);
+        int* err = nullptr;
+        TVARA_CUDA(cudaMallocAsync(&err, sizeof(int), s));
+        TVARA_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        tvara::launch_kv_quantize(rows, int(n), int(dim), reinterpret_cast<signed char*>(codes), scales, err, s);
+        int host = 0;
+        TVARA_CUDA(cudaMemcpyAsync(&host, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+        TVARA_CUDA(cudaFreeAsync(err, s));
+        TVARA_CUDA(cudaStreamSynchronize(s));
+        if (host) throw std::invalid_argument("Nonfinite KV input");
+    });
+}
+
 size_t tvara_quant_matmul_workspace(size_t cols, size_t tokens) {
     return tokens <= 4 ? 0 : tvara::gemm_tc_workspace(int(tokens), int(cols));
 }
@@ -236,6 +260,8 @@ int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t
         g.out = a->out;
         g.kv = a->pool;
         g.kv_f16 = a->kv_dtype == TVARA_KV_F16;
+        g.kv_i8 = a->kv_dtype == TVARA_KV_I8;
+        g.kv_scales = g.kv_i8 ? a->kv_scales : nullptr;
         g.hq = int(a->heads);
         g.hkv = int(a->kv_heads);
         g.dim = int(a->head_dim);

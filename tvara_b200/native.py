@@ -19,7 +19,7 @@ import numpy as np
 from . import load_library
 from ._bindings import OpenOptions, Sampling, F32P, F64P, U32P, U64P, I32P
 
-KV_F32, KV_F16 = 0, 1
+KV_F32, KV_F16, KV_I8 = 0, 1, 2
 STEP_ALL_LOGITS = 1
 STEP_FINITE_ARGMAX = 2
 ARGMAX_NONFINITE = 0xFFFFFFFF
@@ -64,7 +64,8 @@ class NativeModel:
             opts = OpenOptions()
             opts.struct_size = C.sizeof(OpenOptions)
             opts.device = -1 if device is None else int(device)
-            opts.kv_dtype = {None: KV_F32, "f32": KV_F32, "f16": KV_F16, KV_F32: KV_F32, KV_F16: KV_F16}[kv_dtype]
+            opts.kv_dtype = {None: KV_F32, "f32": KV_F32, "f16": KV_F16, "i8": KV_I8, KV_F32: KV_F32, KV_F16: KV_F16,
+                             KV_I8: KV_I8}[kv_dtype]
             opts.max_step_tokens = int(max_step_tokens or 0)
             opts.tp_rank, opts.tp_size = int(tp_rank), int(tp_size)
             opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2, "hilo": 3}[weight_planes]
@@ -285,7 +286,14 @@ class NativeModel:
             self._check_open()
             if self._library.tvara_kv_pool(self._handle, C.byref(info)):
                 self._raise_error()
-        return {f: getattr(info, f) for f, _ in Info._fields_}
+        out = {f: getattr(info, f) for f, _ in Info._fields_}
+        if out["kv_dtype"] == KV_I8:
+            scales = C.c_void_p()
+            with self._lock:
+                if self._library.tvara_kv_pool_scales(self._handle, C.byref(scales)):
+                    self._raise_error()
+            out["scales"] = scales.value  # one F32 per pool row (element offset / head_dim)
+        return out
 
     def reserve(self, sequence, count):
         """Append `count` positions without computing their K/V."""
