@@ -488,11 +488,12 @@ def run_ours(args):
                  "note": "algorithmic bytes count the shared 1024-token prefix once per reader; DRAM traffic "
                          "reads it once (L2 serves the rest), so frac can exceed 1"}
     ach = kernels["projections"]["achieved_tflops"]
-    roof_proj = {"kernel": "tc_gemm_kernel (all projections of a step)", "bound": "tensor", "achieved": ach,
+    roof_proj = {"kernel": "tc_gemm_q4k_kernel (the Q4_K projections of a step)", "bound": "tensor", "achieved": ach,
                  "peak": tensor, "unit": "TFLOP/s", "frac": ach / tensor if ach else None,
                  "traffic": NCU_TRAFFIC["projections"] if full else None, "peak_source": pk_kind,
-                 "algorithmic_flops_per_step": proj_flops_step, "tensor_work_multiplier": 3,
-                 "note": "useful flops 2*T*rows*cols; the exact hi/lo FP16 split issues 3 MMAs per product"}
+                 "algorithmic_flops_per_step": proj_flops_step, "tensor_work_multiplier": 2,
+                 "note": "useful flops 2*T*rows*cols; the Q4_K form issues 2 FP16 MMAs per product (plane of "
+                         "sc*q times the hi and lo activation parts) plus the min term (1/32 of the K range)"}
     roof = roof_attn if attn_ms >= proj_ms else roof_proj
     # survey convention: sum over kernels of max(bytes/BW, flops/P) over the measured step time
     head_bytes = cfg["vocab"] * D * 34 / 32
