@@ -50,7 +50,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes (read + write) per launch from ncu captures of this workload
 # (profiles/attn_mma_llama8b_decode512.txt, profiles/tc_gemm_planes_llama8b_512tok.txt).
-NCU_TRAFFIC = {"attention": 2.63e9, "projections": 2.60e8}
+NCU_TRAFFIC = {"attention": 2.63e9, "projections": 1.42e8}
 
 
 def peaks():
