@@ -49,7 +49,8 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per launch from ncu captures of this workload
-# (profiles/attn_mma_llama8b_decode512.txt, profiles/tc_gemm_planes_llama8b_512tok.txt).
+# (profiles/attn_mma_llama8b_decode512.txt, profiles/tc_gemm_q4k_llama8b_512tok.txt: the average over the four
+# projection launches of a layer).
 NCU_TRAFFIC = {"attention": 2.63e9, "projections": 1.42e8}
 
 
