@@ -52,23 +52,25 @@ def test_kv_quantize_random_rows_and_nonfinite(capi):
     assert status != 0 and b"Nonfinite KV input" in capi.tvara_last_error()
 
 
-@pytest.mark.parametrize("dim", [32, 64, 128])
-@pytest.mark.parametrize("group", [1, 4])
-def test_attention_over_int8_pool_matches_decoded_oracle(capi, dim, group):
+def _int8_attention_case(capi, rng, dim, group, tpb, lengths, spread=0.0):
     """Ragged rows over an int8 pool: within the F32 kernels' tolerance of the
     oracle over the decoded rows.  Slots past each row's length hold codes
-    with huge scales, so reading one would show."""
+    with huge scales, so reading one would show.  `spread`: each slot's rows
+    are scaled by 2^U(-spread, spread), so row scales differ by that many
+    octaves."""
     from oracle import kvquant
     from tests.test_gpu_kernels import attn_close
     from tvara_b200._bindings import AttentionArgs
     torch = torch_dev()
-    rng = np.random.default_rng(dim + group)
-    L, H, tpb, B = 2, 2, 16, 40
+    L, H = 2, 2
+    B = sum((n + tpb - 1) // tpb for n in lengths) + 4
     heads = H * group
     rows = rng.standard_normal((B, L, 2, H, tpb, dim)).astype(np.float32)
+    if spread:  # V rows over 2 * spread octaves, K rows over 4
+        rows[:, :, 1] *= np.exp2(rng.uniform(-spread, spread, (B, L, H, tpb, 1))).astype(np.float32)
+        rows[:, :, 0] *= np.exp2(rng.uniform(-2, 2, (B, L, H, tpb, 1))).astype(np.float32)
     codes, scales = kvquant.encode(rows)
     scales = scales[..., 0].copy()
-    lengths = [1, 15, 16, 17, 33, 70]
     perm = list(rng.permutation(B))
     tables, offsets = [], []
     for n in lengths:
@@ -106,11 +108,33 @@ def test_attention_over_int8_pool_matches_decoded_oracle(capi, dim, group):
         vals = np.stack([decoded[ids[p // tpb], layer, 1, :, p % tpb] for p in range(length)]).astype(np.float64)
         q64 = q[i].astype(np.float64).reshape(heads, dim)
         want = np.empty(heads * dim)
+        mag = np.empty(heads * dim)  # weighted mean of |v|: the size of the summands
         for h in range(heads):
             s = keys[:, h // group] @ q64[h] / np.sqrt(dim)
             w = np.exp(s - s.max())
             want[h * dim:(h + 1) * dim] = (w @ vals[:, h // group]) / w.sum()
-        assert attn_close(got[i], want), (i, np.abs(got[i] - want).max())
+            mag[h * dim:(h + 1) * dim] = (w @ np.abs(vals[:, h // group])) / w.sum()
+        if spread:
+            # summands of very different sizes cancel: F32 rounding is relative to them
+            assert np.all(np.abs(got[i] - want) <= 2e-5 * (1 + np.abs(want) + mag)), (i, np.abs(got[i] - want).max())
+        else:
+            assert attn_close(got[i], want), (i, np.abs(got[i] - want).max())
+
+
+@pytest.mark.parametrize("dim", [32, 64, 128])
+@pytest.mark.parametrize("group", [1, 4])
+def test_attention_over_int8_pool_matches_decoded_oracle(capi, dim, group):
+    _int8_attention_case(capi, np.random.default_rng(dim + group), dim, group, 16, [1, 15, 16, 17, 33, 70])
+
+
+@pytest.mark.parametrize("dim,group,tpb", [(128, 4, 16), (128, 8, 32), (64, 2, 16), (64, 4, 32)])
+def test_attention_int8_long_contexts_and_spread_scales(capi, dim, group, tpb):
+    """Contexts long enough to be split over several work items (partials
+    merged afterwards), with row scales spread over 24 octaves: the int8
+    tensor-core kernel's running V-scale bound rescales O as larger rows
+    arrive."""
+    rng = np.random.default_rng(300 + dim + group + tpb)
+    _int8_attention_case(capi, rng, dim, group, tpb, [5, 250, 1024, 1500, 3001], spread=12.0)
 
 
 def test_engine_int8_kv_matches_quantized_oracle(tiny_path):

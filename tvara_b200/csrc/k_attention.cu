@@ -1045,6 +1045,328 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
     }
 }
 
+// Tensor-core paged attention for int8 KV (head_dim 64 or 128, blocks of a
+// multiple of 16 slots).  The codes are integers in [-127, 127], exact in
+// F16, so the MMAs run on the codes themselves and the row scales enter
+// outside them: S = scale_k[pos] * (code_K . Q^T), and each position's V
+// scale multiplies its softmax weight before P^T meets code_V^T.  CTA and
+// ring as attn_mma_kernel (a four-deep ring: a stage is half the bytes); one
+// TMA box per K or V run of a block (rows of D bytes, 128- or 64-byte
+// swizzle) plus a bulk copy of the block's 2 x tpb scales.
+//   Fragments are read as 32-bit words from the swizzled rows (4 codes of
+// one row) and widened to F16 pairs with byte permutes: for S^T the k order
+// inside a 16-wide step is permuted so a lane's four k slots (2tq, 2tq+1,
+// 2tq+8, 2tq+9) are the 4 consecutive d of one word (Q^T takes the same
+// order); for O^T += V^T P^T two m tiles share one word per position (rows
+// gq, gq+8 of tile 2j are d = 32j + 4gq + {0, 1}, of tile 2j+1 + {2, 3}).
+//   P' = P * scale_v * 2^(15 - ev) with ev a running power-of-two bound of
+// the scales seen (raised like the softmax maximum, O rescaled when it
+// grows), so P' < 2^16 splits into exact hi + lo F16 as P does for F16 KV.
+constexpr int kI8Ring = 4;
+
+// Shared-memory byte offset of (row, byte) in a tile of rows of RB bytes
+// written by TMA with the RB-byte swizzle (RB = 128 or 64).
+template <int RB>
+__device__ __forceinline__ unsigned swz_off(int row, int byte) {
+    if constexpr (RB == 128) return unsigned(row * 128 + ((((byte >> 4) ^ row) & 7) << 4) + (byte & 15));
+    else return unsigned(row * 64 + ((((byte >> 4) ^ (row >> 1)) & 3) << 4) + (byte & 15));
+}
+__device__ __forceinline__ unsigned lds32(unsigned addr) {
+    unsigned v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+// Bytes (b_lo, b_hi) of a biased word (code + 128 per byte) as an F16 pair of
+// the signed codes: 0x64XX is 1024 + XX, exact, minus 1152.
+__device__ __forceinline__ unsigned i8pair_f16(unsigned biased, unsigned sel) {
+    const unsigned w = __byte_perm(biased, 0x64646464u, sel);
+    __half2 h = *reinterpret_cast<const __half2*>(&w);
+    h = __hsub2(h, __half2half2(__ushort_as_half(0x6480)));  // 1152
+    return *reinterpret_cast<const unsigned*>(&h);
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                         AttnArgs a) {
+    constexpr int KS = D / 16;
+    static_assert((D == 64 || D == 128) && G >= 1 && G <= 8, "int8 tensor-core attention shape");
+    extern __shared__ unsigned char att_raw[];
+    __shared__ std::uint64_t bars[kAttnWarps][kI8Ring];
+    __shared__ float s_m[kAttnWarps][8], s_l[kAttnWarps][8];
+    const int tpb = a.tpb;
+    const int run = tpb * D;           // bytes of one K (or V) run of a block
+    const int stage = 2 * run;
+    unsigned char* smem = att_raw + ((1024u - (s_u32(att_raw) & 1023u)) & 1023u);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned char* ring = smem + std::size_t(warp) * kI8Ring * stage;
+    const unsigned ring_s = s_u32(ring);
+    // scales: [warp][stage][K | V][tpb] floats after all rings
+    float* scl = reinterpret_cast<float*>(smem + std::size_t(kAttnWarps) * kI8Ring * stage) +
+                 std::size_t(warp) * kI8Ring * 2 * tpb;
+
+    const int4 wk = a.work[blockIdx.x];
+    const int part = a.work_part[blockIdx.x];
+    const int t = wk.x, toff = wk.y, p0 = wk.z, p1 = wk.w;
+    const int h = blockIdx.y;
+    const int b0 = p0 / tpb, b1 = (p1 - 1) / tpb;
+    const int nblk = b1 - b0 - warp >= 0 ? (b1 - b0 - warp) / kAttnWarps + 1 : 0;
+
+    if (lane == 0) {
+        for (int s = 0; s < kI8Ring; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[warp][s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
+    const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
+    auto issue = [&](int i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        int pb = a.tables[toff + bi];
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;
+        }
+        const long long yk = pb * block_rows + head_row;
+        const long long yv = yk + kind_rows;
+        const int st = (i % kI8Ring);
+        const unsigned dst = ring_s + unsigned(st * stage);
+        std::uint64_t* bar = &bars[warp][st];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)),
+                     "r"(stage + 8 * tpb)
+                     : "memory");
+        tma_load_2d(dst, &kv_map, 0, int(yk), s_u32(bar));
+        tma_load_2d(dst + run, &kv_map, 0, int(yv), s_u32(bar));
+        bulk_g2s(scl + st * 2 * tpb, a.kv_scales + yk, unsigned(4 * tpb), bar);
+        bulk_g2s(scl + st * 2 * tpb + tpb, a.kv_scales + yv, unsigned(4 * tpb), bar);
+    };
+    if (lane == 0)
+        for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i);
+
+    const int gq = lane >> 2, tq = lane & 3;
+    // Q^T as B fragments in the permuted k order: step kk, lane (gq, tq)
+    // holds head gq, d 16kk + 4tq + {0, 1} and {2, 3}; scaled by 2^sh per
+    // head, hi + lo.
+    unsigned qh[KS][2], ql[KS][2];
+    float qinv0, qinv1;
+    {
+        const bool row = gq < G;
+        const float scale = rsqrtf(float(D));
+        const float* qp = a.q + (long long)t * a.hq * D + (h * G + (row ? gq : 0)) * D;
+        float v[KS][4];
+        float mx = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const float4 f = row ? *reinterpret_cast<const float4*>(qp + 16 * kk + 4 * tq)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[kk][0] = f.x * scale;
+            v[kk][1] = f.y * scale;
+            v[kk][2] = f.z * scale;
+            v[kk][3] = f.w * scale;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[kk][e]));
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        int e2 = 0;
+        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);
+        const int sh = max(-100, min(100, 15 - e2));
+        const float up = exp2i(sh);
+        const float inv = exp2i(-sh);
+        qinv0 = __shfl_sync(0xffffffffu, inv, (2 * tq) * 4);
+        qinv1 = __shfl_sync(0xffffffffu, inv, (2 * tq + 1) * 4);
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            split_f16x2(v[kk][0] * up, v[kk][1] * up, qh[kk][0], ql[kk][0]);
+            split_f16x2(v[kk][2] * up, v[kk][3] * up, qh[kk][1], ql[kk][1]);
+        }
+    }
+
+    float o[KS][4];  // tile 2j: d 32j + 4gq + {0 (regs 0, 1), 1 (regs 2, 3)}; tile 2j+1: + {2, 3}
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    int ev = -1000;  // running exponent bound of the V scales (none yet)
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const int bi = b0 + warp + i * kAttnWarps;
+        const int st = i % kI8Ring;
+        const unsigned parity = (i / kI8Ring) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[warp][st], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const unsigned kst = ring_s + unsigned(st * stage);
+        const unsigned vst = kst + run;
+        const float* sk = scl + st * 2 * tpb;
+        const float* sv = sk + tpb;
+        const int s_hi = min(tpb, p1 - bi * tpb);
+        for (int sub = 0; sub < s_hi; sub += 16) {
+            const int pa = sub + gq, pb = sub + gq + 8;
+            const bool va = pa < s_hi, vb = pb < s_hi;
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                const unsigned wa = lds32(kst + swz_off<D>(pa, 16 * kk + 4 * tq)) ^ 0x80808080u;
+                const unsigned wb = lds32(kst + swz_off<D>(pb, 16 * kk + 4 * tq)) ^ 0x80808080u;
+                const unsigned f[4] = {i8pair_f16(wa, 0x4140), i8pair_f16(wb, 0x4140), i8pair_f16(wa, 0x4342),
+                                       i8pair_f16(wb, 0x4342)};
+                mma16816(s, f, qh[kk][0], qh[kk][1]);
+                mma16816(s, f, ql[kk][0], ql[kk][1]);
+            }
+            const float ka = sk[pa], kb = sk[pb];
+            s[0] = va ? s[0] * qinv0 * ka : -INFINITY;
+            s[1] = va ? s[1] * qinv1 * ka : -INFINITY;
+            s[2] = vb ? s[2] * qinv0 * kb : -INFINITY;
+            s[3] = vb ? s[3] * qinv1 * kb : -INFINITY;
+            float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
+            // V scales of the tile's visible positions and their bound 2^et
+            const float fa = va ? sv[pa] : 0.f, fb = vb ? sv[pb] : 0.f;
+            float vm = fmaxf(fa, fb);
+#pragma unroll
+            for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+                vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o2));
+            }
+            int et = -100;
+            if (vm > 0.f && isfinite(vm)) {
+                frexpf(vm, &et);  // vm < 2^et
+                et = max(-100, min(126, et));
+            }
+            float grow = 1.f;
+            if (et > ev) {
+                grow = ev - et >= -126 ? exp2i(ev - et) : 0.f;
+                ev = et;
+            }
+            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+            const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
+            const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
+            m0 = n0;
+            m1 = n1;
+            const float pa0 = __expf(s[0] - n0), pa1 = __expf(s[1] - n1);
+            const float pb0 = __expf(s[2] - n0), pb1 = __expf(s[3] - n1);
+            l0 = fmaf(l0, al0, pa0 + pb0);
+            l1 = fmaf(l1, al1, pa1 + pb1);
+            const float r0 = al0 * grow, r1 = al1 * grow;
+            if (__any_sync(0xffffffffu, r0 != 1.f || r1 != 1.f)) {
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    o[mt][0] *= r0;
+                    o[mt][1] *= r1;
+                    o[mt][2] *= r0;
+                    o[mt][3] *= r1;
+                }
+            }
+            // P' = P * scale_v * 2^(15 - ev); positions past the end have P = 0
+            const float up = exp2i(15 - ev);
+            const float wa = fa * up, wb = fb * up;
+            unsigned ha, la, hb, lb;
+            split_f16x2(pa0 * wa, pa1 * wa, ha, la);
+            split_f16x2(pb0 * wb, pb1 * wb, hb, lb);
+            const unsigned bh0 = movmatrix_t(ha), bh1 = movmatrix_t(hb);
+            const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) {
+                // words of V[sub + k][32j + 4gq ..] for k = 2tq, 2tq+1, 2tq+8, 2tq+9
+                const int c = 32 * j + 4 * gq;
+                const unsigned w0 = lds32(vst + swz_off<D>(sub + 2 * tq, c));
+                const unsigned w1 = lds32(vst + swz_off<D>(sub + 2 * tq + 1, c));
+                const unsigned w8 = lds32(vst + swz_off<D>(sub + 2 * tq + 8, c));
+                const unsigned w9 = lds32(vst + swz_off<D>(sub + 2 * tq + 9, c));
+                // interleave the two positions' bytes: e = 0, 1 | e = 2, 3
+                const unsigned lo01 = __byte_perm(w0, w1, 0x5140) ^ 0x80808080u;
+                const unsigned hi01 = __byte_perm(w0, w1, 0x7362) ^ 0x80808080u;
+                const unsigned lo89 = __byte_perm(w8, w9, 0x5140) ^ 0x80808080u;
+                const unsigned hi89 = __byte_perm(w8, w9, 0x7362) ^ 0x80808080u;
+                const unsigned fe[4] = {i8pair_f16(lo01, 0x4140), i8pair_f16(lo01, 0x4342), i8pair_f16(lo89, 0x4140),
+                                        i8pair_f16(lo89, 0x4342)};
+                const unsigned fo[4] = {i8pair_f16(hi01, 0x4140), i8pair_f16(hi01, 0x4342), i8pair_f16(hi89, 0x4140),
+                                        i8pair_f16(hi89, 0x4342)};
+                mma16816(o[2 * j], fe, bh0, bh1);
+                mma16816(o[2 * j], fe, bl0, bl1);
+                mma16816(o[2 * j + 1], fo, bh0, bh1);
+                mma16816(o[2 * j + 1], fo, bl0, bl1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kI8Ring < nblk) issue(i + kI8Ring);
+    }
+    if (lane == 0 && failed) {
+        for (int i = 0; i < kI8Ring && i < nblk; ++i)
+            for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[warp][i], 0) && !bar_try(&bars[warp][i], 1);
+                 ++spin) {
+            }
+    }
+#pragma unroll
+    for (int o2 = 4; o2 < 32; o2 <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
+    }
+    __syncwarp();
+    // This warp's O (heads < G, scaled back by 2^(ev - 15)) over its own ring.
+    float* acc = reinterpret_cast<float*>(ring);
+    const float down = ev == -1000 ? 0.f : exp2i(ev - 15);
+    const int ha = 2 * tq, hb = 2 * tq + 1;
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+        const int d = 32 * j + 4 * gq;
+        if (ha < G) {
+            acc[ha * D + d] = o[2 * j][0] * down;
+            acc[ha * D + d + 1] = o[2 * j][2] * down;
+            acc[ha * D + d + 2] = o[2 * j + 1][0] * down;
+            acc[ha * D + d + 3] = o[2 * j + 1][2] * down;
+        }
+        if (hb < G) {
+            acc[hb * D + d] = o[2 * j][1] * down;
+            acc[hb * D + d + 1] = o[2 * j][3] * down;
+            acc[hb * D + d + 2] = o[2 * j + 1][1] * down;
+            acc[hb * D + d + 3] = o[2 * j + 1][3] * down;
+        }
+    }
+    if (gq == 0) {
+        s_m[warp][ha] = m0;
+        s_l[warp][ha] = l0;
+        s_m[warp][hb] = m1;
+        s_l[warp][hb] = l1;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, e = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][g]);
+        float L = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (s_m[w][g] == -INFINITY) continue;
+            const float f = __expf(s_m[w][g] - M);
+            L = fmaf(s_l[w][g], f, L);
+            A = fmaf(reinterpret_cast<const float*>(smem + std::size_t(w) * kI8Ring * stage)[g * D + e], f, A);
+        }
+        const int head = h * G + g;
+        if (part < 0) {
+            a.out[(long long)t * a.hq * D + head * D + e] = A / L;
+        } else {
+            float* pp = a.partial + ((long long)part * a.hq + head) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+}
+
 // Merge split partials: out = sum_i A_i e^{M_i-M} / sum_i L_i e^{M_i-M}.
 __global__ void combine_kernel(AttnArgs a) {
     const int4 c = a.combine[blockIdx.x];
@@ -1116,6 +1438,49 @@ void run_mma(const AttnArgs& a, dim3 grid, cudaStream_t s) {
     attn_mma_kernel<D, G><<<grid, kAttnWarps * 32, smem, s>>>(map, a);
 }
 
+// The int8 pool as rows of D bytes, one box per K or V run of a block (tpb
+// rows), swizzled over the row width (128 or 64 bytes).
+CUtensorMap kv_map_i8(const AttnArgs& a, int D) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t((long long)a.max_blocks * (a.block_stride / D))};
+    const cuuint64_t strides[1] = {cuuint64_t(D)};
+    const cuuint32_t box[2] = {cuuint32_t(D), cuuint32_t(a.tpb)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a.kv), dims,
+                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+constexpr long long mma_i8_smem_bytes(int D, int tpb) {
+    return 1024 + (long long)kAttnWarps * kI8Ring * (2 * tpb * D + 8 * tpb);
+}
+
+// Whether the int8 tensor-core kernel takes these arguments: head_dim 64 or
+// 128, blocks of a multiple of 16 slots, 16-byte aligned pool, scales and
+// queries, and every scale run of a block 16-byte aligned (row offsets of
+// blocks, layers and kinds multiples of 4 rows).
+bool mma_i8_ok(const AttnArgs& a) {
+    if (!a.kv_i8 || (a.dim != 64 && a.dim != 128) || a.tpb % 16 || a.tpb > 256) return false;
+    if (reinterpret_cast<std::uintptr_t>(a.kv) % 16 || reinterpret_cast<std::uintptr_t>(a.kv_scales) % 16 ||
+        reinterpret_cast<std::uintptr_t>(a.q) % 16)
+        return false;
+    const long long D = a.dim;
+    if (a.block_stride % (4 * D) || a.layer_offset % (4 * D) || a.kind_stride % (4 * D)) return false;
+    if (mma_i8_smem_bytes(a.dim, a.tpb) > 200 * 1024) return false;
+    return (long long)a.max_blocks * (a.block_stride / D) < (1ll << 31);
+}
+
+template <int D, int G>
+void run_mma_i8(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+    const int smem = int(mma_i8_smem_bytes(D, a.tpb));
+    TVARA_CUDA(cudaFuncSetAttribute(attn_mma_i8_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const CUtensorMap map = kv_map_i8(a, D);
+    attn_mma_i8_kernel<D, G><<<grid, kAttnWarps * 32, smem, s>>>(map, a);
+}
+
 template <int D, typename KV, int G>
 constexpr bool xpose_ok() {
     constexpr int LPS = (D * int(sizeof(KV)) / 16) < 32 ? (D * int(sizeof(KV)) / 16) : 32;
@@ -1152,15 +1517,22 @@ void run_g(const AttnArgs& a, cudaStream_t s) {
     }
 }
 
-// int8 pools: the register-streaming kernel (one 16-byte load per lane and
-// slot, decoded with the slot's scale).
+// int8 pools: the tensor-core kernel where its shape conditions hold, else
+// the register-streaming kernel (one 16-byte load per lane and slot, decoded
+// with the slot's scale).
 template <int D>
 void run_g_i8(const AttnArgs& a, cudaStream_t s) {
     dim3 grid(a.n_work, a.hkv);
+    constexpr bool kMmaShape = D == 64 || D == 128;
+    const bool mma = kMmaShape && mma_i8_ok(a);
     switch (a.hq / a.hkv) {
 #define TV_G(N)                                                                        \
     case N:                                                                            \
-        attn_kernel<D, signed char, N><<<grid, kAttnWarps * 32, 0, s>>>(a);            \
+        if (mma) {                                                                     \
+            if constexpr (kMmaShape) run_mma_i8<D, N>(a, grid, s);                     \
+        } else {                                                                       \
+            attn_kernel<D, signed char, N><<<grid, kAttnWarps * 32, 0, s>>>(a);        \
+        }                                                                              \
         break;
         TV_G(1) TV_G(2) TV_G(3) TV_G(4) TV_G(5) TV_G(6) TV_G(7) TV_G(8)
 #undef TV_G
