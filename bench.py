@@ -482,9 +482,10 @@ def run_ours(args):
     full = args.layers is None and tp == 1 and args.requests == 512
     hbm, tensor = pk["hbm_gbs"], pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
     ach = kernels["attention"]["achieved_gbs"]
-    roof_attn = {"kernel": "attn_mma_kernel (paged attention, one launch per layer)", "bound": "hbm",
+    attn_kernel = {"f16": "attn_mma_kernel", "i8": "attn_mma_i8_kernel"}.get(args.kv, "attn_kernel")
+    roof_attn = {"kernel": f"{attn_kernel} (paged attention, one launch per layer)", "bound": "hbm",
                  "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm if ach else None,
-                 "traffic": NCU_TRAFFIC["attention"] if full else None, "peak_source": pk_kind,
+                 "traffic": NCU_TRAFFIC["attention"] if full and args.kv == "f16" else None, "peak_source": pk_kind,
                  "algorithmic_bytes_per_launch": attn_bytes,
                  "note": "algorithmic bytes count the shared 1024-token prefix once per reader; DRAM traffic "
                          "reads it once (L2 serves the rest), so frac can exceed 1"}
@@ -510,7 +511,7 @@ def run_ours(args):
     line = {
         "metric": "ragged-batch decode tok/s (8B-shape Q4_K)", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (Q4_K/Q8_0 weights, f16 KV)",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": f"f32 (Q4_K/Q8_0 weights, {args.kv} KV)",
         "data": "synthetic",
         "config": {"workload": f"{args.config} ragged decode, {args.requests} requests, shared {args.prefix}-token "
                                f"prefix + U({args.suffix[0]},{args.suffix[1]}) suffix + U(0,out) generated, "

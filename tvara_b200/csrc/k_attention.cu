@@ -1046,23 +1046,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
 }
 
 // Tensor-core paged attention for int8 KV (head_dim 64 or 128, blocks of a
-// multiple of 16 slots).  The codes are integers in [-127, 127], exact in
-// F16, so the MMAs run on the codes themselves and the row scales enter
-// outside them: S = scale_k[pos] * (code_K . Q^T), and each position's V
-// scale multiplies its softmax weight before P^T meets code_V^T.  CTA and
-// ring as attn_mma_kernel (a four-deep ring: a stage is half the bytes); one
-// TMA box per K or V run of a block (rows of D bytes, 128- or 64-byte
-// swizzle) plus a bulk copy of the block's 2 x tpb scales.
-//   Fragments are read as 32-bit words from the swizzled rows (4 codes of
-// one row) and widened to F16 pairs with byte permutes: for S^T the k order
-// inside a 16-wide step is permuted so a lane's four k slots (2tq, 2tq+1,
-// 2tq+8, 2tq+9) are the 4 consecutive d of one word (Q^T takes the same
-// order); for O^T += V^T P^T two m tiles share one word per position (rows
-// gq, gq+8 of tile 2j are d = 32j + 4gq + {0, 1}, of tile 2j+1 + {2, 3}).
-//   P' = P * scale_v * 2^(15 - ev) with ev a running power-of-two bound of
-// the scales seen (raised like the softmax maximum, O rescaled when it
-// grows), so P' < 2^16 splits into exact hi + lo F16 as P does for F16 KV.
-constexpr int kI8Ring = 4;
+// multiple of 16 slots).  CTA and ring as attn_mma_kernel (three stages
+// per warp, four CTAs per SM: a stage is half the bytes); one TMA box per K or V run of a block (rows of
+// D bytes, 128- or 64-byte swizzle) plus a bulk copy of the block's 2 x tpb
+// row scales.  The scales enter outside the MMAs:
+//   S^T = scale_k[pos] * (code_K . Q^T) on the integer tensor path
+// (mma.m16n8k32, s8 x u8/s8 -> s32): the K codes are the A operand straight
+// from ldmatrix, Q^T is 22-bit fixed point (per head 2^sh) as three byte
+// digits (low two unsigned, top signed), so each product is exact and the
+// three digit sums combine in F32;
+//   O^T += code_V^T . P'^T on the F16 path (codes in [-127, 127] are exact
+// F16): ldmatrix.trans of the int8 rows gives each lane two positions x two
+// d per word, widened to F16 pairs by a byte permute (0x64XX = 1024 + XX)
+// and one subtraction; the m rows of a tile are d = 2g (row g) and 2g + 1
+// (row g + 8).  P' = P * scale_v * 2^(15 - ev) with ev a running
+// power-of-two bound of the V scales seen (raised like the softmax maximum,
+// O rescaled when it grows), so P' < 2^15 splits into exact hi + lo F16 as P
+// does for F16 KV.
+constexpr int kI8Ring = 3;
 
 // Shared-memory byte offset of (row, byte) in a tile of rows of RB bytes
 // written by TMA with the RB-byte swizzle (RB = 128 or 64).
@@ -1071,22 +1072,33 @@ __device__ __forceinline__ unsigned swz_off(int row, int byte) {
     if constexpr (RB == 128) return unsigned(row * 128 + ((((byte >> 4) ^ row) & 7) << 4) + (byte & 15));
     else return unsigned(row * 64 + ((((byte >> 4) ^ (row >> 1)) & 3) << 4) + (byte & 15));
 }
-__device__ __forceinline__ unsigned lds32(unsigned addr) {
-    unsigned v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-// Bytes (b_lo, b_hi) of a biased word (code + 128 per byte) as an F16 pair of
-// the signed codes: 0x64XX is 1024 + XX, exact, minus 1152.
+// F16 pair from bytes of a biased word (code + 128 per byte) picked by
+// `sel` next to 0x64 bytes: 0x64XX is 1024 + XX, exact; minus 1152.
 __device__ __forceinline__ unsigned i8pair_f16(unsigned biased, unsigned sel) {
     const unsigned w = __byte_perm(biased, 0x64646464u, sel);
     __half2 h = *reinterpret_cast<const __half2*>(&w);
     h = __hsub2(h, __half2half2(__ushort_as_half(0x6480)));  // 1152
     return *reinterpret_cast<const unsigned*>(&h);
 }
+// d += A b for one m16n8k32 integer tile (A s8 row-major 16x32, b col-major
+// 32x8, u8 or s8).
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const __grid_constant__ CUtensorMap kv_map,
+__global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const __grid_constant__ CUtensorMap kv_map,
                                                                          AttnArgs a) {
     constexpr int KS = D / 16;
     static_assert((D == 64 || D == 128) && G >= 1 && G <= 8, "int8 tensor-core attention shape");
@@ -1144,49 +1156,64 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const _
         for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i);
 
     const int gq = lane >> 2, tq = lane & 3;
-    // Q^T as B fragments in the permuted k order: step kk, lane (gq, tq)
-    // holds head gq, d 16kk + 4tq + {0, 1} and {2, 3}; scaled by 2^sh per
-    // head, hi + lo.
-    unsigned qh[KS][2], ql[KS][2];
-    float qinv0, qinv1;
+    // Q^T in three byte digits (B fragments of m16n8k32): step kk, lane
+    // (gq, tq) holds head gq, d 32kk + 4tq + {0..3} (reg 0) and 32kk + 16 +
+    // 4tq + {0..3} (reg 1) of x = rint(q / sqrt(D) * 2^sh), |x| <= 2^21 per
+    // head; digit j is byte j of x (0, 1 unsigned; 2 signed, two's complement).
+    constexpr int K32 = D / 32;
+    unsigned qd[K32][3][2];
+    float qinv0, qinv1;  // 2^-sh of heads 2tq and 2tq + 1 (this lane's S columns)
     {
         const bool row = gq < G;
         const float scale = rsqrtf(float(D));
         const float* qp = a.q + (long long)t * a.hq * D + (h * G + (row ? gq : 0)) * D;
-        float v[KS][4];
+        float v[K32][2][4];
         float mx = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-            const float4 f = row ? *reinterpret_cast<const float4*>(qp + 16 * kk + 4 * tq)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-            v[kk][0] = f.x * scale;
-            v[kk][1] = f.y * scale;
-            v[kk][2] = f.z * scale;
-            v[kk][3] = f.w * scale;
+        for (int kk = 0; kk < K32; ++kk)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[kk][e]));
-        }
+            for (int r = 0; r < 2; ++r) {
+                const float4 f = row ? *reinterpret_cast<const float4*>(qp + 32 * kk + 16 * r + 4 * tq)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[kk][r][0] = f.x * scale;
+                v[kk][r][1] = f.y * scale;
+                v[kk][r][2] = f.z * scale;
+                v[kk][r][3] = f.w * scale;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[kk][r][e]));
+            }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         int e2 = 0;
-        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);
-        const int sh = max(-100, min(100, 15 - e2));
+        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e2);  // mx < 2^e2
+        const int sh = max(-100, min(100, 21 - e2));
         const float up = exp2i(sh);
         const float inv = exp2i(-sh);
         qinv0 = __shfl_sync(0xffffffffu, inv, (2 * tq) * 4);
         qinv1 = __shfl_sync(0xffffffffu, inv, (2 * tq + 1) * 4);
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-            split_f16x2(v[kk][0] * up, v[kk][1] * up, qh[kk][0], ql[kk][0]);
-            split_f16x2(v[kk][2] * up, v[kk][3] * up, qh[kk][1], ql[kk][1]);
-        }
+        for (int kk = 0; kk < K32; ++kk)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                int x[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) x[e] = __float2int_rn(v[kk][r][e] * up);
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    unsigned w = 0;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) w |= ((unsigned(x[e]) >> (8 * j)) & 255u) << (8 * e);
+                    qd[kk][j][r] = w;
+                }
+            }
     }
 
-    float o[KS][4];  // tile 2j: d 32j + 4gq + {0 (regs 0, 1), 1 (regs 2, 3)}; tile 2j+1: + {2, 3}
+    float o[KS][4];  // O^T tile mt: d 16mt + 2gq (regs 0, 1), + 1 (regs 2, 3); heads 2tq, 2tq + 1
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     int ev = -1000;  // running exponent bound of the V scales (none yet)
+    const int lr = lane & 7, lm = lane >> 3;  // ldmatrix: row within an 8x8 matrix, matrix index
     bool failed = false;
     for (int i = 0; i < nblk; ++i) {
         const int bi = b0 + warp + i * kAttnWarps;
@@ -1213,16 +1240,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const _
         for (int sub = 0; sub < s_hi; sub += 16) {
             const int pa = sub + gq, pb = sub + gq + 8;
             const bool va = pa < s_hi, vb = pb < s_hi;
-            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            // S^T: rows = positions sub + gq (+8), columns = heads 2tq, 2tq + 1
+            int ai[3][4] = {};
 #pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-                const unsigned wa = lds32(kst + swz_off<D>(pa, 16 * kk + 4 * tq)) ^ 0x80808080u;
-                const unsigned wb = lds32(kst + swz_off<D>(pb, 16 * kk + 4 * tq)) ^ 0x80808080u;
-                const unsigned f[4] = {i8pair_f16(wa, 0x4140), i8pair_f16(wb, 0x4140), i8pair_f16(wa, 0x4342),
-                                       i8pair_f16(wb, 0x4342)};
-                mma16816(s, f, qh[kk][0], qh[kk][1]);
-                mma16816(s, f, ql[kk][0], ql[kk][1]);
+            for (int kk = 0; kk < K32; ++kk) {
+                const int pos = sub + 8 * (lm & 1) + lr;
+                unsigned f[4];
+                ldsm_x4(kst + swz_off<D>(pos, 32 * kk + 16 * (lm >> 1)), f);
+                mma_s8u8(ai[0], f, qd[kk][0][0], qd[kk][0][1]);
+                mma_s8u8(ai[1], f, qd[kk][1][0], qd[kk][1][1]);
+                mma_s8s8(ai[2], f, qd[kk][2][0], qd[kk][2][1]);
             }
+            float s[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                s[e] = fmaf(float(ai[2][e]), 65536.f, fmaf(float(ai[1][e]), 256.f, float(ai[0][e])));
             const float ka = sk[pa], kb = sk[pb];
             s[0] = va ? s[0] * qinv0 * ka : -INFINITY;
             s[1] = va ? s[1] * qinv1 * ka : -INFINITY;
@@ -1277,25 +1309,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const _
             const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
 #pragma unroll
             for (int j = 0; j < D / 32; ++j) {
-                // words of V[sub + k][32j + 4gq ..] for k = 2tq, 2tq+1, 2tq+8, 2tq+9
-                const int c = 32 * j + 4 * gq;
-                const unsigned w0 = lds32(vst + swz_off<D>(sub + 2 * tq, c));
-                const unsigned w1 = lds32(vst + swz_off<D>(sub + 2 * tq + 1, c));
-                const unsigned w8 = lds32(vst + swz_off<D>(sub + 2 * tq + 8, c));
-                const unsigned w9 = lds32(vst + swz_off<D>(sub + 2 * tq + 9, c));
-                // interleave the two positions' bytes: e = 0, 1 | e = 2, 3
-                const unsigned lo01 = __byte_perm(w0, w1, 0x5140) ^ 0x80808080u;
-                const unsigned hi01 = __byte_perm(w0, w1, 0x7362) ^ 0x80808080u;
-                const unsigned lo89 = __byte_perm(w8, w9, 0x5140) ^ 0x80808080u;
-                const unsigned hi89 = __byte_perm(w8, w9, 0x7362) ^ 0x80808080u;
-                const unsigned fe[4] = {i8pair_f16(lo01, 0x4140), i8pair_f16(lo01, 0x4342), i8pair_f16(lo89, 0x4140),
-                                        i8pair_f16(lo89, 0x4342)};
-                const unsigned fo[4] = {i8pair_f16(hi01, 0x4140), i8pair_f16(hi01, 0x4342), i8pair_f16(hi89, 0x4140),
-                                        i8pair_f16(hi89, 0x4342)};
-                mma16816(o[2 * j], fe, bh0, bh1);
-                mma16816(o[2 * j], fe, bl0, bl1);
-                mma16816(o[2 * j + 1], fo, bh0, bh1);
-                mma16816(o[2 * j + 1], fo, bl0, bl1);
+                // matrices 0, 1: positions sub + 0..7, 8..15 of d 32j..32j+15; 2, 3: of d 32j+16..
+                const int pos = sub + 8 * (lm & 1) + lr;
+                unsigned w[4];
+                ldsm_x4_t(vst + swz_off<D>(pos, 32 * j + 16 * (lm >> 1)), w);
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    // word: (pos 2tq, d 2gq), (2tq, 2gq+1), (2tq+1, 2gq), (2tq+1, 2gq+1)
+                    const unsigned u0 = w[2 * hf] ^ 0x80808080u, u1 = w[2 * hf + 1] ^ 0x80808080u;
+                    const unsigned f[4] = {i8pair_f16(u0, 0x4240), i8pair_f16(u0, 0x4341), i8pair_f16(u1, 0x4240),
+                                           i8pair_f16(u1, 0x4341)};
+                    mma16816(o[2 * j + hf], f, bh0, bh1);
+                    mma16816(o[2 * j + hf], f, bl0, bl1);
+                }
             }
         }
         __syncwarp();
@@ -1318,19 +1344,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_i8_kernel(const _
     const float down = ev == -1000 ? 0.f : exp2i(ev - 15);
     const int ha = 2 * tq, hb = 2 * tq + 1;
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) {
-        const int d = 32 * j + 4 * gq;
+    for (int mt = 0; mt < KS; ++mt) {
+        const int d = 16 * mt + 2 * gq;
         if (ha < G) {
-            acc[ha * D + d] = o[2 * j][0] * down;
-            acc[ha * D + d + 1] = o[2 * j][2] * down;
-            acc[ha * D + d + 2] = o[2 * j + 1][0] * down;
-            acc[ha * D + d + 3] = o[2 * j + 1][2] * down;
+            acc[ha * D + d] = o[mt][0] * down;
+            acc[ha * D + d + 1] = o[mt][2] * down;
         }
         if (hb < G) {
-            acc[hb * D + d] = o[2 * j][1] * down;
-            acc[hb * D + d + 1] = o[2 * j][3] * down;
-            acc[hb * D + d + 2] = o[2 * j + 1][1] * down;
-            acc[hb * D + d + 3] = o[2 * j + 1][3] * down;
+            acc[hb * D + d] = o[mt][1] * down;
+            acc[hb * D + d + 1] = o[mt][3] * down;
         }
     }
     if (gq == 0) {
