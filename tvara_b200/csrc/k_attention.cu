@@ -1131,9 +1131,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
     __syncwarp();
     const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
     const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
-    auto issue = [&](int i) {
-        const int bi = b0 + warp + i * kAttnWarps;
-        int pb = a.tables[toff + bi];
+    // lane 0: start block i (physical id pb, read from the table beforehand)
+    auto issue = [&](int i, int pb) {
         if (pb < 0 || pb >= a.max_blocks) {
             atomicExch(a.err, 2);
             pb = 0;
@@ -1152,8 +1151,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
         bulk_g2s(scl + st * 2 * tpb, a.kv_scales + yk, unsigned(4 * tpb), bar);
         bulk_g2s(scl + st * 2 * tpb + tpb, a.kv_scales + yv, unsigned(4 * tpb), bar);
     };
+    auto table = [&](int i) { return __ldg(a.tables + toff + b0 + warp + i * kAttnWarps); };
     if (lane == 0)
-        for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i);
+        for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i, table(i));
 
     const int gq = lane >> 2, tq = lane & 3;
     // Q^T in three byte digits (B fragments of m16n8k32): step kk, lane
@@ -1218,6 +1218,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
     for (int i = 0; i < nblk; ++i) {
         const int bi = b0 + warp + i * kAttnWarps;
         const int st = i % kI8Ring;
+        // the table entry of the block issued at the end of this iteration,
+        // loaded now so its latency hides behind the compute
+        const int pnext = lane == 0 && i + kI8Ring < nblk ? table(i + kI8Ring) : 0;
         const unsigned parity = (i / kI8Ring) & 1;
         unsigned ok = 0;
         for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
@@ -1270,11 +1273,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
                 x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
                 vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o2));
             }
-            int et = -100;
-            if (vm > 0.f && isfinite(vm)) {
-                frexpf(vm, &et);  // vm < 2^et
-                et = max(-100, min(126, et));
-            }
+            // vm < 2^et from the exponent field (subnormals and 0 give -126,
+            // clamped to -100 like every bound below 2^-100)
+            const int et = max(-100, min(126, int((__float_as_uint(vm) >> 23) & 255u) - 126));
             float grow = 1.f;
             if (et > ev) {
                 grow = ev - et >= -126 ? exp2i(ev - et) : 0.f;
@@ -1325,7 +1326,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
             }
         }
         __syncwarp();
-        if (lane == 0 && i + kI8Ring < nblk) issue(i + kI8Ring);
+        if (lane == 0 && i + kI8Ring < nblk) issue(i + kI8Ring, pnext);
     }
     if (lane == 0 && failed) {
         for (int i = 0; i < kI8Ring && i < nblk; ++i)
