@@ -1059,11 +1059,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
 // F16): ldmatrix.trans of the int8 rows gives each lane two positions x two
 // d per word, widened to F16 pairs by a byte permute (0x64XX = 1024 + XX)
 // and one subtraction; the m rows of a tile are d = 2g (row g) and 2g + 1
-// (row g + 8).  P' = P * scale_v * 2^(15 - ev) with ev a running
-// power-of-two bound of the V scales seen (raised like the softmax maximum,
-// O rescaled when it grows), so P' < 2^15 splits into exact hi + lo F16 as P
-// does for F16 KV.
+// (row g + 8).  P' = P * scale_v * 2^(11 - ev) with ev a running
+// power-of-two bound of the V scales seen, so P' < 2^15 splits into exact
+// hi + lo F16 as P does for F16 KV.
+//   The softmax reference m (per head) and ev are lazy: a tile reduces and
+// rescales only when one of its scores exceeds m by more than 4 ln 2 (then
+// m becomes the maximum so far) or one of its V scales reaches 2^ev; other
+// tiles use P = e^(s - m) < 16 as they are.  Any reference gives the same
+// softmax, since O and the running sum share it.
 constexpr int kI8Ring = 3;
+constexpr float kLazyMargin = 2.7725887f;  // 4 ln 2: softmax weights stay below 16
 
 // Shared-memory byte offset of (row, byte) in a tile of rows of RB bytes
 // written by TMA with the RB-byte swizzle (RB = 128 or 64).
@@ -1212,8 +1217,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    int ev = -1000;  // running exponent bound of the V scales (none yet)
+    int ev = -1000;     // running exponent bound of the V scales (none yet)
+    float vlim = 0.f;   // 2^ev
+    float up = 0.f;     // 2^(11 - ev)
     const int lr = lane & 7, lm = lane >> 3;  // ldmatrix: row within an 8x8 matrix, matrix index
+    // This lane's ldmatrix row address within a 16-row tile, per 32 columns;
+    // the swizzle depends on the row's low four bits only, so a tile at row
+    // `sub` (a multiple of 16) adds sub * D.
+    unsigned ofs[K32];
+#pragma unroll
+    for (int kk = 0; kk < K32; ++kk) ofs[kk] = swz_off<D>(8 * (lm & 1) + lr, 32 * kk + 16 * (lm >> 1));
     bool failed = false;
     for (int i = 0; i < nblk; ++i) {
         const int bi = b0 + warp + i * kAttnWarps;
@@ -1247,9 +1260,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
             int ai[3][4] = {};
 #pragma unroll
             for (int kk = 0; kk < K32; ++kk) {
-                const int pos = sub + 8 * (lm & 1) + lr;
                 unsigned f[4];
-                ldsm_x4(kst + swz_off<D>(pos, 32 * kk + 16 * (lm >> 1)), f);
+                ldsm_x4(kst + unsigned(sub * D) + ofs[kk], f);
                 mma_s8u8(ai[0], f, qd[kk][0][0], qd[kk][0][1]);
                 mma_s8u8(ai[1], f, qd[kk][1][0], qd[kk][1][1]);
                 mma_s8s8(ai[2], f, qd[kk][2][0], qd[kk][2][1]);
@@ -1263,35 +1275,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
             s[1] = va ? s[1] * qinv1 * ka : -INFINITY;
             s[2] = vb ? s[2] * qinv0 * kb : -INFINITY;
             s[3] = vb ? s[3] * qinv1 * kb : -INFINITY;
-            float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
-            // V scales of the tile's visible positions and their bound 2^et
             const float fa = va ? sv[pa] : 0.f, fb = vb ? sv[pb] : 0.f;
-            float vm = fmaxf(fa, fb);
+            // The reference points m0, m1 (heads 2tq, 2tq + 1) and 2^ev move
+            // only when a score exceeds its reference by more than 4 ln 2 or a
+            // V scale reaches 2^ev: most tiles take no reduction and no rescale.
+            // Afterwards P = e^(s - m) < 16 and P' = P * scale_v * 2^(11 - ev) < 2^15.
+            const bool over = s[0] > m0 + kLazyMargin || s[2] > m0 + kLazyMargin || s[1] > m1 + kLazyMargin ||
+                              s[3] > m1 + kLazyMargin || fmaxf(fa, fb) >= vlim;
+            if (__any_sync(0xffffffffu, over)) {
+                float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
+                float vm = fmaxf(fa, fb);
 #pragma unroll
-            for (int o2 = 4; o2 < 32; o2 <<= 1) {
-                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
-                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
-                vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o2));
-            }
-            // vm < 2^et from the exponent field (subnormals and 0 give -126,
-            // clamped to -100 like every bound below 2^-100)
-            const int et = max(-100, min(126, int((__float_as_uint(vm) >> 23) & 255u) - 126));
-            float grow = 1.f;
-            if (et > ev) {
-                grow = ev - et >= -126 ? exp2i(ev - et) : 0.f;
-                ev = et;
-            }
-            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
-            const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
-            const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
-            m0 = n0;
-            m1 = n1;
-            const float pa0 = __expf(s[0] - n0), pa1 = __expf(s[1] - n1);
-            const float pb0 = __expf(s[2] - n0), pb1 = __expf(s[3] - n1);
-            l0 = fmaf(l0, al0, pa0 + pb0);
-            l1 = fmaf(l1, al1, pa1 + pb1);
-            const float r0 = al0 * grow, r1 = al1 * grow;
-            if (__any_sync(0xffffffffu, r0 != 1.f || r1 != 1.f)) {
+                for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                    x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                    x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+                    vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o2));
+                }
+                // vm < 2^et from the exponent field (subnormals and 0 give -126,
+                // clamped to -100 like every bound below 2^-100)
+                const int et = max(-100, min(126, int((__float_as_uint(vm) >> 23) & 255u) - 126));
+                float grow = 1.f;
+                if (et > ev) {
+                    grow = ev - et >= -126 ? exp2i(ev - et) : 0.f;
+                    ev = et;
+                    vlim = exp2i(ev);
+                    up = exp2i(11 - ev);
+                }
+                const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+                const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
+                const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
+                m0 = n0;
+                m1 = n1;
+                l0 *= al0;
+                l1 *= al1;
+                const float r0 = al0 * grow, r1 = al1 * grow;
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt) {
                     o[mt][0] *= r0;
@@ -1300,8 +1317,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
                     o[mt][3] *= r1;
                 }
             }
-            // P' = P * scale_v * 2^(15 - ev); positions past the end have P = 0
-            const float up = exp2i(15 - ev);
+            const float pa0 = __expf(s[0] - m0), pa1 = __expf(s[1] - m1);
+            const float pb0 = __expf(s[2] - m0), pb1 = __expf(s[3] - m1);
+            l0 += pa0 + pb0;
+            l1 += pa1 + pb1;
+            // positions past the end have P = 0 and scale 0
             const float wa = fa * up, wb = fb * up;
             unsigned ha, la, hb, lb;
             split_f16x2(pa0 * wa, pa1 * wa, ha, la);
@@ -1311,9 +1331,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
 #pragma unroll
             for (int j = 0; j < D / 32; ++j) {
                 // matrices 0, 1: positions sub + 0..7, 8..15 of d 32j..32j+15; 2, 3: of d 32j+16..
-                const int pos = sub + 8 * (lm & 1) + lr;
                 unsigned w[4];
-                ldsm_x4_t(vst + swz_off<D>(pos, 32 * j + 16 * (lm >> 1)), w);
+                ldsm_x4_t(vst + unsigned(sub * D) + ofs[j], w);
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     // word: (pos 2tq, d 2gq), (2tq, 2gq+1), (2tq+1, 2gq), (2tq+1, 2gq+1)
@@ -1340,9 +1359,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
     __syncwarp();
-    // This warp's O (heads < G, scaled back by 2^(ev - 15)) over its own ring.
+    // This warp's O (heads < G, scaled back by 2^(ev - 11)) over its own ring.
     float* acc = reinterpret_cast<float*>(ring);
-    const float down = ev == -1000 ? 0.f : exp2i(ev - 15);
+    const float down = ev == -1000 ? 0.f : exp2i(ev - 11);
     const int ha = 2 * tq, hb = 2 * tq + 1;
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) {
