@@ -757,10 +757,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_xpose_kernel(AttnArgs
 // the group's G <= 8 query heads being the N columns; P^T reaches the B
 // operand layout by an in-register transpose (movmatrix) of the score tile.
 // Q and P enter as exact hi + lo F16 pairs after a power-of-two scaling (Q
-// per head so that |q| < 2^15, P by 2^15), so every product keeps about 22
+// per head so that |q| < 2^15, P by 2^11), so every product keeps about 22
 // significant bits: the F32 attention of the kernels above to within
-// rounding.
+// rounding.  The softmax reference m of a head moves only when a score
+// exceeds it by more than 4 ln 2 (a warp vote; then the reductions and the
+// rescale of O), so P = e^(s - m) < 16 and most tiles skip both.
 constexpr int kMmaRing = 2;
+constexpr float kLazyMargin = 2.7725887f;  // 4 ln 2: softmax weights stay below 16
 
 __device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -831,9 +834,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
     // tensor-map rows: [block][layer][K|V][kv head][slot] rows of D halves
     const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
     const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
-    auto issue = [&](int i) {
-        const int bi = b0 + warp + i * kAttnWarps;
-        int pb = a.tables[toff + bi];
+    // lane 0: start block i (physical id pb, read from the table beforehand)
+    auto issue = [&](int i, int pb) {
         if (pb < 0 || pb >= a.max_blocks) {
             atomicExch(a.err, 2);
             pb = 0;
@@ -850,8 +852,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
             tma_load_2d(st + half_stage + b * box, &kv_map, b * 64, yv, bar);
         }
     };
+    auto table = [&](int i) { return __ldg(a.tables + toff + b0 + warp + i * kAttnWarps); };
     if (lane == 0)
-        for (int i = 0; i < kMmaRing && i < nblk; ++i) issue(i);
+        for (int i = 0; i < kMmaRing && i < nblk; ++i) issue(i, table(i));
 
     const int gq = lane >> 2, tq = lane & 3;
     // Q^T as B fragments: lane holds head gq, d 16kk + 2tq + {0, 1} (+8);
@@ -896,6 +899,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
     bool failed = false;
     for (int i = 0; i < nblk; ++i) {
         const int bi = b0 + warp + i * kAttnWarps;
+        // the table entry of the block issued at the end of this iteration
+        const int pnext = lane == 0 && i + kMmaRing < nblk ? table(i + kMmaRing) : 0;
         const unsigned parity = (i / kMmaRing) & 1;
         unsigned ok = 0;
         for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
@@ -941,22 +946,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
             s[1] = va ? s[1] * qinv1 : -INFINITY;
             s[2] = vb ? s[2] * qinv0 : -INFINITY;
             s[3] = vb ? s[3] * qinv1 : -INFINITY;
-            float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
+            // Lazy reference (as attn_mma_i8_kernel): reduce and rescale only
+            // when a score exceeds m by more than 4 ln 2; then P < 16.
+            const bool over = s[0] > m0 + kLazyMargin || s[2] > m0 + kLazyMargin || s[1] > m1 + kLazyMargin ||
+                              s[3] > m1 + kLazyMargin;
+            if (__any_sync(0xffffffffu, over)) {
+                float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
 #pragma unroll
-            for (int o2 = 4; o2 < 32; o2 <<= 1) {
-                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
-                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
-            }
-            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
-            const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
-            const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
-            m0 = n0;
-            m1 = n1;
-            const float pa0 = __expf(s[0] - n0), pa1 = __expf(s[1] - n1);
-            const float pb0 = __expf(s[2] - n0), pb1 = __expf(s[3] - n1);
-            l0 = fmaf(l0, al0, pa0 + pb0);
-            l1 = fmaf(l1, al1, pa1 + pb1);
-            if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+                for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                    x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                    x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+                }
+                const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+                const float al0 = m0 == -INFINITY ? 0.f : __expf(m0 - n0);
+                const float al1 = m1 == -INFINITY ? 0.f : __expf(m1 - n1);
+                m0 = n0;
+                m1 = n1;
+                l0 *= al0;
+                l1 *= al1;
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt) {
                     o[mt][0] *= al0;
@@ -965,10 +972,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
                     o[mt][3] *= al1;
                 }
             }
-            // P^T (x 2^15) as the B operand: transpose the two 8x8 score tiles
+            const float pa0 = __expf(s[0] - m0), pa1 = __expf(s[1] - m1);
+            const float pb0 = __expf(s[2] - m0), pb1 = __expf(s[3] - m1);
+            l0 += pa0 + pb0;
+            l1 += pa1 + pb1;
+            // P^T (x 2^11 < 2^15) as the B operand: transpose the two 8x8 score tiles
             unsigned ha, la, hb, lb;
-            split_f16x2(pa0 * 32768.f, pa1 * 32768.f, ha, la);
-            split_f16x2(pb0 * 32768.f, pb1 * 32768.f, hb, lb);
+            split_f16x2(pa0 * 2048.f, pa1 * 2048.f, ha, la);
+            split_f16x2(pb0 * 2048.f, pb1 * 2048.f, hb, lb);
             const unsigned bh0 = movmatrix_t(ha), bh1 = movmatrix_t(hb);
             const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
 #pragma unroll
@@ -983,7 +994,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
             }
         }
         __syncwarp();
-        if (lane == 0 && i + kMmaRing < nblk) issue(i + kMmaRing);
+        if (lane == 0 && i + kMmaRing < nblk) issue(i + kMmaRing, pnext);
     }
     if (lane == 0 && failed) {
         for (int i = 0; i < kMmaRing && i < nblk; ++i)
@@ -997,18 +1008,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
     __syncwarp();
-    // This warp's O (heads < G, scaled back by 2^-15) over its own first stage.
+    // This warp's O (heads < G, scaled back by 2^-11) over its own first stage.
     float* acc = reinterpret_cast<float*>(ring);
     const int ha = 2 * tq, hb = 2 * tq + 1;
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) {
         if (ha < G) {
-            acc[ha * D + 16 * mt + gq] = o[mt][0] * (1.f / 32768.f);
-            acc[ha * D + 16 * mt + gq + 8] = o[mt][2] * (1.f / 32768.f);
+            acc[ha * D + 16 * mt + gq] = o[mt][0] * (1.f / 2048.f);
+            acc[ha * D + 16 * mt + gq + 8] = o[mt][2] * (1.f / 2048.f);
         }
         if (hb < G) {
-            acc[hb * D + 16 * mt + gq] = o[mt][1] * (1.f / 32768.f);
-            acc[hb * D + 16 * mt + gq + 8] = o[mt][3] * (1.f / 32768.f);
+            acc[hb * D + 16 * mt + gq] = o[mt][1] * (1.f / 2048.f);
+            acc[hb * D + 16 * mt + gq + 8] = o[mt][3] * (1.f / 2048.f);
         }
     }
     if (gq == 0) {
@@ -1068,7 +1079,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
 // tiles use P = e^(s - m) < 16 as they are.  Any reference gives the same
 // softmax, since O and the running sum share it.
 constexpr int kI8Ring = 3;
-constexpr float kLazyMargin = 2.7725887f;  // 4 ln 2: softmax weights stay below 16
 
 // Shared-memory byte offset of (row, byte) in a tile of rows of RB bytes
 // written by TMA with the RB-byte swizzle (RB = 128 or 64).
