@@ -49,9 +49,9 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per launch from ncu captures of this workload
-# (profiles/attn_mma_llama8b_decode512.txt, profiles/tc_gemm_q4k_llama8b_512tok.txt: the average over the four
-# projection launches of a layer).
-NCU_TRAFFIC = {"attention": 2.63e9, "projections": 1.42e8}
+# (profiles/attn_mma_llama8b_decode512.txt for F16 KV, profiles/attn_mma_i8_llama8b_decode512.txt for int8 KV,
+# profiles/tc_gemm_q4k_llama8b_512tok.txt: the average over the four projection launches of a layer).
+NCU_TRAFFIC = {"attention": {"f16": 2.63e9, "i8": 1.41e9}, "projections": 1.42e8}
 
 
 def peaks():
@@ -485,7 +485,7 @@ def run_ours(args):
     attn_kernel = {"f16": "attn_mma_kernel", "i8": "attn_mma_i8_kernel"}.get(args.kv, "attn_kernel")
     roof_attn = {"kernel": f"{attn_kernel} (paged attention, one launch per layer)", "bound": "hbm",
                  "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm if ach else None,
-                 "traffic": NCU_TRAFFIC["attention"] if full and args.kv == "f16" else None, "peak_source": pk_kind,
+                 "traffic": NCU_TRAFFIC["attention"].get(args.kv) if full else None, "peak_source": pk_kind,
                  "algorithmic_bytes_per_launch": attn_bytes,
                  "note": "algorithmic bytes count the shared 1024-token prefix once per reader; DRAM traffic "
                          "reads it once (L2 serves the rest), so frac can exceed 1"}
