@@ -1116,6 +1116,9 @@ template <int D, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const __grid_constant__ CUtensorMap kv_map,
                                                                          AttnArgs a) {
     constexpr int KS = D / 16;
+    // G <= 4: columns 4..7 of P'^T carry the lo parts of heads 0..3, so one
+    // MMA per V tile takes hi and lo (O^T columns 4..7 are added back at the end)
+    constexpr bool kPackLo = G <= 4;
     static_assert((D == 64 || D == 128) && G >= 1 && G <= 8, "int8 tensor-core attention shape");
     extern __shared__ unsigned char att_raw[];
     __shared__ std::uint64_t bars[kAttnWarps][kI8Ring];
@@ -1146,15 +1149,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
     __syncwarp();
     const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
     const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
-    // lane 0: start block i (physical id pb, read from the table beforehand)
-    auto issue = [&](int i, int pb) {
+    // lane 0: start a block (physical id pb, read from the table beforehand) into stage st
+    auto issue = [&](int st, int pb) {
         if (pb < 0 || pb >= a.max_blocks) {
             atomicExch(a.err, 2);
             pb = 0;
         }
         const long long yk = pb * block_rows + head_row;
         const long long yv = yk + kind_rows;
-        const int st = (i % kI8Ring);
         const unsigned dst = ring_s + unsigned(st * stage);
         std::uint64_t* bar = &bars[warp][st];
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1168,7 +1170,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
     };
     auto table = [&](int i) { return __ldg(a.tables + toff + b0 + warp + i * kAttnWarps); };
     if (lane == 0)
-        for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i, table(i));
+        for (int i = 0; i < kI8Ring && i < nblk; ++i) issue(i, table(i));  // block i into stage i
 
     const int gq = lane >> 2, tq = lane & 3;
     // Q^T in three byte digits (B fragments of m16n8k32): step kk, lane
@@ -1238,13 +1240,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
 #pragma unroll
     for (int kk = 0; kk < K32; ++kk) ofs[kk] = swz_off<D>(8 * (lm & 1) + lr, 32 * kk + 16 * (lm >> 1));
     bool failed = false;
+    int st = 0;           // stage of block i
+    unsigned parity = 0;  // its mbarrier phase
     for (int i = 0; i < nblk; ++i) {
         const int bi = b0 + warp + i * kAttnWarps;
-        const int st = i % kI8Ring;
         // the table entry of the block issued at the end of this iteration,
         // loaded now so its latency hides behind the compute
         const int pnext = lane == 0 && i + kI8Ring < nblk ? table(i + kI8Ring) : 0;
-        const unsigned parity = (i / kI8Ring) & 1;
         unsigned ok = 0;
         for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
             if (bar_try(&bars[warp][st], parity)) {
@@ -1318,7 +1320,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
                 m1 = n1;
                 l0 *= al0;
                 l1 *= al1;
-                const float r0 = al0 * grow, r1 = al1 * grow;
+                float r0 = al0 * grow, r1 = al1 * grow;
+                if constexpr (kPackLo) {  // lanes tq >= 2 hold the lo columns of heads 2tq - 4, 2tq - 3
+                    const float u0 = __shfl_up_sync(0xffffffffu, r0, 2), u1 = __shfl_up_sync(0xffffffffu, r1, 2);
+                    if (tq >= 2) {
+                        r0 = u0;
+                        r1 = u1;
+                    }
+                }
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt) {
                     o[mt][0] *= r0;
@@ -1336,8 +1345,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
             unsigned ha, la, hb, lb;
             split_f16x2(pa0 * wa, pa1 * wa, ha, la);
             split_f16x2(pb0 * wb, pb1 * wb, hb, lb);
-            const unsigned bh0 = movmatrix_t(ha), bh1 = movmatrix_t(hb);
-            const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
+            unsigned bh0, bh1, bl0 = 0, bl1 = 0;
+            if constexpr (kPackLo) {
+                const unsigned la2 = __shfl_up_sync(0xffffffffu, la, 2), lb2 = __shfl_up_sync(0xffffffffu, lb, 2);
+                bh0 = movmatrix_t(tq < 2 ? ha : la2);
+                bh1 = movmatrix_t(tq < 2 ? hb : lb2);
+            } else {
+                bh0 = movmatrix_t(ha);
+                bh1 = movmatrix_t(hb);
+                bl0 = movmatrix_t(la);
+                bl1 = movmatrix_t(lb);
+            }
 #pragma unroll
             for (int j = 0; j < D / 32; ++j) {
                 // matrices 0, 1: positions sub + 0..7, 8..15 of d 32j..32j+15; 2, 3: of d 32j+16..
@@ -1350,12 +1368,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
                     const unsigned f[4] = {i8pair_f16(u0, 0x4240), i8pair_f16(u0, 0x4341), i8pair_f16(u1, 0x4240),
                                            i8pair_f16(u1, 0x4341)};
                     mma16816(o[2 * j + hf], f, bh0, bh1);
-                    mma16816(o[2 * j + hf], f, bl0, bl1);
+                    if constexpr (!kPackLo) mma16816(o[2 * j + hf], f, bl0, bl1);
                 }
             }
         }
         __syncwarp();
-        if (lane == 0 && i + kI8Ring < nblk) issue(i + kI8Ring, pnext);
+        if (lane == 0 && i + kI8Ring < nblk) issue(st, pnext);
+        if (++st == kI8Ring) {
+            st = 0;
+            parity ^= 1;
+        }
     }
     if (lane == 0 && failed) {
         for (int i = 0; i < kI8Ring && i < nblk; ++i)
@@ -1369,6 +1391,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 4) attn_mma_i8_kernel(const _
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
     __syncwarp();
+    if constexpr (kPackLo) {  // hi columns (lanes tq < 2) plus the lo columns two lanes up
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[mt][e] += __shfl_down_sync(0xffffffffu, o[mt][e], 2);
+    }
     // This warp's O (heads < G, scaled back by 2^(ev - 11)) over its own ring.
     float* acc = reinterpret_cast<float*>(ring);
     const float down = ev == -1000 ? 0.f : exp2i(ev - 11);
