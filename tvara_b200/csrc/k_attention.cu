@@ -806,6 +806,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
     constexpr int NB = D / 64;  // 128-byte boxes per slot row
     constexpr int KS = D / 16;  // k-steps of S^T, and m-tiles of O^T
     static_assert(D % 64 == 0 && G >= 1 && G <= 8, "tensor-core attention shape");
+    // G <= 4: columns 4..7 of P^T carry the lo parts of heads 0..3, so one
+    // value MMA per tile takes hi and lo (O^T columns 4..7 are added back at the end)
+    constexpr bool kPackLo = G <= 4;
     extern __shared__ unsigned char att_raw[];
     __shared__ std::uint64_t bars[kAttnWarps][kMmaRing];
     __shared__ float s_m[kAttnWarps][8], s_l[kAttnWarps][8];
@@ -964,12 +967,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
                 m1 = n1;
                 l0 *= al0;
                 l1 *= al1;
+                float r0 = al0, r1 = al1;
+                if constexpr (kPackLo) {  // lanes tq >= 2 hold the lo columns of heads 2tq - 4, 2tq - 3
+                    const float u0 = __shfl_up_sync(0xffffffffu, r0, 2), u1 = __shfl_up_sync(0xffffffffu, r1, 2);
+                    if (tq >= 2) {
+                        r0 = u0;
+                        r1 = u1;
+                    }
+                }
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt) {
-                    o[mt][0] *= al0;
-                    o[mt][1] *= al1;
-                    o[mt][2] *= al0;
-                    o[mt][3] *= al1;
+                    o[mt][0] *= r0;
+                    o[mt][1] *= r1;
+                    o[mt][2] *= r0;
+                    o[mt][3] *= r1;
                 }
             }
             const float pa0 = __expf(s[0] - m0), pa1 = __expf(s[1] - m1);
@@ -980,8 +991,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
             unsigned ha, la, hb, lb;
             split_f16x2(pa0 * 2048.f, pa1 * 2048.f, ha, la);
             split_f16x2(pb0 * 2048.f, pb1 * 2048.f, hb, lb);
-            const unsigned bh0 = movmatrix_t(ha), bh1 = movmatrix_t(hb);
-            const unsigned bl0 = movmatrix_t(la), bl1 = movmatrix_t(lb);
+            unsigned bh0, bh1, bl0 = 0, bl1 = 0;
+            if constexpr (kPackLo) {
+                const unsigned la2 = __shfl_up_sync(0xffffffffu, la, 2), lb2 = __shfl_up_sync(0xffffffffu, lb, 2);
+                bh0 = movmatrix_t(tq < 2 ? ha : la2);
+                bh1 = movmatrix_t(tq < 2 ? hb : lb2);
+            } else {
+                bh0 = movmatrix_t(ha);
+                bh1 = movmatrix_t(hb);
+                bl0 = movmatrix_t(la);
+                bl1 = movmatrix_t(lb);
+            }
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
                 // V^T tile [d 16mt.., positions sub..]: matrices (pos +0/+8) x (d +0/+8)
@@ -990,7 +1010,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
                 unsigned f[4];
                 ldsm_x4_t(vst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
                 mma16816(o[mt], f, bh0, bh1);
-                mma16816(o[mt], f, bl0, bl1);
+                if constexpr (!kPackLo) mma16816(o[mt], f, bl0, bl1);
             }
         }
         __syncwarp();
@@ -1008,6 +1028,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
     __syncwarp();
+    if constexpr (kPackLo) {  // hi columns (lanes tq < 2) plus the lo columns two lanes up
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[mt][e] += __shfl_down_sync(0xffffffffu, o[mt][e], 2);
+    }
     // This warp's O (heads < G, scaled back by 2^-11) over its own first stage.
     float* acc = reinterpret_cast<float*>(ring);
     const int ha = 2 * tq, hb = 2 * tq + 1;
