@@ -141,8 +141,9 @@ TVARA_API int tvara_batch_step(tvara_model* model, size_t n_seq, const uint64_t*
                                size_t count, uint32_t* argmax, size_t argmax_count);
 
 /* Device-side logit post-processing of a step (the sampler of
- * python/tvara/native.py:301-336 up to its random draw; SURVEY's "next"
- * row for cutting the full-vocabulary copy).  Per sequence, in float64 with
+ * python/tvara/native.py:301-336 up to its random draw, so that only the
+ * chosen token or a few candidates cross to the host instead of the
+ * full-vocabulary row).  Per sequence, in float64 with
  * the reference's numpy operations: repetition / frequency / presence
  * penalties from the tokens already in the sequence (this step's included),
  * then the token mask (token_masks.py:228-241: disallowed -> -inf).
@@ -294,6 +295,22 @@ TVARA_API size_t tvara_kv_book_references(tvara_kv_book* book, size_t id);
 TVARA_API int tvara_kv_book_table(tvara_kv_book* book, uint64_t sequence, uint64_t* ids, uint64_t* generations,
                                   size_t capacity, size_t* count);
 TVARA_API int tvara_kv_book_audit(tvara_kv_book* book);
+
+/* Prefix cache over a host-only book (the same trie the engine uses, with
+ * radix.hpp:17-130's node ids, splits, pins and LRU eviction), so its
+ * accounting can be replayed without a GPU.  Node ids, return codes and
+ * errors are those of the tvara_prefix_* calls above. */
+TVARA_API uint64_t tvara_kv_book_prefix_insert(tvara_kv_book* book, const int32_t* tokens, size_t token_count);
+TVARA_API int tvara_kv_book_prefix_attach(tvara_kv_book* book, uint64_t node, uint64_t sequence);
+TVARA_API int tvara_kv_book_prefix_lookup(tvara_kv_book* book, const int32_t* tokens, size_t token_count,
+                                          uint64_t* node, size_t* matched);
+TVARA_API uint64_t tvara_kv_book_prefix_reuse(tvara_kv_book* book, const int32_t* tokens, size_t token_count,
+                                              int partial, size_t* reused);
+TVARA_API int tvara_kv_book_prefix_pin(tvara_kv_book* book, uint64_t node);
+TVARA_API int tvara_kv_book_prefix_unpin(tvara_kv_book* book, uint64_t node);
+TVARA_API int tvara_kv_book_prefix_touch(tvara_kv_book* book, uint64_t node);
+TVARA_API int tvara_kv_book_prefix_evict_one(tvara_kv_book* book);
+TVARA_API size_t tvara_kv_book_prefix_size(tvara_kv_book* book);
 
 #ifdef __cplusplus
 }

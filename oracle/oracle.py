@@ -140,6 +140,20 @@ def ref():
     return _ref
 
 
+def reference_module(name: str):
+    """A module of the reference's own Python package (python/tvara/<name>.py),
+    staged unchanged into oracle/_ref/python by the Makefile; None when it was
+    not staged here."""
+    import importlib
+    import sys
+    root = ORACLE_DIR / "_ref" / "python"
+    if not (root / "tvara" / f"{name}.py").exists():
+        return None
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    return importlib.import_module(f"tvara.{name}")
+
+
 def ref_capi():
     """The reference engine's C ABI library (None when not built here)."""
     global _capi

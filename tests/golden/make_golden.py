@@ -1,7 +1,8 @@
 """Regenerate the golden fixtures in this directory from the reference engine.
 
-Run in an environment where the Tvara sources are present and oracle/_ref was
-built (``make -C oracle``):
+Run where oracle/_ref was built from a Tvara checkout
+(``make -C oracle REFERENCE=/path/to/Tvara``, which also stages the
+reference's Python package into oracle/_ref/python):
 
     python tests/golden/make_golden.py
 
@@ -44,6 +45,7 @@ sys.path.insert(0, str(ROOT))
 from tvara_b200 import gguf  # noqa: E402
 from oracle import oracle as O  # noqa: E402
 from oracle.model import RefEngine  # noqa: E402
+from oracle.oracle import reference_module  # noqa: E402
 from tests.golden.sampling_cases import SAMPLING_CASES, EvenTokens  # noqa: E402
 
 TINY_PROMPT_SEED = 1
@@ -82,8 +84,7 @@ def random_blocks(rng, kind, n):
 
 def sampling_golden(tiny_path):
     import os
-    sys.path.insert(0, "/root/reference/python")
-    from tvara.native import NativeModel as RefNativeModel
+    RefNativeModel = reference_module("native").NativeModel
     lib = ROOT / "oracle" / "_ref" / "libtvara_capi.so"
     os.environ["TVARA_LIBRARY"] = str(lib)
     prompt = [int(t) for t in tiny_prompt()[:24]]
@@ -98,8 +99,7 @@ def sampling_golden(tiny_path):
 
 
 def quantized_kv_golden():
-    sys.path.insert(0, "/root/reference/python")
-    from tvara.quantized_kv import QuantizedKV
+    QuantizedKV = reference_module("quantized_kv").QuantizedKV
     rng = np.random.default_rng(4242)
     d = 64
     rows = [np.zeros(d, np.float32), np.full(d, 1e-44, np.float32), np.full(d, 1e-30, np.float32),

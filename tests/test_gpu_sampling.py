@@ -125,14 +125,33 @@ def tiny(tiny_path):
 
 
 @pytest.mark.parametrize("name", sorted(SAMPLING_CASES))
-@pytest.mark.parametrize("device", [True, False])
-def test_iter_tokens_reproduce_reference_golden(tiny, name, device):
+def test_iter_tokens_reproduce_reference_golden(tiny, name):
     g = np.load(GOLDEN / "sampling.npz")
     kw = dict(SAMPLING_CASES[name])
     constraint = EvenTokens(tiny.vocab_size) if kw.pop("constraint", False) else None
     toks = tiny.generate([int(t) for t in g["prompt"]], max_new_tokens=len(g[name]), token_constraint=constraint,
-                         device_sampling=device, **kw)
+                         **kw)
     assert toks == g[name].tolist()
+
+
+def test_iter_tokens_argument_errors(tiny):
+    """The reference's checks and texts (python/tvara/native.py:220-262)."""
+    cases = [(dict(prompt=[]), "Invalid prompt token IDs"), (dict(prompt=[True]), "Invalid prompt token IDs"),
+             (dict(prompt=[tiny.vocab_size]), "Invalid prompt token IDs"),
+             (dict(max_new_tokens=10 ** 9), "Generation exceeds context limits"),
+             (dict(max_new_tokens=1.0), "Generation exceeds context limits"),
+             (dict(temperature="0"), "Sampling parameters must be real scalars"),
+             (dict(top_p=True), "Sampling parameters must be real scalars"),
+             (dict(temperature=-1), "Invalid sampling parameters"), (dict(top_p=0), "Invalid sampling parameters"),
+             (dict(min_p=1.5), "Invalid sampling parameters"), (dict(top_k=-1), "Invalid sampling filters"),
+             (dict(repetition=0), "Invalid sampling filters"), (dict(frequency=np.inf), "Invalid sampling filters"),
+             (dict(eos_id=tiny.vocab_size), "Invalid EOS ID"), (dict(seed=True), "Invalid random seed"),
+             (dict(seed=-1), "Invalid random seed"),
+             (dict(temperature=0.5, top_k=0), "device sampling needs")]
+    for kw, msg in cases:
+        prompt = kw.pop("prompt", [1, 2])
+        with pytest.raises(ValueError, match=msg):
+            tiny.generate(prompt, **kw)
 
 
 def test_batch_sample_histories_forks_and_masks(tiny):

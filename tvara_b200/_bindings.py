@@ -103,6 +103,15 @@ SIGNATURES = {
     "tvara_kv_book_references": (SZ, [P, SZ]),
     "tvara_kv_book_table": (C.c_int, [P, U64, U64P, U64P, SZ, SZP]),
     "tvara_kv_book_audit": (C.c_int, [P]),
+    "tvara_kv_book_prefix_insert": (U64, [P, I32P, SZ]),
+    "tvara_kv_book_prefix_attach": (C.c_int, [P, U64, U64]),
+    "tvara_kv_book_prefix_lookup": (C.c_int, [P, I32P, SZ, U64P, SZP]),
+    "tvara_kv_book_prefix_reuse": (U64, [P, I32P, SZ, C.c_int, SZP]),
+    "tvara_kv_book_prefix_pin": (C.c_int, [P, U64]),
+    "tvara_kv_book_prefix_unpin": (C.c_int, [P, U64]),
+    "tvara_kv_book_prefix_touch": (C.c_int, [P, U64]),
+    "tvara_kv_book_prefix_evict_one": (C.c_int, [P]),
+    "tvara_kv_book_prefix_size": (SZ, [P]),
     # kernel level (include/tvara_kernels.h)
     "tvara_dequantize": (C.c_int, [C.c_int, P, SZ, P, P]),
     "tvara_packed_bytes": (SZ, [C.c_int, SZ, SZ]),

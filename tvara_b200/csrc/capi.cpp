@@ -24,8 +24,13 @@ struct tvara_model {
 };
 
 struct tvara_kv_book {
-    tvara::PagedBook book;
+    tvara::SequenceBook book;
+    std::unique_ptr<tvara::PrefixTrie> trie;  // declared after book: released first
     explicit tvara_kv_book(tvara::CacheGeometry g) : book(g) {}
+    tvara::PrefixTrie& prefixes() {
+        if (!trie) trie = std::make_unique<tvara::PrefixTrie>(book, "tvara-kv-book");
+        return *trie;
+    }
 };
 
 #include <atomic>
@@ -305,7 +310,7 @@ int tvara_kv_stats(tvara_model* model, size_t* available, size_t* max_blocks) {
     return guarded<int>(-1, [&] {
         auto& e = engine_of(model);
         std::lock_guard lock(model->mutex);
-        if (available) *available = e.book().pool().available();
+        if (available) *available = e.book().ledger().available();
         if (max_blocks) *max_blocks = e.book().geometry().max_blocks;
         return 0;
     });
@@ -340,7 +345,7 @@ int tvara_kv_references(tvara_model* model, size_t id, size_t* references) {
     return guarded<int>(-1, [&] {
         auto& e = engine_of(model);
         std::lock_guard lock(model->mutex);
-        if (references) *references = e.book().pool().references_by_id(id);
+        if (references) *references = e.book().ledger().references_by_id(id);
         return 0;
     });
 }
@@ -543,9 +548,9 @@ int tvara_kv_book_truncate(tvara_kv_book* b, uint64_t s, size_t n) {
 uint64_t tvara_kv_book_import(tvara_kv_book* b, uint64_t s, size_t n) {
     return guarded<uint64_t>(0, [&] { return b->book.import_sequence(b->book.sequence(s), n); });
 }
-size_t tvara_kv_book_available(tvara_kv_book* b) { return b->book.pool().available(); }
+size_t tvara_kv_book_available(tvara_kv_book* b) { return b->book.ledger().available(); }
 size_t tvara_kv_book_references(tvara_kv_book* b, size_t id) {
-    return guarded<size_t>(0, [&] { return b->book.pool().references_by_id(id); });
+    return guarded<size_t>(0, [&] { return b->book.ledger().references_by_id(id); });
 }
 int tvara_kv_book_table(tvara_kv_book* b, uint64_t s, uint64_t* ids, uint64_t* gens, size_t capacity, size_t* count) {
     return guarded<int>(-1, [&] {
@@ -560,9 +565,69 @@ int tvara_kv_book_table(tvara_kv_book* b, uint64_t s, uint64_t* ids, uint64_t* g
 }
 int tvara_kv_book_audit(tvara_kv_book* b) {
     return guarded<int>(-1, [&] {
-        b->book.audit();
+        if (b->trie) {
+            const auto held = b->trie->external_references();
+            b->book.audit(held);
+        } else {
+            b->book.audit();
+        }
         return 0;
     });
+}
+uint64_t tvara_kv_book_prefix_insert(tvara_kv_book* b, const int32_t* tokens, size_t token_count) {
+    return guarded<uint64_t>(0, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        return b->prefixes().insert({tokens, token_count});
+    });
+}
+int tvara_kv_book_prefix_attach(tvara_kv_book* b, uint64_t node, uint64_t sequence) {
+    return guarded<int>(-1, [&] {
+        b->prefixes().attach(node, sequence);
+        return 0;
+    });
+}
+int tvara_kv_book_prefix_lookup(tvara_kv_book* b, const int32_t* tokens, size_t token_count, uint64_t* node,
+                                size_t* matched) {
+    return guarded<int>(-1, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        const auto r = b->prefixes().lookup({tokens, token_count});
+        if (node) *node = r.first;
+        if (matched) *matched = r.second;
+        return 0;
+    });
+}
+uint64_t tvara_kv_book_prefix_reuse(tvara_kv_book* b, const int32_t* tokens, size_t token_count, int partial,
+                                    size_t* reused) {
+    return guarded<uint64_t>(0, [&] {
+        if (!tokens && token_count) throw std::invalid_argument("invalid token buffer");
+        const auto r = b->prefixes().reuse({tokens, token_count}, partial != 0);
+        if (reused) *reused = r.second;
+        return r.first;
+    });
+}
+int tvara_kv_book_prefix_pin(tvara_kv_book* b, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        b->prefixes().pin(node);
+        return 0;
+    });
+}
+int tvara_kv_book_prefix_unpin(tvara_kv_book* b, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        b->prefixes().unpin(node);
+        return 0;
+    });
+}
+int tvara_kv_book_prefix_touch(tvara_kv_book* b, uint64_t node) {
+    return guarded<int>(-1, [&] {
+        b->prefixes().touch(node);
+        return 0;
+    });
+}
+int tvara_kv_book_prefix_evict_one(tvara_kv_book* b) {
+    return guarded<int>(-1, [&] { return b->prefixes().evict_one() ? 1 : 0; });
+}
+size_t tvara_kv_book_prefix_size(tvara_kv_book* b) {
+    return guarded<size_t>(0, [&] { return b->prefixes().size(); });
 }
 
 }  // extern "C"

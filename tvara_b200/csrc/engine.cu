@@ -91,8 +91,8 @@ Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t bloc
     tmax_ = std::max(1, opt.max_step_tokens);
 
     CacheGeometry g{cfg_.layers, cfg_.kv_heads, cfg_.head_dim(), block_tokens, max_blocks};
-    book_ = std::make_unique<PagedBook>(g);
-    radix_ = std::make_unique<RadixBook>(*book_, "tvara-b200-engine");
+    book_ = std::make_unique<SequenceBook>(g);
+    radix_ = std::make_unique<PrefixTrie>(*book_, "tvara-b200-engine");
 
     TVARA_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     if (tp > 1) {

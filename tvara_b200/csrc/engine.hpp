@@ -70,8 +70,8 @@ public:
 
     const gguf::LlamaConfig& config() const { return cfg_; }
     const std::string& metadata() const { return metadata_; }
-    PagedBook& book() { return *book_; }
-    RadixBook& radix() { return *radix_; }
+    SequenceBook& book() { return *book_; }
+    PrefixTrie& radix() { return *radix_; }
     const EngineOptions& options() const { return opt_; }
 
     // One ragged step; see tvara_batch_step.  Rows of logits / argmax are
@@ -149,8 +149,8 @@ private:
     std::string metadata_;
     int device_ = 0;
     cudaStream_t stream_ = nullptr;
-    std::unique_ptr<PagedBook> book_;
-    std::unique_ptr<RadixBook> radix_;
+    std::unique_ptr<SequenceBook> book_;
+    std::unique_ptr<PrefixTrie> radix_;
     std::unique_ptr<Collective> coll_;
 
     // local (per tensor-parallel rank) shapes

@@ -1,29 +1,43 @@
-// Host-side accounting of the device KV pool: block handles with generation
-// tags, reference counts, the LIFO free list, per-sequence block tables,
-// copy-on-write of shared partial tails, and the radix prefix cache.
+// Host-side bookkeeping of the device KV pool.
 //
-// The accounting is the reference's, step for step, so block ids,
-// generations, reference counts and free-list order match it exactly for the
-// same operation sequence:
-//   CacheGeometry / kv_offset        core/include/tvara/kv.hpp:12-33
-//   BlockPool                        kv.hpp:36-75
-//   PagedCache                       kv.hpp:78-165
-//   RadixCache                       core/include/tvara/radix.hpp:17-130
-// What differs is where the payload lives: block contents are in HBM, owned
-// by the engine.  Operations that touch payload (copy-on-write) are reported
-// to the caller as device copies to enqueue; allocation does not clear the
-// block on the device because no kernel reads a slot at or past a sequence's
-// length (tests poison those slots with NaN).
+// Three pieces, each holding only integers (the K/V payload lives in HBM and
+// is owned by the engine):
+//
+//   BlockLedger   per-block reference count and generation in two parallel
+//                 arrays, with the free blocks threaded through a third array
+//                 as an intrusive LIFO chain (no separate free-list vector).
+//   SequenceBook  one block table per sequence in a hash map; appends,
+//                 copy-on-write of a shared partial tail, forks, truncation,
+//                 prefix imports and the consistency audit.
+//   PrefixTrie    a compressed token trie whose nodes live in an arena
+//                 (vector + vacant-slot stack) addressed through a map from
+//                 public node id to slot; children are a sorted flat vector,
+//                 edges are matched with std::mismatch.
+//
+// The observable results are fixed by the reference so that an engine and the
+// reference given the same operations hand out the same block ids,
+// generations, sequence ids and prefix-node ids and end with the same
+// reference counts and free-block order:
+//   geometry checks and texts           core/include/tvara/kv.hpp:12-29
+//   pool (LIFO reuse, generations)      kv.hpp:36-75
+//   paged cache (append/CoW/fork/...)   kv.hpp:78-165
+//   prefix cache (ids, splits, LRU)     core/include/tvara/radix.hpp:17-130
+// Those contracts are replayed operation by operation against the reference
+// compiled from its own sources (tests/test_host.py).
+//
+// Block allocation does not clear the device block: no kernel reads a slot at
+// or past a sequence's length.  Copy-on-write is reported to the caller as a
+// (source, destination) block pair to copy on the device.
 #pragma once
 #include <algorithm>
 #include <cstddef>
 #include <cstdint>
 #include <limits>
-#include <map>
 #include <optional>
 #include <span>
 #include <stdexcept>
 #include <string>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 
@@ -31,25 +45,30 @@ namespace tvara {
 
 struct CacheGeometry {
     std::size_t layers = 1, kv_heads = 1, head_dim = 4, tokens_per_block = 16, max_blocks = 64;
+
+    // Width of one token's K (or V) row in elements; overflow-checked.
     std::size_t kv_width() const {
-        if (!kv_heads || !head_dim || kv_heads > std::numeric_limits<std::size_t>::max() / head_dim)
-            throw std::invalid_argument("KV width overflow");
-        return kv_heads * head_dim;
+        if (kv_heads == 0 || head_dim == 0) throw std::invalid_argument("KV width overflow");
+        std::size_t w = 0;
+        if (__builtin_mul_overflow(kv_heads, head_dim, &w)) throw std::invalid_argument("KV width overflow");
+        return w;
     }
+    // Elements of one block: layers x {K, V} x slots x width.
     std::size_t elements_per_block() const {
-        std::size_t n = kv_width();
-        for (auto d : {layers, tokens_per_block, std::size_t(2)}) {
-            if (!d || n > std::numeric_limits<std::size_t>::max() / d) throw std::invalid_argument("KV block overflow");
-            n *= d;
-        }
-        return n;
+        std::size_t e = kv_width();
+        const std::size_t factors[] = {layers, tokens_per_block, 2};
+        for (std::size_t f : factors)
+            if (f == 0 || __builtin_mul_overflow(e, f, &e)) throw std::invalid_argument("KV block overflow");
+        return e;
     }
     void validate() const {
-        const auto e = elements_per_block();
-        if (!max_blocks || max_blocks > 1000000 || e > std::numeric_limits<std::size_t>::max() / sizeof(float) / max_blocks ||
-            tokens_per_block > std::numeric_limits<std::size_t>::max() / max_blocks)
-            throw std::invalid_argument("KV capacity overflow");
+        const std::size_t e = elements_per_block();
+        const std::size_t top = std::numeric_limits<std::size_t>::max();
+        const bool bad = max_blocks == 0 || max_blocks > 1000000 || e > top / sizeof(float) / max_blocks ||
+                         tokens_per_block > top / max_blocks;
+        if (bad) throw std::invalid_argument("KV capacity overflow");
     }
+    std::size_t blocks_for(std::size_t tokens) const { return (tokens + tokens_per_block - 1) / tokens_per_block; }
 };
 
 class CacheExhausted : public std::runtime_error {
@@ -65,381 +84,442 @@ struct BlockTable {
     std::vector<BlockHandle> blocks;
     std::size_t length = 0;
 };
-
-// Device work implied by accounting operations, drained by the engine.
+// A device block copy implied by copy-on-write, drained by the engine.
 struct BlockCopy {
     std::size_t from = 0, to = 0;
 };
 
-class BlockPool {
+class BlockLedger {
+    static constexpr std::size_t kEnd = std::numeric_limits<std::size_t>::max();
+
 public:
-    explicit BlockPool(CacheGeometry g) : geometry_(g) {
+    explicit BlockLedger(CacheGeometry g) : geometry_(g) {
         g.validate();
-        refs_.assign(g.max_blocks, 0);
-        gens_.assign(g.max_blocks, 0);
-        free_.reserve(g.max_blocks);
-        for (std::size_t i = g.max_blocks; i > 0; --i) free_.push_back(i - 1);
+        const std::size_t n = g.max_blocks;
+        refs_.assign(n, 0);
+        generation_.assign(n, 0);
+        chain_.resize(n);
+        // Initially every block is free and block 0 is handed out first.
+        for (std::size_t i = 0; i < n; ++i) chain_[i] = i + 1 < n ? i + 1 : kEnd;
+        head_ = 0;
+        free_count_ = n;
     }
-    BlockHandle allocate() {
-        if (free_.empty()) throw CacheExhausted();
-        const auto id = free_.back();
-        if (gens_[id] == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("KV generation exhausted");
-        free_.pop_back();
+
+    BlockHandle take() {
+        if (head_ == kEnd) throw CacheExhausted();
+        const std::size_t id = head_;
+        if (generation_[id] == std::numeric_limits<std::uint64_t>::max())
+            throw std::runtime_error("KV generation exhausted");
+        head_ = chain_[id];
+        chain_[id] = kEnd;
+        --free_count_;
         refs_[id] = 1;
-        ++gens_[id];
-        return {id, gens_[id]};
+        return {id, ++generation_[id]};
     }
-    void retain(BlockHandle h) {
-        check(h);
-        if (refs_[h.id] == std::numeric_limits<std::size_t>::max()) throw std::runtime_error("KV reference overflow");
-        ++refs_[h.id];
+    void share(BlockHandle h) {
+        std::uint64_t& r = refs_[checked(h)];
+        if (r == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("KV reference overflow");
+        ++r;
     }
-    void release(BlockHandle h) {
-        check(h);
-        if (--refs_[h.id] == 0) free_.push_back(h.id);
-    }
-    std::size_t references(BlockHandle h) const {
-        check(h);
-        return refs_[h.id];
-    }
-    std::size_t references_by_id(std::size_t id) const { return refs_.at(id); }
-    std::uint64_t generation_by_id(std::size_t id) const { return gens_.at(id); }
-    std::size_t available() const { return free_.size(); }
-    const CacheGeometry& geometry() const { return geometry_; }
-    const std::vector<std::size_t>& free_list() const { return free_; }
-    void check(BlockHandle h) const {
-        if (h.id >= refs_.size() || !refs_[h.id] || gens_[h.id] != h.generation)
-            throw std::invalid_argument("stale or invalid KV handle");
-    }
-    void audit() const {
-        std::vector<bool> seen(refs_.size());
-        for (auto id : free_) {
-            if (id >= refs_.size() || seen[id] || refs_[id]) throw std::logic_error("KV free-list invariant");
-            seen[id] = true;
+    void unshare(BlockHandle h) {
+        const std::size_t id = checked(h);
+        if (--refs_[id] == 0) {
+            chain_[id] = head_;
+            head_ = id;
+            ++free_count_;
         }
+    }
+    bool shared(BlockHandle h) const { return refs_[checked(h)] > 1; }
+    std::size_t references(BlockHandle h) const { return refs_[checked(h)]; }
+    std::size_t references_by_id(std::size_t id) const {
+        if (id >= refs_.size()) throw std::out_of_range("KV block id out of range");
+        return refs_[id];
+    }
+    std::size_t available() const { return free_count_; }
+    const CacheGeometry& geometry() const { return geometry_; }
+    std::size_t checked(BlockHandle h) const {
+        if (h.id >= refs_.size() || refs_[h.id] == 0 || generation_[h.id] != h.generation)
+            throw std::invalid_argument("stale or invalid KV handle");
+        return h.id;
+    }
+    // Free chain well-formed (in range, acyclic, only unreferenced blocks),
+    // and every unreferenced block on it.
+    void audit() const {
+        std::vector<char> on_chain(refs_.size(), 0);
+        std::size_t walked = 0;
+        for (std::size_t id = head_; id != kEnd; id = chain_[id]) {
+            if (id >= refs_.size() || on_chain[id] || refs_[id] != 0) throw std::logic_error("KV free-list invariant");
+            on_chain[id] = 1;
+            ++walked;
+        }
+        if (walked != free_count_) throw std::logic_error("KV free-list invariant");
         for (std::size_t i = 0; i < refs_.size(); ++i)
-            if (seen[i] != (refs_[i] == 0)) throw std::logic_error("KV allocation invariant");
+            if (bool(on_chain[i]) != (refs_[i] == 0)) throw std::logic_error("KV allocation invariant");
     }
 
 private:
     CacheGeometry geometry_;
-    std::vector<std::size_t> refs_;
-    std::vector<std::uint64_t> gens_;
-    std::vector<std::size_t> free_;
+    std::vector<std::uint64_t> refs_, generation_;
+    std::vector<std::size_t> chain_;  // next free block after this one
+    std::size_t head_ = kEnd, free_count_ = 0;
 };
 
-class PagedBook {
+class SequenceBook {
 public:
-    explicit PagedBook(CacheGeometry g) : pool_(g) {}
-    const CacheGeometry& geometry() const { return pool_.geometry(); }
-    BlockPool& pool() { return pool_; }
-    const BlockPool& pool() const { return pool_; }
+    explicit SequenceBook(CacheGeometry g) : ledger_(g) {}
+    const CacheGeometry& geometry() const { return ledger_.geometry(); }
+    BlockLedger& ledger() { return ledger_; }
+    const BlockLedger& ledger() const { return ledger_; }
 
-    std::uint64_t create_sequence() {
-        if (next_ == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("sequence ID exhausted");
-        const auto id = ++next_;
-        tables_.emplace(id, BlockTable{});
-        return id;
-    }
+    std::uint64_t create_sequence() { return add(BlockTable{}); }
     const BlockTable& sequence(std::uint64_t id) const {
-        auto it = tables_.find(id);
+        const auto it = tables_.find(id);
         if (it == tables_.end()) throw std::invalid_argument("unknown KV sequence");
         return it->second;
     }
-    bool contains(std::uint64_t id) const { return tables_.count(id) != 0; }
-    BlockHandle physical_block(std::uint64_t id, std::size_t position) const {
-        const auto& t = sequence(id);
-        if (position >= t.length) throw std::invalid_argument("KV position beyond sequence");
-        return t.blocks.at(position / geometry().tokens_per_block);
-    }
+    bool contains(std::uint64_t id) const { return tables_.find(id) != tables_.end(); }
+    std::size_t sequences() const { return tables_.size(); }
 
-    // kv.hpp:91-108, accounting half: a fresh block at slot 0; a shared
-    // partial tail is replaced by a private copy (reported in *copy).
+    // One more position.  A position opening a block takes a fresh block; a
+    // position landing in a partial tail that another table also holds moves
+    // the tail to a private block first (the pair is reported in *copy).
     void append(std::uint64_t id, BlockCopy* copy = nullptr) {
-        auto& t = mutable_sequence(id);
-        const auto& g = geometry();
+        BlockTable& t = table(id);
+        const CacheGeometry& g = geometry();
         if (t.length >= g.max_blocks * g.tokens_per_block) throw std::invalid_argument("invalid paged KV append dimensions");
-        const auto slot = t.length % g.tokens_per_block;
-        if (slot == 0) {
-            auto b = pool_.allocate();
-            try {
-                t.blocks.push_back(b);
-            } catch (...) {
-                pool_.release(b);
-                throw;
-            }
-        }
-        if (slot != 0 && pool_.references(t.blocks.back()) > 1) {
-            const auto original = t.blocks.back();
-            const auto replacement = pool_.allocate();
-            if (copy) *copy = {original.id, replacement.id};
-            t.blocks.back() = replacement;
-            pool_.release(original);
+        if (t.length % g.tokens_per_block == 0) {
+            t.blocks.reserve(t.blocks.size() + 1);  // so the push below cannot throw after take()
+            t.blocks.push_back(ledger_.take());
+        } else if (ledger_.shared(t.blocks.back())) {
+            const BlockHandle mine = ledger_.take();
+            const BlockHandle theirs = std::exchange(t.blocks.back(), mine);
+            if (copy) *copy = {theirs.id, mine.id};
+            ledger_.unshare(theirs);
         }
         ++t.length;
     }
     void drop(std::uint64_t id) {
-        auto& t = mutable_sequence(id);
-        for (auto b : t.blocks) pool_.release(b);
-        tables_.erase(id);
+        const auto it = tables_.find(id);
+        if (it == tables_.end()) throw std::invalid_argument("unknown KV sequence");
+        for (const BlockHandle& b : it->second.blocks) ledger_.unshare(b);
+        tables_.erase(it);
     }
     std::uint64_t fork(std::uint64_t id) {
-        const auto copy = sequence(id);
-        std::size_t retained = 0;
-        try {
-            for (auto b : copy.blocks) {
-                pool_.retain(b);
-                ++retained;
-            }
-            if (next_ == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("sequence ID exhausted");
-            const auto r = ++next_;
-            tables_.emplace(r, copy);
-            return r;
-        } catch (...) {
-            for (std::size_t i = 0; i < retained; ++i) pool_.release(copy.blocks[i]);
-            throw;
-        }
+        const BlockTable& src = sequence(id);
+        return add_sharing(src, src.length);
     }
     void truncate(std::uint64_t id, std::size_t length) {
-        auto& t = mutable_sequence(id);
+        BlockTable& t = table(id);
         if (length > t.length) throw std::invalid_argument("cannot extend KV by truncating");
-        const auto tpb = geometry().tokens_per_block;
-        const auto keep = length / tpb + (length % tpb ? 1 : 0);
-        for (std::size_t i = keep; i < t.blocks.size(); ++i) pool_.release(t.blocks[i]);
-        t.blocks.resize(keep);
+        const std::size_t keep = geometry().blocks_for(length);
+        for (std::size_t i = keep; i < t.blocks.size(); ++i) ledger_.unshare(t.blocks[i]);
+        t.blocks.erase(t.blocks.begin() + std::ptrdiff_t(keep), t.blocks.end());
         t.length = length;
     }
-    std::uint64_t import_sequence(const BlockTable& source, std::size_t length) {
-        if (length > source.length) throw std::invalid_argument("prefix exceeds snapshot");
-        const auto tpb = geometry().tokens_per_block;
-        const auto count = length / tpb + (length % tpb ? 1 : 0);
-        if (source.blocks.size() < count) throw std::invalid_argument("invalid prefix snapshot");
-        BlockTable t;
-        t.length = length;
-        t.blocks.assign(source.blocks.begin(), source.blocks.begin() + static_cast<std::ptrdiff_t>(count));
-        std::size_t retained = 0;
-        try {
-            for (auto h : t.blocks) {
-                pool_.retain(h);
-                ++retained;
-            }
-            if (next_ == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("sequence ID exhausted");
-            const auto id = ++next_;
-            tables_.emplace(id, std::move(t));
-            return id;
-        } catch (...) {
-            for (std::size_t i = 0; i < retained; ++i) pool_.release(source.blocks[i]);
-            throw;
-        }
+    // A new sequence holding the first `length` positions of `snapshot`.
+    std::uint64_t import_sequence(const BlockTable& snapshot, std::size_t length) {
+        if (length > snapshot.length) throw std::invalid_argument("prefix exceeds snapshot");
+        if (snapshot.blocks.size() < geometry().blocks_for(length)) throw std::invalid_argument("invalid prefix snapshot");
+        return add_sharing(snapshot, length);
     }
+    // Ledger consistent, every table's block count matches its length, and
+    // each block's reference count equals the tables holding it plus
+    // `external` (references held elsewhere, e.g. by the prefix trie).
     void audit(std::span<const std::size_t> external = {}) const {
-        pool_.audit();
-        std::vector<std::size_t> counts(geometry().max_blocks);
-        if (!external.empty() && external.size() != counts.size())
-            throw std::invalid_argument("external reference counts mismatch");
-        const auto tpb = geometry().tokens_per_block;
-        for (const auto& [id, t] : tables_) {
-            const auto expected = t.length / tpb + (t.length % tpb ? 1 : 0);
-            if (t.blocks.size() != expected) throw std::logic_error("KV block table length invariant");
-            for (auto b : t.blocks) {
-                pool_.check(b);
-                ++counts.at(b.id);
-            }
+        ledger_.audit();
+        const std::size_t n = geometry().max_blocks;
+        if (!external.empty() && external.size() != n) throw std::invalid_argument("external reference counts mismatch");
+        std::vector<std::size_t> held(n, 0);
+        if (!external.empty()) std::copy(external.begin(), external.end(), held.begin());
+        for (const auto& entry : tables_) {
+            const BlockTable& t = entry.second;
+            if (t.blocks.size() != geometry().blocks_for(t.length)) throw std::logic_error("KV block table length invariant");
+            for (const BlockHandle& b : t.blocks) ++held[ledger_.checked(b)];
         }
-        for (std::size_t i = 0; i < counts.size(); ++i)
-            if (counts[i] + (external.empty() ? 0 : external[i]) != pool_.references_by_id(i))
-                throw std::logic_error("KV reference invariant");
+        for (std::size_t i = 0; i < n; ++i)
+            if (held[i] != ledger_.references_by_id(i)) throw std::logic_error("KV reference invariant");
     }
-    std::size_t sequences() const { return tables_.size(); }
 
 private:
-    BlockTable& mutable_sequence(std::uint64_t id) {
-        auto it = tables_.find(id);
+    BlockTable& table(std::uint64_t id) {
+        const auto it = tables_.find(id);
         if (it == tables_.end()) throw std::invalid_argument("unknown KV sequence");
         return it->second;
     }
-    BlockPool pool_;
-    std::map<std::uint64_t, BlockTable> tables_;
-    std::uint64_t next_ = 0;
-};
-
-// Token-path trie over cached prefixes (radix.hpp:17-130): compressed edges,
-// per-node snapshots of a sequence's block table holding one reference per
-// block, pins along the path, LRU eviction of unpinned leaves.
-struct RadixNode {
-    std::uint64_t id = 0, parent = 0;
-    std::vector<std::int32_t> edge;
-    std::map<std::int32_t, std::uint64_t> children;
-    std::optional<BlockTable> kv;
-    std::size_t pins = 0;
-    std::uint64_t accessed = 0;
-};
-
-class RadixBook {
-public:
-    RadixBook(PagedBook& cache, std::string isolation) : cache_(cache), isolation_(std::move(isolation)) {
-        if (isolation_.empty()) throw std::invalid_argument("prefix isolation key is required");
-        nodes_.emplace(0, RadixNode{});
+    std::uint64_t next_id() {
+        if (last_id_ == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("sequence ID exhausted");
+        return ++last_id_;
     }
-    RadixBook(const RadixBook&) = delete;
-    RadixBook& operator=(const RadixBook&) = delete;
-    ~RadixBook() {
-        for (auto& [id, n] : nodes_)
-            if (n.kv)
-                for (auto b : n.kv->blocks) cache_.pool().release(b);
+    std::uint64_t add(BlockTable t) {
+        const std::uint64_t id = next_id();
+        tables_.emplace(id, std::move(t));
+        return id;
     }
-    const RadixNode& node(std::uint64_t id) const { return nodes_.at(id); }
-    std::size_t size() const { return nodes_.size() - 1; }
-
-    std::pair<std::uint64_t, std::size_t> lookup(std::span<const std::int32_t> tokens) const {
-        std::uint64_t cur = 0;
-        std::size_t off = 0;
-        std::pair<std::uint64_t, std::size_t> r{0, 0};
-        while (off < tokens.size()) {
-            const auto& parent = nodes_.at(cur);
-            auto it = parent.children.find(tokens[off]);
-            if (it == parent.children.end()) break;
-            const auto& child = nodes_.at(it->second);
-            std::size_t common = 0;
-            while (common < child.edge.size() && off + common < tokens.size() && child.edge[common] == tokens[off + common])
-                ++common;
-            off += common;
-            r = {child.id, off};
-            if (common != child.edge.size()) break;
-            cur = child.id;
-        }
-        return r;
-    }
-
-    std::uint64_t insert(std::span<const std::int32_t> tokens) {
-        if (tokens.empty()) throw std::invalid_argument("cannot cache empty prefix");
-        std::uint64_t cur = 0;
-        std::size_t off = 0;
-        while (off < tokens.size()) {
-            auto& parent = nodes_.at(cur);
-            auto found = parent.children.find(tokens[off]);
-            if (found == parent.children.end()) {
-                if (next_ == std::numeric_limits<std::uint64_t>::max()) throw std::overflow_error("radix ID exhausted");
-                const auto id = ++next_;
-                RadixNode child;
-                child.id = id;
-                child.parent = cur;
-                child.edge.assign(tokens.begin() + static_cast<std::ptrdiff_t>(off), tokens.end());
-                nodes_.emplace(id, std::move(child));
-                nodes_.at(cur).children.emplace(tokens[off], id);
-                return id;
-            }
-            auto& child = nodes_.at(found->second);
-            std::size_t common = 0;
-            while (common < child.edge.size() && off + common < tokens.size() && child.edge[common] == tokens[off + common])
-                ++common;
-            if (common != child.edge.size()) {
-                if (next_ == std::numeric_limits<std::uint64_t>::max()) throw std::overflow_error("radix ID exhausted");
-                const auto split = ++next_;
-                RadixNode middle;
-                middle.id = split;
-                middle.parent = cur;
-                middle.pins = child.pins;
-                middle.edge.assign(child.edge.begin(), child.edge.begin() + static_cast<std::ptrdiff_t>(common));
-                child.edge.erase(child.edge.begin(), child.edge.begin() + static_cast<std::ptrdiff_t>(common));
-                middle.children.emplace(child.edge.front(), child.id);
-                child.parent = split;
-                nodes_.at(cur).children[tokens[off]] = split;
-                nodes_.emplace(split, std::move(middle));
-                cur = split;
-                off += common;
-                continue;
-            }
-            cur = child.id;
-            off += common;
-        }
-        return cur;
-    }
-
-    void attach(std::uint64_t id, std::uint64_t sequence) {
-        auto& entry = nodes_.at(id);
-        auto source = cache_.sequence(sequence);
-        std::size_t depth = 0;
-        for (auto c = id; c; c = nodes_.at(c).parent) depth += nodes_.at(c).edge.size();
-        if (source.length != depth) throw std::invalid_argument("token and KV prefix lengths differ");
-        std::size_t retained = 0;
+    // New table over the leading blocks of `src` covering `length` positions,
+    // each block's count raised; on any failure the counts already raised are
+    // lowered again and nothing else changes.
+    std::uint64_t add_sharing(const BlockTable& src, std::size_t length) {
+        BlockTable t;
+        t.length = length;
+        t.blocks.assign(src.blocks.begin(), src.blocks.begin() + std::ptrdiff_t(geometry().blocks_for(length)));
+        if (last_id_ == std::numeric_limits<std::uint64_t>::max()) throw std::runtime_error("sequence ID exhausted");
+        std::size_t raised = 0;
         try {
-            for (auto b : source.blocks) {
-                cache_.pool().retain(b);
-                ++retained;
-            }
+            for (; raised < t.blocks.size(); ++raised) ledger_.share(t.blocks[raised]);
+            return add(std::move(t));
         } catch (...) {
-            for (std::size_t i = 0; i < retained; ++i) cache_.pool().release(source.blocks[i]);
+            while (raised) ledger_.unshare(src.blocks[--raised]);
             throw;
         }
-        if (entry.kv)
-            for (auto b : entry.kv->blocks) cache_.pool().release(b);
-        entry.kv = std::move(source);
+    }
+
+    BlockLedger ledger_;
+    std::unordered_map<std::uint64_t, BlockTable> tables_;
+    std::uint64_t last_id_ = 0;
+};
+
+class PrefixTrie {
+    static constexpr std::uint32_t kNone = std::numeric_limits<std::uint32_t>::max();
+    struct Node {
+        std::uint64_t id = 0;
+        std::uint32_t up = kNone;  // parent slot
+        std::vector<std::int32_t> edge;
+        std::vector<std::pair<std::int32_t, std::uint32_t>> kids;  // (first edge token, slot), sorted
+        std::optional<BlockTable> snapshot;
+        std::size_t pins = 0;
+        std::uint64_t stamp = 0;
+    };
+
+public:
+    PrefixTrie(SequenceBook& book, std::string isolation) : book_(book), isolation_(std::move(isolation)) {
+        if (isolation_.empty()) throw std::invalid_argument("prefix isolation key is required");
+        clear_arena();
+    }
+    PrefixTrie(const PrefixTrie&) = delete;
+    PrefixTrie& operator=(const PrefixTrie&) = delete;
+    ~PrefixTrie() {
+        for (std::uint32_t s : slots_by_id()) release_snapshot(arena_[s]);
+    }
+    std::size_t size() const { return slot_of_.size() - 1; }
+
+    // Deepest node reached by `tokens` and how many tokens matched; the last
+    // node may be matched only part way along its edge.
+    std::pair<std::uint64_t, std::size_t> lookup(std::span<const std::int32_t> tokens) const {
+        std::pair<std::uint64_t, std::size_t> hit{0, 0};
+        std::uint32_t at = 0;
+        std::size_t done = 0;
+        while (done < tokens.size()) {
+            const std::uint32_t kid = child(at, tokens[done]);
+            if (kid == kNone) break;
+            const std::size_t same = matched(arena_[kid].edge, tokens.subspan(done));
+            done += same;
+            hit = {arena_[kid].id, done};
+            if (same < arena_[kid].edge.size()) break;
+            at = kid;
+        }
+        return hit;
+    }
+
+    // Node for exactly `tokens`, creating a leaf and splitting an edge where
+    // the path leaves the trie part way along one.
+    std::uint64_t insert(std::span<const std::int32_t> tokens) {
+        if (tokens.empty()) throw std::invalid_argument("cannot cache empty prefix");
+        std::uint32_t at = 0;
+        std::size_t done = 0;
+        while (done < tokens.size()) {
+            const std::uint32_t kid = child(at, tokens[done]);
+            if (kid == kNone) {
+                const std::uint32_t leaf = make_node(at, {tokens.begin() + std::ptrdiff_t(done), tokens.end()});
+                link(at, leaf);
+                return arena_[leaf].id;
+            }
+            const std::size_t same = matched(arena_[kid].edge, tokens.subspan(done));
+            if (same < arena_[kid].edge.size()) {
+                std::vector<std::int32_t>& tail = arena_[kid].edge;
+                const std::uint32_t mid = make_node(at, {tail.begin(), tail.begin() + std::ptrdiff_t(same)});
+                Node& m = arena_[mid];
+                Node& k = arena_[kid];  // arena_ may have grown: take references afresh
+                m.pins = k.pins;
+                k.edge.erase(k.edge.begin(), k.edge.begin() + std::ptrdiff_t(same));
+                k.up = mid;
+                m.kids.push_back({k.edge.front(), kid});
+                replace_child(at, tokens[done], mid);
+                at = mid;
+            } else {
+                at = kid;
+            }
+            done += same;
+        }
+        return arena_[at].id;
+    }
+
+    // Node `id` keeps its own reference to every block of `sequence`, whose
+    // length must equal the node's depth in tokens; a previous snapshot is
+    // released.
+    void attach(std::uint64_t id, std::uint64_t sequence) {
+        const std::uint32_t s = slot(id);
+        BlockTable copy = book_.sequence(sequence);
+        std::size_t depth = 0;
+        for (std::uint32_t c = s; c != 0; c = arena_[c].up) depth += arena_[c].edge.size();
+        if (copy.length != depth) throw std::invalid_argument("token and KV prefix lengths differ");
+        std::size_t raised = 0;
+        try {
+            for (; raised < copy.blocks.size(); ++raised) book_.ledger().share(copy.blocks[raised]);
+        } catch (...) {
+            while (raised) book_.ledger().unshare(copy.blocks[--raised]);
+            throw;
+        }
+        release_snapshot(arena_[s]);
+        arena_[s].snapshot = std::move(copy);
     }
 
     std::vector<std::size_t> external_references() const {
-        std::vector<std::size_t> counts(cache_.geometry().max_blocks);
-        for (const auto& [id, n] : nodes_)
-            if (n.kv)
-                for (auto b : n.kv->blocks) ++counts.at(b.id);
-        return counts;
+        std::vector<std::size_t> held(book_.geometry().max_blocks, 0);
+        for (const auto& [id, s] : slot_of_)
+            if (arena_[s].snapshot)
+                for (const BlockHandle& b : arena_[s].snapshot->blocks) ++held.at(b.id);
+        return held;
     }
 
+    // A new sequence sharing the longest cached prefix of `tokens` (whole
+    // blocks only unless `partial`), or an empty one; returns (sequence,
+    // positions shared).
     std::pair<std::uint64_t, std::size_t> reuse(std::span<const std::int32_t> tokens, bool partial = false) {
-        auto m = lookup(tokens);
-        if (!m.first || !nodes_.at(m.first).kv) return {cache_.create_sequence(), 0};
-        std::size_t length = m.second;
-        if (!partial) length -= length % cache_.geometry().tokens_per_block;
-        return {cache_.import_sequence(*nodes_.at(m.first).kv, length), length};
+        const auto [node, count] = lookup(tokens);
+        if (node == 0) return {book_.create_sequence(), 0};
+        const Node& n = arena_[slot(node)];
+        if (!n.snapshot) return {book_.create_sequence(), 0};
+        const std::size_t tpb = book_.geometry().tokens_per_block;
+        const std::size_t length = partial ? count : count / tpb * tpb;
+        return {book_.import_sequence(*n.snapshot, length), length};
     }
 
     void pin(std::uint64_t id) {
-        for (auto c = id; c; c = nodes_.at(c).parent)
-            if (nodes_.at(c).pins == std::numeric_limits<std::size_t>::max()) throw std::overflow_error("prefix pin overflow");
-        for (auto c = id; c; c = nodes_.at(c).parent) ++nodes_.at(c).pins;
+        const std::uint32_t s = slot(id);
+        for (std::uint32_t c = s; c != 0; c = arena_[c].up)
+            if (arena_[c].pins == std::numeric_limits<std::size_t>::max()) throw std::overflow_error("prefix pin overflow");
+        for (std::uint32_t c = s; c != 0; c = arena_[c].up) ++arena_[c].pins;
     }
     void unpin(std::uint64_t id) {
-        for (auto c = id; c; c = nodes_.at(c).parent)
-            if (!nodes_.at(c).pins) throw std::invalid_argument("prefix pin underflow");
-        for (auto c = id; c; c = nodes_.at(c).parent) --nodes_.at(c).pins;
+        const std::uint32_t s = slot(id);
+        for (std::uint32_t c = s; c != 0; c = arena_[c].up)
+            if (arena_[c].pins == 0) throw std::invalid_argument("prefix pin underflow");
+        for (std::uint32_t c = s; c != 0; c = arena_[c].up) --arena_[c].pins;
     }
     void touch(std::uint64_t id) {
-        auto& e = nodes_.at(id);
+        Node& n = arena_[slot(id)];
         if (clock_ == std::numeric_limits<std::uint64_t>::max()) throw std::overflow_error("prefix access clock exhausted");
-        e.accessed = ++clock_;
+        n.stamp = ++clock_;
     }
+    // Least recently touched unpinned leaf; ties go to the lowest node id.
     std::optional<std::uint64_t> eviction_candidate() const {
-        std::optional<std::uint64_t> r;
-        for (const auto& [id, e] : nodes_)
-            if (id && e.children.empty() && !e.pins && (!r || e.accessed < nodes_.at(*r).accessed)) r = id;
-        return r;
+        std::optional<std::pair<std::uint64_t, std::uint64_t>> best;  // (stamp, id)
+        for (const auto& [id, s] : slot_of_) {
+            const Node& n = arena_[s];
+            if (id == 0 || !n.kids.empty() || n.pins) continue;
+            const std::pair<std::uint64_t, std::uint64_t> key{n.stamp, id};
+            if (!best || key < *best) best = key;
+        }
+        if (!best) return std::nullopt;
+        return best->second;
     }
     bool evict_one() {
-        auto cand = eviction_candidate();
-        if (!cand) return false;
-        auto& e = nodes_.at(*cand);
-        if (e.kv)
-            for (auto b : e.kv->blocks) cache_.pool().release(b);
-        nodes_.at(e.parent).children.erase(e.edge.front());
-        nodes_.erase(*cand);
+        const auto victim = eviction_candidate();
+        if (!victim) return false;
+        const std::uint32_t s = slot(*victim);
+        release_snapshot(arena_[s]);
+        unlink(arena_[s].up, arena_[s].edge.front());
+        free_node(s);
         return true;
     }
+    // Drops every node (ids keep counting up); refused while any is pinned.
     void reset() {
-        for (const auto& [id, e] : nodes_)
-            if (id && e.pins) throw std::logic_error("cannot reset pinned prefix nodes");
-        for (auto& [id, e] : nodes_)
-            if (e.kv)
-                for (auto b : e.kv->blocks) cache_.pool().release(b);
-        nodes_.clear();
-        nodes_.emplace(0, RadixNode{});
+        for (const auto& [id, s] : slot_of_)
+            if (id != 0 && arena_[s].pins) throw std::logic_error("cannot reset pinned prefix nodes");
+        for (std::uint32_t s : slots_by_id()) release_snapshot(arena_[s]);
+        clear_arena();
         clock_ = 0;
     }
 
 private:
-    PagedBook& cache_;
+    static std::size_t matched(const std::vector<std::int32_t>& edge, std::span<const std::int32_t> rest) {
+        const std::size_t n = std::min(edge.size(), rest.size());
+        return std::size_t(std::mismatch(edge.begin(), edge.begin() + std::ptrdiff_t(n), rest.begin()).first - edge.begin());
+    }
+    std::uint32_t slot(std::uint64_t id) const {
+        const auto it = slot_of_.find(id);
+        if (it == slot_of_.end()) throw std::invalid_argument("unknown prefix node");
+        return it->second;
+    }
+    std::uint32_t child(std::uint32_t at, std::int32_t token) const {
+        const auto& k = arena_[at].kids;
+        const auto it = std::lower_bound(k.begin(), k.end(), token, [](const auto& e, std::int32_t t) { return e.first < t; });
+        return it != k.end() && it->first == token ? it->second : kNone;
+    }
+    void link(std::uint32_t at, std::uint32_t kid) {
+        auto& k = arena_[at].kids;
+        const std::int32_t token = arena_[kid].edge.front();
+        const auto it = std::lower_bound(k.begin(), k.end(), token, [](const auto& e, std::int32_t t) { return e.first < t; });
+        k.insert(it, {token, kid});
+    }
+    void replace_child(std::uint32_t at, std::int32_t token, std::uint32_t kid) {
+        for (auto& e : arena_[at].kids)
+            if (e.first == token) e.second = kid;
+    }
+    void unlink(std::uint32_t at, std::int32_t token) {
+        auto& k = arena_[at].kids;
+        k.erase(std::remove_if(k.begin(), k.end(), [&](const auto& e) { return e.first == token; }), k.end());
+    }
+    std::uint32_t make_node(std::uint32_t up, std::vector<std::int32_t> edge) {
+        if (last_id_ == std::numeric_limits<std::uint64_t>::max()) throw std::overflow_error("radix ID exhausted");
+        std::uint32_t s;
+        if (!vacant_.empty()) {
+            s = vacant_.back();
+            vacant_.pop_back();
+            arena_[s] = Node{};
+        } else {
+            s = std::uint32_t(arena_.size());
+            arena_.emplace_back();
+        }
+        Node& n = arena_[s];
+        n.id = ++last_id_;
+        n.up = up;
+        n.edge = std::move(edge);
+        slot_of_.emplace(n.id, s);
+        return s;
+    }
+    void free_node(std::uint32_t s) {
+        slot_of_.erase(arena_[s].id);
+        arena_[s] = Node{};
+        vacant_.push_back(s);
+    }
+    void release_snapshot(Node& n) {
+        if (!n.snapshot) return;
+        for (const BlockHandle& b : n.snapshot->blocks) book_.ledger().unshare(b);
+        n.snapshot.reset();
+    }
+    // Live slots in ascending node id, the order releases reach the free chain.
+    std::vector<std::uint32_t> slots_by_id() const {
+        std::vector<std::pair<std::uint64_t, std::uint32_t>> v(slot_of_.begin(), slot_of_.end());
+        std::sort(v.begin(), v.end());
+        std::vector<std::uint32_t> out;
+        out.reserve(v.size());
+        for (const auto& e : v) out.push_back(e.second);
+        return out;
+    }
+    void clear_arena() {
+        arena_.assign(1, Node{});
+        vacant_.clear();
+        slot_of_.clear();
+        slot_of_.emplace(0, 0);
+    }
+
+    SequenceBook& book_;
     std::string isolation_;
-    std::map<std::uint64_t, RadixNode> nodes_;
-    std::uint64_t next_ = 0, clock_ = 0;
+    std::vector<Node> arena_;
+    std::vector<std::uint32_t> vacant_;
+    std::unordered_map<std::uint64_t, std::uint32_t> slot_of_;
+    std::uint64_t last_id_ = 0, clock_ = 0;
 };
 
 }  // namespace tvara

@@ -1,6 +1,7 @@
-"""Owned ctypes handle over the B200 engine, mirroring the reference's
-python/tvara/native.py:27-345 (same constructor, ``logits``, ``iter_tokens``,
-``generate``, ``metadata`` and error behaviour), plus the additive calls:
+"""Owned ctypes handle over the B200 engine with the reference's
+python/tvara/native.py:27-345 surface (same constructor, ``logits``,
+``iter_tokens`` / ``generate`` sampled on the device, ``metadata`` and error
+behaviour), plus the additive calls:
 ``decode_batch`` (multi-token append with rollback), ``batch_step`` (one
 device step over a ragged batch of sequences), ``fork``, ``truncate``, KV
 inspection and the radix prefix cache.
@@ -46,6 +47,58 @@ def tp_shard(path, tp_rank: int, tp_size: int, library=None) -> dict:
     if lib.tvara_tp_shard(str(Path(path).resolve()).encode("utf-8"), int(tp_rank), int(tp_size), C.byref(info)):
         raise RuntimeError(lib.tvara_last_error().decode("utf-8", "replace"))
     return {name: int(getattr(info, name)) for name, _ in TpShardInfo._fields_ if name != "struct_size"}
+
+
+def _is_flag(v) -> bool:
+    return isinstance(v, (bool, np.bool_))
+
+
+def _is_int(v) -> bool:
+    return isinstance(v, (int, np.integer)) and not _is_flag(v)
+
+
+def _is_pyint(v) -> bool:
+    return isinstance(v, int) and not _is_flag(v)
+
+
+class _GenerationSettings:
+    """Checked generation arguments.  Checks run in the reference's order and
+    raise its texts (python/tvara/native.py:220-262), so callers see the same
+    errors for the same bad input."""
+
+    def __init__(self, vocab, context, prompt, max_new_tokens, temperature, seed, eos_id, top_p, top_k, min_p,
+                 repetition, frequency, presence):
+        self.prompt = list(prompt)
+        if not self.prompt or not all(_is_int(t) and 0 <= t < vocab for t in self.prompt):
+            raise ValueError("Invalid prompt token IDs")
+        if not (_is_pyint(max_new_tokens) and 0 <= max_new_tokens <= context - len(self.prompt)):
+            raise ValueError("Generation exceeds context limits")
+        self.max_new_tokens = max_new_tokens
+        reals = {}
+        for name, v in (("temperature", temperature), ("top_p", top_p), ("min_p", min_p),
+                        ("repetition", repetition), ("frequency", frequency), ("presence", presence)):
+            if _is_flag(v) or not isinstance(v, (int, float, np.integer, np.floating)):
+                raise ValueError("Sampling parameters must be real scalars")
+            reals[name] = float(v)
+        self.temperature, self.top_p, self.min_p = reals["temperature"], reals["top_p"], reals["min_p"]
+        self.repetition, self.frequency, self.presence = reals["repetition"], reals["frequency"], reals["presence"]
+        finite = np.isfinite
+        if not (finite(self.temperature) and self.temperature >= 0 and finite(self.top_p) and 0 < self.top_p <= 1
+                and finite(self.min_p) and 0 <= self.min_p <= 1):
+            raise ValueError("Invalid sampling parameters")
+        if not (_is_pyint(top_k) and top_k >= 0 and finite(self.repetition) and self.repetition > 0
+                and finite(self.frequency) and finite(self.presence)):
+            raise ValueError("Invalid sampling filters or penalties")
+        self.top_k = top_k
+        if eos_id is not None and not (_is_int(eos_id) and 0 <= eos_id < vocab):
+            raise ValueError("Invalid EOS ID")
+        self.eos_id = eos_id
+        if _is_flag(seed):
+            raise ValueError("Invalid random seed")
+        try:
+            self.rng = np.random.default_rng(seed)
+        except (ValueError, TypeError, OverflowError) as error:
+            raise ValueError("Invalid random seed") from error
 
 
 class NativeModel:
@@ -398,97 +451,29 @@ class NativeModel:
 
     # ------------------------------------------------------------ generation
     def iter_tokens(self, prompt, max_new_tokens=16, temperature=0, seed=0, eos_id=None, top_p=1, top_k=0,
-                    min_p=0, repetition=1, frequency=0, presence=0, token_constraint=None, device_sampling=True):
-        """The reference's sampler (python/tvara/native.py:220-340): same
-        parameter checks, penalties, mask and filter order.  With
-        device_sampling, the penalties, the mask, the checks and either the
-        argmax (temperature 0: bit-identical to the host path) or the top
-        candidates (1 <= top_k <= 48) are computed on the device and only
-        those cross to the host; the random draw stays numpy's.  On the
+                    min_p=0, repetition=1, frequency=0, presence=0, token_constraint=None):
+        """Generation with the reference's arguments, errors and tokens
+        (python/tvara/native.py:220-340), sampled on the device: the penalties,
+        the token constraint's mask, the finiteness checks and either the
+        argmax (temperature 0: the reference's token bit for bit) or the
+        top_k + 16 largest adjusted logits are computed by tvara_batch_sample,
+        and only those cross to the host, where numpy draws the token.  On the
         candidate path the probabilities are normalised over the candidates
-        instead of the whole vocabulary, which changes them by rounding only:
-        the drawn token can differ only if the uniform draw falls within that
-        rounding of a boundary of the cumulative distribution.  Other
-        settings copy full logits and sample on the host."""
-        prompt = list(prompt)
-        if not prompt or any(isinstance(t, (bool, np.bool_)) or not isinstance(t, (int, np.integer))
-                             or not 0 <= t < self.vocab_size for t in prompt):
-            raise ValueError("Invalid prompt token IDs")
-        if (isinstance(max_new_tokens, (bool, np.bool_)) or not isinstance(max_new_tokens, int)
-                or max_new_tokens < 0 or len(prompt) + max_new_tokens > self.context_size):
-            raise ValueError("Generation exceeds context limits")
+        rather than the whole vocabulary, which changes them by rounding
+        only: the drawn token can differ only if the uniform draw falls within
+        that rounding of a boundary of the cumulative distribution.
 
-        def real(value):
-            if isinstance(value, (bool, np.bool_)) or not isinstance(value, (int, float, np.integer, np.floating)):
-                raise ValueError("Sampling parameters must be real scalars")
-            return float(value)
-
-        temperature, top_p, min_p, repetition, frequency, presence = (
-            real(v) for v in (temperature, top_p, min_p, repetition, frequency, presence))
-        if (not np.isfinite(temperature) or temperature < 0 or not np.isfinite(top_p) or not 0 < top_p <= 1
-                or not np.isfinite(min_p) or not 0 <= min_p <= 1):
-            raise ValueError("Invalid sampling parameters")
-        if (isinstance(top_k, (bool, np.bool_)) or not isinstance(top_k, int) or top_k < 0
-                or not np.isfinite(repetition) or repetition <= 0 or not np.isfinite(frequency)
-                or not np.isfinite(presence)):
-            raise ValueError("Invalid sampling filters or penalties")
-        if eos_id is not None and (not isinstance(eos_id, (int, np.integer)) or isinstance(eos_id, bool)
-                                   or not 0 <= eos_id < self.vocab_size):
-            raise ValueError("Invalid EOS ID")
-        if isinstance(seed, (bool, np.bool_)):
-            raise ValueError("Invalid random seed")
-        try:
-            rng = np.random.default_rng(seed)
-        except (ValueError, TypeError, OverflowError) as error:
-            raise ValueError("Invalid random seed") from error
-        on_device = device_sampling and (temperature == 0 or 1 <= top_k <= SAMPLE_MAX_K - SAMPLE_MARGIN)
-        if on_device:
-            yield from self._iter_tokens_device(prompt, max_new_tokens, temperature, rng, eos_id, top_p, top_k,
-                                                min_p, repetition, frequency, presence, token_constraint)
-            return
-        sequence = self._new_sequence()
-        history = prompt.copy()
-        try:
-            # the prompt is one device step (all rows computed, last one kept)
-            logits = self.decode_batch(sequence, prompt)[-1]
-            for index in range(max_new_tokens):
-                logits = logits.astype(np.float64, copy=True)
-                if not np.isfinite(logits).all():
-                    raise ValueError("Nonfinite model logits")
-                counts = np.bincount(history, minlength=self.vocab_size)
-                seen = counts > 0
-                with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
-                    logits[seen] = np.where(logits[seen] >= 0, logits[seen] / repetition, logits[seen] * repetition)
-                    logits -= counts * frequency + seen * presence
-                if not np.isfinite(logits).all():
-                    raise ValueError("Nonfinite adjusted sampling logits")
-                if token_constraint is not None:
-                    logits = token_constraint.mask_logits(logits)
-                if temperature == 0:
-                    token = int(logits.argmax())
-                else:
-                    values = (logits - float(logits.max())) / temperature
-                    p = np.exp(values)
-                    p /= p.sum()
-                    order = np.argsort(-p, kind="stable")
-                    if top_k:
-                        p[order[top_k:]] = 0
-                    p[p < p.max() * min_p] = 0
-                    p /= p.sum()
-                    cumulative = np.cumsum(p[order])
-                    p[order[np.r_[False, cumulative[:-1] >= top_p]]] = 0
-                    p /= p.sum()
-                    token = int(rng.choice(self.vocab_size, p=p))
-                if token_constraint is not None:
-                    token_constraint.accept(token)
-                history.append(token)
-                yield token
-                if token == eos_id:
-                    break
-                if index + 1 < max_new_tokens:
-                    logits = self.logits(sequence, token)
-        finally:
-            self._drop_sequence(sequence)
+        Settings the device does not cover -- temperature > 0 with top_k 0 or
+        above 48 -- raise ValueError; the reference's own NativeModel, loaded
+        on this library through TVARA_LIBRARY, samples those on the host."""
+        s = _GenerationSettings(self.vocab_size, self.context_size, prompt, max_new_tokens, temperature, seed,
+                                eos_id, top_p, top_k, min_p, repetition, frequency, presence)
+        if not (s.temperature == 0 or 1 <= s.top_k <= SAMPLE_MAX_K - SAMPLE_MARGIN):
+            raise ValueError("device sampling needs temperature 0 or 1 <= top_k <= 48; use the reference "
+                             "NativeModel on this library for other settings")
+        yield from self._iter_tokens_device(s.prompt, s.max_new_tokens, s.temperature, s.rng, s.eos_id, s.top_p,
+                                            s.top_k, s.min_p, s.repetition, s.frequency, s.presence,
+                                            token_constraint)
 
     def _iter_tokens_device(self, prompt, max_new_tokens, temperature, rng, eos_id, top_p, top_k, min_p, repetition,
                             frequency, presence, token_constraint):
