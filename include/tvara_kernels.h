@@ -98,9 +98,16 @@ typedef struct tvara_attention_args {
     const float* kv_scales;
 } tvara_attention_args;
 
-/* Device scratch (bytes) tvara_paged_attention needs for these arguments. */
+/* Device scratch (bytes) tvara_paged_attention needs for these arguments;
+ * 0 with an error for invalid arguments, including a block id outside
+ * [0, max_blocks) in any block a query reads. */
 TVARA_API size_t tvara_paged_attention_workspace(const tvara_attention_args* args);
-/* Runs the attention; workspace is device memory of at least the size above. */
+/* Runs the attention; workspace is device memory of at least the size above.
+ * The call uploads the block tables and work list from host memory and, after
+ * the kernels, reads their error word back, so it returns only when the
+ * attention has finished on `stream`; a device-side error (a copy wait that
+ * timed out) returns -1 with its text.  Not capturable into a CUDA graph: a
+ * capturing stream is refused with an error before anything is enqueued. */
 TVARA_API int tvara_paged_attention(const tvara_attention_args* args, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
@@ -113,8 +120,9 @@ TVARA_API int tvara_paged_attention(const tvara_attention_args* args, void* work
  * cudaMalloc's device-wide synchronisation.  It allocates nothing.  Arguments
  * needing more scratch than the maximum (tvara_paged_attention_workspace) are
  * rejected with an error and nothing is launched.  The first call on a device,
- * with that device current, resolves the scratch address; make it before any
- * stream capture begins.  One scratch per device: calls overlapping on one
+ * with that device current, resolves the scratch address.  Synchronous on
+ * `stream` and not capturable, as tvara_paged_attention; device-side errors
+ * are returned the same way.  One scratch per device: calls overlapping on one
  * device (other streams or threads) race and must be serialised by the
  * caller. */
 TVARA_API size_t tvara_paged_attention_noalloc_max(void);

@@ -70,10 +70,19 @@ AttnLayout layout_for(const tvara_attention_args* a) {
         throw std::invalid_argument("invalid attention geometry");
     AttnLayout L;
     std::vector<int> vis(a->n_queries), off(a->n_queries);
+    if (a->n_queries && (!a->visible || !a->table_offset || !a->tables))
+        throw std::invalid_argument("invalid attention arguments");
+    if (!a->max_blocks || a->max_blocks > 0x7fffffff) throw std::invalid_argument("invalid KV pool size");
     for (std::size_t i = 0; i < a->n_queries; ++i) {
         if (!a->visible[i]) throw std::invalid_argument("empty fused attention");
         const std::size_t blocks = (a->visible[i] + a->block_tokens - 1) / a->block_tokens;
         if (a->table_offset[i] + blocks > a->tables_len) throw std::invalid_argument("block table shorter than visible range");
+        // every block a query reads must be a pool block: checked here, before
+        // anything is enqueued, rather than left to the kernels' guard
+        for (std::size_t b = 0; b < blocks; ++b) {
+            const std::int32_t id = a->tables[a->table_offset[i] + b];
+            if (id < 0 || std::size_t(id) >= a->max_blocks) throw std::invalid_argument("block id outside the KV pool");
+        }
         vis[i] = int(a->visible[i]);
         off[i] = int(a->table_offset[i]);
     }
@@ -247,6 +256,12 @@ int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t
         auto L = layout_for(a);
         if (!workspace || workspace_bytes < L.total) throw std::invalid_argument("attention workspace too small");
         auto s = static_cast<cudaStream_t>(stream);
+        // The call stages its tables from a host buffer that dies on return and
+        // waits for the kernels' error word: it cannot be recorded into a graph.
+        cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+        TVARA_CUDA(cudaStreamIsCapturing(s, &capturing));
+        if (capturing != cudaStreamCaptureStatusNone)
+            throw std::invalid_argument("paged attention cannot be captured into a CUDA graph");
         auto* base = static_cast<std::uint8_t*>(workspace);
         std::vector<std::uint8_t> host(L.off_partial);
         std::memcpy(host.data() + L.off_tables, a->tables, a->tables_len * 4);
@@ -279,6 +294,14 @@ int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t
         g.max_blocks = int(a->max_blocks);
         g.err = reinterpret_cast<int*>(base + L.off_err);
         tvara::launch_attention(g, s);
+        // the kernels' error word: 2 a block id outside the pool, 4 a bounded
+        // wait on a copy that never completed
+        int word = 0;
+        TVARA_CUDA(cudaMemcpyAsync(&word, base + L.off_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+        TVARA_CUDA(cudaStreamSynchronize(s));
+        if (word == 2) throw std::runtime_error("paged attention read a block id outside the KV pool");
+        if (word) throw std::runtime_error("paged attention timed out waiting for a KV copy (error " +
+                                           std::to_string(word) + ")");
     });
 }
 

@@ -15,8 +15,11 @@
 //    before any device work is enqueued;
 //  * the first call on a device, with that device current, resolves the
 //    scratch address (cudaGetSymbolAddress, which may load this library's
-//    device code onto the device); make that first call before any stream
-//    capture begins;
+//    device code onto the device);
+//  * like tvara_paged_attention, a call stages its block tables and work list
+//    from a host buffer and waits for the kernels' error word before it
+//    returns, so it is synchronous on `stream` and cannot be recorded into a
+//    CUDA graph (a capturing stream is refused before anything is enqueued);
 //  * there is one scratch per device: calls that overlap on one device (two
 //    streams, or two host threads, before the first has finished on the
 //    device) race on it and must be serialised by the caller.
@@ -77,6 +80,12 @@ int tvara_paged_attention_noalloc(const tvara_attention_args* args, void* stream
     if (need > kScratchBytes) {
         tvara::last_error() = "paged attention scratch of " + std::to_string(need) +
                               " bytes exceeds the static maximum of " + std::to_string(kScratchBytes) + " bytes";
+        return -1;
+    }
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &capturing) != cudaSuccess ||
+        capturing != cudaStreamCaptureStatusNone) {
+        tvara::last_error() = "paged attention cannot be captured into a CUDA graph";
         return -1;
     }
     void* scratch = nullptr;
