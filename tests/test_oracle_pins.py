@@ -283,3 +283,23 @@ def orc_book(L, blocks, tpb):
 @pytest.mark.parametrize("blocks,tpb,seed", [(8, 2, 0), (16, 3, 1), (64, 16, 2), (5, 4, 3)])
 def test_kv_accounting_restatement_matches_reference(oracle_lib, ref_shim, blocks, tpb, seed):
     _replay([ref_book(ref_shim, blocks, tpb), orc_book(oracle_lib, blocks, tpb)], seed)
+
+
+def test_batch_oracle_equals_token_by_token_executor(tiny_path):
+    """BatchOracle (float64 matrix products over all rows of a ragged step)
+    reproduces OracleModel.decode token by token, bit for bit, on sequences
+    with committed history and several new tokens each."""
+    from oracle.model import BatchOracle, OracleModel
+    o, b = OracleModel(tiny_path, max_positions=128), BatchOracle(tiny_path, max_positions=128)
+    rng = np.random.default_rng(0)
+    batch, want = [], []
+    for n, m in [(10, 1), (0, 3), (5, 2), (33, 4)]:
+        st = o.new_state()
+        for t in rng.integers(0, 512, n):
+            o.decode(st, int(t))
+        hist = {layer: (np.array(st["k"][layer], np.float32).reshape(n, o.kv_width),
+                        np.array(st["v"][layer], np.float32).reshape(n, o.kv_width)) for layer in range(o.layers)}
+        new = rng.integers(0, 512, m).tolist()
+        want += [o.decode(st, t) for t in new]
+        batch.append(dict(tokens=new, start=n, history=lambda layer, h=hist: h[layer]))
+    assert np.array_equal(b.step(batch), np.stack(want))
