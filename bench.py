@@ -391,6 +391,17 @@ def standalone_gemv(lib, hbm_gbs, cpu=True):
 
 
 # ------------------------------------------------------- the other configs
+def guard(fn, *args, **kw):
+    """Runs one single-rank measurement; an exception is reported in the
+    result line (and on stderr) instead of losing the whole line."""
+    import traceback
+    try:
+        return fn(*args, **kw)
+    except Exception as e:  # noqa: BLE001 -- reported, not swallowed
+        traceback.print_exc()
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
 def nccl_unique_id(rank, world):
     """A fresh NCCL unique id, made on rank 0 and shared over torch.distributed."""
     import torch.distributed as dist
@@ -562,7 +573,7 @@ def attention_config(lib, hbm_gbs, seed=0, cpu=True):
                 vis = ctx.astype(np.uint32)
                 off = offs
             else:
-                rows = [(i, int(n) - 512 + j + 1) for i, n in enumerate(ctx) for j in range(min(512, int(n)))]
+                rows = [(i, int(n) - min(512, int(n)) + j + 1) for i, n in enumerate(ctx) for j in range(min(512, int(n)))]
                 vis = np.array([v for _, v in rows], np.uint32)
                 off = offs[[i for i, _ in rows]]
             q = torch.randn(len(vis), H * D, device="cuda")
@@ -802,15 +813,16 @@ def run_ours(args):
     torch.cuda.empty_cache()
     single = rank == 0 and world == 1
     extras = not args.no_extras
-    gemv = standalone_gemv(lib, hbm, cpu=cpu_job is not None) if single and not args.no_standalone and extras else None
-    cpu = reference_cpu(path, cfg, mean_ctx, cpu_job) if cpu_job else None
+    gemv = guard(standalone_gemv, lib, hbm, cpu=cpu_job is not None) \
+        if single and not args.no_standalone and extras else None
+    cpu = guard(reference_cpu, path, cfg, mean_ctx, cpu_job) if cpu_job else None
     parity = parity_check(args, rank, world, local, barrier) if extras else None
     other = {}
     if extras:
         other["smollm2"] = smollm2_replicas(args, rank, world, local, barrier, dist)
         if single:
-            other["tiny"] = tiny_generate(args, local)
-            other["attention"] = attention_config(lib, hbm, cpu=cpu_job is not None)
+            other["tiny"] = guard(tiny_generate, args, local)
+            other["attention"] = guard(attention_config, lib, hbm, cpu=cpu_job is not None)
     line = {
         "metric": "ragged-batch decode tok/s (8B-shape Q4_K)", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,

@@ -271,7 +271,9 @@ class BatchOracle(OracleModel):
         out = np.einsum("hgp,phd->hgd", w, v64) / w.sum(axis=2)[..., None]
         return out.astype(np.float32).reshape(-1)
 
-    def step(self, batch) -> np.ndarray:
+    def step(self, batch, kv_round=None) -> np.ndarray:
+        """kv_round: optional function applied to the step's new K and V rows
+        before they are attended (e.g. rounding to the pool's F16)."""
         rows = [(i, j) for i, e in enumerate(batch) for j in range(len(e["tokens"]))]
         tokens = np.array([batch[i]["tokens"][j] for i, j in rows], np.int64)
         pos = np.array([batch[i]["start"] + j for i, j in rows], np.int64)
@@ -284,6 +286,8 @@ class BatchOracle(OracleModel):
             q = self.rotary_rows(self.mm(b["attn_q"], xn), self.heads, pos)
             k = self.rotary_rows(self.mm(b["attn_k"], xn), self.kv_heads, pos)
             v = self.mm(b["attn_v"], xn)
+            if kv_round is not None:
+                k, v = kv_round(k), kv_round(v)
             att = np.empty((len(rows), self.hidden), np.float32)
             for i, e in enumerate(batch):
                 hk, hv = e["history"](layer)

@@ -38,7 +38,7 @@ class _DeviceView:
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
 
 
-def build_step(model, *, seed, requests, prefix, suffix, extra_rows, rank=0, world=1):
+def build_step(model, *, seed, requests, prefix, suffix, extra_rows, rank=0, world=1, f16_values=False):
     """Sets up the sequences on `model` (an open tvara_b200 NativeModel) and
     returns the step to run and what the oracle needs.  Every rank of a
     tensor-parallel model calls it with the same arguments."""
@@ -58,6 +58,8 @@ def build_step(model, *, seed, requests, prefix, suffix, extra_rows, rank=0, wor
     full = rng.standard_normal((B, L, 2, hk, tpb, d), dtype=np.float32)
     if info["kv_dtype"] == 1:
         full = full.astype(np.float16)
+    elif f16_values:  # F32 pool holding F16-representable values (to compare the two pool types)
+        full = full.astype(np.float16).astype(np.float32)
     mine = np.ascontiguousarray(full[:, :, :, rank * hk_local:(rank + 1) * hk_local])
     typestr = "<f2" if info["kv_dtype"] == 1 else "<f4"
     n = B * info["block_elements"]
@@ -92,7 +94,7 @@ def build_step(model, *, seed, requests, prefix, suffix, extra_rows, rank=0, wor
                 tpb=tpb, layers=L, kv_width=hk * d, src=src, node=node)
 
 
-def oracle_rows(path, case, max_positions):
+def oracle_rows(path, case, max_positions, kv_round=None):
     full, copies, tpb = case["full"], case["copies"], case["tpb"]
     B, L, _, hk, _, d = full.shape
 
@@ -108,7 +110,7 @@ def oracle_rows(path, case, max_positions):
     oracle = BatchOracle(path, max_positions=max_positions)
     batch = [dict(tokens=t, start=s, history=history(tab, s))
              for t, s, tab in zip(case["tokens"], case["starts"], case["tables"])]
-    return oracle.step(batch)
+    return oracle.step(batch, kv_round)
 
 
 def compare(got, want) -> dict:

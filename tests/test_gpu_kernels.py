@@ -340,3 +340,63 @@ def test_attention_block_size_seven_and_many_rows(capi):
     for i, n in enumerate(lens):
         ref = oracle_attention(q[i], pool, tables[offs[i]:offs[i] + (n + 6) // 7], n, 2, 9)
         assert attn_close(got[i], ref)
+
+
+@pytest.mark.parametrize("dim,heads,kv_heads,tpb", [(128, 32, 8, 16), (128, 16, 2, 32), (64, 8, 8, 16),
+                                                    (64, 16, 8, 16), (128, 8, 4, 16)])
+def test_attention_prefill_chunks(capi, dim, heads, kv_heads, tpb):
+    """Chunked prefill (attention.hpp:85-89 fused_prompt_attention): query
+    rows at consecutive positions of one sequence, row i seeing
+    [0, start + i].  Runs of rows go to the chunk kernel (one K/V read per
+    chunk of 64 / G rows) for F16 pools; ragged chunk lengths (1..70 rows),
+    contexts to 3k, NaN-poisoned tail slots, and a few single decode rows in
+    the same launch."""
+    rng = np.random.default_rng(dim + heads + tpb)
+    lens, rows_of = [], []
+    for n, r in [(40, 40), (700, 33), (3000, 70), (17, 5), (129, 2), (1, 1), (256, 16), (900, 1), (64, 17)]:
+        lens.append(n)
+        rows_of.append(r)
+    pool = Pool(1, kv_heads, dim, tpb, sum((n + tpb - 1) // tpb for n in lens) + 4, dtype=np.float16, rng=rng)
+    tables, offs, vis, toff = [], [], [], []
+    for n, r in zip(lens, rows_of):
+        o = len(tables)
+        tables += pool.sequence(n, scale=0.6)
+        for i in range(r):
+            vis.append(n - r + i + 1)
+            toff.append(o)
+        offs.append(o)
+    q = rng.standard_normal((len(vis), heads * dim)).astype(np.float32)
+    got = run_attention(capi, pool, 0, heads, q, tables, toff, vis, kv_dtype=1)
+    k = 0
+    for s, (n, r) in enumerate(zip(lens, rows_of)):
+        ids = tables[offs[s]:offs[s] + (n + tpb - 1) // tpb]
+        for i in range(r):
+            ref = oracle_attention(q[k], pool, ids, vis[k], 0, heads)
+            assert attn_close(got[k], ref, 5e-5), (n, r, i, np.abs(got[k] - ref).max())
+            k += 1
+
+
+def test_attention_chunk_many_short_runs(capi):
+    """Speculative-verify shape: many sequences appending 2..8 rows each, so
+    the chunk pieces fill the grid; F16, head_dim 128, G = 4."""
+    rng = np.random.default_rng(77)
+    tpb, dim, heads, kv_heads = 16, 128, 32, 8
+    lens = [int(x) for x in rng.integers(20, 1500, 40)]
+    rows_of = [int(x) for x in rng.integers(2, 9, 40)]
+    pool = Pool(1, kv_heads, dim, tpb, sum((n + tpb - 1) // tpb for n in lens) + 4, dtype=np.float16, rng=rng)
+    tables, offs, vis, toff = [], [], [], []
+    for n, r in zip(lens, rows_of):
+        o = len(tables)
+        tables += pool.sequence(n, scale=0.6)
+        offs.append(o)
+        for i in range(r):
+            vis.append(n - r + i + 1)
+            toff.append(o)
+    q = rng.standard_normal((len(vis), heads * dim)).astype(np.float32)
+    got = run_attention(capi, pool, 0, heads, q, tables, toff, vis, kv_dtype=1)
+    k = 0
+    for s, (n, r) in enumerate(zip(lens, rows_of)):
+        ids = tables[offs[s]:offs[s] + (n + tpb - 1) // tpb]
+        for i in range(r):
+            assert attn_close(got[k], oracle_attention(q[k], pool, ids, vis[k], 0, heads), 5e-5), (n, r, i)
+            k += 1

@@ -586,7 +586,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         vis[t] = s.pos[t] + 1;
         toff[t] = s.table_off[s.seq_of[t]];
     }
-    AttnPlan plan = plan_attention(vis, toff, tpb, hkv_, partial_cap_);
+    AttnPlan plan = plan_attention(vis, toff, tpb, hkv_, partial_cap_, 148,
+                                   attention_chunk_rows(opt_.kv_f16, d, hq_ / hkv_, tpb));
     auto& work = plan.work;
     auto& comb = plan.comb;
     auto& wpart = plan.part;
@@ -624,6 +625,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         }
     }
     const std::size_t need = std::size_t(T) * 4 + s.tables.size() + work.size() * 5 + comb.size() * 4 +
+                             plan.chunk.size() * 4 + 4 +
                              s.copies.size() * 2 + R + 64 +
                              (sp ? std::size_t(R) * (8 + (sp->allowed ? words : 0)) + 16 : 0);
     if (need > meta_cap_) {
@@ -652,6 +654,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     int4* d_work = reinterpret_cast<int4*>(put(work.data(), work.size() * 4));
     int* d_wpart = put(wpart.data(), wpart.size());
     int4* d_comb = reinterpret_cast<int4*>(put(comb.data(), comb.size() * 4));
+    int4* d_chunk = reinterpret_cast<int4*>(put(plan.chunk.data(), plan.chunk.size() * 4));
     int2* d_copy = reinterpret_cast<int2*>(put(s.copies.data(), s.copies.size() * 2));
     int* d_rows = put(s.out_rows.data(), R);
     int *d_hlen = nullptr, *d_toff = nullptr;
@@ -756,6 +759,8 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         aa.partial = partial_;
         aa.combine = d_comb;
         aa.n_combine = int(comb.size());
+        aa.chunk_work = d_chunk;
+        aa.n_chunk = int(plan.chunk.size());
         aa.max_blocks = int(book_->geometry().max_blocks);
         aa.err = err_;
         timed(kProfAttention, [&] { launch_attention(aa, stream_); });

@@ -1082,6 +1082,273 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
     }
 }
 
+// Tensor-core attention for a chunk of consecutive query rows of one sequence
+// (chunked prefill: row r of the chunk sees positions [0, v0 + r)), F16 KV,
+// head_dim 64 or 128, blocks of a multiple of 16 slots, 16 % G == 0.
+//
+// CTA = 4 warps on one (chunk, KV head); the chunk's R = 64 / G rows x G
+// query heads are 64 query vectors, 16 per warp, on the M dimension of
+// mma.m16n8k16 (the flash-attention layout: positions on N for S = Q K^T, on
+// K for O += P V).  Every K/V tile is loaded once per CTA by TMA (boxes of 64
+// halves x tpb slots, 128-byte swizzle, a ring of kChunkRing blocks filled by
+// thread 0) and used by all four warps, so a chunk reads its KV once instead
+// of once per row.  Q and P enter as exact hi + lo F16 pairs after
+// power-of-two scaling (per query vector, P by 2^11), as in attn_mma_kernel;
+// the softmax reference of a row moves only when a score exceeds it by more
+// than 4 ln 2.
+constexpr int kChunkRing = 4;
+
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                        AttnArgs a) {
+    constexpr int NB = D / 64;   // 128-byte boxes per slot row
+    constexpr int KS = D / 16;   // k-steps of S = Q K^T
+    constexpr int NT = D / 8;    // n8 tiles of O
+    constexpr int RW = 16 / G;   // rows per warp
+    static_assert(D % 64 == 0 && 16 % G == 0, "chunk attention shape");
+    extern __shared__ unsigned char att_raw[];
+    __shared__ std::uint64_t bars[kChunkRing];
+    const int tpb = a.tpb;
+    const int box = tpb * 128;
+    const int half_stage = NB * box;
+    const int stage = 2 * half_stage;
+    unsigned char* smem = att_raw + ((1024u - (s_u32(att_raw) & 1023u)) & 1023u);
+    const unsigned ring_s = s_u32(smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int lr = lane & 7, lm = lane >> 3;
+
+    const int4 wk = a.chunk_work[blockIdx.x];
+    const int t0 = wk.x, toff = wk.y, v0 = wk.z, nrows = wk.w;
+    const int h = blockIdx.y;
+    const int vlast = v0 + nrows - 1;              // positions the chunk's last row sees
+    const int nblk = (vlast + tpb - 1) / tpb;
+    const bool warp_live = warp * RW < nrows;      // warps without rows only help with the ring
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kChunkRing; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
+    const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
+    auto issue = [&](int i) {
+        int pb = __ldg(a.tables + toff + i);
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;
+        }
+        const int yk = int(pb * block_rows + head_row);
+        const int yv = int(yk + kind_rows);
+        const unsigned st = ring_s + unsigned((i % kChunkRing) * stage);
+        const unsigned bar = s_u32(&bars[i % kChunkRing]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(stage) : "memory");
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            tma_load_2d(st + b * box, &kv_map, b * 64, yk, bar);
+            tma_load_2d(st + half_stage + b * box, &kv_map, b * 64, yv, bar);
+        }
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kChunkRing && i < nblk; ++i) issue(i);
+
+    // This lane's query vectors: m = gq (row half 0) and gq + 8 (row half 1);
+    // vector m is chunk row warp * RW + m / G, query head h * G + m % G.
+    int vis[2];
+    const float* qp[2];
+    bool live[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int m = gq + 8 * hf;
+        const int r = warp * RW + m / G;
+        live[hf] = r < nrows;
+        const int rr = live[hf] ? r : 0;  // rows past the chunk compute row 0 and store nothing
+        vis[hf] = v0 + rr;
+        qp[hf] = a.q + (long long)(t0 + rr) * a.hq * D + (h * G + m % G) * D;
+    }
+    // Q as A fragments (row-major 16 x 16 per k-step): a0 (gq, 2tq), a1 (gq + 8, 2tq),
+    // a2 (gq, 2tq + 8), a3 (gq + 8, 2tq + 8); scaled per vector by 2^sh, hi + lo.
+    unsigned qh[KS][4], ql[KS][4];
+    float qinv[2];
+    {
+        const float scale = rsqrtf(float(D));
+        float v[KS][8];
+        float mx[2] = {0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const float2 x = *reinterpret_cast<const float2*>(qp[hf] + 16 * kk + 8 * c + 2 * tq);
+                    v[kk][4 * c + 2 * hf] = x.x * scale;
+                    v[kk][4 * c + 2 * hf + 1] = x.y * scale;
+                    mx[hf] = fmaxf(mx[hf], fmaxf(fabsf(x.x * scale), fabsf(x.y * scale)));
+                }
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 1));
+            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 2));
+        }
+        float up[2];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            int e2 = 0;
+            if (mx[hf] > 0.f && isfinite(mx[hf])) frexpf(mx[hf], &e2);
+            const int sh = max(-100, min(100, 15 - e2));
+            up[hf] = exp2i(sh);
+            qinv[hf] = exp2i(-sh);
+        }
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            // v[kk]: [c][hf][2] -> fragments a0 (c0 hf0), a1 (c0 hf1), a2 (c1 hf0), a3 (c1 hf1)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+                    split_f16x2(v[kk][4 * c + 2 * hf] * up[hf], v[kk][4 * c + 2 * hf + 1] * up[hf],
+                                qh[kk][2 * c + hf], ql[kk][2 * c + hf]);
+        }
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const unsigned parity = (i / kChunkRing) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[i % kChunkRing], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const unsigned kst = ring_s + unsigned((i % kChunkRing) * stage);
+        const unsigned vst = kst + half_stage;
+        const int base = i * tpb;
+        const int s_hi = min(tpb, vlast - base);
+        if (s_hi % 16) {
+            // V rows past the last row's visible end may hold anything (NaN
+            // included): P is zero there, but 0 * NaN is NaN
+            unsigned char* vrows = smem + std::size_t(i % kChunkRing) * stage + half_stage;
+            const int rows = ((s_hi + 15) & ~15) - s_hi;
+            for (int idx = threadIdx.x; idx < rows * NB * 8; idx += blockDim.x) {
+                const int r = s_hi + idx / (NB * 8), c = idx % (NB * 8);
+                *reinterpret_cast<uint4*>(vrows + (c >> 3) * box + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+            __syncthreads();
+        }
+        for (int sub = 0; warp_live && sub < s_hi; sub += 16) {
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                // K rows sub + 8 (lm >> 1) + lr, d chunk 2kk + (lm & 1): matrices
+                // (pos 0-7, d 0-7), (pos 0-7, d 8-15), (pos 8-15, d 0-7), (pos 8-15, d 8-15)
+                const int pos = sub + 8 * (lm >> 1) + lr;
+                const int c = 2 * kk + (lm & 1);
+                unsigned f[4];
+                ldsm_x4(kst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
+                mma16816(s[0], qh[kk], f[0], f[1]);
+                mma16816(s[0], ql[kk], f[0], f[1]);
+                mma16816(s[1], qh[kk], f[2], f[3]);
+                mma16816(s[1], ql[kk], f[2], f[3]);
+            }
+            // scale back, mask: position p counts for vector (row) hf when p < vis[hf]
+            bool over = false;
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int hf = e >> 1;
+                    const int p = base + sub + 8 * n + 2 * tq + (e & 1);
+                    s[n][e] = p < vis[hf] ? s[n][e] * qinv[hf] : -INFINITY;
+                    over |= s[n][e] > mrow[hf] + kLazyMargin;
+                }
+            if (__any_sync(0xffffffffu, over)) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    float x = fmaxf(fmaxf(s[0][2 * hf], s[0][2 * hf + 1]), fmaxf(s[1][2 * hf], s[1][2 * hf + 1]));
+                    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+                    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+                    const float nm = fmaxf(mrow[hf], x);
+                    const float al = mrow[hf] == -INFINITY ? 0.f : __expf(mrow[hf] - nm);
+                    mrow[hf] = nm;
+                    lrow[hf] *= al;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        o[nt][2 * hf] *= al;
+                        o[nt][2 * hf + 1] *= al;
+                    }
+                }
+            }
+            float p[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    p[n][e] = __expf(s[n][e] - mrow[e >> 1]);
+                    lrow[e >> 1] += p[n][e];
+                }
+            // P (x 2^11 < 2^15) as A fragments: a0 (gq, pos 2tq) = p[0][0..1],
+            // a1 (gq + 8) = p[0][2..3], a2 (gq, pos 2tq + 8) = p[1][0..1], a3 = p[1][2..3]
+            unsigned ph[4], pl[4];
+            split_f16x2(p[0][0] * 2048.f, p[0][1] * 2048.f, ph[0], pl[0]);
+            split_f16x2(p[0][2] * 2048.f, p[0][3] * 2048.f, ph[1], pl[1]);
+            split_f16x2(p[1][0] * 2048.f, p[1][1] * 2048.f, ph[2], pl[2]);
+            split_f16x2(p[1][2] * 2048.f, p[1][3] * 2048.f, ph[3], pl[3]);
+#pragma unroll
+            for (int dt = 0; dt < NT / 2; ++dt) {
+                // V^T fragments by transposed loads: matrices (pos 0-7, d 16dt..+7),
+                // (pos 8-15, same d), (pos 0-7, d 16dt+8..), (pos 8-15, d 16dt+8..)
+                const int pos = sub + 8 * (lm & 1) + lr;
+                const int c = 2 * dt + (lm >> 1);
+                unsigned f[4];
+                ldsm_x4_t(vst + (c >> 3) * box + pos * 128 + (((c & 7) ^ lr) << 4), f);
+                mma16816(o[2 * dt], ph, f[0], f[1]);
+                mma16816(o[2 * dt], pl, f[0], f[1]);
+                mma16816(o[2 * dt + 1], ph, f[2], f[3]);
+                mma16816(o[2 * dt + 1], pl, f[2], f[3]);
+            }
+        }
+        __syncthreads();  // every warp is done with this stage
+        if (threadIdx.x == 0 && i + kChunkRing < nblk) issue(i + kChunkRing);
+    }
+    if (failed) {
+        // wait (bounded) for this CTA's copies still in flight before exiting
+        if (threadIdx.x == 0)
+            for (int i = 0; i < kChunkRing && i < nblk; ++i)
+                for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[i], 0) && !bar_try(&bars[i], 1); ++spin) {
+                }
+        return;
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        lrow[hf] += __shfl_xor_sync(0xffffffffu, lrow[hf], 1);
+        lrow[hf] += __shfl_xor_sync(0xffffffffu, lrow[hf], 2);
+    }
+    if (!warp_live) return;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        if (!live[hf]) continue;
+        const int m = gq + 8 * hf;
+        const int r = warp * RW + m / G;
+        const float inv = 1.f / (lrow[hf] * 2048.f);
+        float* op = a.out + (long long)(t0 + r) * a.hq * D + (h * G + m % G) * D;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float2*>(op + 8 * nt + 2 * tq) = make_float2(o[nt][2 * hf] * inv, o[nt][2 * hf + 1] * inv);
+    }
+}
+
 // Tensor-core paged attention for int8 KV (head_dim 64 or 128, blocks of a
 // multiple of 16 slots).  CTA and ring as attn_mma_kernel (three stages
 // per warp, four CTAs per SM: a stage is half the bytes); one TMA box per K or V run of a block (rows of
@@ -1579,6 +1846,27 @@ bool mma_i8_ok(const AttnArgs& a) {
     return (long long)a.max_blocks * (a.block_stride / D) < (1ll << 31);
 }
 
+constexpr long long chunk_smem_bytes(int D, int tpb) { return 1024 + (long long)kChunkRing * 2 * (D / 64) * tpb * 128; }
+
+template <int D, int G>
+void run_chunk(const AttnArgs& a, cudaStream_t s) {
+    const int smem = int(chunk_smem_bytes(D, a.tpb));
+    TVARA_CUDA(cudaFuncSetAttribute(attn_chunk_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const CUtensorMap map = kv_map_f16(a, D);
+    attn_chunk_kernel<D, G><<<dim3(a.n_chunk, a.hkv), kAttnWarps * 32, smem, s>>>(map, a);
+}
+
+template <int D>
+void run_chunk_g(const AttnArgs& a, cudaStream_t s) {
+    switch (a.hq / a.hkv) {
+        case 1: run_chunk<D, 1>(a, s); break;
+        case 2: run_chunk<D, 2>(a, s); break;
+        case 4: run_chunk<D, 4>(a, s); break;
+        case 8: run_chunk<D, 8>(a, s); break;
+        default: throw std::invalid_argument("chunk attention needs 16 % (query / KV heads) == 0");
+    }
+}
+
 template <int D, int G>
 void run_mma_i8(const AttnArgs& a, dim3 grid, cudaStream_t s) {
     const int smem = int(mma_i8_smem_bytes(D, a.tpb));
@@ -1660,7 +1948,20 @@ void run_d(const AttnArgs& a, cudaStream_t s) {
 
 }  // namespace
 
+int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb) {
+    if (!kv_f16 || (dim != 64 && dim != 128) || group < 1 || 16 % group || tpb % 16 || tpb > 256) return 0;
+    if (chunk_smem_bytes(dim, tpb) > 200 * 1024) return 0;
+    return 64 / group;
+}
+
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
+    if (a.n_chunk > 0) {
+        if (!attention_chunk_rows(a.kv_f16, a.dim, a.hq / a.hkv, a.tpb) || !mma_ok(a))
+            throw std::invalid_argument("chunk attention does not apply to this pool");
+        if (a.dim == 64) run_chunk_g<64>(a, s);
+        else run_chunk_g<128>(a, s);
+        TVARA_LAUNCHED();
+    }
     if (a.n_work <= 0) return;
     if (a.kv_i8) {
         if (!a.kv_scales) throw std::invalid_argument("int8 KV needs its scales");

@@ -129,8 +129,17 @@ struct AttnArgs {
     int n_combine = 0;
     int max_blocks = 0;
     int* err = nullptr;
+    // chunks of consecutive query rows of one sequence, run by the chunk
+    // kernel: {first row, table offset, visible positions of the first row
+    // (row r sees one more per r), rows}
+    const int4* chunk_work = nullptr;
+    int n_chunk = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+// Rows per chunk the chunk kernel takes for this shape (F16 pool, head_dim 64
+// or 128, 16 % group == 0, blocks of a multiple of 16 slots), 0 when it does
+// not apply.
+int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb);
 
 // ---- output ---------------------------------------------------------------
 // argmax of each row (first index of the maximum; NaN counts as maximal);

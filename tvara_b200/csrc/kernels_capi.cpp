@@ -53,7 +53,8 @@ tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, 
 
 struct AttnLayout {
     tvara::AttnPlan plan;
-    std::size_t off_tables = 0, off_work = 0, off_part = 0, off_comb = 0, off_partial = 0, off_err = 0, total = 0;
+    std::size_t off_tables = 0, off_work = 0, off_chunk = 0, off_part = 0, off_comb = 0, off_partial = 0, off_err = 0,
+                total = 0;
 };
 
 constexpr std::size_t kPartsCap = 16384;
@@ -86,12 +87,17 @@ AttnLayout layout_for(const tvara_attention_args* a) {
         vis[i] = int(a->visible[i]);
         off[i] = int(a->table_offset[i]);
     }
-    L.plan = tvara::plan_attention(vis, off, int(a->block_tokens), int(a->kv_heads), kPartsCap);
+    L.plan = tvara::plan_attention(
+        vis, off, int(a->block_tokens), int(a->kv_heads), kPartsCap, 148,
+        tvara::attention_chunk_rows(a->kv_dtype == TVARA_KV_F16, int(a->head_dim), int(a->heads / a->kv_heads),
+                                    int(a->block_tokens)));
     std::size_t at = 0;
     L.off_tables = at;
     at = align256(at + a->tables_len * 4);
     L.off_work = at;
     at = align256(at + L.plan.work.size() * 16);
+    L.off_chunk = at;
+    at = align256(at + L.plan.chunk.size() * 16);
     L.off_part = at;
     at = align256(at + L.plan.part.size() * 4);
     L.off_comb = at;
@@ -266,6 +272,7 @@ int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t
         std::vector<std::uint8_t> host(L.off_partial);
         std::memcpy(host.data() + L.off_tables, a->tables, a->tables_len * 4);
         std::memcpy(host.data() + L.off_work, L.plan.work.data(), L.plan.work.size() * 16);
+        std::memcpy(host.data() + L.off_chunk, L.plan.chunk.data(), L.plan.chunk.size() * 16);
         std::memcpy(host.data() + L.off_part, L.plan.part.data(), L.plan.part.size() * 4);
         std::memcpy(host.data() + L.off_comb, L.plan.comb.data(), L.plan.comb.size() * 16);
         TVARA_CUDA(cudaMemcpyAsync(base, host.data(), host.size(), cudaMemcpyHostToDevice, s));
@@ -292,6 +299,8 @@ int tvara_paged_attention(const tvara_attention_args* a, void* workspace, size_t
         g.combine = reinterpret_cast<const int4*>(base + L.off_comb);
         g.n_combine = int(L.plan.comb.size());
         g.max_blocks = int(a->max_blocks);
+        g.chunk_work = reinterpret_cast<const int4*>(base + L.off_chunk);
+        g.n_chunk = int(L.plan.chunk.size());
         g.err = reinterpret_cast<int*>(base + L.off_err);
         tvara::launch_attention(g, s);
         // the kernels' error word: 2 a block id outside the pool, 4 a bounded
