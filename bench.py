@@ -446,8 +446,14 @@ def parity_check(args, rank, world, local, barrier):
         model.close()
     res = None
     if rank == 0:
-        want = parity.oracle_rows(path, case, max_positions=prefix + suffix[1] + 16)
+        f16 = (lambda x: x.astype(np.float16).astype(np.float32)) if args.kv == "f16" else None
+        want = parity.oracle_rows(path, case, max_positions=prefix + suffix[1] + 16, kv_round=f16)
         res = parity.compare(got, want)
+        if f16 is not None:  # distance of the F16-stored rows from the reference's F32 KV
+            ref = parity.oracle_rows(path, case, max_positions=prefix + suffix[1] + 16)
+            res["vs_f32_reference"] = {"max_abs": float(np.abs(got - ref).max()),
+                                       "note": "the oracle above stores the step's new K/V rows in F16 as the pool "
+                                               "does; this is the same rows against the reference's F32 KV"}
         res.update({"case": f"llama8b widths, 2 layers, tp{world}, {args.kv} KV, {requests} sequences sharing a "
                             f"{prefix}-position radix prefix + U({suffix[0]},{suffix[1]}) own positions, "
                             f"{len(want)} rows in one step",

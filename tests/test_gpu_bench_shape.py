@@ -7,7 +7,14 @@ of them -- that share a 1000-position prefix through the radix cache
 own, so contexts reach ~2k and the projections run at ~300 rows with the
 tile / split-K planner at 8B widths.  Every row's logits are checked against
 the CPU oracle (oracle/parity.py): |d| <= 2e-3 + 1e-3 |want|, argmax equal
-except on near-ties.  F16 KV (the benchmark's) and F32 KV (the reference's)."""
+except on near-ties.
+
+F32 KV (the reference's format) is checked against the reference's
+arithmetic directly.  An F16 pool stores each new K/V row rounded to F16; at
+these widths that storage alone moves logits by up to ~1e-2 from the F32
+reference (the CPU oracle shows the same when it rounds the new rows), so the
+F16 case is checked against the oracle with that rounding applied and the
+distance to the F32 reference is bounded separately."""
 
 import numpy as np
 import pytest
@@ -42,6 +49,10 @@ def test_llama8b_widths_ragged_step_matches_oracle(llama8b_2l, kv):
         m._drop_sequence(case["src"])
         m.kv_audit()
     assert got.shape == (sum(len(t) for t in case["tokens"]), 128256)
-    want = parity.oracle_rows(llama8b_2l, case, max_positions=PREFIX + SUFFIX[1] + 16)
+    f16 = (lambda a: a.astype(np.float16).astype(np.float32)) if kv == "f16" else None
+    want = parity.oracle_rows(llama8b_2l, case, max_positions=PREFIX + SUFFIX[1] + 16, kv_round=f16)
     res = parity.compare(got, want)
     assert res["ok"], res
+    if kv == "f16":
+        ref = parity.oracle_rows(llama8b_2l, case, max_positions=PREFIX + SUFFIX[1] + 16)
+        assert np.abs(got - ref).max() <= 3e-2

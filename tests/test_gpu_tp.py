@@ -27,7 +27,12 @@ def _rank(rank, world, nccl_id, path, prompts, out):
         chunk, _ = m.batch_step(seqs, [p[:-1] for p in prompts], all_logits=True)
         # then the last tokens one sequence at a time, through the reference ABI call
         last = np.stack([m.logits(s, p[-1]) for s, p in zip(seqs, prompts)])
-        np.savez(out % rank, chunk=chunk, last=last)
+        # a decode step with the vocabulary-split head's gathered argmax and
+        # the device sampler over the reassembled rows
+        step, am = m.batch_step(seqs, [[5], [77], [300]], logits=True, argmax=True, finite_argmax=True)
+        smp = m.batch_sample(seqs, [[6], [7], [8]], repetition=1.2, top_k=5, logits=True)
+        np.savez(out % rank, chunk=chunk, last=last, step=step, am=am, s_logits=smp["logits"], s_am=smp["argmax"],
+                 s_ids=smp["top_ids"])
 
 
 def _nccl_unique_id():
@@ -67,3 +72,14 @@ def test_tp2_matches_oracle(tiny_path, tmp_path):
     want_last = np.stack([r[-1] for r in refs])
     assert np.abs(r0["chunk"] - want_chunk).max() <= ATOL
     assert np.abs(r0["last"] - want_last).max() <= ATOL
+    for k in ("step", "am", "s_logits", "s_am", "s_ids"):
+        assert np.array_equal(r0[k], r1[k]), k
+    assert np.array_equal(r0["am"], np.argmax(r0["step"], axis=1))
+    refs = [oracle.forward(p + [t]) for p, t in zip(prompts, [5, 77, 300])]
+    assert np.abs(r0["step"] - np.stack([r[-1] for r in refs])).max() <= ATOL
+    from oracle import sampler
+    hist = [p + [t, u] for p, t, u in zip(prompts, [5, 77, 300], [6, 7, 8])]
+    for i in range(3):
+        adj = sampler.adjust(r0["s_logits"][i], hist[i], 1.2)
+        ids, _ = sampler.top_candidates(adj, 5)
+        assert r0["s_am"][i] == int(np.argmax(adj)) and r0["s_ids"][i].tolist() == ids.tolist()

@@ -1,5 +1,6 @@
 // NCCL over NVLink/NVSwitch for the tensor-parallel allreduce after o_proj and
-// down_proj.  Only the stable NCCL C entry points are used.
+// down_proj and the gathers of the vocabulary-split LM head.  Only the stable
+// NCCL C entry points are used.
 #include "collective.hpp"
 
 #include <dlfcn.h>
@@ -16,9 +17,11 @@ struct UniqueId {
 };
 using InitRank = int (*)(void**, int, UniqueId, int);
 using AllReduce = int (*)(const void*, void*, std::size_t, int, int, void*, cudaStream_t);
+using AllGather = int (*)(const void*, void*, std::size_t, int, void*, cudaStream_t);
 using Destroy = int (*)(void*);
 using ErrorString = const char* (*)(int);
 constexpr int kNcclFloat32 = 7;
+constexpr int kNcclUint8 = 1;
 constexpr int kNcclSum = 0;
 
 void* open_nccl() {
@@ -58,6 +61,10 @@ Collective::~Collective() {
 void Collective::allreduce_sum(float* data, std::size_t n, cudaStream_t stream) {
     check(lib_, sym<AllReduce>(lib_, "ncclAllReduce")(data, data, n, kNcclFloat32, kNcclSum, comm_, stream),
           "ncclAllReduce");
+}
+
+void Collective::allgather(const void* send, void* recv, std::size_t bytes, cudaStream_t stream) {
+    check(lib_, sym<AllGather>(lib_, "ncclAllGather")(send, recv, bytes, kNcclUint8, comm_, stream), "ncclAllGather");
 }
 
 }  // namespace tvara

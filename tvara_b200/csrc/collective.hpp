@@ -18,6 +18,8 @@ public:
     Collective& operator=(const Collective&) = delete;
     // In-place sum over the group of n floats on `stream`.
     void allreduce_sum(float* data, std::size_t n, cudaStream_t stream);
+    // recv[r * bytes .. (r + 1) * bytes) = rank r's `bytes` of send, on every rank.
+    void allgather(const void* send, void* recv, std::size_t bytes, cudaStream_t stream);
     int rank() const { return rank_; }
     int size() const { return size_; }
 

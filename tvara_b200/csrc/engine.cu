@@ -86,6 +86,11 @@ Engine::Engine(const std::string& path, std::size_t max_blocks, std::size_t bloc
     hkv_ = shard.kv_heads;
     ffn_ = shard.ffn;
     qkv_w_ = (hq_ + 2 * hkv_) * dim_;
+    // the LM head splits by vocabulary rows under tensor parallelism
+    head_ld_ = (vocab_ + tp - 1) / tp;
+    head_row0_ = opt.tp_rank * head_ld_;
+    head_rows_ = std::min(head_ld_, vocab_ - head_row0_);
+    if (head_rows_ < 1) throw std::invalid_argument("tensor-parallel size exceeds the vocabulary");
     if (dim_ != 16 && dim_ != 32 && dim_ != 64 && dim_ != 128 && dim_ != 256)
         throw std::invalid_argument("unsupported head_dim (16, 32, 64, 128, 256)");
     tmax_ = std::max(1, opt.max_step_tokens);
@@ -138,7 +143,8 @@ void Engine::load(const gguf::File& f) {
     std::vector<std::pair<std::string, const float**>> norms;
     lw_.assign(layers_, {});
     plans.push_back({{{"token_embd.weight", 0, vocab_, 0, D}}, false, &embed_});
-    if (!tied) plans.push_back({{{"output.weight", 0, vocab_, 0, D}}, false, &head_});
+    if (!tied || tp > 1)  // this rank's vocabulary rows of the head (all of them at tp 1)
+        plans.push_back({{{tied ? "token_embd.weight" : "output.weight", head_row0_, head_rows_, 0, D}}, false, &head_});
     norms.push_back({"output_norm.weight", &final_norm_});
     auto type_of = [&](const std::string& n) { return static_cast<int>(f.info(n).type); };
     for (int l = 0; l < layers_; ++l) {
@@ -238,7 +244,7 @@ void Engine::load(const gguf::File& f) {
             launch_finite_check(nm, flag, stream_);
             *n.second = out;
         }
-        if (tied) head_ = embed_;
+        if (tied && tp == 1) head_ = embed_;
         int bad = 0;
         TVARA_CUDA(cudaMemcpyAsync(&bad, flag, sizeof(int), cudaMemcpyDeviceToHost, stream_));
         TVARA_CUDA(cudaStreamSynchronize(stream_));
@@ -336,8 +342,11 @@ void Engine::load(const gguf::File& f) {
     const std::size_t T = tmax_;
     partial_cap_ = 8192;
     const std::size_t ff_w = std::size_t(ffn_) * (gate_up_fused_ ? 1 : 2);
+    const std::size_t split_head = tp > 1 ? T * std::size_t(head_ld_) * tp + T * vocab_ +
+                                                T * argmax_part_bytes() * (tp + 1) / 4 + 64 * 3
+                                          : 0;
     const std::size_t floats = T * D * 2 + T * qkv_w_ + T * hq_ * d * 2 + T * ff_w + T * vocab_ +
-                               partial_cap_ * hq_ * (d + 2) + 64 * 8;
+                               partial_cap_ * hq_ * (d + 2) + 64 * 8 + split_head;
     std::size_t bytes = floats * 4 + T * 4 + 4096;
     TVARA_CUDA(cudaMalloc(&x_, bytes));
     float* c = x_;
@@ -356,6 +365,11 @@ void Engine::load(const gguf::File& f) {
     logits_ = take(T * vocab_);
     partial_ = take(partial_cap_ * hq_ * (d + 2));
     argmax_ = reinterpret_cast<unsigned*>(take(T));
+    if (tp > 1) {
+        gather_ = take(T * std::size_t(head_ld_) * tp);
+        full_ = take(T * vocab_);
+        amparts_ = take(T * argmax_part_bytes() * (tp + 1) / 4);
+    }
     const int max_k = std::max({D, hq_ * d, ffn_});
     tc_ws_bytes_ = gemm_tc_workspace(int(T), max_k);
     TVARA_CUDA(cudaMalloc(&tc_ws_, tc_ws_bytes_));
@@ -785,11 +799,36 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
     if (R > 0) {
         timed(kProfHead, [&] {
             const bool hsplit = norm(final_norm_, d_rows, R, {&head_});
-            projection(head_, xn_, D, R, logits_, vocab_, kStore, hsplit);
-            if (argmax) launch_argmax(logits_, R, vocab_, argmax_, finite_argmax_, stream_);
+            const float* rows_full = logits_;  // [R][vocab] where the sampler reads
+            if (!coll_) {
+                projection(head_, xn_, D, R, logits_, vocab_, kStore, hsplit);
+                if (argmax) launch_argmax(logits_, R, vocab_, argmax_, finite_argmax_, stream_);
+            } else {
+                // this rank's vocabulary slice; only argmax records (and, when
+                // asked for, the logits) cross NVLink
+                const int tp = coll_->size();
+                projection(head_, xn_, D, R, logits_, head_ld_, kStore, hsplit);
+                if (argmax) {
+                    auto* mine = static_cast<unsigned char*>(amparts_);
+                    auto* all = mine + std::size_t(R) * argmax_part_bytes();
+                    launch_argmax_part(logits_, R, head_ld_, head_rows_, head_row0_, mine, stream_);
+                    coll_->allgather(mine, all, std::size_t(R) * argmax_part_bytes(), stream_);
+                    launch_argmax_merge(all, R, tp, argmax_, finite_argmax_, stream_);
+                }
+                if (logits || sp) coll_->allgather(logits_, gather_, std::size_t(R) * head_ld_ * 4, stream_);
+                if (sp) {
+                    for (int k = 0; k < tp; ++k) {
+                        const int cols = std::min(head_ld_, vocab_ - k * head_ld_);
+                        TVARA_CUDA(cudaMemcpy2DAsync(full_ + std::size_t(k) * head_ld_, std::size_t(vocab_) * 4,
+                                                     gather_ + std::size_t(k) * R * head_ld_, std::size_t(head_ld_) * 4,
+                                                     std::size_t(cols) * 4, R, cudaMemcpyDeviceToDevice, stream_));
+                    }
+                    rows_full = full_;
+                }
+            }
             if (sp) {
                 SampleJob job;
-                job.logits = logits_;
+                job.logits = rows_full;
                 job.ld = vocab_;
                 job.rows = R;
                 job.vocab = vocab_;
@@ -846,8 +885,18 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         while (k < R) {
             int e = k + 1;
             while (e < R && s.out_dest[e] == s.out_dest[e - 1] + 1) ++e;
-            TVARA_CUDA(cudaMemcpyAsync(logits + s.out_dest[k] * vocab_, logits_ + (long long)k * vocab_,
-                                       std::size_t(e - k) * vocab_ * 4, cudaMemcpyDeviceToHost, stream_));
+            if (!coll_) {
+                TVARA_CUDA(cudaMemcpyAsync(logits + s.out_dest[k] * vocab_, logits_ + (long long)k * vocab_,
+                                           std::size_t(e - k) * vocab_ * 4, cudaMemcpyDeviceToHost, stream_));
+            } else {
+                for (int r = 0; r < coll_->size(); ++r) {  // rank r's columns of rows k..e
+                    const int cols = std::min(head_ld_, vocab_ - r * head_ld_);
+                    TVARA_CUDA(cudaMemcpy2DAsync(logits + s.out_dest[k] * vocab_ + std::size_t(r) * head_ld_,
+                                                 std::size_t(vocab_) * 4,
+                                                 gather_ + (std::size_t(r) * R + k) * head_ld_, std::size_t(head_ld_) * 4,
+                                                 std::size_t(cols) * 4, e - k, cudaMemcpyDeviceToHost, stream_));
+                }
+            }
             k = e;
         }
     }

@@ -155,6 +155,10 @@ private:
 
     // local (per tensor-parallel rank) shapes
     int hq_ = 0, hkv_ = 0, dim_ = 0, ffn_ = 0, hidden_ = 0, vocab_ = 0, layers_ = 0, qkv_w_ = 0;
+    // LM head rows of this rank: [head_row0_, head_row0_ + head_rows_) of the
+    // vocabulary (all of it without tensor parallelism); head_ld_ = the
+    // per-rank slice width every rank's logits buffer is laid out with
+    int head_row0_ = 0, head_rows_ = 0, head_ld_ = 0;
     bool gate_up_fused_ = true;
 
     // device memory
@@ -179,6 +183,10 @@ private:
     int tmax_ = 0;
     float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *ff_ = nullptr,
           *ffu_ = nullptr, *logits_ = nullptr, *partial_ = nullptr, *xo_ = nullptr;
+    // tensor parallelism: every rank's logits slices ([rank][row][head_ld_]),
+    // the rows reassembled ([row][vocab], for the sampler), argmax records
+    float *gather_ = nullptr, *full_ = nullptr;
+    void* amparts_ = nullptr;
     unsigned* argmax_ = nullptr;
     bool finite_argmax_ = false;
     const SampleSpec* sample_ = nullptr;  // during a sampling step

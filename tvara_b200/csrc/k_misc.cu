@@ -237,6 +237,74 @@ __global__ void argmax_kernel(const float* logits, int vocab, unsigned* out, int
     }
 }
 
+// Argmax over a vocabulary split across ranks: each rank reduces its slice
+// of columns [col0, col0 + cols) of every row to one record (the slice's
+// best value and global index with numpy.argmax's rules -- the first NaN
+// ranks above every number -- and whether it saw a non-finite value); the
+// records of all ranks (gathered [rank][row]) merge to the row's answer.
+struct ArgmaxPart {
+    float best;
+    int idx;   // global column; INT_MAX when the slice is empty
+    int nan;   // idx is the slice's first NaN
+    int bad;   // a NaN or an infinity in the slice
+};
+
+__device__ __forceinline__ void argmax_take(float& best, int& idx, bool& nan, float ob, int oi, bool on) {
+    if (on && (!nan || oi < idx)) {
+        nan = true;
+        idx = oi;
+    } else if (!on && !nan && (ob > best || (ob == best && oi < idx))) {
+        best = ob;
+        idx = oi;
+    }
+}
+
+__global__ void argmax_part_kernel(const float* logits, int ld, int cols, int col0, ArgmaxPart* out) {
+    const float* row = logits + (long long)blockIdx.x * ld;
+    float best = -INFINITY;
+    int idx = INT_MAX;
+    bool nan = false, bad = false;
+    for (int k = threadIdx.x; k < cols; k += blockDim.x) {
+        const float v = row[k];
+        bad |= !isfinite(v);
+        argmax_take(best, idx, nan, v, col0 + k, isnan(v));
+    }
+    __shared__ float sb[32];
+    __shared__ int si[32], sn[32];
+    const int any_bad = __syncthreads_or(bad);
+    for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        const int on = __shfl_xor_sync(0xffffffffu, int(nan), o);
+        argmax_take(best, idx, nan, ob, oi, on);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        sb[w] = best;
+        si[w] = idx;
+        sn[w] = nan;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int j = 1; j < int(blockDim.x >> 5); ++j) argmax_take(best, idx, nan, sb[j], si[j], sn[j]);
+        out[blockIdx.x] = ArgmaxPart{best, idx, int(nan), any_bad};
+    }
+}
+
+__global__ void argmax_merge_kernel(const ArgmaxPart* parts, int rows, int ranks, unsigned* out, int finite_check) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    float best = -INFINITY;
+    int idx = INT_MAX;
+    bool nan = false, bad = false;
+    for (int k = 0; k < ranks; ++k) {
+        const ArgmaxPart p = parts[(long long)k * rows + r];
+        bad |= p.bad != 0;
+        if (p.idx != INT_MAX) argmax_take(best, idx, nan, p.best, p.idx, p.nan != 0);
+    }
+    out[r] = finite_check && bad ? 0xFFFFFFFFu : unsigned(idx == INT_MAX ? 0 : idx);
+}
+
 __global__ void swiglu_kernel(float* g, const float* u, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float x = g[i];
@@ -320,6 +388,21 @@ void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
 void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, bool finite_check, cudaStream_t s) {
     if (rows <= 0) return;
     argmax_kernel<<<rows, 512, 0, s>>>(logits, vocab, out, int(finite_check));
+    TVARA_LAUNCHED();
+}
+
+std::size_t argmax_part_bytes() { return sizeof(ArgmaxPart); }
+
+void launch_argmax_part(const float* logits, int rows, int ld, int cols, int col0, void* parts, cudaStream_t s) {
+    if (rows <= 0) return;
+    argmax_part_kernel<<<rows, 512, 0, s>>>(logits, ld, cols, col0, static_cast<ArgmaxPart*>(parts));
+    TVARA_LAUNCHED();
+}
+
+void launch_argmax_merge(const void* parts, int rows, int ranks, unsigned* out, bool finite_check, cudaStream_t s) {
+    if (rows <= 0) return;
+    argmax_merge_kernel<<<(rows + 127) / 128, 128, 0, s>>>(static_cast<const ArgmaxPart*>(parts), rows, ranks, out,
+                                                           int(finite_check));
     TVARA_LAUNCHED();
 }
 

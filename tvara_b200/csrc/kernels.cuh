@@ -145,6 +145,12 @@ int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb);
 // argmax of each row (first index of the maximum; NaN counts as maximal);
 // with finite_check, rows holding a NaN or infinity report 0xFFFFFFFF.
 void launch_argmax(const float* logits, int rows, int vocab, unsigned* out, bool finite_check, cudaStream_t s);
+// The same over a vocabulary split across ranks: each rank reduces columns
+// [col0, col0 + cols) of its rows (row stride ld) to argmax_part_bytes()
+// per row; the gathered parts [rank][row] merge into out.
+std::size_t argmax_part_bytes();
+void launch_argmax_part(const float* logits, int rows, int ld, int cols, int col0, void* parts, cudaStream_t s);
+void launch_argmax_merge(const void* parts, int rows, int ranks, unsigned* out, bool finite_check, cudaStream_t s);
 // Copies whole KV blocks (copy-on-write): pairs of (from, to) block ids.
 void launch_block_copy(void* kv, long long block_bytes, const int2* pairs, int n, cudaStream_t s);
 // The same pairs over the token id plane ([block][per_block] ints).
