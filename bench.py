@@ -81,8 +81,9 @@ def parse():
     ap.add_argument("--no-standalone", action="store_true", help="skip the standalone GEMV / matmul figures")
     ap.add_argument("--no-extras", action="store_true",
                     help="only the timed decode step: no parity check, standalone kernels or other configs")
-    ap.add_argument("--planes", choices=["auto", "hilo", "off"], default="auto",
-                    help="tensor-core weight form: auto (Q4_K plane of sc*q, other types hi/lo), hilo, off")
+    ap.add_argument("--planes", choices=["auto", "hilo", "off", "q4kplane"], default="auto",
+                    help="tensor-core weight form: auto (Q4_K read packed with side arrays, other types hi/lo), "
+                         "hilo, off, q4kplane (Q4_K as a prebuilt FP16 plane of sc*q)")
     ap.add_argument("--standalone-only", action="store_true",
                     help="only the standalone GEMV / matmul figures (one JSON line; used for kernel profiles)")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens the reference CPU engine decodes")
@@ -448,7 +449,7 @@ def parity_check(args, rank, world, local, barrier):
     if rank == 0:
         f16 = (lambda x: x.astype(np.float16).astype(np.float32)) if args.kv == "f16" else None
         want = parity.oracle_rows(path, case, max_positions=prefix + suffix[1] + 16, kv_round=f16)
-        res = parity.compare(got, want)
+        res = parity.compare(got, want) if f16 is None else parity.compare(got, want, parity.F16_ATOL, parity.F16_RTOL)
         if f16 is not None:  # distance of the F16-stored rows from the reference's F32 KV
             ref = parity.oracle_rows(path, case, max_positions=prefix + suffix[1] + 16)
             res["vs_f32_reference"] = {"max_abs": float(np.abs(got - ref).max()),
@@ -842,8 +843,11 @@ def run_ours(args):
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,
                    "weights_gb": {"packed": round(wbytes["packed"] / 1e9, 2),
                                   "tensor_core_forms": round(wbytes["planes"] / 1e9, 2)},
-                   "tensor_core_weight_form": {"auto": "Q4_K: FP16 plane of sc*q + block scales + minima "
-                                                       "(2 MMAs per K-step); other types: exact hi/lo FP16 planes",
+                   "tensor_core_weight_form": {"auto": "Q4_K: packed rows, sc*q built in shared memory, block "
+                                                       "scales + minima in side arrays (2 MMAs per K-step); other "
+                                                       "types: exact hi/lo FP16 planes",
+                                               "q4kplane": "Q4_K: prebuilt FP16 plane of sc*q (2 MMAs per K-step); "
+                                                           "other types: exact hi/lo FP16 planes",
                                                "hilo": "exact hi/lo FP16 planes (3 MMAs per K-step)",
                                                "off": "packed rows dequantised by producer warps"}[args.planes],
                    "l2": "inputs larger than L2 (KV ~%.0f GB, weights ~4.5 GB)" % (blocks * 2 * 2 ** 20 / 1e9)},

@@ -81,13 +81,14 @@ typedef struct tvara_open_options {
     uint32_t tp_size;          /* tensor-parallel group size; 0 or 1 = no TP */
     const void* nccl_id;       /* 128-byte ncclUniqueId shared by the group (tp_size > 1) */
     uint32_t weight_planes;    /* tensor-core forms of the projections for batches of >= 5 tokens:
-                                  Q4_K rows (width a multiple of 256, >= 1024) as an FP16 plane of
-                                  sc*q with block scales and minima (2 bytes per weight), other
-                                  types as exact FP16 hi/lo planes of their values (4 bytes per
-                                  weight, like the reference's F32 expansion).  0 = when they fit
-                                  beside the KV pool, 1 = always, 2 = never, 3 = hi/lo planes for
-                                  every type, when they fit.  Callers built against the shorter
-                                  struct get 0. */
+                                  Q4_K rows (width a multiple of 256, >= 1024) read packed, with
+                                  side arrays of sub-block scales, block scales and minima (about
+                                  0.16 bytes per weight), other types as exact FP16 hi/lo planes of
+                                  their values (4 bytes per weight, like the reference's F32
+                                  expansion).  0 = when they fit beside the KV pool, 1 = always,
+                                  2 = never, 3 = hi/lo planes for every type, when they fit, 4 = as
+                                  0 with Q4_K rows as a prebuilt FP16 plane of sc*q (2 bytes per
+                                  weight).  Callers built against the shorter struct get 0. */
 } tvara_open_options;
 
 /* tvara_model_open with options; NULL options equal tvara_model_open.

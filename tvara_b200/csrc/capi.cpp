@@ -91,7 +91,7 @@ tvara_model* open_model(const char* path, size_t blocks, size_t tokens, const tv
             opt.has_nccl_id = true;
         }
         if (o->struct_size >= offsetof(tvara_open_options, weight_planes) + sizeof(uint32_t)) {
-            if (o->weight_planes > 3) throw std::invalid_argument("invalid weight planes option");
+            if (o->weight_planes > 4) throw std::invalid_argument("invalid weight planes option");
             opt.weight_planes = int(o->weight_planes);
         }
     }

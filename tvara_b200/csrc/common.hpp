@@ -51,6 +51,10 @@ struct DeviceMatrix {
     // qscale [rows][cols/256] the block scales d; qmin_hi / qmin_lo
     // [rows][cols/32] FP16 the exact split of dmin*m * 2^qmin_shift[row].
     const std::uint16_t* qplane = nullptr;
+    // Packed form (qplane null): the same factorisation with the codes read
+    // from the packed rows (qs) and sc*q built in shared memory by the
+    // kernel; qsc [rows][cols/32] holds each sub-block's 6-bit scale sc.
+    const std::uint8_t* qsc = nullptr;
     const float* qscale = nullptr;
     const std::uint16_t* qmin_hi = nullptr;
     const std::uint16_t* qmin_lo = nullptr;

@@ -257,11 +257,12 @@ void Engine::load(const gguf::File& f) {
     cudaFree(staging_dev);
     cudaFree(flag);
 
-    // ---- tensor-core forms of the projections: Q4_K rows as an FP16 plane
-    // of sc*q with block scales and the min term (2 bytes per weight, two
-    // MMAs per K-step), other types as exact FP16 hi/lo planes of their
-    // values (4 bytes per weight, the footprint of the reference's own F32
-    // expansion); batches of <= 4 tokens keep streaming the packed rows.
+    // ---- tensor-core forms of the projections: Q4_K rows as sc*q built
+    // from the packed rows inside the kernel, with block scales and the min
+    // term in side arrays (about 0.16 bytes per weight beside the packed
+    // 0.5625; two MMAs per K-step), other types as exact FP16 hi/lo planes of
+    // their values (4 bytes per weight, the footprint of the reference's own
+    // F32 expansion); batches of <= 4 tokens keep streaming the packed rows.
     if (opt_.weight_planes != 2) {
         std::vector<DeviceMatrix*> mats;
         for (auto& L : lw_) {
@@ -271,11 +272,16 @@ void Engine::load(const gguf::File& f) {
             mats.push_back(&L.down);
         }
         mats.push_back(&head_);
+        // Q4_K rows: the two-MMA factorisation, from the packed rows (side
+        // arrays only; default) or from a prebuilt FP16 plane of sc*q (mode 4)
         auto q4k_form = [&](const DeviceMatrix* m) {
             return opt_.weight_planes != 3 && m->type == kQ4_K && m->cols % 256 == 0 && m->cols >= 1024;
         };
+        const bool q4k_plane = opt_.weight_planes == 4;
         auto form_bytes = [&](const DeviceMatrix* m) -> std::size_t {
-            if (q4k_form(m)) return (q4k_planes_bytes(m->rows, m->cols) + 255) & ~std::size_t(255);
+            if (q4k_form(m))
+                return ((q4k_plane ? q4k_planes_bytes(m->rows, m->cols) : q4k_packed_form_bytes(m->rows, m->cols)) +
+                        255) & ~std::size_t(255);
             return m->cols % 32 == 0 ? std::size_t(m->rows) * m->cols * 4 : 0;
         };
         std::size_t need = 0;
@@ -296,7 +302,8 @@ void Engine::load(const gguf::File& f) {
                 const std::size_t bytes = form_bytes(m);
                 if (!bytes) continue;
                 if (q4k_form(m)) {
-                    launch_q4k_planes(*m, at, stream_);
+                    if (q4k_plane) launch_q4k_planes(*m, at, stream_);
+                    else launch_q4k_packed_form(*m, at, stream_);
                 } else {
                     const std::size_t n = std::size_t(m->rows) * m->cols;
                     auto* p = reinterpret_cast<std::uint16_t*>(at);

@@ -1084,10 +1084,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_mma_kernel(const __gr
 
 // Tensor-core attention for a chunk of consecutive query rows of one sequence
 // (chunked prefill: row r of the chunk sees positions [0, v0 + r)), F16 KV,
-// head_dim 64 or 128, blocks of a multiple of 16 slots, 16 % G == 0.
+// head_dim 64 or 128, blocks of a multiple of 16 slots, G = 1..8 query heads
+// per KV head.
 //
-// CTA = 4 warps on one (chunk, KV head); the chunk's R = 64 / G rows x G
-// query heads are 64 query vectors, 16 per warp, on the M dimension of
+// CTA = 4 warps on one (chunk, KV head); each warp holds RW = floor(16 / G)
+// rows x G query heads (16 query vectors when G divides 16; the spare
+// vectors of G = 3, 5, 6, 7 repeat a live one and are not stored) on the M dimension of
 // mma.m16n8k16 (the flash-attention layout: positions on N for S = Q K^T, on
 // K for O += P V).  Every K/V tile is loaded once per CTA by TMA (boxes of 64
 // halves x tpb slots, 128-byte swizzle, a ring of kChunkRing blocks filled by
@@ -1105,7 +1107,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const __
     constexpr int KS = D / 16;   // k-steps of S = Q K^T
     constexpr int NT = D / 8;    // n8 tiles of O
     constexpr int RW = 16 / G;   // rows per warp
-    static_assert(D % 64 == 0 && 16 % G == 0, "chunk attention shape");
+    static_assert(D % 64 == 0 && G >= 1 && G <= 8, "chunk attention shape");
     extern __shared__ unsigned char att_raw[];
     __shared__ std::uint64_t bars[kChunkRing];
     const int tpb = a.tpb;
@@ -1161,11 +1163,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const __
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
         const int m = gq + 8 * hf;
-        const int r = warp * RW + m / G;
-        live[hf] = r < nrows;
-        const int rr = live[hf] ? r : 0;  // rows past the chunk compute row 0 and store nothing
+        const bool vec = m < RW * G;  // a query vector of this warp (else a spare)
+        const int r = warp * RW + (vec ? m / G : 0);
+        live[hf] = vec && r < nrows;
+        const int rr = live[hf] ? r : 0;  // spares and rows past the chunk compute row 0 and store nothing
         vis[hf] = v0 + rr;
-        qp[hf] = a.q + (long long)(t0 + rr) * a.hq * D + (h * G + m % G) * D;
+        qp[hf] = a.q + (long long)(t0 + rr) * a.hq * D + (h * G + (vec ? m % G : 0)) * D;
     }
     // Q as A fragments (row-major 16 x 16 per k-step): a0 (gq, 2tq), a1 (gq + 8, 2tq),
     // a2 (gq, 2tq + 8), a3 (gq + 8, 2tq + 8); scaled per vector by 2^sh, hi + lo.
@@ -1340,7 +1343,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const __
     for (int hf = 0; hf < 2; ++hf) {
         if (!live[hf]) continue;
         const int m = gq + 8 * hf;
-        const int r = warp * RW + m / G;
+        const int r = warp * RW + m / G;  // live: m < RW * G
         const float inv = 1.f / (lrow[hf] * 2048.f);
         float* op = a.out + (long long)(t0 + r) * a.hq * D + (h * G + m % G) * D;
 #pragma unroll
@@ -1861,9 +1864,13 @@ void run_chunk_g(const AttnArgs& a, cudaStream_t s) {
     switch (a.hq / a.hkv) {
         case 1: run_chunk<D, 1>(a, s); break;
         case 2: run_chunk<D, 2>(a, s); break;
+        case 3: run_chunk<D, 3>(a, s); break;
         case 4: run_chunk<D, 4>(a, s); break;
+        case 5: run_chunk<D, 5>(a, s); break;
+        case 6: run_chunk<D, 6>(a, s); break;
+        case 7: run_chunk<D, 7>(a, s); break;
         case 8: run_chunk<D, 8>(a, s); break;
-        default: throw std::invalid_argument("chunk attention needs 16 % (query / KV heads) == 0");
+        default: throw std::invalid_argument("chunk attention needs 1..8 query heads per KV head");
     }
 }
 
@@ -1949,9 +1956,9 @@ void run_d(const AttnArgs& a, cudaStream_t s) {
 }  // namespace
 
 int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb) {
-    if (!kv_f16 || (dim != 64 && dim != 128) || group < 1 || 16 % group || tpb % 16 || tpb > 256) return 0;
+    if (!kv_f16 || (dim != 64 && dim != 128) || group < 1 || group > 8 || tpb % 16 || tpb > 256) return 0;
     if (chunk_smem_bytes(dim, tpb) > 200 * 1024) return 0;
-    return 64 / group;
+    return kAttnWarps * (16 / group);
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {

@@ -972,6 +972,313 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same two-MMA Q4_K product without the FP16 plane in memory: the A
+// operand sc*q is built in shared memory from the packed rows at every
+// K-step.  Per K-step (one 32-element sub-block) the TMA warp loads the 16
+// packed bytes of each of the tile's 128 rows (2 KB) beside the x_hi / x_lo
+// tiles; the eight epilogue warps, which the epilogue keeps busy only about a
+// tenth of the time, turn them into the 64-byte swizzled K-major rows the MMA
+// reads: thread (row r, half h) takes the low (h = 0) or high (h = 1) nibbles
+// of the row's 16 bytes -- elements 16h .. 16h + 15 -- builds 1024 + q as
+// FP16 pairs with one byte permute per pair and gets sc*q = (1024 + q)*sc -
+// 1024*sc from one fused multiply-add per pair, exact because sc*q is an
+// integer below 1024 and the fused result is rounded once.  DRAM then carries
+// the packed 0.5625 bytes per weight plus about 0.16 bytes of side arrays
+// (qsc, qscale, the min-term split) instead of the plane's 2.  Barriers per
+// stage: tma_full (the packed tile landed; producers wait), full (x tiles
+// landed and eight producer warps arrived; the MMA waits), empty (MMAs done).
+// The producers drain block j's accumulator once they have produced kLead
+// K-steps of block j + 1, so the MMAs keep running through the epilogue.
+constexpr int kPackedTile = kBM * 16;  // packed bytes of one K-step of a tile
+constexpr int kLead = 3;               // K-steps produced past a block before draining it
+
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    tc_gemm_q4kp_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                        const __grid_constant__ CUtensorMap map_pk, const __grid_constant__ CUtensorMap map_mhi,
+                        const __grid_constant__ CUtensorMap map_mlo, const __grid_constant__ CUtensorMap map_shi,
+                        const __grid_constant__ CUtensorMap map_slo, Q4kArgs q, TileSpace ts) {
+    const TcArgs& a = q.t;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int b_bytes = a.n_tile * kBK * 2;
+    const int stage_bytes = 2 * kATile + 2 * kBTileMax;
+    unsigned char* stages = base;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(base + kStages * stage_bytes);
+    std::uint64_t* empty = full + kStages;
+    std::uint64_t* tma_full = empty + kStages;
+    std::uint64_t* acc_full = tma_full + kStages;  // [2] block accumulator ready
+    std::uint64_t* acc_empty = acc_full + 2;       // [2] epilogue done with it
+    unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = a.w.cols / 256;  // blocks per row
+    const int units = a.w.cols / 32;     // sub-blocks per row
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1 + kEpilogueWarps);
+            mbar_init(&empty[s], 1);
+            mbar_init(&tma_full[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kEpilogueWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarpP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp == kTmaWarpP) {
+        unsigned tma_issued = 0, tma_phase = 0;
+        int qq = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+            for (int ks = 0; ks < steps; ++ks, ++qq) {
+                int ok = 1;
+                if (lane == 0) {
+                    const int s = qq % kStages;
+                    const unsigned ph = (qq / kStages) & 1;
+                    ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                    if (ok) {
+                        unsigned char* st = stages + s * stage_bytes;
+                        const unsigned bar = smem_u32(&full[s]);
+                        if (ks < a.k_steps) {
+                            const int k0 = (kstep0 + ks) * kBK;
+                            mbar_expect_tx(&full[s], 2 * b_bytes);
+                            tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
+                            mbar_expect_tx(&tma_full[s], kPackedTile);
+                            tma_load_2d(smem_u32(st + kATile), &map_pk, k0 / 2, row0, smem_u32(&tma_full[s]));
+                        } else {
+                            const int c0 = (ks - a.k_steps) * kBK;
+                            mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
+                            tma_load_2d(smem_u32(st), &map_mhi, c0, row0, bar);
+                            tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
+                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
+                            mbar_arrive(&tma_full[s]);
+                        }
+                        tma_issued |= 1u << s;
+                        tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    go = false;
+                    break;
+                }
+            }
+        }
+        if (lane == 0)
+            for (int s = 0; s < kStages; ++s)
+                if (tma_issued >> s & 1u)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full[s], (tma_phase >> s) & 1u); ++i) {
+                    }
+    } else if (warp == kMmaWarpP) {
+        if (lane == 0) {
+            int qq = 0, gb = 0;
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+                const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+                for (int j = 0; j < nb && go; ++j, ++gb) {
+                    const int b = gb & 1;
+                    if (!mbar_wait(&acc_empty[b], ((gb >> 1) & 1) ^ 1, abort_flag, a.err, 15, false)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const unsigned acc = tmem + unsigned(b * 256);
+                    const bool minterm = j == q.blocks;
+                    const int n_steps = minterm ? q.min_steps : 256 / kBK;
+                    for (int ks = 0; ks < n_steps; ++ks, ++qq) {
+                        const int s = qq % kStages;
+                        const unsigned ph = (qq / kStages) & 1;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, 13, false)) {
+                            go = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;");
+                        unsigned char* st = stages + s * stage_bytes;
+                        const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+                        const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                            mma_f16(acc, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
+                            mma_f16(acc, ahi + adv, blo + adv, a.idesc, 1);
+                            if (minterm) mma_f16(acc, alo + adv, bhi + adv, a.idesc, 1);
+                        }
+                        mma_commit(&empty[s]);
+                    }
+                    if (go) mma_commit(&acc_full[b]);
+                }
+            }
+        }
+    } else {
+        // producers and epilogue: thread (r, hf); TMEM lane r = weight row
+        // row0 + r; warps w and w+4 share lanes 32*(w%4).. and take token
+        // columns [0, 128) and [128, 256), and the low / high nibbles
+        const int r = threadIdx.x % kBM;
+        const int hf = threadIdx.x / kBM;
+        int gb = 0, qq = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+            const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+            const long long row = row0 + r;
+            const bool live = row < a.w.rows;
+            const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
+            float acc[128];
+#pragma unroll
+            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
+            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
+            int drained = 0;
+            // drains block `drained` (accumulator b) into acc with its scale
+            auto drain = [&]() -> bool {
+                const int b = gb & 1;
+                const float scale = !live ? 0.f : drained < q.blocks ? qs_row[drained] : min_scale;
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0))
+                    return false;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
+                    unsigned u[32];
+                    const unsigned taddr =
+                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                        : "r"(taddr));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                ++gb;
+                ++drained;
+                return true;
+            };
+            for (int p = 0; p < steps && go; ++p, ++qq) {
+                const int s = qq % kStages;
+                const unsigned ph = (qq / kStages) & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(&tma_full[s], ph, abort_flag, a.err, 16) ? 1 : 0)) {
+                    go = false;
+                    break;
+                }
+                if (p < a.k_steps) {
+                    unsigned char* st = stages + s * stage_bytes;
+                    const uint4 w = *reinterpret_cast<const uint4*>(st + kATile + r * 16);
+                    const unsigned sc = live ? sc_row[p] : 0u;
+                    const __half2 sc2 = __half2half2(__uint2half_rn(sc));
+                    const __half2 off2 = __half2half2(__uint2half_rn(1024u * sc));
+                    const unsigned words[4] = {w.x, w.y, w.z, w.w};
+                    unsigned out[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const unsigned nib = hf ? (words[k] >> 4) & 0x0F0F0F0Fu : words[k] & 0x0F0F0F0Fu;
+                        const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
+                        const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
+                        const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, __hneg2(off2));
+                        const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, __hneg2(off2));
+                        out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
+                        out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                    }
+                    *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf)) = make_uint4(out[0], out[1], out[2], out[3]);
+                    *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + 1)) = make_uint4(out[4], out[5], out[6], out[7]);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+                // block `drained` ends at K-step 8 (drained + 1) (the min term at the tile's last step)
+                while (drained < nb && go) {
+                    const int end = drained < q.blocks ? 8 * (drained + 1) : steps;
+                    if (end + kLead > p + 1 && p + 1 < steps) break;
+                    if (end > p + 1) break;
+                    go = drain();
+                }
+            }
+            while (go && drained < nb) go = drain();
+            if (!go) break;
+            // store, 32 token columns at a time (as tc_gemm_q4k_kernel)
+            for (int c = 0; c < 4; ++c) {
+                const int col0 = hf * 128 + c * 32;
+                if (col0 >= a.n_tile) break;  // warp-uniform
+                float v[32];
+                switch (c) {
+#define TVARA_TAKE(C)                                        \
+    case C:                                                  \
+        _Pragma("unroll") for (int jj = 0; jj < 32; ++jj) v[jj] = acc[C * 32 + jj]; \
+        break;
+                    TVARA_TAKE(0)
+                    TVARA_TAKE(1)
+                    TVARA_TAKE(2)
+                    TVARA_TAKE(3)
+#undef TVARA_TAKE
+                }
+                const int tl = tok0 + col0 + lane;
+                const float inv_l = tl < a.tokens ? pow2(-a.x_shift[tl]) : 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] *= __shfl_sync(0xffffffffu, inv_l, jj);
+                const int ncol = min(32, min(a.n_tile - col0, a.tokens - (tok0 + col0)));
+                if (a.epilogue == kSwiGLU) {
+                    const bool odd = r & 1;
+                    float* dst = a.y + (long long)(tok0 + col0 + odd) * a.ldy + row / 2;
+#pragma unroll
+                    for (int pr = 0; pr < 16; ++pr) {
+                        const float pe = __shfl_xor_sync(0xffffffffu, v[2 * pr], 1);
+                        const float po = __shfl_xor_sync(0xffffffffu, v[2 * pr + 1], 1);
+                        if (live && 2 * pr + odd < ncol) {
+                            const float g = odd ? po : v[2 * pr];
+                            const float u = odd ? v[2 * pr + 1] : pe;
+                            dst[(long long)(2 * pr) * a.ldy] = swiglu_12(g, u);
+                        }
+                    }
+                } else if (live) {
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {
+                        if (jj >= ncol) break;
+                        float* dst = a.y + (long long)(tok0 + col0 + jj) * a.ldy + row;
+                        if (a.atomic || a.epilogue == kAdd) atomicAdd(dst, v[jj]);
+                        else *dst = v[jj];
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == kMmaWarpP) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
 // that puts max|x| in [2^14, 2^15), then the exact split (split.cuh).  One
 // block per token; float4 loads and 8-byte stores (K % 4 == 0, rows 16-byte
@@ -1029,6 +1336,21 @@ CUtensorMap make_map(const __half* base, int K, int T, int n_tile) {
     const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
                                    box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+// Packed Q4_K rows as a 2-D byte tensor: the 16 bytes of one sub-block of
+// each of a tile's 128 rows per box (no swizzle: producers read row r at r*16).
+CUtensorMap make_packed_map(const std::uint8_t* qs, std::size_t row_bytes, int rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+    const cuuint32_t box[2] = {16, cuuint32_t(kBM)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<std::uint8_t*>(qs), dims,
+                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return m;
 }
@@ -1133,7 +1455,8 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
-    if (g.w.qplane)  // whole 256-element blocks per split
+    const bool q4k_form = g.w.qplane || g.w.qsc;
+    if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
     const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
     TcArgs a;
@@ -1153,11 +1476,12 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
     const CUtensorMap mh = make_map(hi, K, T, n_tile), ml = make_map(lo, K, T, n_tile);
     const dim3 grid(token_tiles, row_tiles, splits);
-    if (g.w.qplane) {
+    if (q4k_form) {
         // Q4_K two-MMA kernel: splits whole 256-element blocks; y was zeroed above for split K
         if (steps % (8 * splits)) throw std::logic_error("Q4_K split does not divide the blocks");
         const int units = K / 32;  // sub-block sums written with the split
-        const CUtensorMap mq = make_map(reinterpret_cast<const __half*>(g.w.qplane), K, g.w.rows, kBM);
+        const CUtensorMap mq = g.w.qplane ? make_map(reinterpret_cast<const __half*>(g.w.qplane), K, g.w.rows, kBM)
+                                          : make_packed_map(g.w.qs, g.w.qs_row, g.w.rows);
         const CUtensorMap mmh = make_map(reinterpret_cast<const __half*>(g.w.qmin_hi), units, g.w.rows, kBM);
         const CUtensorMap mml = make_map(reinterpret_cast<const __half*>(g.w.qmin_lo), units, g.w.rows, kBM);
         const CUtensorMap msh = make_map(shi, units, T, n_tile), msl = make_map(slo, units, T, n_tile);
@@ -1167,9 +1491,16 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         qa.min_steps = (units + kBK - 1) / kBK;
         TileSpace ts{token_tiles, row_tiles, splits, token_tiles * row_tiles * splits};
         const int smem = kStages * (2 * kATile + 2 * kBTileMax) + 1024 + 256;
-        TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        tc_gemm_q4k_kernel<<<std::min(ts.n_tiles, sm_count()), kPersistThreads, smem, s>>>(mh, ml, mq, mmh, mml, msh,
-                                                                                              msl, qa, ts);
+        const int grid_n = std::min(ts.n_tiles, sm_count());
+        if (g.w.qplane) {
+            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            tc_gemm_q4k_kernel<<<grid_n, kPersistThreads, smem, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+        } else {
+            if (g.w.qs_row % 16 || reinterpret_cast<std::uintptr_t>(g.w.qs) % 16)
+                throw std::invalid_argument("packed Q4_K rows must be 16-byte aligned");
+            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            tc_gemm_q4kp_kernel<<<grid_n, kPersistThreads, smem, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+        }
         TVARA_LAUNCHED();
         return;
     }

@@ -282,6 +282,30 @@ __global__ void q4k_planes_kernel(DeviceMatrix w, unsigned* qplane, float* qscal
     }
 }
 
+// Side arrays of the packed Q4_K tensor-core form (the codes stay in the
+// packed rows): qsc, the 6-bit scale sc of every 32-element sub-block as a
+// byte; qscale, d per 256-element block; qmin_hi / qmin_lo, the exact split of
+// dmin * m * 2^shift per sub-block.  One thread per (row, sub-block).
+__global__ void q4k_side_kernel(DeviceMatrix w, unsigned char* qsc, float* qscale, unsigned short* min_hi,
+                                unsigned short* min_lo, const signed char* shift) {
+    const int units = w.cols / 32;
+    const long long n = (long long)w.rows * units;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / units;
+        const int u = int(i % units);
+        const unsigned char* blk = w.meta + r * (long long)w.meta_row + (u >> 3) * 16;
+        unsigned sc, m;
+        q4k_scale_min(blk + 4, u & 7, sc, m);
+        qsc[i] = (unsigned char)sc;
+        const float f = __uint_as_float(unsigned(127 + shift[r]) << 23);
+        unsigned hi, lo;
+        split_exact(h2f((unsigned short)(blk[2] | (blk[3] << 8))) * float(m) * f, 0.f, hi, lo);
+        min_hi[i] = (unsigned short)(hi & 0xffffu);
+        min_lo[i] = (unsigned short)(lo & 0xffffu);
+        if ((u & 7) == 0) qscale[r * (w.cols / 256) + (u >> 3)] = h2f((unsigned short)(blk[0] | (blk[1] << 8)));
+    }
+}
+
 __global__ void embed_kernel(DeviceMatrix w, const int* tokens, float* x, int ldx, int* ids, const int* blk,
                              const int* slot, int tpb) {
     const int t = blockIdx.x;
@@ -1308,6 +1332,36 @@ void launch_q4k_planes(DeviceMatrix& w, void* storage, cudaStream_t s) {
     q4k_planes_kernel<<<148 * 8, 256, 0, s>>>(w, reinterpret_cast<unsigned*>(qplane), qscale, min_hi, min_lo, shift);
     TVARA_LAUNCHED();
     w.qplane = qplane;
+    w.qscale = qscale;
+    w.qmin_hi = min_hi;
+    w.qmin_lo = min_lo;
+    w.qmin_shift = shift;
+}
+
+std::size_t q4k_packed_form_bytes(int rows, int cols) {
+    return std::size_t(rows) * (cols / 32) * 5 + std::size_t(rows) * (cols / 256) * 4 + std::size_t(rows) + 5 * 256;
+}
+
+void launch_q4k_packed_form(DeviceMatrix& w, void* storage, cudaStream_t s) {
+    if (w.type != kQ4_K || w.cols % 256) throw std::invalid_argument("the packed Q4_K form needs Q4_K rows");
+    auto* at = static_cast<unsigned char*>(storage);
+    auto take = [&](std::size_t bytes) {
+        unsigned char* p = at;
+        at += (bytes + 255) & ~std::size_t(255);
+        return p;
+    };
+    const std::size_t units = std::size_t(w.rows) * (w.cols / 32);
+    auto* qsc = take(units);
+    auto* min_hi = reinterpret_cast<std::uint16_t*>(take(units * 2));
+    auto* min_lo = reinterpret_cast<std::uint16_t*>(take(units * 2));
+    auto* qscale = reinterpret_cast<float*>(take(std::size_t(w.rows) * (w.cols / 256) * 4));
+    auto* shift = reinterpret_cast<signed char*>(take(std::size_t(w.rows)));
+    q4k_min_shift_kernel<<<(w.rows + 7) / 8, 256, 0, s>>>(w, shift);
+    TVARA_LAUNCHED();
+    q4k_side_kernel<<<148 * 8, 256, 0, s>>>(w, qsc, qscale, min_hi, min_lo, shift);
+    TVARA_LAUNCHED();
+    w.qplane = nullptr;
+    w.qsc = qsc;
     w.qscale = qscale;
     w.qmin_hi = min_hi;
     w.qmin_lo = min_lo;

@@ -59,6 +59,10 @@ void launch_planes(const DeviceMatrix& w, std::uint16_t* hi, std::uint16_t* lo, 
 // q4k_planes_bytes; sets the matrix's pointers.
 std::size_t q4k_planes_bytes(int rows, int cols);
 void launch_q4k_planes(DeviceMatrix& w, void* storage, cudaStream_t s);
+// The packed Q4_K form (DeviceMatrix::qsc ...): side arrays only, about 0.16
+// bytes per weight, the codes staying in the packed rows.
+std::size_t q4k_packed_form_bytes(int rows, int cols);
+void launch_q4k_packed_form(DeviceMatrix& w, void* storage, cudaStream_t s);
 // Minimum token count routed to the tensor-core projection.
 void set_tc_min_tokens(int n);
 
@@ -137,8 +141,8 @@ struct AttnArgs {
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 // Rows per chunk the chunk kernel takes for this shape (F16 pool, head_dim 64
-// or 128, 16 % group == 0, blocks of a multiple of 16 slots), 0 when it does
-// not apply.
+// or 128, 1..8 query heads per KV head, blocks of a multiple of 16 slots), 0
+// when it does not apply.
 int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb);
 
 // ---- output ---------------------------------------------------------------

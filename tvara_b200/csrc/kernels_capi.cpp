@@ -32,6 +32,9 @@ int guarded(F&& body) {
 
 std::size_t align256(std::size_t n) { return (n + 255) & ~std::size_t(255); }
 
+// Q4_K rows the tensor-core path reads packed (with side arrays).
+bool has_q4k_side(int type, std::size_t cols) { return type == tvara::kQ4_K && cols % 256 == 0 && cols >= 1024; }
+
 tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, std::size_t cols) {
     std::size_t e = 0, w = 0;
     if (!tvara::block_shape(type, e, w)) throw std::invalid_argument("unsupported quantized type");
@@ -48,6 +51,19 @@ tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, 
     m.qs = static_cast<const std::uint8_t*>(packed);
     m.meta = m.qs + align256(m.qs_row * rows);
     m.row_shift = reinterpret_cast<const signed char*>(m.meta + align256(m.meta_row * rows));
+    if (has_q4k_side(type, cols)) {  // side arrays of the packed Q4_K tensor-core form, as launch_q4k_packed_form lays them
+        const std::uint8_t* at = reinterpret_cast<const std::uint8_t*>(m.row_shift) + align256(rows);
+        const std::size_t units = rows * (cols / 32);
+        m.qsc = at;
+        at += align256(units);
+        m.qmin_hi = reinterpret_cast<const std::uint16_t*>(at);
+        at += align256(units * 2);
+        m.qmin_lo = reinterpret_cast<const std::uint16_t*>(at);
+        at += align256(units * 2);
+        m.qscale = reinterpret_cast<const float*>(at);
+        at += align256(rows * (cols / 256) * 4);
+        m.qmin_shift = reinterpret_cast<const signed char*>(at);
+    }
     return m;
 }
 
@@ -121,7 +137,7 @@ size_t tvara_packed_bytes(int type, size_t rows, size_t cols) {
     std::size_t e = 0, w = 0;
     if (!tvara::block_shape(type, e, w) || !cols || cols % e) return 0;
     return align256(tvara::qs_row_bytes(type, cols) * rows) + align256(tvara::meta_row_bytes(type, cols) * rows) +
-           align256(rows);
+           align256(rows) + (has_q4k_side(type, cols) ? tvara::q4k_packed_form_bytes(int(rows), int(cols)) : 0);
 }
 
 int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* packed, void* stream) {
@@ -131,6 +147,10 @@ int tvara_pack(int type, const void* gguf_rows, size_t rows, size_t cols, void* 
         tvara::launch_repack(type, gguf_rows, int(rows), int(cols), const_cast<std::uint8_t*>(m.qs),
                              const_cast<std::uint8_t*>(m.meta), s);
         tvara::launch_row_shift(m, const_cast<signed char*>(m.row_shift), s);
+        if (has_q4k_side(type, cols)) {
+            tvara::DeviceMatrix side = m;
+            tvara::launch_q4k_packed_form(side, const_cast<signed char*>(m.row_shift) + align256(rows), s);
+        }
     });
 }
 

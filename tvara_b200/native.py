@@ -121,7 +121,8 @@ class NativeModel:
                              KV_I8: KV_I8}[kv_dtype]
             opts.max_step_tokens = int(max_step_tokens or 0)
             opts.tp_rank, opts.tp_size = int(tp_rank), int(tp_size)
-            opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2, "hilo": 3}[weight_planes]
+            opts.weight_planes = {None: 0, "auto": 0, True: 1, "on": 1, False: 2, "off": 2, "hilo": 3,
+                                  "q4kplane": 4}[weight_planes]
             self._nccl_id = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
             opts.nccl_id = C.cast(self._nccl_id, C.c_void_p) if self._nccl_id is not None else None
             self._handle = lib.tvara_model_open_ex(encoded, max_blocks, block_tokens, C.byref(opts))
