@@ -8,7 +8,10 @@
 #include <set>
 
 #include "attention_plan.hpp"
+#include <cstdlib>
+
 #include "collective.hpp"
+#include "p2p_allreduce.hpp"
 #include "tp_plan.hpp"
 
 namespace tvara {
@@ -120,6 +123,7 @@ Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     for (auto e : events_) cudaEventDestroy(e);
     radix_.reset();
+    peer_.reset();  // closes the peers' buffers before this rank's scratch is freed
     coll_.reset();
     for (void* p : {static_cast<void*>(weights_), static_cast<void*>(planes_), static_cast<void*>(rope_cos_), static_cast<void*>(rope_sin_), kv_, static_cast<void*>(token_ids_), static_cast<void*>(kv_scales_),
                     static_cast<void*>(x_), static_cast<void*>(meta_dev_), static_cast<void*>(err_), tc_ws_, sample_buf_})
@@ -383,6 +387,20 @@ void Engine::load(const gguf::File& f) {
     TVARA_CUDA(cudaMalloc(&err_, sizeof(int)));
     TVARA_CUDA(cudaMemset(err_, 0, sizeof(int)));
     TVARA_CUDA(cudaHostAlloc(&err_host_, sizeof(int), cudaHostAllocDefault));
+    // tensor parallelism: the residual x_ (the start of the scratch, at the
+    // same offset on every rank) is summed over NVLink peer memory; callers
+    // may keep NCCL's allreduce with TVARA_ALLREDUCE=nccl (every rank must
+    // see the same setting)
+    if (coll_) {
+        const char* mode = std::getenv("TVARA_ALLREDUCE");
+        if (!(mode && std::string(mode) == "nccl"))
+            peer_ = std::make_unique<PeerAllreduce>(*coll_, x_, T * std::size_t(D), stream_);
+    }
+}
+
+void Engine::allreduce_residual(std::size_t n) {
+    if (peer_ && peer_->applies(x_, n)) peer_->allreduce_sum(x_, n, err_, stream_);
+    else coll_->allreduce_sum(x_, n, stream_);
 }
 
 void Engine::projection(const DeviceMatrix& w, const float* x, int ldx, int tokens, float* y, int ldy, int epi,
@@ -789,7 +807,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         // Under tensor parallelism rank 0 adds its partial to the residual and
         // the others store theirs, so the sum over ranks is x + sum(partials).
         timed(kProfProjection, [&] { projection(L.o, att_, hq_ * d, T, x_, D, lead ? kAdd : kStore); });
-        if (coll_) timed(kProfCollective, [&] { coll_->allreduce_sum(x_, std::size_t(T) * D, stream_); });
+        if (coll_) timed(kProfCollective, [&] { allreduce_residual(std::size_t(T) * D); });
         timed(kProfOther, [&] { split = norm(L.ffn_norm, nullptr, T, gu_in); });
         timed(kProfProjection, [&] {
             if (L.gateup.size() == 1) {
@@ -801,7 +819,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
             }
         });
         timed(kProfProjection, [&] { projection(L.down, ff_, ffn_, T, x_, D, lead ? kAdd : kStore); });
-        if (coll_) timed(kProfCollective, [&] { coll_->allreduce_sum(x_, std::size_t(T) * D, stream_); });
+        if (coll_) timed(kProfCollective, [&] { allreduce_residual(std::size_t(T) * D); });
     }
     if (R > 0) {
         timed(kProfHead, [&] {
@@ -915,6 +933,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         const int code = *err_host_;
         TVARA_CUDA(cudaMemsetAsync(err_, 0, sizeof(int), stream_));
         if (code == 3) throw std::invalid_argument("Nonfinite KV input");
+        if (code == 5) throw std::runtime_error("tensor-parallel peer did not reach the allreduce (wait timed out)");
         throw std::runtime_error("device bounds check failed (code " + std::to_string(code) + ")");
     }
     if (argmax)

@@ -17,6 +17,7 @@
 #include "gguf.hpp"
 #include "kernels.cuh"
 #include "kvbook.hpp"
+#include "p2p_allreduce.hpp"
 
 namespace tvara {
 
@@ -152,6 +153,8 @@ private:
     std::unique_ptr<SequenceBook> book_;
     std::unique_ptr<PrefixTrie> radix_;
     std::unique_ptr<Collective> coll_;
+    std::unique_ptr<PeerAllreduce> peer_;  // tensor-parallel residual sums over peer memory
+    void allreduce_residual(std::size_t n);
 
     // local (per tensor-parallel rank) shapes
     int hq_ = 0, hkv_ = 0, dim_ = 0, ffn_ = 0, hidden_ = 0, vocab_ = 0, layers_ = 0, qkv_w_ = 0;

@@ -975,25 +975,30 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // ---------------------------------------------------------------------------
 // The same two-MMA Q4_K product without the FP16 plane in memory: the A
 // operand sc*q is built in shared memory from the packed rows at every
-// K-step.  Per K-step (one 32-element sub-block) the TMA warp loads the 16
-// packed bytes of each of the tile's 128 rows (2 KB) beside the x_hi / x_lo
-// tiles; the eight epilogue warps, which the epilogue keeps busy only about a
-// tenth of the time, turn them into the 64-byte swizzled K-major rows the MMA
-// reads: thread (row r, half h) takes the low (h = 0) or high (h = 1) nibbles
-// of the row's 16 bytes -- elements 16h .. 16h + 15 -- builds 1024 + q as
-// FP16 pairs with one byte permute per pair and gets sc*q = (1024 + q)*sc -
-// 1024*sc from one fused multiply-add per pair, exact because sc*q is an
-// integer below 1024 and the fused result is rounded once.  DRAM then carries
-// the packed 0.5625 bytes per weight plus about 0.16 bytes of side arrays
-// (qsc, qscale, the min-term split) instead of the plane's 2.  Barriers per
-// stage: tma_full (the packed tile landed; producers wait), full (x tiles
-// landed and eight producer warps arrived; the MMA waits), empty (MMAs done).
-// The producers drain block j's accumulator once they have produced kLead
-// K-steps of block j + 1, so the MMAs keep running through the epilogue.
+// K-step.  Per K-step (one 32-element sub-block) a packed warp loads the 16
+// packed bytes of each of the tile's 128 rows (2 KB) into a ring of its own,
+// kPkStages deep, running ahead of the main stages; the eight epilogue warps,
+// which the epilogue keeps busy only about a tenth of the time, turn them
+// into the 64-byte swizzled K-major rows the MMA reads as soon as the MMA has
+// released the stage: thread (row r, half h) takes the low (h = 0) or high
+// (h = 1) nibbles of the row's 16 bytes -- elements 16h .. 16h + 15 -- builds
+// 1024 + q as FP16 pairs with one byte permute per pair and gets sc*q =
+// (1024 + q)*sc - 1024*sc from one fused multiply-add per pair, exact because
+// sc*q is an integer below 1024 and the fused result is rounded once.  DRAM
+// then carries the packed 0.5625 bytes per weight plus about 0.16 bytes of
+// side arrays (qsc, qscale, the min-term split) instead of the plane's 2.
+// Barriers: full (x tiles landed and eight producer warps arrived; the MMA
+// waits), empty (MMAs done with the stage; the TMA warp and the producers
+// wait), pk_full / pk_empty for the packed ring.  The producers drain block
+// j's accumulator once they have produced kLead K-steps past it, so the
+// MMAs keep running through the drain.
 constexpr int kPackedTile = kBM * 16;  // packed bytes of one K-step of a tile
+constexpr int kPkStages = 8;
 constexpr int kLead = 3;               // K-steps produced past a block before draining it
+constexpr int kPkWarp = 10;
+constexpr int kQ4kpThreads = 352;      // 8 producer / epilogue warps, MMA, TMA, packed
 
-__global__ void __launch_bounds__(kPersistThreads, 1)
+__global__ void __launch_bounds__(kQ4kpThreads, 1)
     tc_gemm_q4kp_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                         const __grid_constant__ CUtensorMap map_pk, const __grid_constant__ CUtensorMap map_mhi,
                         const __grid_constant__ CUtensorMap map_mlo, const __grid_constant__ CUtensorMap map_shi,
@@ -1004,11 +1009,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     const int b_bytes = a.n_tile * kBK * 2;
     const int stage_bytes = 2 * kATile + 2 * kBTileMax;
     unsigned char* stages = base;
-    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(base + kStages * stage_bytes);
+    unsigned char* pk_ring = base + kStages * stage_bytes;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(pk_ring + kPkStages * kPackedTile);
     std::uint64_t* empty = full + kStages;
-    std::uint64_t* tma_full = empty + kStages;
-    std::uint64_t* acc_full = tma_full + kStages;  // [2] block accumulator ready
-    std::uint64_t* acc_empty = acc_full + 2;       // [2] epilogue done with it
+    std::uint64_t* pk_full = empty + kStages;
+    std::uint64_t* pk_empty = pk_full + kPkStages;
+    std::uint64_t* acc_full = pk_empty + kPkStages;  // [2] block accumulator ready
+    std::uint64_t* acc_empty = acc_full + 2;         // [2] epilogue done with it
     unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1019,7 +1026,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1 + kEpilogueWarps);
             mbar_init(&empty[s], 1);
-            mbar_init(&tma_full[s], 1);
+        }
+        for (int s = 0; s < kPkStages; ++s) {
+            mbar_init(&pk_full[s], 1);
+            mbar_init(&pk_empty[s], kEpilogueWarps);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -1038,21 +1048,29 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const unsigned tmem = *tmem_slot;
 
-    if (warp == kTmaWarpP) {
-        unsigned tma_issued = 0, tma_phase = 0;
+    if (warp == kTmaWarpP || warp == kPkWarp) {
+        // TMA warp: x tiles (and the min-term tiles) into the main stages;
+        // packed warp: the packed codes of the production steps into its ring
+        const bool pk = warp == kPkWarp;
+        unsigned issued = 0, phase = 0;
         int qq = 0;
         bool go = true;
         for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
             int row0, tok0, kstep0;
             tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+            const int steps = pk ? a.k_steps : a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
             for (int ks = 0; ks < steps; ++ks, ++qq) {
                 int ok = 1;
                 if (lane == 0) {
-                    const int s = qq % kStages;
-                    const unsigned ph = (qq / kStages) & 1;
-                    ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 11, false);
-                    if (ok) {
+                    const int ring = pk ? kPkStages : kStages;
+                    const int s = qq % ring;
+                    const unsigned ph = (qq / ring) & 1;
+                    ok = !*abort_flag && mbar_wait(pk ? &pk_empty[s] : &empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                    if (ok && pk) {
+                        mbar_expect_tx(&pk_full[s], kPackedTile);
+                        tma_load_2d(smem_u32(pk_ring + s * kPackedTile), &map_pk, (kstep0 + ks) * kBK / 2, row0,
+                                    smem_u32(&pk_full[s]));
+                    } else if (ok) {
                         unsigned char* st = stages + s * stage_bytes;
                         const unsigned bar = smem_u32(&full[s]);
                         if (ks < a.k_steps) {
@@ -1060,8 +1078,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                             mbar_expect_tx(&full[s], 2 * b_bytes);
                             tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
                             tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
-                            mbar_expect_tx(&tma_full[s], kPackedTile);
-                            tma_load_2d(smem_u32(st + kATile), &map_pk, k0 / 2, row0, smem_u32(&tma_full[s]));
                         } else {
                             const int c0 = (ks - a.k_steps) * kBK;
                             mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
@@ -1069,10 +1085,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                             tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
                             tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
                             tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
-                            mbar_arrive(&tma_full[s]);
                         }
-                        tma_issued |= 1u << s;
-                        tma_phase = (tma_phase & ~(1u << s)) | (ph << s);
+                    }
+                    if (ok) {
+                        issued |= 1u << s;
+                        phase = (phase & ~(1u << s)) | (ph << s);
                     }
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -1082,9 +1099,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             }
         }
         if (lane == 0)
-            for (int s = 0; s < kStages; ++s)
-                if (tma_issued >> s & 1u)
-                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full[s], (tma_phase >> s) & 1u); ++i) {
+            for (int s = 0; s < (pk ? kPkStages : kStages); ++s)
+                if (issued >> s & 1u)
+                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(pk ? &pk_full[s] : &full[s], (phase >> s) & 1u); ++i) {
                     }
     } else if (warp == kMmaWarpP) {
         if (lane == 0) {
@@ -1134,7 +1151,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         // columns [0, 128) and [128, 256), and the low / high nibbles
         const int r = threadIdx.x % kBM;
         const int hf = threadIdx.x / kBM;
-        int gb = 0, qq = 0;
+        int gb = 0, qq = 0, pq = 0;
         bool go = true;
         for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
             int row0, tok0, kstep0;
@@ -1144,85 +1161,93 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             const long long row = row0 + r;
             const bool live = row < a.w.rows;
             const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
+            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
             float acc[128];
 #pragma unroll
             for (int c = 0; c < 128; ++c) acc[c] = 0.f;
-            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
-            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
             int drained = 0;
-            // drains block `drained` (accumulator b) into acc with its scale
-            auto drain = [&]() -> bool {
-                const int b = gb & 1;
-                const float scale = !live ? 0.f : drained < q.blocks ? qs_row[drained] : min_scale;
-                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0))
-                    return false;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
-                    unsigned u[32];
-                    const unsigned taddr =
-                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
-                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
-                          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
-                          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
-                          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
-                        : "r"(taddr));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
-                }
-                asm volatile("tcgen05.fence::before_thread_sync;");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[b]);
-                ++gb;
-                ++drained;
-                return true;
-            };
             for (int p = 0; p < steps && go; ++p, ++qq) {
                 const int s = qq % kStages;
                 const unsigned ph = (qq / kStages) & 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&tma_full[s], ph, abort_flag, a.err, 16) ? 1 : 0)) {
+                // the stage is free once the MMAs of its previous use are done
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 16) ? 1 : 0)) {
                     go = false;
                     break;
                 }
                 if (p < a.k_steps) {
+                    const int ps = pq % kPkStages;
+                    const unsigned pph = (pq / kPkStages) & 1;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&pk_full[ps], pph, abort_flag, a.err, 17) ? 1 : 0)) {
+                        go = false;
+                        break;
+                    }
                     unsigned char* st = stages + s * stage_bytes;
-                    const uint4 w = *reinterpret_cast<const uint4*>(st + kATile + r * 16);
                     const unsigned sc = live ? sc_row[p] : 0u;
                     const __half2 sc2 = __half2half2(__uint2half_rn(sc));
-                    const __half2 off2 = __half2half2(__uint2half_rn(1024u * sc));
-                    const unsigned words[4] = {w.x, w.y, w.z, w.w};
-                    unsigned out[8];
+                    const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
+                    // two 8-byte halves of the row's 16 bytes: elements 16 hf + 0..7, then + 8..15
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const unsigned nib = hf ? (words[k] >> 4) & 0x0F0F0F0Fu : words[k] & 0x0F0F0F0Fu;
-                        const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
-                        const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
-                        const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, __hneg2(off2));
-                        const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, __hneg2(off2));
-                        out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
-                        out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                    for (int c = 0; c < 2; ++c) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(pk_ring + ps * kPackedTile + r * 16 + c * 8);
+                        unsigned out[4];
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const unsigned word = k ? w.y : w.x;
+                            const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+                            const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
+                            const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
+                            const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
+                            const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
+                            out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
+                            out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                        }
+                        *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + c)) = make_uint4(out[0], out[1], out[2], out[3]);
                     }
-                    *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf)) = make_uint4(out[0], out[1], out[2], out[3]);
-                    *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + 1)) = make_uint4(out[4], out[5], out[6], out[7]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
+                    ++pq;
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
-                // block `drained` ends at K-step 8 (drained + 1) (the min term at the tile's last step)
-                while (drained < nb && go) {
+                // drain blocks whose MMAs are kLead steps behind (all at the tile's last step)
+                while (go && drained < nb) {
                     const int end = drained < q.blocks ? 8 * (drained + 1) : steps;
-                    if (end + kLead > p + 1 && p + 1 < steps) break;
+                    if (p + 1 < steps && end + kLead > p + 1) break;
                     if (end > p + 1) break;
-                    go = drain();
+                    const int b = gb & 1;
+                    const float scale = !live ? 0.f : drained < q.blocks ? qs_row[drained] : -32.f * pow2(-a.w.qmin_shift[row]);
+                    if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
+                        unsigned u[32];
+                        const unsigned taddr =
+                            tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
+                        asm volatile(
+                            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                            : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+                              "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+                              "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]),
+                              "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]),
+                              "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                            : "r"(taddr));
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
+                    }
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+                    ++gb;
+                    ++drained;
                 }
             }
-            while (go && drained < nb) go = drain();
             if (!go) break;
             // store, 32 token columns at a time (as tc_gemm_q4k_kernel)
             for (int c = 0; c < 4; ++c) {
@@ -1498,8 +1523,9 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         } else {
             if (g.w.qs_row % 16 || reinterpret_cast<std::uintptr_t>(g.w.qs) % 16)
                 throw std::invalid_argument("packed Q4_K rows must be 16-byte aligned");
-            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            tc_gemm_q4kp_kernel<<<grid_n, kPersistThreads, smem, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+            const int smem_p = smem + kPkStages * kPackedTile;
+            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
+            tc_gemm_q4kp_kernel<<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
         }
         TVARA_LAUNCHED();
         return;
