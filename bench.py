@@ -417,6 +417,31 @@ def nccl_unique_id(rank, world):
     return obj[0]
 
 
+def allreduce_standalone(world, n=512 * 4096, reps=20):
+    """NCCL's allreduce of the step's residual (512 x 4096 F32 = 8 MB) on
+    its own, through torch.distributed: device time per call (CUDA events,
+    max over ranks) and the bus bandwidth 2 (N-1)/N x bytes / time."""
+    import torch
+    import torch.distributed as dist
+    x = torch.ones(n, device="cuda")
+    for _ in range(5):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        dist.all_reduce(x)
+    e1.record()
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) * 1e3 / reps], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    return {"bytes": n * 4, "us": round(us, 1), "bus_gbs": round(2 * (world - 1) / world * n * 4 / us / 1e3, 1),
+            "note": "torch.distributed NCCL allreduce alone, 20 calls back to back; the engine's own residual "
+                    "allreduce (kernels.collective) runs over NVLink peer memory unless TVARA_ALLREDUCE=nccl"}
+
+
 def parity_check(args, rank, world, local, barrier):
     """The checker, outside every timed region: a 2-layer model with the
     benchmark's widths (llama8b shape, Q4_K / Q8_0), split over the same ranks
@@ -824,6 +849,11 @@ def run_ours(args):
         if single and not args.no_standalone and extras else None
     cpu = guard(reference_cpu, path, cfg, mean_ctx, cpu_job) if cpu_job else None
     parity = parity_check(args, rank, world, local, barrier) if extras else None
+    if world > 1:
+        kernels["collective"]["nccl_allreduce_8mb_alone"] = allreduce_standalone(world)
+        kernels["collective"]["implementation"] = ("NCCL allreduce" if os.environ.get("TVARA_ALLREDUCE") == "nccl"
+                                                   else "two-shot allreduce over NVLink peer memory (p2p_allreduce.cu)")
+        kernels["collective"]["calls_per_step"] = 2 * cfg["layers"]
     other = {}
     if extras:
         other["smollm2"] = smollm2_replicas(args, rank, world, local, barrier, dist)

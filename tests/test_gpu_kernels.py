@@ -401,3 +401,19 @@ def test_attention_chunk_many_short_runs(capi):
         for i in range(r):
             assert attn_close(got[k], oracle_attention(q[k], pool, ids, vis[k], 0, heads), 5e-5), (n, r, i)
             k += 1
+
+
+@pytest.mark.parametrize("tokens", [5, 8, 17, 32, 40, 64, 65])
+@pytest.mark.parametrize("rows,cols", [(300, 2816), (129, 4096)])
+def test_small_batch_q4k_matches_oracle(capi, tokens, rows, cols):
+    """Small batches of Q4_K rows (5..64 tokens: the mma.sync kernel on the
+    packed rows, split K where the blocks allow; 65 tokens: tensor cores):
+    token tiles of 8/16/32/64, partial row tiles, K of 11 blocks (no split)
+    and of 16 blocks (split), activations spanning four orders of magnitude
+    per token."""
+    rng = np.random.default_rng(tokens * 31 + rows + cols)
+    raw = make_weights(gguf.Q4_K, rows, cols, rng)
+    x = (rng.standard_normal((tokens, cols)) * rng.uniform(0.01, 30, (tokens, 1))).astype(np.float32)
+    got = matmul(capi, gguf.Q4_K, packed(capi, gguf.Q4_K, raw, rows, cols), rows, cols, x)
+    ref, mag = oracle_matmul(gguf.Q4_K, raw, rows, cols, x)
+    assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()

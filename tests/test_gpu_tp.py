@@ -3,7 +3,9 @@ GPU opens its shard of the tiny model with an NCCL unique id, both ranks run
 the same prefill chunk, ragged batch step and decodes in the same order, and
 the logits must match the reference's F32 forward (the pinned oracle) within
 the logit tolerance on both ranks -- the allreduce leaves every rank with the
-same residual, so the ranks' logits are identical."""
+same residual, so the ranks' logits are identical.  Both residual allreduces
+are covered (peer memory, NCCL), as are the vocabulary-split head's gathered
+argmax and the device sampler over the gathered rows."""
 
 import ctypes as C
 
@@ -15,10 +17,13 @@ pytestmark = pytest.mark.gpu
 ATOL = 2e-3
 
 
-def _rank(rank, world, nccl_id, path, prompts, out):
+def _rank(rank, world, nccl_id, path, prompts, out, allreduce):
+    import os
     import torch
     from tvara_b200.native import NativeModel
 
+    if allreduce == "nccl":
+        os.environ["TVARA_ALLREDUCE"] = "nccl"
     torch.cuda.set_device(rank)
     with NativeModel(path, max_blocks=64, block_tokens=16, device=rank, tp_rank=rank, tp_size=world,
                      nccl_id=nccl_id) as m:
@@ -43,7 +48,10 @@ def _nccl_unique_id():
     return buf.raw
 
 
-def test_tp2_matches_oracle(tiny_path, tmp_path):
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
+def test_tp2_matches_oracle(tiny_path, tmp_path, allreduce):
+    """peer: the residual allreduce runs over NVLink peer memory (the
+    default); nccl: NCCL's allreduce (TVARA_ALLREDUCE=nccl)."""
     import torch
     import torch.multiprocessing as mp
     from oracle.model import OracleModel
@@ -55,7 +63,8 @@ def test_tp2_matches_oracle(tiny_path, tmp_path):
     out = str(tmp_path / "rank%d.npz")
     nccl_id = _nccl_unique_id()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, str(tiny_path), prompts, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, str(tiny_path), prompts, out, allreduce))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -1162,6 +1162,12 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
             const bool live = row < a.w.rows;
             const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
             const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
+            // the sub-block scales of a block (8 bytes) and the block scales
+            // are loaded a block ahead of use, off the producers' critical path
+            uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
+            uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
+            float d_next = live && q.blocks > 0 ? qs_row[0] : 0.f;
+            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
             float acc[128];
 #pragma unroll
             for (int c = 0; c < 128; ++c) acc[c] = 0.f;
@@ -1182,7 +1188,12 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                         break;
                     }
                     unsigned char* st = stages + s * stage_bytes;
-                    const unsigned sc = live ? sc_row[p] : 0u;
+                    if ((p & 7) == 0 && p > 0) {
+                        sc_cur = sc_next;
+                        sc_next = live && p + 8 < a.k_steps ? __ldg(reinterpret_cast<const uint2*>(sc_row + p + 8))
+                                                            : make_uint2(0, 0);
+                    }
+                    const unsigned sc = (((p & 4) ? sc_cur.y : sc_cur.x) >> (8 * (p & 3))) & 255u;
                     const __half2 sc2 = __half2half2(__uint2half_rn(sc));
                     const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
                     // two 8-byte halves of the row's 16 bytes: elements 16 hf + 0..7, then + 8..15
@@ -1216,7 +1227,8 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     if (p + 1 < steps && end + kLead > p + 1) break;
                     if (end > p + 1) break;
                     const int b = gb & 1;
-                    const float scale = !live ? 0.f : drained < q.blocks ? qs_row[drained] : -32.f * pow2(-a.w.qmin_shift[row]);
+                    const float scale = drained < q.blocks ? d_next : min_scale;
+                    if (drained + 1 < q.blocks) d_next = live ? qs_row[drained + 1] : 0.f;
                     if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
                         go = false;
                         break;
@@ -1302,6 +1314,196 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
+}
+
+// ---------------------------------------------------------------------------
+// Small batches (5 .. 64 tokens) of Q4_K rows on mma.sync, straight from the
+// packed rows: the weights are read once per launch for all the tokens, the
+// activations (hi / lo FP16 with their per-token power of two, as the
+// tensor-core path splits them) pass through shared memory in chunks of
+// kSmallChunk elements.  A CTA is eight warps on 128 weight rows -- 16 per
+// warp -- and one slice of K (split K across CTAs so that the grid covers the
+// SMs; none for the SwiGLU epilogue, which needs whole sums).  Per 32-element
+// sub-block a lane takes one 32-bit word of each of its two rows (bytes
+// 4tq .. 4tq + 3 of the row's 16 packed bytes: elements 4tq .. 4tq + 3 in the
+// low nibbles, 16 + 4tq .. in the high ones) from a register ring kept
+// kSmallDepth sub-blocks ahead, and builds the A fragments of both K-halves
+// from it, sc*q exact in FP16 as in tc_gemm_q4kp_kernel.  The fragment's K
+// order is a fixed permutation of the sub-block's (logical k 2tq + e <->
+// element 4tq + e, 2tq + 8 + e <-> element 4tq + 2 + e); the activations are
+// read with the same permutation, so every dot product is unchanged.  Each
+// 256-element block accumulates on its own and is added with its scale d;
+// the min term sum_sub dmin*m * sum(x) is F32 multiply-adds on the sub-block
+// sums.  Partial rows are added to y with atomics when K is split.
+constexpr int kSmallRows = 128;
+constexpr int kSmallThreads = 256;
+constexpr int kSmallChunk = 512;  // K elements of x staged at a time
+constexpr int kSmallDepth = 8;    // sub-blocks of packed words in flight per lane
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int small_xs(int chunk) { return chunk * 2 + 32; }  // bytes per token row (padded)
+constexpr std::size_t small_smem_bytes(int nt) {
+    return std::size_t(8 * nt) * small_xs(kSmallChunk) * 2 + std::size_t(8 * nt) * (kSmallChunk / 32) * 4;
+}
+
+template <int NT>  // 8-token tiles: up to 8 * NT tokens
+__global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMatrix w, const __half* xhi,
+                                                                      const __half* xlo, const int* xshift,
+                                                                      const __half* shi, const __half* slo, int tokens,
+                                                                      int kslice, float* y, int ldy, int epilogue,
+                                                                      int atomic) {
+    constexpr int MT = 8 * NT;
+    constexpr int XS = small_xs(kSmallChunk);
+    constexpr int CU = kSmallChunk / 32;  // sub-blocks per chunk
+    extern __shared__ __align__(16) unsigned char small_smem[];
+    unsigned char* xh_s = small_smem;
+    unsigned char* xl_s = xh_s + MT * XS;
+    float* sx_s = reinterpret_cast<float*>(xl_s + MT * XS);  // [MT][CU] sub-block sums (x 2^(shift - 5))
+    const int units = w.cols / 32, kblocks = w.cols / 256;
+    const int u0 = blockIdx.y * (kslice / 32);  // first sub-block of this CTA
+    const int su = kslice / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int row_a = blockIdx.x * kSmallRows + warp * 16 + gq, row_b = row_a + 8;
+    const bool live_a = row_a < w.rows, live_b = row_b < w.rows;
+    const long long ra = live_a ? row_a : 0, rb = live_b ? row_b : 0;
+    const unsigned* qa = reinterpret_cast<const unsigned*>(w.qs + ra * (long long)w.qs_row + u0 * 16 + 4 * tq);
+    const unsigned* qb = reinterpret_cast<const unsigned*>(w.qs + rb * (long long)w.qs_row + u0 * 16 + 4 * tq);
+    const unsigned char* sca = w.qsc + ra * units + u0;
+    const unsigned char* scb = w.qsc + rb * units + u0;
+    float tot[NT][4], blk[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tot[n][e] = blk[n][e] = 0.f;
+    unsigned ring_a[kSmallDepth], ring_b[kSmallDepth];
+#pragma unroll
+    for (int i = 0; i < kSmallDepth; ++i) {
+        ring_a[i] = i < su ? __ldg(qa + 4 * i) : 0u;
+        ring_b[i] = i < su ? __ldg(qb + 4 * i) : 0u;
+    }
+    // sub-block scales of the next eight sub-blocks (one block), a group ahead
+    uint2 sc_a = live_a ? __ldg(reinterpret_cast<const uint2*>(sca)) : make_uint2(0, 0);
+    uint2 sc_b = live_b ? __ldg(reinterpret_cast<const uint2*>(scb)) : make_uint2(0, 0);
+    for (int c0 = 0; c0 < su; c0 += CU) {  // one chunk of x at a time
+        const int cu = min(CU, su - c0);
+        __syncthreads();  // the previous chunk is no longer read
+        for (int i = threadIdx.x; i < MT * (cu * 4); i += blockDim.x) {
+            const int t = i / (cu * 4), c = i % (cu * 4);
+            uint4 h = make_uint4(0, 0, 0, 0), l = h;
+            if (t < tokens) {
+                const long long off = (long long)t * w.cols + (u0 + c0) * 32 + 8 * c;
+                h = *reinterpret_cast<const uint4*>(xhi + off);
+                l = *reinterpret_cast<const uint4*>(xlo + off);
+            }
+            *reinterpret_cast<uint4*>(xh_s + t * XS + 16 * c) = h;
+            *reinterpret_cast<uint4*>(xl_s + t * XS + 16 * c) = l;
+        }
+        for (int i = threadIdx.x; i < MT * cu; i += blockDim.x) {
+            const int t = i / cu, u = i % cu;
+            const long long off = (long long)t * units + u0 + c0 + u;
+            sx_s[t * CU + u] = t < tokens ? __half2float(shi[off]) + __half2float(slo[off]) : 0.f;
+        }
+        __syncthreads();
+        for (int uu = 0; uu < cu; uu += kSmallDepth) {
+            const uint2 ga = sc_a, gbk = sc_b;  // this group's scales; the next group's are loaded now
+            const float da = live_a ? w.qscale[ra * kblocks + ((u0 + c0 + uu) >> 3)] : 0.f;
+            const float db = live_b ? w.qscale[rb * kblocks + ((u0 + c0 + uu) >> 3)] : 0.f;
+            if (c0 + uu + kSmallDepth < su) {
+                sc_a = live_a ? __ldg(reinterpret_cast<const uint2*>(sca + c0 + uu + kSmallDepth)) : make_uint2(0, 0);
+                sc_b = live_b ? __ldg(reinterpret_cast<const uint2*>(scb + c0 + uu + kSmallDepth)) : make_uint2(0, 0);
+            }
+#pragma unroll
+            for (int i = 0; i < kSmallDepth; ++i) {
+                const int u = c0 + uu + i;  // sub-block within the CTA's slice
+                const unsigned wa = ring_a[i], wb = ring_b[i];
+                const int nxt = u + kSmallDepth;
+                ring_a[i] = nxt < su ? __ldg(qa + 4 * nxt) : 0u;
+                ring_b[i] = nxt < su ? __ldg(qb + 4 * nxt) : 0u;
+                const unsigned sa = ((i < 4 ? ga.x : ga.y) >> (8 * (i & 3))) & 255u;
+                const unsigned sb = ((i < 4 ? gbk.x : gbk.y) >> (8 * (i & 3))) & 255u;
+                const __half2 sa2 = __half2half2(__uint2half_rn(sa)), sb2 = __half2half2(__uint2half_rn(sb));
+                const __half2 oa2 = __hneg2(__half2half2(__uint2half_rn(1024u * sa)));
+                const __half2 ob2 = __hneg2(__half2half2(__uint2half_rn(1024u * sb)));
+#pragma unroll
+                for (int hk = 0; hk < 2; ++hk) {  // low nibbles: elements 0..15, high: 16..31
+                    const unsigned ma = hk ? (wa >> 4) & 0x0F0F0F0Fu : wa & 0x0F0F0F0Fu;
+                    const unsigned mb = hk ? (wb >> 4) & 0x0F0F0F0Fu : wb & 0x0F0F0F0Fu;
+                    unsigned a[4];
+                    const unsigned p0 = __byte_perm(ma, 0x64646464u, 0x4140), p1 = __byte_perm(mb, 0x64646464u, 0x4140);
+                    const unsigned p2 = __byte_perm(ma, 0x64646464u, 0x4342), p3 = __byte_perm(mb, 0x64646464u, 0x4342);
+                    const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sa2, oa2);
+                    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sb2, ob2);
+                    const __half2 h2 = __hfma2(*reinterpret_cast<const __half2*>(&p2), sa2, oa2);
+                    const __half2 h3 = __hfma2(*reinterpret_cast<const __half2*>(&p3), sb2, ob2);
+                    a[0] = *reinterpret_cast<const unsigned*>(&h0);  // row gq, elements 4tq, 4tq + 1
+                    a[1] = *reinterpret_cast<const unsigned*>(&h1);  // row gq + 8
+                    a[2] = *reinterpret_cast<const unsigned*>(&h2);  // row gq, elements 4tq + 2, 4tq + 3
+                    a[3] = *reinterpret_cast<const unsigned*>(&h3);
+                    const int koff = ((uu + i) * 32 + 16 * hk + 4 * tq) * 2;
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) {
+                        const uint2 bh = *reinterpret_cast<const uint2*>(xh_s + (8 * n + gq) * XS + koff);
+                        const uint2 bl = *reinterpret_cast<const uint2*>(xl_s + (8 * n + gq) * XS + koff);
+                        mma_16816(blk[n], a, bh.x, bh.y);
+                        mma_16816(blk[n], a, bl.x, bl.y);
+                    }
+                }
+                if (i == kSmallDepth - 1) {  // end of a 256-element block: add it with its scale d
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) {
+                        tot[n][0] = fmaf(da, blk[n][0], tot[n][0]);
+                        tot[n][1] = fmaf(da, blk[n][1], tot[n][1]);
+                        tot[n][2] = fmaf(db, blk[n][2], tot[n][2]);
+                        tot[n][3] = fmaf(db, blk[n][3], tot[n][3]);
+                        blk[n][0] = blk[n][1] = blk[n][2] = blk[n][3] = 0.f;
+                    }
+                }
+            }
+        }
+        // min term of this chunk: - sum_sub dmin*m * sum(x) (sums are x 2^(shift - 5): times 32)
+        const float ia = live_a ? pow2(-w.qmin_shift[ra]) * 32.f : 0.f;
+        const float ib = live_b ? pow2(-w.qmin_shift[rb]) * 32.f : 0.f;
+        for (int u = 0; u < cu; ++u) {
+            const long long ua = ra * units + u0 + c0 + u, ub = rb * units + u0 + c0 + u;
+            const float ma = (__half2float(__ushort_as_half(w.qmin_hi[ua])) + __half2float(__ushort_as_half(w.qmin_lo[ua]))) * ia;
+            const float mb = (__half2float(__ushort_as_half(w.qmin_hi[ub])) + __half2float(__ushort_as_half(w.qmin_lo[ub]))) * ib;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const float s0 = sx_s[(8 * n + 2 * tq) * CU + u], s1 = sx_s[(8 * n + 2 * tq + 1) * CU + u];
+                tot[n][0] = fmaf(-ma, s0, tot[n][0]);
+                tot[n][1] = fmaf(-ma, s1, tot[n][1]);
+                tot[n][2] = fmaf(-mb, s0, tot[n][2]);
+                tot[n][3] = fmaf(-mb, s1, tot[n][3]);
+            }
+        }
+    }
+    // out: accumulator (row gq / gq + 8, tokens 8n + 2tq, + 1), scaled back by 2^-shift
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int t = 8 * n + 2 * tq + (e & 1);
+            const bool rlive = e < 2 ? live_a : live_b;
+            const int row = e < 2 ? row_a : row_b;
+            const float v = t < tokens ? tot[n][e] * pow2(-xshift[t]) : 0.f;
+            if (epilogue == kSwiGLU) {
+                // rows (2i, 2i + 1) = (gate_i, up_i) sit in lanes gq and gq ^ 1 (4 lanes apart)
+                const float other = __shfl_xor_sync(0xffffffffu, v, 4);
+                if (rlive && t < tokens && !(gq & 1)) y[(long long)t * ldy + row / 2] = swiglu_12(v, other);
+            } else if (rlive && t < tokens) {
+                float* dst = y + (long long)t * ldy + row;
+                if (atomic || epilogue == kAdd) atomicAdd(dst, v);
+                else *dst = v;
+            }
+        }
 }
 
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
@@ -1391,6 +1593,7 @@ void run_tc(const CUtensorMap& hi, const CUtensorMap& lo, const CUtensorMap& ahi
 }
 
 int g_tc_min_tokens = 5;  // below this the CUDA-core GEMV streams weights once per <=4 tokens
+bool g_small_batches = true;  // 5..64 tokens of packed Q4_K rows: gemm_small_q4k_kernel
 bool g_tc_persistent = true;  // plane path: persistent kernel (else one CTA per tile)
 
 int sm_count() {
@@ -1477,6 +1680,35 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         TVARA_LAUNCHED();
     }
 
+    if (g.w.qsc && T <= 64 && g_small_batches) {
+        // small batches: packed Q4_K rows on mma.sync, weights read once for all tokens
+        const int nt = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
+        const int row_tiles = (g.w.rows + kSmallRows - 1) / kSmallRows;
+        const int blocks = K / 256;
+        int splits = 1;
+        if (g.epilogue != kSwiGLU)
+            while (splits * 2 <= blocks && blocks % (splits * 2) == 0 && row_tiles * splits < 3 * sm_count()) splits *= 2;
+        if (splits > 1 && g.epilogue == kStore)
+            TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
+        const dim3 grid(row_tiles, splits);
+        const int kslice = K / splits;
+        const int smem = int(small_smem_bytes(nt));
+        switch (nt) {
+#define TVARA_SMALL(N)                                                                                             \
+    case N:                                                                                                        \
+        TVARA_CUDA(cudaFuncSetAttribute(gemm_small_q4k_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
+        gemm_small_q4k_kernel<N><<<grid, kSmallThreads, smem, s>>>(g.w, hi, lo, shift, shi, slo, T, kslice, g.y, g.ldy, \
+                                                                   g.epilogue, splits > 1);                        \
+        break;
+            TVARA_SMALL(1)
+            TVARA_SMALL(2)
+            TVARA_SMALL(4)
+            TVARA_SMALL(8)
+#undef TVARA_SMALL
+        }
+        TVARA_LAUNCHED();
+        return;
+    }
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
