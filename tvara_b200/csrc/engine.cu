@@ -626,7 +626,7 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         toff[t] = s.table_off[s.seq_of[t]];
     }
     AttnPlan plan = plan_attention(vis, toff, tpb, hkv_, partial_cap_, 148,
-                                   attention_chunk_rows(opt_.kv_f16, d, hq_ / hkv_, tpb));
+                                   attention_chunk_rows(opt_.kv_i8 ? 2 : opt_.kv_f16 ? 1 : 0, d, hq_ / hkv_, tpb));
     auto& work = plan.work;
     auto& comb = plan.comb;
     auto& wpart = plan.part;

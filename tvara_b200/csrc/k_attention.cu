@@ -1352,6 +1352,297 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const __
     }
 }
 
+// The chunk kernel for F32 pools (the reference's KV format).  Same CTA,
+// work items and softmax as attn_chunk_kernel; the K/V tiles are F32 rows in
+// shared memory (TMA boxes of 32 floats x tpb slots, 128-byte swizzle), and
+// the MMA operands are built from them in registers as exact hi + lo F16
+// pairs after a per-tile power-of-two scaling: S = Q_hi K_hi + Q_lo K_hi +
+// Q_hi K_lo and O += P_hi V_hi + P_lo V_hi + P_hi V_lo (the lo x lo products
+// are below 2^-22 of the result), so K and V keep about 22 of their 24 bits.
+// The tile's scale of K (or V) is the power of two that brings its largest
+// |value| below 2^15, found by one pass over the tile in shared memory.
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_f32_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                            AttnArgs a) {
+    constexpr int NB = D / 32;   // 128-byte boxes (32 floats) per slot row
+    constexpr int KS = D / 16;   // k-steps of S = Q K^T
+    constexpr int NT = D / 8;    // n8 tiles of O
+    constexpr int RW = 16 / G;   // rows per warp
+    static_assert(D % 32 == 0 && G >= 1 && G <= 8, "chunk attention shape");
+    extern __shared__ unsigned char att_raw[];
+    __shared__ std::uint64_t bars[kChunkRing];
+    __shared__ float tile_scale[2];  // 2^-e of the current tile's K and V maxima
+    const int tpb = a.tpb;
+    const int box = tpb * 128;
+    const int half_stage = NB * box;
+    const int stage = 2 * half_stage;
+    unsigned char* smem = att_raw + ((1024u - (s_u32(att_raw) & 1023u)) & 1023u);
+    const unsigned ring_s = s_u32(smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gq = lane >> 2, tq = lane & 3;
+
+    const int4 wk = a.chunk_work[blockIdx.x];
+    const int t0 = wk.x, toff = wk.y, v0 = wk.z, nrows = wk.w;
+    const int h = blockIdx.y;
+    const int vlast = v0 + nrows - 1;
+    const int nblk = (vlast + tpb - 1) / tpb;
+    const bool warp_live = warp * RW < nrows;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kChunkRing; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_u32(&bars[s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const long long head_row = (a.layer_offset + (long long)h * tpb * D) / D;
+    const long long block_rows = a.block_stride / D, kind_rows = a.kind_stride / D;
+    auto issue = [&](int i) {
+        int pb = __ldg(a.tables + toff + i);
+        if (pb < 0 || pb >= a.max_blocks) {
+            atomicExch(a.err, 2);
+            pb = 0;
+        }
+        const int yk = int(pb * block_rows + head_row);
+        const int yv = int(yk + kind_rows);
+        const unsigned st = ring_s + unsigned((i % kChunkRing) * stage);
+        const unsigned bar = s_u32(&bars[i % kChunkRing]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(stage) : "memory");
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            tma_load_2d(st + b * box, &kv_map, b * 32, yk, bar);
+            tma_load_2d(st + half_stage + b * box, &kv_map, b * 32, yv, bar);
+        }
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kChunkRing && i < nblk; ++i) issue(i);
+
+    int vis[2];
+    const float* qp[2];
+    bool live[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int m = gq + 8 * hf;
+        const bool vec = m < RW * G;
+        const int r = warp * RW + (vec ? m / G : 0);
+        live[hf] = vec && r < nrows;
+        const int rr = live[hf] ? r : 0;
+        vis[hf] = v0 + rr;
+        qp[hf] = a.q + (long long)(t0 + rr) * a.hq * D + (h * G + (vec ? m % G : 0)) * D;
+    }
+    unsigned qh[KS][4], ql[KS][4];
+    float qinv[2];
+    {
+        const float scale = rsqrtf(float(D));
+        float v[KS][8];
+        float mx[2] = {0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const float2 x = *reinterpret_cast<const float2*>(qp[hf] + 16 * kk + 8 * c + 2 * tq);
+                    v[kk][4 * c + 2 * hf] = x.x * scale;
+                    v[kk][4 * c + 2 * hf + 1] = x.y * scale;
+                    mx[hf] = fmaxf(mx[hf], fmaxf(fabsf(x.x * scale), fabsf(x.y * scale)));
+                }
+        float up[2];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 1));
+            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 2));
+            int e2 = 0;
+            if (mx[hf] > 0.f && isfinite(mx[hf])) frexpf(mx[hf], &e2);
+            const int sh = max(-100, min(100, 15 - e2));
+            up[hf] = exp2i(sh);
+            qinv[hf] = exp2i(-sh);
+        }
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+                    split_f16x2(v[kk][4 * c + 2 * hf] * up[hf], v[kk][4 * c + 2 * hf + 1] * up[hf], qh[kk][2 * c + hf],
+                                ql[kk][2 * c + hf]);
+    }
+    // element (pos, d) of a K or V tile: box d / 32, 16-byte chunk (d % 32) / 4 swizzled with the row
+    auto f32_at = [&](const unsigned char* tile, int pos, int d) -> const float* {
+        return reinterpret_cast<const float*>(tile + (d >> 5) * box + pos * 128 + ((((d & 31) >> 2) ^ (pos & 7)) << 4) +
+                                              (d & 3) * 4);
+    };
+
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    bool failed = false;
+    for (int i = 0; i < nblk; ++i) {
+        const unsigned parity = (i / kChunkRing) & 1;
+        unsigned ok = 0;
+        for (unsigned spin = 0; spin < kAttnSpin; ++spin) {
+            if (bar_try(&bars[i % kChunkRing], parity)) {
+                ok = 1;
+                break;
+            }
+            if (spin > 32) __nanosleep(32);
+        }
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) atomicExch(a.err, 4);
+            failed = true;
+            break;
+        }
+        const unsigned char* kst = smem + std::size_t(i % kChunkRing) * stage;
+        const unsigned char* vst = kst + half_stage;
+        const int base = i * tpb;
+        const int s_hi = min(tpb, vlast - base);
+        {
+            // rows past the last row's visible end may hold anything: zero them
+            // (K and V) so that the tile maxima and 0 * V stay finite; then the
+            // power-of-two scales of this tile's K and V
+            unsigned char* krows = smem + std::size_t(i % kChunkRing) * stage;
+            const int pad = ((s_hi + 15) & ~15) - s_hi;
+            for (int idx = threadIdx.x; idx < 2 * pad * NB * 8; idx += blockDim.x) {
+                const int kind = idx / (pad * NB * 8), rem = idx % (pad * NB * 8);
+                const int r = s_hi + rem / (NB * 8), c = rem % (NB * 8);
+                *reinterpret_cast<uint4*>(krows + kind * half_stage + (c >> 3) * box + r * 128 + (c & 7) * 16) =
+                    make_uint4(0, 0, 0, 0);
+            }
+            float mk = 0.f, mv = 0.f;
+            for (int idx = threadIdx.x; idx < s_hi * D / 4; idx += blockDim.x) {
+                const int r = idx / (D / 4), c = idx % (D / 4);  // 16-byte chunk c of row r (any order will do)
+                const float4 kq = *reinterpret_cast<const float4*>(krows + (c >> 3) * box + r * 128 + (c & 7) * 16);
+                const float4 vq = *reinterpret_cast<const float4*>(krows + half_stage + (c >> 3) * box + r * 128 + (c & 7) * 16);
+                mk = fmaxf(mk, fmaxf(fmaxf(fabsf(kq.x), fabsf(kq.y)), fmaxf(fabsf(kq.z), fabsf(kq.w))));
+                mv = fmaxf(mv, fmaxf(fmaxf(fabsf(vq.x), fabsf(vq.y)), fmaxf(fabsf(vq.z), fabsf(vq.w))));
+            }
+            for (int o2 = 16; o2; o2 >>= 1) {
+                mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o2));
+                mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o2));
+            }
+            __shared__ float red[2][kAttnWarps];
+            if (lane == 0) {
+                red[0][warp] = mk;
+                red[1][warp] = mv;
+            }
+            __syncthreads();
+            if (threadIdx.x < 2) {
+                float m = 0.f;
+                for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, red[threadIdx.x][w]);
+                int e2 = 0;
+                if (m > 0.f && isfinite(m)) frexpf(m, &e2);
+                tile_scale[threadIdx.x] = exp2i(max(-100, min(100, 15 - e2)));
+            }
+            __syncthreads();
+        }
+        const float ks_up = tile_scale[0], vs_up = tile_scale[1];
+        const float ks_inv = 1.f / ks_up, vs_inv = 1.f / vs_up;  // exact: powers of two
+        for (int sub = 0; warp_live && sub < s_hi; sub += 16) {
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+                for (int n = 0; n < 2; ++n) {
+                    // B = K^T: (k = d 16kk + 2tq, + 1 | + 8, + 9; n = position sub + 8n + gq)
+                    const int pos = sub + 8 * n + gq;
+                    const float2 k0 = *reinterpret_cast<const float2*>(f32_at(kst, pos, 16 * kk + 2 * tq));
+                    const float2 k1 = *reinterpret_cast<const float2*>(f32_at(kst, pos, 16 * kk + 8 + 2 * tq));
+                    unsigned bh0, bl0, bh1, bl1;
+                    split_f16x2(k0.x * ks_up, k0.y * ks_up, bh0, bl0);
+                    split_f16x2(k1.x * ks_up, k1.y * ks_up, bh1, bl1);
+                    mma16816(s[n], qh[kk], bh0, bh1);
+                    mma16816(s[n], ql[kk], bh0, bh1);
+                    mma16816(s[n], qh[kk], bl0, bl1);
+                }
+            }
+            bool over = false;
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int hf = e >> 1;
+                    const int p = base + sub + 8 * n + 2 * tq + (e & 1);
+                    s[n][e] = p < vis[hf] ? s[n][e] * qinv[hf] * ks_inv : -INFINITY;
+                    over |= s[n][e] > mrow[hf] + kLazyMargin;
+                }
+            if (__any_sync(0xffffffffu, over)) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    float x = fmaxf(fmaxf(s[0][2 * hf], s[0][2 * hf + 1]), fmaxf(s[1][2 * hf], s[1][2 * hf + 1]));
+                    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+                    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+                    const float nm = fmaxf(mrow[hf], x);
+                    const float al = mrow[hf] == -INFINITY ? 0.f : __expf(mrow[hf] - nm);
+                    mrow[hf] = nm;
+                    lrow[hf] *= al;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        o[nt][2 * hf] *= al;
+                        o[nt][2 * hf + 1] *= al;
+                    }
+                }
+            }
+            float p[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    p[n][e] = __expf(s[n][e] - mrow[e >> 1]);
+                    lrow[e >> 1] += p[n][e];
+                }
+            unsigned ph[4], pl[4];
+            split_f16x2(p[0][0] * 2048.f, p[0][1] * 2048.f, ph[0], pl[0]);
+            split_f16x2(p[0][2] * 2048.f, p[0][3] * 2048.f, ph[1], pl[1]);
+            split_f16x2(p[1][0] * 2048.f, p[1][1] * 2048.f, ph[2], pl[2]);
+            split_f16x2(p[1][2] * 2048.f, p[1][3] * 2048.f, ph[3], pl[3]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                // B = V: (k = position sub + 2tq, + 1 | + 8, + 9; n = d 8nt + gq), scaled by the tile's power of two
+                const int d = 8 * nt + gq;
+                const float va = *f32_at(vst, sub + 2 * tq, d);
+                const float vb = *f32_at(vst, sub + 2 * tq + 1, d);
+                const float vc = *f32_at(vst, sub + 2 * tq + 8, d);
+                const float vd = *f32_at(vst, sub + 2 * tq + 9, d);
+                unsigned bh0, bl0, bh1, bl1;
+                split_f16x2(va * vs_up, vb * vs_up, bh0, bl0);
+                split_f16x2(vc * vs_up, vd * vs_up, bh1, bl1);
+                float t4[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(t4, ph, bh0, bh1);
+                mma16816(t4, pl, bh0, bh1);
+                mma16816(t4, ph, bl0, bl1);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[nt][e] = fmaf(t4[e], vs_inv, o[nt][e]);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && i + kChunkRing < nblk) issue(i + kChunkRing);
+    }
+    if (failed) {
+        if (threadIdx.x == 0)
+            for (int i = 0; i < kChunkRing && i < nblk; ++i)
+                for (unsigned spin = 0; spin < kAttnSpin && !bar_try(&bars[i], 0) && !bar_try(&bars[i], 1); ++spin) {
+                }
+        return;
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        lrow[hf] += __shfl_xor_sync(0xffffffffu, lrow[hf], 1);
+        lrow[hf] += __shfl_xor_sync(0xffffffffu, lrow[hf], 2);
+    }
+    if (!warp_live) return;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        if (!live[hf]) continue;
+        const int m = gq + 8 * hf;
+        const int r = warp * RW + m / G;
+        const float inv = 1.f / (lrow[hf] * 2048.f);
+        float* op = a.out + (long long)(t0 + r) * a.hq * D + (h * G + m % G) * D;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float2*>(op + 8 * nt + 2 * tq) = make_float2(o[nt][2 * hf] * inv, o[nt][2 * hf + 1] * inv);
+    }
+}
+
 // Tensor-core paged attention for int8 KV (head_dim 64 or 128, blocks of a
 // multiple of 16 slots).  CTA and ring as attn_mma_kernel (three stages
 // per warp, four CTAs per SM: a stage is half the bytes); one TMA box per K or V run of a block (rows of
@@ -1849,14 +2140,38 @@ bool mma_i8_ok(const AttnArgs& a) {
     return (long long)a.max_blocks * (a.block_stride / D) < (1ll << 31);
 }
 
-constexpr long long chunk_smem_bytes(int D, int tpb) { return 1024 + (long long)kChunkRing * 2 * (D / 64) * tpb * 128; }
+constexpr long long chunk_smem_bytes(int D, int tpb, int elem = 2) {
+    return 1024 + (long long)kChunkRing * 2 * (D * elem / 128) * tpb * 128;
+}
+
+// The F32 pool as rows of D floats, boxes of 32 floats x tpb rows, 128-byte swizzle.
+CUtensorMap kv_map_f32(const AttnArgs& a, int D) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t((long long)a.max_blocks * (a.block_stride / D))};
+    const cuuint64_t strides[1] = {cuuint64_t(D) * 4};
+    const cuuint32_t box[2] = {32, cuuint32_t(a.tpb)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(a.kv), dims,
+                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
 
 template <int D, int G>
 void run_chunk(const AttnArgs& a, cudaStream_t s) {
-    const int smem = int(chunk_smem_bytes(D, a.tpb));
-    TVARA_CUDA(cudaFuncSetAttribute(attn_chunk_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const CUtensorMap map = kv_map_f16(a, D);
-    attn_chunk_kernel<D, G><<<dim3(a.n_chunk, a.hkv), kAttnWarps * 32, smem, s>>>(map, a);
+    if (a.kv_f16) {
+        const int smem = int(chunk_smem_bytes(D, a.tpb));
+        TVARA_CUDA(cudaFuncSetAttribute(attn_chunk_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        const CUtensorMap map = kv_map_f16(a, D);
+        attn_chunk_kernel<D, G><<<dim3(a.n_chunk, a.hkv), kAttnWarps * 32, smem, s>>>(map, a);
+    } else {
+        const int smem = int(chunk_smem_bytes(D, a.tpb, 4));
+        TVARA_CUDA(cudaFuncSetAttribute(attn_chunk_f32_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        const CUtensorMap map = kv_map_f32(a, D);
+        attn_chunk_f32_kernel<D, G><<<dim3(a.n_chunk, a.hkv), kAttnWarps * 32, smem, s>>>(map, a);
+    }
 }
 
 template <int D>
@@ -1955,15 +2270,18 @@ void run_d(const AttnArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb) {
-    if (!kv_f16 || (dim != 64 && dim != 128) || group < 1 || group > 8 || tpb % 16 || tpb > 256) return 0;
-    if (chunk_smem_bytes(dim, tpb) > 200 * 1024) return 0;
+int attention_chunk_rows(int kv_kind, int dim, int group, int tpb) {
+    if (kv_kind > 1 || (dim != 64 && dim != 128) || group < 1 || group > 8 || tpb % 16 || tpb > 256) return 0;
+    if (chunk_smem_bytes(dim, tpb, kv_kind == 1 ? 2 : 4) > 200 * 1024) return 0;
     return kAttnWarps * (16 / group);
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_chunk > 0) {
-        if (!attention_chunk_rows(a.kv_f16, a.dim, a.hq / a.hkv, a.tpb) || !mma_ok(a))
+        const int kind = a.kv_i8 ? 2 : a.kv_f16 ? 1 : 0;
+        const bool addressable = reinterpret_cast<std::uintptr_t>(a.kv) % 16 == 0 &&
+                                 (long long)a.max_blocks * (a.block_stride / a.dim) < (1ll << 31);
+        if (!attention_chunk_rows(kind, a.dim, a.hq / a.hkv, a.tpb) || !addressable)
             throw std::invalid_argument("chunk attention does not apply to this pool");
         if (a.dim == 64) run_chunk_g<64>(a, s);
         else run_chunk_g<128>(a, s);

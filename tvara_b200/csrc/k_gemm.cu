@@ -975,28 +975,33 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // ---------------------------------------------------------------------------
 // The same two-MMA Q4_K product without the FP16 plane in memory: the A
 // operand sc*q is built in shared memory from the packed rows at every
-// K-step.  Per K-step (one 32-element sub-block) a packed warp loads the 16
-// packed bytes of each of the tile's 128 rows (2 KB) into a ring of its own,
-// kPkStages deep, running ahead of the main stages; the eight epilogue warps,
-// which the epilogue keeps busy only about a tenth of the time, turn them
-// into the 64-byte swizzled K-major rows the MMA reads as soon as the MMA has
-// released the stage: thread (row r, half h) takes the low (h = 0) or high
-// (h = 1) nibbles of the row's 16 bytes -- elements 16h .. 16h + 15 -- builds
-// 1024 + q as FP16 pairs with one byte permute per pair and gets sc*q =
-// (1024 + q)*sc - 1024*sc from one fused multiply-add per pair, exact because
-// sc*q is an integer below 1024 and the fused result is rounded once.  DRAM
-// then carries the packed 0.5625 bytes per weight plus about 0.16 bytes of
+// K-step.  Roles, by warpgroup (setmaxnreg gives each its own register
+// budget: 200 for the epilogue, 64 for the producers, 48 for the rest):
+//   warps 0-7   epilogue: TMEM lane = weight row, warps w and w+4 take token
+//               columns [0, 128) and [128, 256); each block's accumulator is
+//               added with its scale d into registers, the tile stored at the
+//               end (as tc_gemm_q4k_kernel);
+//   warps 8-11  producers: thread r (0..127) turns weight row r's 16 packed
+//               bytes of a K-step into the 64-byte swizzled K-major row the
+//               MMA reads -- 1024 + q as FP16 pairs from one byte permute per
+//               pair, sc*q = (1024 + q)*sc - 1024*sc from one fused
+//               multiply-add per pair, exact because sc*q is an integer below
+//               1024 and the fused result is rounded once;
+//   warp 12     issues the MMAs; warp 13 the TMA loads of x (and the min-term
+//               tiles) into the main stages; warp 14 the TMA loads of the
+//               packed codes (128 rows x 16 bytes per K-step) into a ring of
+//               its own, kPkStages deep, ahead of the producers.
+// DRAM carries the packed 0.5625 bytes per weight plus about 0.16 bytes of
 // side arrays (qsc, qscale, the min-term split) instead of the plane's 2.
-// Barriers: full (x tiles landed and eight producer warps arrived; the MMA
-// waits), empty (MMAs done with the stage; the TMA warp and the producers
-// wait), pk_full / pk_empty for the packed ring.  The producers drain block
-// j's accumulator once they have produced kLead K-steps past it, so the
-// MMAs keep running through the drain.
+// Barriers: full (x tiles landed and the four producer warps arrived; the MMA
+// waits), empty (MMAs done with the stage; TMA warp and producers wait),
+// pk_full / pk_empty (packed ring), acc_full / acc_empty (block accumulators).
 constexpr int kPackedTile = kBM * 16;  // packed bytes of one K-step of a tile
 constexpr int kPkStages = 8;
-constexpr int kLead = 3;               // K-steps produced past a block before draining it
-constexpr int kPkWarp = 10;
-constexpr int kQ4kpThreads = 352;      // 8 producer / epilogue warps, MMA, TMA, packed
+constexpr int kProducerWarpsP = 4;
+constexpr int kProducerWarp0 = 8;
+constexpr int kMmaWarpQ = 12, kTmaWarpQ = 13, kPkWarpQ = 14;
+constexpr int kQ4kpThreads = 512;
 
 __global__ void __launch_bounds__(kQ4kpThreads, 1)
     tc_gemm_q4kp_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
@@ -1024,12 +1029,12 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1 + kEpilogueWarps);
+            mbar_init(&full[s], 1 + kProducerWarpsP);
             mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < kPkStages; ++s) {
             mbar_init(&pk_full[s], 1);
-            mbar_init(&pk_empty[s], kEpilogueWarps);
+            mbar_init(&pk_empty[s], kProducerWarpsP);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -1038,7 +1043,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarpP) {
+    if (warp == kMmaWarpQ) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -1048,63 +1053,65 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const unsigned tmem = *tmem_slot;
 
-    if (warp == kTmaWarpP || warp == kPkWarp) {
-        // TMA warp: x tiles (and the min-term tiles) into the main stages;
-        // packed warp: the packed codes of the production steps into its ring
-        const bool pk = warp == kPkWarp;
-        unsigned issued = 0, phase = 0;
-        int qq = 0;
-        bool go = true;
-        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
-            int row0, tok0, kstep0;
-            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int steps = pk ? a.k_steps : a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
-            for (int ks = 0; ks < steps; ++ks, ++qq) {
-                int ok = 1;
-                if (lane == 0) {
-                    const int ring = pk ? kPkStages : kStages;
-                    const int s = qq % ring;
-                    const unsigned ph = (qq / ring) & 1;
-                    ok = !*abort_flag && mbar_wait(pk ? &pk_empty[s] : &empty[s], ph ^ 1, abort_flag, a.err, 11, false);
-                    if (ok && pk) {
-                        mbar_expect_tx(&pk_full[s], kPackedTile);
-                        tma_load_2d(smem_u32(pk_ring + s * kPackedTile), &map_pk, (kstep0 + ks) * kBK / 2, row0,
-                                    smem_u32(&pk_full[s]));
-                    } else if (ok) {
-                        unsigned char* st = stages + s * stage_bytes;
-                        const unsigned bar = smem_u32(&full[s]);
-                        if (ks < a.k_steps) {
-                            const int k0 = (kstep0 + ks) * kBK;
-                            mbar_expect_tx(&full[s], 2 * b_bytes);
-                            tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
-                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
-                        } else {
-                            const int c0 = (ks - a.k_steps) * kBK;
-                            mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
-                            tma_load_2d(smem_u32(st), &map_mhi, c0, row0, bar);
-                            tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
-                            tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
-                            tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
+    if (warp >= kMmaWarpQ) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 48;");
+        if (warp == kTmaWarpQ || warp == kPkWarpQ) {
+            // TMA warp: x tiles (and the min-term tiles) into the main stages;
+            // packed warp: the packed codes of the production steps into its ring
+            const bool pk = warp == kPkWarpQ;
+            unsigned issued = 0, phase = 0;
+            int qq = 0;
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+                const int steps = pk ? a.k_steps : a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+                for (int ks = 0; ks < steps; ++ks, ++qq) {
+                    int ok = 1;
+                    if (lane == 0) {
+                        const int ring = pk ? kPkStages : kStages;
+                        const int s = qq % ring;
+                        const unsigned ph = (qq / ring) & 1;
+                        ok = !*abort_flag && mbar_wait(pk ? &pk_empty[s] : &empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                        if (ok && pk) {
+                            mbar_expect_tx(&pk_full[s], kPackedTile);
+                            tma_load_2d(smem_u32(pk_ring + s * kPackedTile), &map_pk, (kstep0 + ks) * kBK / 2, row0,
+                                        smem_u32(&pk_full[s]));
+                        } else if (ok) {
+                            unsigned char* st = stages + s * stage_bytes;
+                            const unsigned bar = smem_u32(&full[s]);
+                            if (ks < a.k_steps) {
+                                const int k0 = (kstep0 + ks) * kBK;
+                                mbar_expect_tx(&full[s], 2 * b_bytes);
+                                tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
+                                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
+                            } else {
+                                const int c0 = (ks - a.k_steps) * kBK;
+                                mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
+                                tma_load_2d(smem_u32(st), &map_mhi, c0, row0, bar);
+                                tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
+                                tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
+                                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
+                            }
+                        }
+                        if (ok) {
+                            issued |= 1u << s;
+                            phase = (phase & ~(1u << s)) | (ph << s);
                         }
                     }
-                    if (ok) {
-                        issued |= 1u << s;
-                        phase = (phase & ~(1u << s)) | (ph << s);
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                        go = false;
+                        break;
                     }
-                }
-                if (!__shfl_sync(0xffffffffu, ok, 0)) {
-                    go = false;
-                    break;
                 }
             }
-        }
-        if (lane == 0)
-            for (int s = 0; s < (pk ? kPkStages : kStages); ++s)
-                if (issued >> s & 1u)
-                    for (unsigned i = 0; i < kSpinLimit && !mbar_try(pk ? &pk_full[s] : &full[s], (phase >> s) & 1u); ++i) {
-                    }
-    } else if (warp == kMmaWarpP) {
-        if (lane == 0) {
+            if (lane == 0)
+                for (int s = 0; s < (pk ? kPkStages : kStages); ++s)
+                    if (issued >> s & 1u)
+                        for (unsigned i = 0; i < kSpinLimit && !mbar_try(pk ? &pk_full[s] : &full[s], (phase >> s) & 1u);
+                             ++i) {
+                        }
+        } else if (warp == kMmaWarpQ && lane == 0) {
             int qq = 0, gb = 0;
             bool go = true;
             for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
@@ -1145,34 +1152,23 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                 }
             }
         }
-    } else {
-        // producers and epilogue: thread (r, hf); TMEM lane r = weight row
-        // row0 + r; warps w and w+4 share lanes 32*(w%4).. and take token
-        // columns [0, 128) and [128, 256), and the low / high nibbles
-        const int r = threadIdx.x % kBM;
-        const int hf = threadIdx.x / kBM;
-        int gb = 0, qq = 0, pq = 0;
+    } else if (warp >= kProducerWarp0) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+        // producers: thread r = weight row row0 + r, both nibble halves
+        const int r = threadIdx.x - kProducerWarp0 * 32;
+        int qq = 0, pq = 0;
         bool go = true;
         for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
             int row0, tok0, kstep0;
             tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
             const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
             const long long row = row0 + r;
             const bool live = row < a.w.rows;
             const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
-            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
-            // the sub-block scales of a block (8 bytes) and the block scales
-            // are loaded a block ahead of use, off the producers' critical path
+            // sub-block scales of a block (8 bytes), loaded a block ahead
             uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
             uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
-            float d_next = live && q.blocks > 0 ? qs_row[0] : 0.f;
-            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
-            float acc[128];
-#pragma unroll
-            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
-            int drained = 0;
-            for (int p = 0; p < steps && go; ++p, ++qq) {
+            for (int p = 0; p < steps; ++p, ++qq) {
                 const int s = qq % kStages;
                 const unsigned ph = (qq / kStages) & 1;
                 // the stage is free once the MMAs of its previous use are done
@@ -1187,7 +1183,10 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                         go = false;
                         break;
                     }
-                    unsigned char* st = stages + s * stage_bytes;
+                    const uint4 w = *reinterpret_cast<const uint4*>(pk_ring + ps * kPackedTile + r * 16);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
+                    ++pq;
                     if ((p & 7) == 0 && p > 0) {
                         sc_cur = sc_next;
                         sc_next = live && p + 8 < a.k_steps ? __ldg(reinterpret_cast<const uint2*>(sc_row + p + 8))
@@ -1196,69 +1195,83 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     const unsigned sc = (((p & 4) ? sc_cur.y : sc_cur.x) >> (8 * (p & 3))) & 255u;
                     const __half2 sc2 = __half2half2(__uint2half_rn(sc));
                     const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
-                    // two 8-byte halves of the row's 16 bytes: elements 16 hf + 0..7, then + 8..15
+                    unsigned char* st = stages + s * stage_bytes;
+                    const unsigned words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        const uint2 w = *reinterpret_cast<const uint2*>(pk_ring + ps * kPackedTile + r * 16 + c * 8);
-                        unsigned out[4];
+                    for (int hf = 0; hf < 2; ++hf)      // low nibbles: elements 0..15, high: 16..31
 #pragma unroll
-                        for (int k = 0; k < 2; ++k) {
-                            const unsigned word = k ? w.y : w.x;
-                            const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
-                            const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
-                            const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
-                            const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
-                            const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
-                            out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
-                            out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                        for (int c = 0; c < 2; ++c) {   // 16-byte chunk 2 hf + c: elements 16 hf + 8 c .. + 7
+                            unsigned out[4];
+#pragma unroll
+                            for (int k = 0; k < 2; ++k) {
+                                const unsigned word = words[2 * c + k];
+                                const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+                                const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
+                                const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
+                                const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
+                                const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
+                                out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
+                                out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                            }
+                            *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + c)) = make_uint4(out[0], out[1], out[2], out[3]);
                         }
-                        *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + c)) = make_uint4(out[0], out[1], out[2], out[3]);
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
-                    ++pq;
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
-                // drain blocks whose MMAs are kLead steps behind (all at the tile's last step)
-                while (go && drained < nb) {
-                    const int end = drained < q.blocks ? 8 * (drained + 1) : steps;
-                    if (p + 1 < steps && end + kLead > p + 1) break;
-                    if (end > p + 1) break;
-                    const int b = gb & 1;
-                    const float scale = drained < q.blocks ? d_next : min_scale;
-                    if (drained + 1 < q.blocks) d_next = live ? qs_row[drained + 1] : 0.f;
-                    if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
-                        go = false;
-                        break;
-                    }
-                    asm volatile("tcgen05.fence::after_thread_sync;");
+            }
+        }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
+        // epilogue: TMEM lane r = weight row row0 + r; warps w and w+4 share
+        // lanes 32*(w%4).. and take token columns [0, 128) and [128, 256)
+        const int r = threadIdx.x % kBM;
+        const int hf = threadIdx.x / kBM;
+        int gb = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+            const long long row = row0 + r;
+            const bool live = row < a.w.rows;
+            float acc[128];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
-                        unsigned u[32];
-                        const unsigned taddr =
-                            tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
-                        asm volatile(
-                            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                            : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
-                              "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
-                              "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]),
-                              "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]),
-                              "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
-                            : "r"(taddr));
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
-                    }
-                    asm volatile("tcgen05.fence::before_thread_sync;");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[b]);
-                    ++gb;
-                    ++drained;
+            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
+            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
+            float next = live && q.blocks > 0 ? qs_row[0] : 0.f;
+            for (int j = 0; j < nb; ++j, ++gb) {
+                const int b = gb & 1;
+                const float scale = !live ? 0.f : j < q.blocks ? next : min_scale;
+                if (live && j + 1 < q.blocks) next = qs_row[j + 1];
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
+                    go = false;
+                    break;
                 }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
+                    unsigned u[32];
+                    const unsigned taddr =
+                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                        : "r"(taddr));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
             }
             if (!go) break;
             // store, 32 token columns at a time (as tc_gemm_q4k_kernel)
@@ -1309,7 +1322,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
-    if (warp == kMmaWarpP) {
+    if (warp == kMmaWarpQ) {
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));

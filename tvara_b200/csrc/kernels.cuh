@@ -140,10 +140,10 @@ struct AttnArgs {
     int n_chunk = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
-// Rows per chunk the chunk kernel takes for this shape (F16 pool, head_dim 64
-// or 128, 1..8 query heads per KV head, blocks of a multiple of 16 slots), 0
-// when it does not apply.
-int attention_chunk_rows(bool kv_f16, int dim, int group, int tpb);
+// Rows per chunk the chunk kernels take for this shape (kv_kind 0 = F32 or
+// 1 = F16 pool, head_dim 64 or 128, 1..8 query heads per KV head, blocks of a
+// multiple of 16 slots), 0 when they do not apply (int8 pools: kv_kind 2).
+int attention_chunk_rows(int kv_kind, int dim, int group, int tpb);
 
 // ---- output ---------------------------------------------------------------
 // argmax of each row (first index of the maximum; NaN counts as maximal);

@@ -105,7 +105,7 @@ AttnLayout layout_for(const tvara_attention_args* a) {
     }
     L.plan = tvara::plan_attention(
         vis, off, int(a->block_tokens), int(a->kv_heads), kPartsCap, 148,
-        tvara::attention_chunk_rows(a->kv_dtype == TVARA_KV_F16, int(a->head_dim), int(a->heads / a->kv_heads),
+        tvara::attention_chunk_rows(int(a->kv_dtype), int(a->head_dim), int(a->heads / a->kv_heads),
                                     int(a->block_tokens)));
     std::size_t at = 0;
     L.off_tables = at;
