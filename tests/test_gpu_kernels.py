@@ -342,22 +342,24 @@ def test_attention_block_size_seven_and_many_rows(capi):
         assert attn_close(got[i], ref)
 
 
+@pytest.mark.parametrize("kv", ["f16", "f32"])
 @pytest.mark.parametrize("dim,heads,kv_heads,tpb", [(128, 32, 8, 16), (128, 16, 2, 32), (64, 8, 8, 16),
                                                     (64, 16, 8, 16), (128, 8, 4, 16), (64, 9, 3, 16),
                                                     (128, 12, 2, 16), (64, 7, 1, 32)])
-def test_attention_prefill_chunks(capi, dim, heads, kv_heads, tpb):
+def test_attention_prefill_chunks(capi, dim, heads, kv_heads, tpb, kv):
     """Chunked prefill (attention.hpp:85-89 fused_prompt_attention): query
     rows at consecutive positions of one sequence, row i seeing
-    [0, start + i].  Runs of rows go to the chunk kernel (one K/V read per
-    chunk of 64 / G rows) for F16 pools; ragged chunk lengths (1..70 rows),
-    contexts to 3k, NaN-poisoned tail slots, and a few single decode rows in
-    the same launch."""
+    [0, start + i].  Runs of rows go to the chunk kernels (one K/V read per
+    chunk of 4 * floor(16 / G) rows; F16 pools and F32 pools, the latter as
+    exact hi + lo F16 pairs); ragged chunk lengths (1..70 rows), contexts to
+    3k, unused tail slots, and a few single decode rows in the same launch."""
+    dtype, code, tol = KV_DTYPES[kv]
     rng = np.random.default_rng(dim + heads + tpb)
     lens, rows_of = [], []
     for n, r in [(40, 40), (700, 33), (3000, 70), (17, 5), (129, 2), (1, 1), (256, 16), (900, 1), (64, 17)]:
         lens.append(n)
         rows_of.append(r)
-    pool = Pool(1, kv_heads, dim, tpb, sum((n + tpb - 1) // tpb for n in lens) + 4, dtype=np.float16, rng=rng)
+    pool = Pool(1, kv_heads, dim, tpb, sum((n + tpb - 1) // tpb for n in lens) + 4, dtype=dtype, rng=rng)
     tables, offs, vis, toff = [], [], [], []
     for n, r in zip(lens, rows_of):
         o = len(tables)
@@ -367,7 +369,7 @@ def test_attention_prefill_chunks(capi, dim, heads, kv_heads, tpb):
             toff.append(o)
         offs.append(o)
     q = rng.standard_normal((len(vis), heads * dim)).astype(np.float32)
-    got = run_attention(capi, pool, 0, heads, q, tables, toff, vis, kv_dtype=1)
+    got = run_attention(capi, pool, 0, heads, q, tables, toff, vis, kv_dtype=code)
     k = 0
     for s, (n, r) in enumerate(zip(lens, rows_of)):
         ids = tables[offs[s]:offs[s] + (n + tpb - 1) // tpb]

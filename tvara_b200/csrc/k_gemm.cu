@@ -1362,8 +1362,10 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const unsigned (&a)[4],
 }
 
 constexpr int small_xs(int chunk) { return chunk * 2 + 32; }  // bytes per token row (padded)
+// x hi / lo rows, the sub-block sums of x, and the chunk's min terms of the CTA's rows
 constexpr std::size_t small_smem_bytes(int nt) {
-    return std::size_t(8 * nt) * small_xs(kSmallChunk) * 2 + std::size_t(8 * nt) * (kSmallChunk / 32) * 4;
+    return std::size_t(8 * nt) * small_xs(kSmallChunk) * 2 + std::size_t(8 * nt) * (kSmallChunk / 32) * 4 +
+           std::size_t(kSmallRows) * (kSmallChunk / 32) * 4;
 }
 
 template <int NT>  // 8-token tiles: up to 8 * NT tokens
@@ -1379,6 +1381,7 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMat
     unsigned char* xh_s = small_smem;
     unsigned char* xl_s = xh_s + MT * XS;
     float* sx_s = reinterpret_cast<float*>(xl_s + MT * XS);  // [MT][CU] sub-block sums (x 2^(shift - 5))
+    float* mn_s = sx_s + MT * CU;                             // [rows][CU] dmin*m * 32 of the CTA's rows
     const int units = w.cols / 32, kblocks = w.cols / 256;
     const int u0 = blockIdx.y * (kslice / 32);  // first sub-block of this CTA
     const int su = kslice / 32;
@@ -1423,6 +1426,28 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMat
             const int t = i / cu, u = i % cu;
             const long long off = (long long)t * units + u0 + c0 + u;
             sx_s[t * CU + u] = t < tokens ? __half2float(shi[off]) + __half2float(slo[off]) : 0.f;
+        }
+        // the min terms of this chunk, for all the CTA's rows (off the sub-block loop's critical path):
+        // thread (row, 8 sub-blocks) issues its three loads at once
+        for (int i = threadIdx.x; i < kSmallRows * (cu / 8); i += blockDim.x) {
+            const int rr = i / (cu / 8), g = i % (cu / 8);
+            const long long row = (long long)blockIdx.x * kSmallRows + rr;
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (row < w.rows) {
+                const long long off = row * units + u0 + c0 + 8 * g;  // a multiple of 8: 16-byte aligned
+                const uint4 hi = __ldg(reinterpret_cast<const uint4*>(w.qmin_hi + off));
+                const uint4 lo = __ldg(reinterpret_cast<const uint4*>(w.qmin_lo + off));
+                const float f = pow2(-w.qmin_shift[row]) * 32.f;
+                const unsigned hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const unsigned short hh = (unsigned short)(hw[k >> 1] >> (16 * (k & 1)));
+                    const unsigned short ll = (unsigned short)(lw[k >> 1] >> (16 * (k & 1)));
+                    v[k] = (__half2float(__ushort_as_half(hh)) + __half2float(__ushort_as_half(ll))) * f;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mn_s[rr * CU + 8 * g + k] = v[k];
         }
         __syncthreads();
         for (int uu = 0; uu < cu; uu += kSmallDepth) {
@@ -1482,12 +1507,8 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMat
             }
         }
         // min term of this chunk: - sum_sub dmin*m * sum(x) (sums are x 2^(shift - 5): times 32)
-        const float ia = live_a ? pow2(-w.qmin_shift[ra]) * 32.f : 0.f;
-        const float ib = live_b ? pow2(-w.qmin_shift[rb]) * 32.f : 0.f;
         for (int u = 0; u < cu; ++u) {
-            const long long ua = ra * units + u0 + c0 + u, ub = rb * units + u0 + c0 + u;
-            const float ma = (__half2float(__ushort_as_half(w.qmin_hi[ua])) + __half2float(__ushort_as_half(w.qmin_lo[ua]))) * ia;
-            const float mb = (__half2float(__ushort_as_half(w.qmin_hi[ub])) + __half2float(__ushort_as_half(w.qmin_lo[ub]))) * ib;
+            const float ma = mn_s[(warp * 16 + gq) * CU + u], mb = mn_s[(warp * 16 + gq + 8) * CU + u];
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
                 const float s0 = sx_s[(8 * n + 2 * tq) * CU + u], s1 = sx_s[(8 * n + 2 * tq + 1) * CU + u];
