@@ -81,7 +81,7 @@ typedef struct tvara_open_options {
     uint32_t tp_size;          /* tensor-parallel group size; 0 or 1 = no TP */
     const void* nccl_id;       /* 128-byte ncclUniqueId shared by the group (tp_size > 1) */
     uint32_t weight_planes;    /* tensor-core forms of the projections for batches of >= 5 tokens:
-                                  Q4_K rows (width a multiple of 256, >= 1024) read packed, with
+                                  Q4_K rows (width a multiple of 256) read packed, with
                                   side arrays of sub-block scales, block scales and minima (about
                                   0.16 bytes per weight), other types as exact FP16 hi/lo planes of
                                   their values (4 bytes per weight, like the reference's F32

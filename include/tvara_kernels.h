@@ -30,8 +30,8 @@ TVARA_API int tvara_dequantize(int type, const void* blocks, size_t nblocks, flo
 /* Bytes of the engine's packed layout for a [rows][cols] matrix: the codes of
  * every row (16-byte aligned rows), then the block headers, then one signed
  * byte per row (the power-of-two scale of the tensor-core path), each part at
- * a 256-byte aligned offset.  Q4_K rows whose width is a multiple of 256 and
- * at least 1024 are followed by the side arrays the tensor-core path reads
+ * a 256-byte aligned offset.  Q4_K rows (width a multiple of 256) are
+ * followed by the side arrays the tensor-core path reads
  * beside the packed codes (sub-block scales, block scales, the split minima:
  * about 0.16 bytes per weight). */
 TVARA_API size_t tvara_packed_bytes(int type, size_t rows, size_t cols);

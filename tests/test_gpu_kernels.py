@@ -146,6 +146,21 @@ def test_tensor_core_matmul_matches_oracle(capi, kind, tokens):
     assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
 
 
+@pytest.mark.parametrize("tokens", [5, 33, 64, 65, 200, 512])
+@pytest.mark.parametrize("rows,cols", [(331, 256), (129, 512), (1000, 768)])
+def test_narrow_q4k_rows_matches_oracle(capi, tokens, rows, cols):
+    """Q4_K rows of one to three blocks (a tensor-parallel shard of o_proj is
+    512 wide at 8 ranks): the min-term tile of the tensor-core kernels is
+    wider than the row's sub-blocks (the copy fills the rest with zeros), and
+    the small-batch kernel runs a single short chunk."""
+    rng = np.random.default_rng(tokens * 13 + rows + cols)
+    raw = make_weights(gguf.Q4_K, rows, cols, rng)
+    x = (rng.standard_normal((tokens, cols)) * rng.uniform(0.01, 30, (tokens, 1))).astype(np.float32)
+    got = matmul(capi, gguf.Q4_K, packed(capi, gguf.Q4_K, raw, rows, cols), rows, cols, x)
+    ref, mag = oracle_matmul(gguf.Q4_K, raw, rows, cols, x)
+    assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
+
+
 @pytest.mark.parametrize("kind", [gguf.Q4_K, gguf.Q8_0, gguf.Q4_0])
 def test_quant_matmul_standalone_config_shape(capi, kind):
     """BASELINE standalone config: 11008 x 4096, d/dmin ~ U(0.001, 0.05)."""

@@ -15,6 +15,8 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 ATOL = 2e-3
+NEXT = [5, 77, 300, 41]
+THEN = [6, 7, 8, 9]
 
 
 def _rank(rank, world, nccl_id, path, prompts, out, allreduce):
@@ -34,8 +36,8 @@ def _rank(rank, world, nccl_id, path, prompts, out, allreduce):
         last = np.stack([m.logits(s, p[-1]) for s, p in zip(seqs, prompts)])
         # a decode step with the vocabulary-split head's gathered argmax and
         # the device sampler over the reassembled rows
-        step, am = m.batch_step(seqs, [[5], [77], [300]], logits=True, argmax=True, finite_argmax=True)
-        smp = m.batch_sample(seqs, [[6], [7], [8]], repetition=1.2, top_k=5, logits=True)
+        step, am = m.batch_step(seqs, [[t] for t in NEXT], logits=True, argmax=True, finite_argmax=True)
+        smp = m.batch_sample(seqs, [[t] for t in THEN], repetition=1.2, top_k=5, logits=True)
         np.savez(out % rank, chunk=chunk, last=last, step=step, am=am, s_logits=smp["logits"], s_am=smp["argmax"],
                  s_ids=smp["top_ids"])
 
@@ -59,7 +61,9 @@ def test_tp2_matches_oracle(tiny_path, tmp_path, allreduce):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     rng = np.random.default_rng(8)
-    prompts = [rng.integers(0, 512, n).tolist() for n in (9, 3, 17)]
+    # the 300-token prompt makes the chunk step's allreduce run on more CTAs
+    # than the one-token calls after it (the barrier counts must follow)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (9, 3, 17, 300)]
     out = str(tmp_path / "rank%d.npz")
     nccl_id = _nccl_unique_id()
     ctx = mp.get_context("spawn")
@@ -75,7 +79,7 @@ def test_tp2_matches_oracle(tiny_path, tmp_path, allreduce):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     r0, r1 = np.load(out % 0), np.load(out % 1)
     assert np.array_equal(r0["chunk"], r1["chunk"]) and np.array_equal(r0["last"], r1["last"])
-    oracle = OracleModel(tiny_path, max_positions=64)
+    oracle = OracleModel(tiny_path, max_positions=320)
     refs = [oracle.forward(p) for p in prompts]
     want_chunk = np.concatenate([r[:-1] for r in refs])
     want_last = np.stack([r[-1] for r in refs])
@@ -84,11 +88,11 @@ def test_tp2_matches_oracle(tiny_path, tmp_path, allreduce):
     for k in ("step", "am", "s_logits", "s_am", "s_ids"):
         assert np.array_equal(r0[k], r1[k]), k
     assert np.array_equal(r0["am"], np.argmax(r0["step"], axis=1))
-    refs = [oracle.forward(p + [t]) for p, t in zip(prompts, [5, 77, 300])]
+    refs = [oracle.forward(p + [t]) for p, t in zip(prompts, NEXT)]
     assert np.abs(r0["step"] - np.stack([r[-1] for r in refs])).max() <= ATOL
     from oracle import sampler
-    hist = [p + [t, u] for p, t, u in zip(prompts, [5, 77, 300], [6, 7, 8])]
-    for i in range(3):
+    hist = [p + [t, u] for p, t, u in zip(prompts, NEXT, THEN)]
+    for i in range(len(prompts)):
         adj = sampler.adjust(r0["s_logits"][i], hist[i], 1.2)
         ids, _ = sampler.top_candidates(adj, 5)
         assert r0["s_am"][i] == int(np.argmax(adj)) and r0["s_ids"][i].tolist() == ids.tolist()

@@ -279,7 +279,7 @@ void Engine::load(const gguf::File& f) {
         // Q4_K rows: the two-MMA factorisation, from the packed rows (side
         // arrays only; default) or from a prebuilt FP16 plane of sc*q (mode 4)
         auto q4k_form = [&](const DeviceMatrix* m) {
-            return opt_.weight_planes != 3 && m->type == kQ4_K && m->cols % 256 == 0 && m->cols >= 1024;
+            return opt_.weight_planes != 3 && m->type == kQ4_K && m->cols % 256 == 0;
         };
         const bool q4k_plane = opt_.weight_planes == 4;
         auto form_bytes = [&](const DeviceMatrix* m) -> std::size_t {

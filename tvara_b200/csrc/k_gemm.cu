@@ -28,6 +28,8 @@
 // All TMA loads are per-CTA loads of this GPU's own memory.  Every mbarrier
 // wait is bounded: on timeout the kernel records an error code, waits
 // (bounded) for its own TMA copies, frees TMEM and exits.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -110,6 +112,14 @@ __device__ __forceinline__ void mma_f16(unsigned tmem_d, std::uint64_t a, std::u
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
         "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// A from tensor memory (lane = row, column = 2 K elements, even element in
+// the low half), B from shared memory.
+__device__ __forceinline__ void mma_f16_ts(unsigned tmem_d, unsigned tmem_a, std::uint64_t b, unsigned idesc, int acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -1003,6 +1013,17 @@ constexpr int kProducerWarp0 = 8;
 constexpr int kMmaWarpQ = 12, kTmaWarpQ = 13, kPkWarpQ = 14;
 constexpr int kQ4kpThreads = 512;
 
+// kTmemA: the producers write sc*q into a ring of kStages 16-column slots of
+// tensor memory (columns kTmemACol..511, the producer thread's own lane = its
+// weight row) with tcgen05.st, and the MMAs read A from there; shared memory
+// then carries only the activation tiles (and the min term), which is what
+// bounds the shared-memory form (A written once and read twice per K-step).
+// The two block accumulators then take kQ4kpAccCols = 224 columns each, so
+// token tiles are at most 224 wide.
+constexpr unsigned kTmemACol = 448;
+constexpr int kQ4kpTmemMaxN = 224;
+
+template <bool kTmemA>
 __global__ void __launch_bounds__(kQ4kpThreads, 1)
     tc_gemm_q4kp_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                         const __grid_constant__ CUtensorMap map_pk, const __grid_constant__ CUtensorMap map_mhi,
@@ -1026,6 +1047,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = a.w.cols / 256;  // blocks per row
     const int units = a.w.cols / 32;     // sub-blocks per row
+    constexpr unsigned kAccCols = kTmemA ? 224u : 256u;  // columns per block accumulator
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -1125,7 +1147,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    const unsigned acc = tmem + unsigned(b * 256);
+                    const unsigned acc = tmem + unsigned(b) * kAccCols;
                     const bool minterm = j == q.blocks;
                     const int n_steps = minterm ? q.min_steps : 256 / kBK;
                     for (int ks = 0; ks < n_steps; ++ks, ++qq) {
@@ -1139,12 +1161,23 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                         unsigned char* st = stages + s * stage_bytes;
                         const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
                         const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
+                        if (kTmemA && !minterm) {
+                            // A from the stage's tensor-memory slot: 8 columns per 16 K elements
+                            const unsigned at = tmem + kTmemACol + unsigned(s * 16);
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk) {
-                            const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
-                            mma_f16(acc, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
-                            mma_f16(acc, ahi + adv, blo + adv, a.idesc, 1);
-                            if (minterm) mma_f16(acc, alo + adv, bhi + adv, a.idesc, 1);
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                                mma_f16_ts(acc, at + unsigned(kk * 8), bhi + adv, a.idesc, ks > 0 || kk > 0);
+                                mma_f16_ts(acc, at + unsigned(kk * 8), blo + adv, a.idesc, 1);
+                            }
+                        } else {
+#pragma unroll
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                                mma_f16(acc, ahi + adv, bhi + adv, a.idesc, ks > 0 || kk > 0);
+                                mma_f16(acc, ahi + adv, blo + adv, a.idesc, 1);
+                                if (minterm) mma_f16(acc, alo + adv, bhi + adv, a.idesc, 1);
+                            }
                         }
                         mma_commit(&empty[s]);
                     }
@@ -1176,6 +1209,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     go = false;
                     break;
                 }
+                if (kTmemA) asm volatile("tcgen05.fence::after_thread_sync;");
                 if (p < a.k_steps) {
                     const int ps = pq % kPkStages;
                     const unsigned pph = (pq / kPkStages) & 1;
@@ -1213,9 +1247,24 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                                 out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
                                 out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
                             }
-                            *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + c)) = make_uint4(out[0], out[1], out[2], out[3]);
+                            if (kTmemA) {
+                                // elements 8 (2 hf + c) .. + 7: columns 4 (2 hf + c) .. + 3 of the slot
+                                const unsigned taddr = tmem + ((unsigned)((warp % 4) * 32) << 16) + kTmemACol +
+                                                       unsigned(s * 16 + (2 * hf + c) * 4);
+                                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+                                             "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
+                                             : "memory");
+                            } else {
+                                *reinterpret_cast<uint4*>(st + sw64(r, 2 * hf + c)) =
+                                    make_uint4(out[0], out[1], out[2], out[3]);
+                            }
                         }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    if (kTmemA) {
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        asm volatile("tcgen05.fence::before_thread_sync;");
+                    } else {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
@@ -1255,7 +1304,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
                     unsigned u[32];
                     const unsigned taddr =
-                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b * 256 + hf * 128 + c * 32);
+                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b) * kAccCols + unsigned(hf * 128 + c * 32);
                     asm volatile(
                         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -1648,12 +1697,12 @@ struct TilePlan {
 // which is nonlinear).  Per tile: K-steps x (width + a fixed per-step cost)
 // plus a fixed cost for the pipeline fill and the epilogue (which grows with
 // the width and, for split K, with the atomic accumulation).
-TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sms) {
+TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sms, int max_n = kMaxN) {
     TilePlan best{0, 0, 0};
     double best_cost = 0;
-    for (int tt = (tokens + kMaxN - 1) / kMaxN; tt <= (tokens + 15) / 16 && tt <= 64; ++tt) {
+    for (int tt = (tokens + max_n - 1) / max_n; tt <= (tokens + 15) / 16 && tt <= 64; ++tt) {
         const int width = (((tokens + tt - 1) / tt) + 15) / 16 * 16;
-        if (width > kMaxN) continue;
+        if (width > max_n) continue;
         const int token_tiles = (tokens + width - 1) / width;
         for (int sp = 1; sp <= 16; sp *= 2) {
             if (sp > 1 && (!can_split || steps % sp || steps / sp < 8)) break;
@@ -1745,8 +1794,15 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     }
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
-    TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count());
     const bool q4k_form = g.w.qplane || g.w.qsc;
+    // the packed Q4_K kernel keeps A in tensor memory unless TVARA_Q4K_A=smem
+    // (the shared-memory form, kept for comparison)
+    static const bool q4k_smem_a = [] {
+        const char* v = std::getenv("TVARA_Q4K_A");
+        return v && std::strcmp(v, "smem") == 0;
+    }();
+    const bool tmem_a = !g.w.qplane && g.w.qsc && !q4k_smem_a;
+    TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count(), tmem_a ? kQ4kpTmemMaxN : kMaxN);
     if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
     const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
@@ -1790,8 +1846,16 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
             if (g.w.qs_row % 16 || reinterpret_cast<std::uintptr_t>(g.w.qs) % 16)
                 throw std::invalid_argument("packed Q4_K rows must be 16-byte aligned");
             const int smem_p = smem + kPkStages * kPackedTile;
-            TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
-            tc_gemm_q4kp_kernel<<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+            if (tmem_a) {
+                if (n_tile > kQ4kpTmemMaxN) throw std::logic_error("token tile too wide for the tensor-memory A form");
+                TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                smem_p));
+                tc_gemm_q4kp_kernel<true><<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+            } else {
+                TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                smem_p));
+                tc_gemm_q4kp_kernel<false><<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
+            }
         }
         TVARA_LAUNCHED();
         return;

@@ -33,7 +33,7 @@ int guarded(F&& body) {
 std::size_t align256(std::size_t n) { return (n + 255) & ~std::size_t(255); }
 
 // Q4_K rows the tensor-core path reads packed (with side arrays).
-bool has_q4k_side(int type, std::size_t cols) { return type == tvara::kQ4_K && cols % 256 == 0 && cols >= 1024; }
+bool has_q4k_side(int type, std::size_t cols) { return type == tvara::kQ4_K && cols % 256 == 0 && cols > 0; }
 
 tvara::DeviceMatrix packed_view(int type, const void* packed, std::size_t rows, std::size_t cols) {
     std::size_t e = 0, w = 0;

@@ -32,8 +32,10 @@ public:
 private:
     int rank_ = 0, size_ = 1, sms_ = 148;
     std::size_t capacity_ = 0;
-    unsigned epoch_ = 0;
-    unsigned* counters_ = nullptr;  // this rank's two barrier counters
+    // cumulative values this rank's counters reach once the last call issued
+    // completes: arrivals, ranks done, this rank's CTAs done
+    unsigned arrived_ = 0, done_ = 0, ctas_ = 0;
+    unsigned* counters_ = nullptr;  // this rank's three barrier counters
     float* bufs_[kMaxPeerRanks] = {};
     unsigned* cnts_[kMaxPeerRanks] = {};
     std::vector<void*> opened_;
