@@ -926,9 +926,9 @@ void Engine::run(Sub& s, float* logits, std::uint32_t* argmax, std::size_t) {
         }
     }
     TVARA_CUDA(cudaStreamSynchronize(stream_));
+    profile_collect();  // before the idle stamp: reading the events is profiling cost, not the step's
     host_idle_since_ = std::chrono::steady_clock::now();
     host_idle_valid_ = true;
-    profile_collect();
     if (*err_host_) {
         const int code = *err_host_;
         TVARA_CUDA(cudaMemsetAsync(err_, 0, sizeof(int), stream_));

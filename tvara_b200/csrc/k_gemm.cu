@@ -999,29 +999,56 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 //               1024 and the fused result is rounded once;
 //   warp 12     issues the MMAs; warp 13 the TMA loads of x (and the min-term
 //               tiles) into the main stages; warp 14 the TMA loads of the
-//               packed codes (128 rows x 16 bytes per K-step) into a ring of
-//               its own, kPkStages deep, ahead of the producers.
+//               packed codes (128 rows x 16 bytes per K-step; four K-steps a
+//               stage in the tensor-memory form) into a ring of its own,
+//               ahead of the producers.
 // DRAM carries the packed 0.5625 bytes per weight plus about 0.16 bytes of
 // side arrays (qsc, qscale, the min-term split) instead of the plane's 2.
 // Barriers: full (x tiles landed and the four producer warps arrived; the MMA
 // waits), empty (MMAs done with the stage; TMA warp and producers wait),
 // pk_full / pk_empty (packed ring), acc_full / acc_empty (block accumulators).
-constexpr int kPackedTile = kBM * 16;  // packed bytes of one K-step of a tile
 constexpr int kPkStages = 8;
 constexpr int kProducerWarpsP = 4;
 constexpr int kProducerWarp0 = 8;
 constexpr int kMmaWarpQ = 12, kTmaWarpQ = 13, kPkWarpQ = 14;
 constexpr int kQ4kpThreads = 512;
 
-// kTmemA: the producers write sc*q into a ring of kStages 16-column slots of
-// tensor memory (columns kTmemACol..511, the producer thread's own lane = its
-// weight row) with tcgen05.st, and the MMAs read A from there; shared memory
-// then carries only the activation tiles (and the min term), which is what
-// bounds the shared-memory form (A written once and read twice per K-step).
-// The two block accumulators then take kQ4kpAccCols = 224 columns each, so
-// token tiles are at most 224 wide.
-constexpr unsigned kTmemACol = 448;
-constexpr int kQ4kpTmemMaxN = 224;
+// Two forms of the A operand:
+//   kTmemA = false: producers write sc*q into the stage's shared-memory A
+//     tile (64-byte swizzled K-major rows); 4 stages of A + x tiles.
+//   kTmemA = true: producers write sc*q into tensor memory with tcgen05.st
+//     (the producer thread's own lane = its weight row, 16 columns per
+//     K-step) and the MMAs read A from there, so a shared-memory stage holds
+//     only the x_hi / x_lo tiles (24 KB at the 192-token maximum) and the
+//     ring can be 8 deep.  The depth is what matters: a stage comes back to
+//     the TMA warp only when its MMAs complete, about 1700-2500 cycles after
+//     they were issued (measured with clock stamps), and its x tiles take
+//     about 1000 cycles more to land from L2, so a 4-deep ring caps the pace
+//     at one K-step per ~1000 cycles against ~350 cycles of MMA work at a
+//     176-token tile.  Tensor memory: two block accumulators of 192 columns
+//     and 8 A slots of 16 columns.  The min term uses the same slots: each
+//     32-unit chunk is two ring steps, the first with the rows' qmin_hi as A
+//     (times the hi and lo sub-block sums), the second with qmin_lo (times
+//     the hi sums); the producers copy those 64-byte rows from global memory
+//     into the slot.
+template <bool kTmemA>
+struct Q4kpForm {
+    static constexpr int kRing = kTmemA ? 8 : kStages;
+    static constexpr int kMaxTok = kTmemA ? 192 : kMaxN;
+    static constexpr int kBTile = kMaxTok * kBK * 2;                   // one x_hi or x_lo tile
+    static constexpr int kStageBytes = kTmemA ? 2 * kBTile : 2 * kATile + 2 * kBTileMax;
+    static constexpr unsigned kAccCols = kTmemA ? 192u : 256u;         // columns per block accumulator
+    static constexpr unsigned kACol = 384;                             // first A slot column (TMEM form)
+    // packed-code ring: K-steps per stage (TMA box of 16 bytes per step per row), depth
+    static constexpr int kPkSteps = kTmemA ? 4 : 1;
+    static constexpr int kPkDepth = kTmemA ? 4 : kPkStages;
+    static constexpr int kPkBytes = kBM * 16 * kPkSteps;
+    static constexpr int kBarrierBytes = 512;
+    static constexpr int smem_bytes() {
+        return kRing * kStageBytes + kPkDepth * kPkBytes + 1024 + kBarrierBytes;
+    }
+};
+constexpr int kQ4kpTmemMaxN = Q4kpForm<true>::kMaxTok;
 
 template <bool kTmemA>
 __global__ void __launch_bounds__(kQ4kpThreads, 1)
@@ -1032,29 +1059,36 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     const TcArgs& a = q.t;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    using F = Q4kpForm<kTmemA>;
+    constexpr int kSt = F::kRing;
     const int b_bytes = a.n_tile * kBK * 2;
-    const int stage_bytes = 2 * kATile + 2 * kBTileMax;
+    const int stage_bytes = F::kStageBytes;
     unsigned char* stages = base;
-    unsigned char* pk_ring = base + kStages * stage_bytes;
-    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(pk_ring + kPkStages * kPackedTile);
-    std::uint64_t* empty = full + kStages;
-    std::uint64_t* pk_full = empty + kStages;
-    std::uint64_t* pk_empty = pk_full + kPkStages;
-    std::uint64_t* acc_full = pk_empty + kPkStages;  // [2] block accumulator ready
+    unsigned char* pk_ring = base + kSt * stage_bytes;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(pk_ring + F::kPkDepth * F::kPkBytes);
+    std::uint64_t* empty = full + kSt;
+    std::uint64_t* pk_full = empty + kSt;
+    std::uint64_t* pk_empty = pk_full + F::kPkDepth;
+    std::uint64_t* acc_full = pk_empty + F::kPkDepth;  // [2] block accumulator ready
     std::uint64_t* acc_empty = acc_full + 2;         // [2] epilogue done with it
     unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = a.w.cols / 256;  // blocks per row
     const int units = a.w.cols / 32;     // sub-blocks per row
-    constexpr unsigned kAccCols = kTmemA ? 224u : 256u;  // columns per block accumulator
+    constexpr unsigned kAccCols = F::kAccCols;
+    // operand tiles of a stage: A (shared-memory form only) and x
+    auto tile_bhi = [&](unsigned char* st) { return kTmemA ? st : st + 2 * kATile; };
+    auto tile_blo = [&](unsigned char* st) { return kTmemA ? st + F::kBTile : st + 2 * kATile + kBTileMax; };
+    // ring steps of a tile's min term: TMEM form two per 32-unit chunk
+    const int min_ring = kTmemA ? 2 * q.min_steps : q.min_steps;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kSt; ++s) {
             mbar_init(&full[s], 1 + kProducerWarpsP);
             mbar_init(&empty[s], 1);
         }
-        for (int s = 0; s < kPkStages; ++s) {
+        for (int s = 0; s < F::kPkDepth; ++s) {
             mbar_init(&pk_full[s], 1);
             mbar_init(&pk_empty[s], kProducerWarpsP);
         }
@@ -1087,17 +1121,17 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
             for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
                 int row0, tok0, kstep0;
                 tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-                const int steps = pk ? a.k_steps : a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+                const int steps = pk ? a.k_steps / F::kPkSteps : a.k_steps + (kstep0 == 0 ? min_ring : 0);
                 for (int ks = 0; ks < steps; ++ks, ++qq) {
                     int ok = 1;
                     if (lane == 0) {
-                        const int ring = pk ? kPkStages : kStages;
+                        const int ring = pk ? F::kPkDepth : kSt;
                         const int s = qq % ring;
                         const unsigned ph = (qq / ring) & 1;
                         ok = !*abort_flag && mbar_wait(pk ? &pk_empty[s] : &empty[s], ph ^ 1, abort_flag, a.err, 11, false);
                         if (ok && pk) {
-                            mbar_expect_tx(&pk_full[s], kPackedTile);
-                            tma_load_2d(smem_u32(pk_ring + s * kPackedTile), &map_pk, (kstep0 + ks) * kBK / 2, row0,
+                            mbar_expect_tx(&pk_full[s], F::kPkBytes);
+                            tma_load_2d(smem_u32(pk_ring + s * F::kPkBytes), &map_pk, (kstep0 + ks * F::kPkSteps) * kBK / 2, row0,
                                         smem_u32(&pk_full[s]));
                         } else if (ok) {
                             unsigned char* st = stages + s * stage_bytes;
@@ -1105,15 +1139,22 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                             if (ks < a.k_steps) {
                                 const int k0 = (kstep0 + ks) * kBK;
                                 mbar_expect_tx(&full[s], 2 * b_bytes);
-                                tma_load_2d(smem_u32(st + 2 * kATile), &map_xhi, k0, tok0, bar);
-                                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_xlo, k0, tok0, bar);
+                                tma_load_2d(smem_u32(tile_bhi(st)), &map_xhi, k0, tok0, bar);
+                                tma_load_2d(smem_u32(tile_blo(st)), &map_xlo, k0, tok0, bar);
+                            } else if (kTmemA) {
+                                // min term: sub-block sums of x (hi; and lo on the qmin_hi step)
+                                const int mi = ks - a.k_steps;
+                                const int c0 = (mi >> 1) * kBK;
+                                mbar_expect_tx(&full[s], (mi & 1 ? 1 : 2) * b_bytes);
+                                tma_load_2d(smem_u32(tile_bhi(st)), &map_shi, c0, tok0, bar);
+                                if (!(mi & 1)) tma_load_2d(smem_u32(tile_blo(st)), &map_slo, c0, tok0, bar);
                             } else {
                                 const int c0 = (ks - a.k_steps) * kBK;
                                 mbar_expect_tx(&full[s], 2 * kATile + 2 * b_bytes);
                                 tma_load_2d(smem_u32(st), &map_mhi, c0, row0, bar);
                                 tma_load_2d(smem_u32(st + kATile), &map_mlo, c0, row0, bar);
-                                tma_load_2d(smem_u32(st + 2 * kATile), &map_shi, c0, tok0, bar);
-                                tma_load_2d(smem_u32(st + 2 * kATile + kBTileMax), &map_slo, c0, tok0, bar);
+                                tma_load_2d(smem_u32(tile_bhi(st)), &map_shi, c0, tok0, bar);
+                                tma_load_2d(smem_u32(tile_blo(st)), &map_slo, c0, tok0, bar);
                             }
                         }
                         if (ok) {
@@ -1128,7 +1169,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                 }
             }
             if (lane == 0)
-                for (int s = 0; s < (pk ? kPkStages : kStages); ++s)
+                for (int s = 0; s < (pk ? F::kPkDepth : kSt); ++s)
                     if (issued >> s & 1u)
                         for (unsigned i = 0; i < kSpinLimit && !mbar_try(pk ? &pk_full[s] : &full[s], (phase >> s) & 1u);
                              ++i) {
@@ -1149,28 +1190,30 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;");
                     const unsigned acc = tmem + unsigned(b) * kAccCols;
                     const bool minterm = j == q.blocks;
-                    const int n_steps = minterm ? q.min_steps : 256 / kBK;
+                    const int n_steps = minterm ? min_ring : 256 / kBK;
                     for (int ks = 0; ks < n_steps; ++ks, ++qq) {
-                        const int s = qq % kStages;
-                        const unsigned ph = (qq / kStages) & 1;
+                        const int s = qq % kSt;
+                        const unsigned ph = (qq / kSt) & 1;
                         if (!mbar_wait(&full[s], ph, abort_flag, a.err, 13, false)) {
                             go = false;
                             break;
                         }
                         asm volatile("tcgen05.fence::after_thread_sync;");
                         unsigned char* st = stages + s * stage_bytes;
-                        const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
-                        const std::uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTileMax);
-                        if (kTmemA && !minterm) {
-                            // A from the stage's tensor-memory slot: 8 columns per 16 K elements
-                            const unsigned at = tmem + kTmemACol + unsigned(s * 16);
+                        const std::uint64_t bhi = smem_desc(tile_bhi(st)), blo = smem_desc(tile_blo(st));
+                        if (kTmemA) {
+                            // A from the step's tensor-memory slot: 8 columns per 16 K elements; on
+                            // the min term's qmin_lo steps (odd) only the hi sums
+                            const unsigned at = tmem + F::kACol + unsigned(s * 16);
+                            const bool two = !minterm || !(ks & 1);
 #pragma unroll
                             for (int kk = 0; kk < kBK / 16; ++kk) {
                                 const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
                                 mma_f16_ts(acc, at + unsigned(kk * 8), bhi + adv, a.idesc, ks > 0 || kk > 0);
-                                mma_f16_ts(acc, at + unsigned(kk * 8), blo + adv, a.idesc, 1);
+                                if (two) mma_f16_ts(acc, at + unsigned(kk * 8), blo + adv, a.idesc, 1);
                             }
                         } else {
+                            const std::uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
 #pragma unroll
                             for (int kk = 0; kk < kBK / 16; ++kk) {
                                 const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
@@ -1185,6 +1228,114 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                 }
             }
         }
+    } else if (kTmemA && warp >= kProducerWarp0) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+        // producers, tensor-memory form: thread r = weight row row0 + r.  Ring
+        // steps go in groups of up to four (one packed-ring stage holds four
+        // K-steps): the group's slot waits and full arrivals are issued by
+        // lanes 0..G-1 together, so the barrier latency is paid once a group.
+        const int r = threadIdx.x - kProducerWarp0 * 32;
+        const unsigned lane_row = (unsigned)((warp % 4) * 32) << 16;
+        int qq = 0, pq = 0;
+        bool go = true;
+        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+            int row0, tok0, kstep0;
+            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+            const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
+            const long long row = row0 + r;
+            const bool live = row < a.w.rows;
+            const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
+            uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
+            uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
+            for (int p = 0; p < steps;) {
+                const bool main = p < a.k_steps;  // main steps come in whole blocks of 8
+                const int G = main ? F::kPkSteps : min(F::kPkSteps, steps - p);
+                // the group's slots are free once the MMAs of their previous use are done
+                bool ok = true;
+                if (lane < G) {
+                    const int q2 = qq + lane;
+                    ok = mbar_wait(&empty[q2 % kSt], ((q2 / kSt) & 1) ^ 1, abort_flag, a.err, 16);
+                }
+                if (!__all_sync(0xffffffffu, ok ? 1 : 0)) {
+                    go = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                if (main) {
+                    const int ps = pq % F::kPkDepth;
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&pk_full[ps], (pq / F::kPkDepth) & 1, abort_flag, a.err, 17) ? 1 : 0)) {
+                        go = false;
+                        break;
+                    }
+                    if ((p & 7) == 0 && p > 0) {
+                        sc_cur = sc_next;
+                        sc_next = live && p + 8 < a.k_steps ? __ldg(reinterpret_cast<const uint2*>(sc_row + p + 8))
+                                                            : make_uint2(0, 0);
+                    }
+                    const unsigned char* pk = pk_ring + ps * F::kPkBytes;
+#pragma unroll
+                    for (int i = 0; i < F::kPkSteps; ++i) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(pk + sw64(r, i));
+                        const int pi = p + i;
+                        const unsigned sc = (((pi & 4) ? sc_cur.y : sc_cur.x) >> (8 * (pi & 3))) & 255u;
+                        const __half2 sc2 = __half2half2(__uint2half_rn(sc));
+                        const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
+                        const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
+                        const unsigned words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf)      // low nibbles: elements 0..15, high: 16..31
+#pragma unroll
+                            for (int c = 0; c < 2; ++c) {   // elements 16 hf + 8 c .. + 7: columns 4 (2 hf + c) ..
+                                unsigned out[4];
+#pragma unroll
+                                for (int k = 0; k < 2; ++k) {
+                                    const unsigned word = words[2 * c + k];
+                                    const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+                                    const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
+                                    const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
+                                    const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
+                                    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
+                                    out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
+                                    out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                                }
+                                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                                 slot + unsigned((2 * hf + c) * 4)),
+                                             "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
+                                             : "memory");
+                            }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
+                    ++pq;
+                } else {
+                    // min term: this row's 32 split minima of each chunk (qmin_hi on even
+                    // min steps, qmin_lo on odd ones) into the slot; zero past the row's units
+                    for (int i = 0; i < G; ++i) {
+                        const int mi = p + i - a.k_steps;
+                        const int c0 = (mi >> 1) * kBK;
+                        const unsigned short* src = ((mi & 1) ? a.w.qmin_lo : a.w.qmin_hi) + (live ? row : 0) * units;
+                        const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint4 v = live && c0 + 8 * j < units
+                                                ? __ldg(reinterpret_cast<const uint4*>(src + c0 + 8 * j))
+                                                : make_uint4(0, 0, 0, 0);
+                            asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                             slot + unsigned(j * 4)),
+                                         "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                                         : "memory");
+                        }
+                    }
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane < G) mbar_arrive(&full[(qq + lane) % kSt]);
+                p += G;
+                qq += G;
+            }
+        }
     } else if (warp >= kProducerWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
         // producers: thread r = weight row row0 + r, both nibble halves
@@ -1194,7 +1345,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
             int row0, tok0, kstep0;
             tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int steps = a.k_steps + (kstep0 == 0 ? q.min_steps : 0);
+            const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
             const long long row = row0 + r;
             const bool live = row < a.w.rows;
             const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
@@ -1202,8 +1353,8 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
             uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
             uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
             for (int p = 0; p < steps; ++p, ++qq) {
-                const int s = qq % kStages;
-                const unsigned ph = (qq / kStages) & 1;
+                const int s = qq % kSt;
+                const unsigned ph = (qq / kSt) & 1;
                 // the stage is free once the MMAs of its previous use are done
                 if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err, 16) ? 1 : 0)) {
                     go = false;
@@ -1211,13 +1362,13 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                 }
                 if (kTmemA) asm volatile("tcgen05.fence::after_thread_sync;");
                 if (p < a.k_steps) {
-                    const int ps = pq % kPkStages;
-                    const unsigned pph = (pq / kPkStages) & 1;
+                    const int ps = pq % F::kPkDepth;
+                    const unsigned pph = (pq / F::kPkDepth) & 1;
                     if (!__all_sync(0xffffffffu, mbar_wait(&pk_full[ps], pph, abort_flag, a.err, 17) ? 1 : 0)) {
                         go = false;
                         break;
                     }
-                    const uint4 w = *reinterpret_cast<const uint4*>(pk_ring + ps * kPackedTile + r * 16);
+                    const uint4 w = *reinterpret_cast<const uint4*>(pk_ring + ps * F::kPkBytes + r * 16);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&pk_empty[ps]);
                     ++pq;
@@ -1249,7 +1400,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                             }
                             if (kTmemA) {
                                 // elements 8 (2 hf + c) .. + 7: columns 4 (2 hf + c) .. + 3 of the slot
-                                const unsigned taddr = tmem + ((unsigned)((warp % 4) * 32) << 16) + kTmemACol +
+                                const unsigned taddr = tmem + ((unsigned)((warp % 4) * 32) << 16) + F::kACol +
                                                        unsigned(s * 16 + (2 * hf + c) * 4);
                                 asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
                                              "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
@@ -1265,6 +1416,25 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                     } else {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     }
+                } else if (kTmemA) {
+                    // min term: this row's 32 split minima of the chunk (qmin_hi on even
+                    // steps, qmin_lo on odd ones) into the slot; zero past the row's units
+                    const int mi = p - a.k_steps;
+                    const int c0 = (mi >> 1) * kBK;
+                    const unsigned short* src = ((mi & 1) ? a.w.qmin_lo : a.w.qmin_hi) + (live ? row : 0) * units;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint4 v = live && c0 + 8 * j < units
+                                            ? __ldg(reinterpret_cast<const uint4*>(src + c0 + 8 * j))
+                                            : make_uint4(0, 0, 0, 0);
+                        const unsigned taddr =
+                            tmem + ((unsigned)((warp % 4) * 32) << 16) + F::kACol + unsigned(s * 16 + j * 4);
+                        asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+                                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                                     : "memory");
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    asm volatile("tcgen05.fence::before_thread_sync;");
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
@@ -1652,14 +1822,17 @@ CUtensorMap make_map(const __half* base, int K, int T, int n_tile) {
 
 // Packed Q4_K rows as a 2-D byte tensor: the 16 bytes of one sub-block of
 // each of a tile's 128 rows per box (no swizzle: producers read row r at r*16).
-CUtensorMap make_packed_map(const std::uint8_t* qs, std::size_t row_bytes, int rows) {
+// steps > 1: a box of `steps` sub-blocks (16 * steps bytes) per row, with the
+// 64-byte swizzle (producers read step i of row r at sw64(r, i)).
+CUtensorMap make_packed_map(const std::uint8_t* qs, std::size_t row_bytes, int rows, int steps = 1) {
     CUtensorMap m;
     const cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
     const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
-    const cuuint32_t box[2] = {16, cuuint32_t(kBM)};
+    const cuuint32_t box[2] = {cuuint32_t(16 * steps), cuuint32_t(kBM)};
     const cuuint32_t elem[2] = {1, 1};
     const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<std::uint8_t*>(qs), dims,
-                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                            strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            steps > 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return m;
@@ -1795,13 +1968,13 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     const bool q4k_form = g.w.qplane || g.w.qsc;
-    // the packed Q4_K kernel keeps A in tensor memory unless TVARA_Q4K_A=smem
-    // (the shared-memory form, kept for comparison)
-    static const bool q4k_smem_a = [] {
+    // the packed Q4_K kernel builds A in shared memory; TVARA_Q4K_A=tmem
+    // selects the tensor-memory form (measured slower so far)
+    static const bool q4k_tmem_a = [] {
         const char* v = std::getenv("TVARA_Q4K_A");
-        return v && std::strcmp(v, "smem") == 0;
+        return v && std::strcmp(v, "tmem") == 0;
     }();
-    const bool tmem_a = !g.w.qplane && g.w.qsc && !q4k_smem_a;
+    const bool tmem_a = !g.w.qplane && g.w.qsc && q4k_tmem_a;
     TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count(), tmem_a ? kQ4kpTmemMaxN : kMaxN);
     if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
@@ -1828,7 +2001,8 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         if (steps % (8 * splits)) throw std::logic_error("Q4_K split does not divide the blocks");
         const int units = K / 32;  // sub-block sums written with the split
         const CUtensorMap mq = g.w.qplane ? make_map(reinterpret_cast<const __half*>(g.w.qplane), K, g.w.rows, kBM)
-                                          : make_packed_map(g.w.qs, g.w.qs_row, g.w.rows);
+                                          : make_packed_map(g.w.qs, g.w.qs_row, g.w.rows,
+                                                            tmem_a ? Q4kpForm<true>::kPkSteps : 1);
         const CUtensorMap mmh = make_map(reinterpret_cast<const __half*>(g.w.qmin_hi), units, g.w.rows, kBM);
         const CUtensorMap mml = make_map(reinterpret_cast<const __half*>(g.w.qmin_lo), units, g.w.rows, kBM);
         const CUtensorMap msh = make_map(shi, units, T, n_tile), msl = make_map(slo, units, T, n_tile);
@@ -1845,13 +2019,16 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         } else {
             if (g.w.qs_row % 16 || reinterpret_cast<std::uintptr_t>(g.w.qs) % 16)
                 throw std::invalid_argument("packed Q4_K rows must be 16-byte aligned");
-            const int smem_p = smem + kPkStages * kPackedTile;
             if (tmem_a) {
                 if (n_tile > kQ4kpTmemMaxN) throw std::logic_error("token tile too wide for the tensor-memory A form");
+                constexpr int smem_p = Q4kpForm<true>::smem_bytes();
+                static_assert(smem_p <= 227 * 1024, "tensor-memory A form exceeds shared memory");
                 TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 smem_p));
                 tc_gemm_q4kp_kernel<true><<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
             } else {
+                constexpr int smem_p = Q4kpForm<false>::smem_bytes();
+                static_assert(smem_p <= 227 * 1024, "shared-memory A form exceeds shared memory");
                 TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4kp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 smem_p));
                 tc_gemm_q4kp_kernel<false><<<grid_n, kQ4kpThreads, smem_p, s>>>(mh, ml, mq, mmh, mml, msh, msl, qa, ts);
