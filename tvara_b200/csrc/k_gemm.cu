@@ -1043,6 +1043,15 @@ struct Q4kpForm {
     static constexpr int kPkSteps = kTmemA ? 4 : 1;
     static constexpr int kPkDepth = kTmemA ? 4 : kPkStages;
     static constexpr int kPkBytes = kBM * 16 * kPkSteps;
+    // K-steps per barrier stage: every full / empty round trip (wait, arrive
+    // or commit, the refill behind it) costs each role a few hundred cycles
+    // whatever it covers -- measured on B200, a bare TMA -> MMA ring runs at
+    // ~755 cycles per K-step with one K-step per stage, ~517 with two and
+    // ~447 with four (352 of MMA work at a 176-token tile) -- so the
+    // tensor-memory form synchronises once per four K-steps: two stages over
+    // its eight slots; a tile's steps are padded to whole stages.
+    static constexpr int kSub = kTmemA ? 4 : 1;
+    static constexpr int kStagesB = kRing / kSub;
     static constexpr int kBarrierBytes = 512;
     static constexpr int smem_bytes() {
         return kRing * kStageBytes + kPkDepth * kPkBytes + 1024 + kBarrierBytes;
@@ -1084,7 +1093,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     const int min_ring = kTmemA ? 2 * q.min_steps : q.min_steps;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSt; ++s) {
+        for (int s = 0; s < F::kStagesB; ++s) {
             mbar_init(&full[s], 1 + kProducerWarpsP);
             mbar_init(&empty[s], 1);
         }
@@ -1111,7 +1120,59 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
 
     if (warp >= kMmaWarpQ) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 48;");
-        if (warp == kTmaWarpQ || warp == kPkWarpQ) {
+        if (kTmemA && warp == kTmaWarpQ) {
+            // TMA warp, tensor-memory form: the x tiles of a whole stage (kSub
+            // K-steps) under one expect_tx; min-term steps load the sub-block
+            // sums (hi; and lo on the qmin_hi steps)
+            unsigned issued = 0, phase = 0;
+            int qq = 0;  // ring slot of the stage's first K-step (a multiple of kSub)
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+                const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
+                for (int p0 = 0; p0 < steps && go; p0 += F::kSub, qq += F::kSub) {
+                    int ok = 1;
+                    if (lane == 0) {
+                        const int bs = (qq / F::kSub) % F::kStagesB;
+                        const unsigned ph = (qq / kSt) & 1;
+                        ok = !*abort_flag && mbar_wait(&empty[bs], ph ^ 1, abort_flag, a.err, 11, false);
+                        if (ok) {
+                            const int n = min(F::kSub, steps - p0);
+                            unsigned bytes = 0;
+                            for (int i = 0; i < n; ++i) {
+                                const int p = p0 + i;
+                                bytes += unsigned(p < a.k_steps || !((p - a.k_steps) & 1) ? 2 : 1) * unsigned(b_bytes);
+                            }
+                            mbar_expect_tx(&full[bs], bytes);
+                            const unsigned bar = smem_u32(&full[bs]);
+                            for (int i = 0; i < n; ++i) {
+                                const int p = p0 + i;
+                                unsigned char* st = stages + ((qq + i) % kSt) * stage_bytes;
+                                if (p < a.k_steps) {
+                                    const int k0 = (kstep0 + p) * kBK;
+                                    tma_load_2d(smem_u32(tile_bhi(st)), &map_xhi, k0, tok0, bar);
+                                    tma_load_2d(smem_u32(tile_blo(st)), &map_xlo, k0, tok0, bar);
+                                } else {
+                                    const int mi = p - a.k_steps;
+                                    const int c0 = (mi >> 1) * kBK;
+                                    tma_load_2d(smem_u32(tile_bhi(st)), &map_shi, c0, tok0, bar);
+                                    if (!(mi & 1)) tma_load_2d(smem_u32(tile_blo(st)), &map_slo, c0, tok0, bar);
+                                }
+                            }
+                            issued |= 1u << bs;
+                            phase = (phase & ~(1u << bs)) | (ph << bs);
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) go = false;
+                }
+            }
+            if (lane == 0)
+                for (int bs = 0; bs < F::kStagesB; ++bs)
+                    if (issued >> bs & 1u)
+                        for (unsigned i = 0; i < kSpinLimit && !mbar_try(&full[bs], (phase >> bs) & 1u); ++i) {
+                        }
+        } else if (warp == kTmaWarpQ || warp == kPkWarpQ) {
             // TMA warp: x tiles (and the min-term tiles) into the main stages;
             // packed warp: the packed codes of the production steps into its ring
             const bool pk = warp == kPkWarpQ;
@@ -1174,6 +1235,55 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                         for (unsigned i = 0; i < kSpinLimit && !mbar_try(pk ? &pk_full[s] : &full[s], (phase >> s) & 1u);
                              ++i) {
                         }
+        } else if (kTmemA && warp == kMmaWarpQ && lane == 0) {
+            // MMA thread, tensor-memory form: one full wait and one commit per
+            // stage; a main block (8 K-steps) is two stages, the min block
+            // ceil(min_ring / kSub) (the last one padded)
+            int qq = 0, gb = 0;
+            bool go = true;
+            for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
+                const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+                for (int j = 0; j < nb && go; ++j, ++gb) {
+                    const int b = gb & 1;
+                    if (!mbar_wait(&acc_empty[b], ((gb >> 1) & 1) ^ 1, abort_flag, a.err, 15, false)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const unsigned acc = tmem + unsigned(b) * kAccCols;
+                    const bool minterm = j == q.blocks;
+                    const int n_steps = minterm ? min_ring : 256 / kBK;
+                    for (int p0 = 0; p0 < n_steps; p0 += F::kSub, qq += F::kSub) {
+                        const int bs = (qq / F::kSub) % F::kStagesB;
+                        if (!mbar_wait(&full[bs], (qq / kSt) & 1, abort_flag, a.err, 13, false)) {
+                            go = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;");
+                        const int n = min(F::kSub, n_steps - p0);
+                        for (int i = 0; i < n; ++i) {
+                            const int ks = p0 + i;  // K-step within the block
+                            const int s = (qq + i) % kSt;
+                            unsigned char* st = stages + s * stage_bytes;
+                            const std::uint64_t bhi = smem_desc(tile_bhi(st)), blo = smem_desc(tile_blo(st));
+                            // A from the slot: 8 columns per 16 K elements; on the min term's
+                            // qmin_lo steps (odd) only the hi sums
+                            const unsigned at = tmem + F::kACol + unsigned(s * 16);
+                            const bool two = !minterm || !(ks & 1);
+#pragma unroll
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                                mma_f16_ts(acc, at + unsigned(kk * 8), bhi + adv, a.idesc, ks > 0 || kk > 0);
+                                if (two) mma_f16_ts(acc, at + unsigned(kk * 8), blo + adv, a.idesc, 1);
+                            }
+                        }
+                        mma_commit(&empty[bs]);
+                    }
+                    if (go) mma_commit(&acc_full[b]);
+                }
+            }
         } else if (warp == kMmaWarpQ && lane == 0) {
             int qq = 0, gb = 0;
             bool go = true;
@@ -1247,16 +1357,13 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
             const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
             uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
             uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
-            for (int p = 0; p < steps;) {
+            static_assert(F::kSub == F::kPkSteps, "a stage is one packed-ring stage");
+            for (int p = 0; p < steps; p += F::kSub, qq += F::kSub) {
                 const bool main = p < a.k_steps;  // main steps come in whole blocks of 8
-                const int G = main ? F::kPkSteps : min(F::kPkSteps, steps - p);
-                // the group's slots are free once the MMAs of their previous use are done
-                bool ok = true;
-                if (lane < G) {
-                    const int q2 = qq + lane;
-                    ok = mbar_wait(&empty[q2 % kSt], ((q2 / kSt) & 1) ^ 1, abort_flag, a.err, 16);
-                }
-                if (!__all_sync(0xffffffffu, ok ? 1 : 0)) {
+                const int G = min(F::kSub, steps - p);
+                const int bs = (qq / F::kSub) % F::kStagesB;
+                // the stage's slots are free once the MMAs of their previous use are done
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[bs], ((qq / kSt) & 1) ^ 1, abort_flag, a.err, 16) ? 1 : 0)) {
                     go = false;
                     break;
                 }
@@ -1331,9 +1438,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;");
                 __syncwarp();
-                if (lane < G) mbar_arrive(&full[(qq + lane) % kSt]);
-                p += G;
-                qq += G;
+                if (lane == 0) mbar_arrive(&full[bs]);
             }
         }
     } else if (warp >= kProducerWarp0) {
@@ -1968,13 +2073,13 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     const bool q4k_form = g.w.qplane || g.w.qsc;
-    // the packed Q4_K kernel builds A in shared memory; TVARA_Q4K_A=tmem
-    // selects the tensor-memory form (measured slower so far)
-    static const bool q4k_tmem_a = [] {
+    // the packed Q4_K kernel builds A in tensor memory; TVARA_Q4K_A=smem
+    // selects the shared-memory form (kept for comparison)
+    static const bool q4k_smem_a = [] {
         const char* v = std::getenv("TVARA_Q4K_A");
-        return v && std::strcmp(v, "tmem") == 0;
+        return v && std::strcmp(v, "smem") == 0;
     }();
-    const bool tmem_a = !g.w.qplane && g.w.qsc && q4k_tmem_a;
+    const bool tmem_a = !g.w.qplane && g.w.qsc && !q4k_smem_a;
     TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count(), tmem_a ? kQ4kpTmemMaxN : kMaxN);
     if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
