@@ -51,7 +51,11 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) from small-case ncu captures (profiles/), scaled to the benchmark's launches:
 # attention per distinct K/V position of a launch (its traffic grows with the positions it reads), and the
 # four projection launches of one layer at 512 tokens (their traffic does not depend on the layer count).
-NCU_TRAFFIC = {"attention_per_distinct_position": {}, "projections_per_layer": None}
+# DRAM bytes from small ncu captures (profiles/), scaled by the units a launch
+# processes: attention per distinct K/V position per layer launch (2-layer,
+# 64-request case), the Q4_K projections per layer at 512 tokens (1-layer case:
+# QKV, o_proj, gate/up, down)
+NCU_TRAFFIC = {"attention_per_distinct_position": {"f16": 4150.0}, "projections_per_layer": 227.4e6}
 
 
 def peaks():

@@ -532,11 +532,12 @@ struct TileSpace {
     int token_tiles, row_tiles, splits, n_tiles;
 };
 
+// row_unit: weight rows per tile (kBM; two kBM halves in the CTA-pair form)
 __device__ __forceinline__ void tile_coords(const TileSpace& ts, int t, int n_tile, int k_steps, int& row0, int& tok0,
-                                            int& kstep0) {
+                                            int& kstep0, int row_unit = kBM) {
     const int tt = t % ts.token_tiles;
     const int rest = t / ts.token_tiles;
-    row0 = (rest % ts.row_tiles) * kBM;
+    row0 = (rest % ts.row_tiles) * row_unit;
     tok0 = tt * n_tile;
     kstep0 = (rest / ts.row_tiles) * k_steps;
 }
@@ -1031,6 +1032,64 @@ constexpr int kQ4kpThreads = 512;
 //     (times the hi and lo sub-block sums), the second with qmin_lo (times
 //     the hi sums); the producers copy those 64-byte rows from global memory
 //     into the slot.
+// Cluster (CTA-pair) helpers, used by the pair form below.
+constexpr int kPairRows = 2 * kBM;
+
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the variable at shared::cta address `local` in CTA `rank`
+__device__ __forceinline__ unsigned cluster_addr(unsigned local, unsigned rank) {
+    unsigned r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+// arrival on a barrier of another CTA of the cluster (default semantics, as
+// CUTLASS's 2-SM arrivals: an explicit .release.cluster measured ~0.8 us a
+// call, and the data it guards -- TMA bytes, tensor-memory stores -- is already
+// complete when the arriving thread observed its own barrier)
+__device__ __forceinline__ void mbar_arrive_cluster(unsigned cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// wait on a barrier that the other CTA also signals: default (CTA-scope)
+// semantics, as CUTLASS's cluster barriers -- what it guards is async-proxy
+// data (TMA bytes, MMA completion) or data the signalling thread had already
+// observed complete; an explicit .acquire.cluster cost ~0.4 us a wait
+__device__ __forceinline__ bool mbar_try_cluster(std::uint64_t* bar, unsigned parity) { return mbar_try(bar, parity); }
+// mbar_wait with cluster-scope acquire (arrivals come from the other CTA too)
+__device__ __forceinline__ bool mbar_wait_cluster(std::uint64_t* bar, unsigned parity, volatile int* abort_flag,
+                                                  int* err, int code, bool backoff = true) {
+    for (unsigned i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_cluster(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (backoff && i > 64) __nanosleep(64);
+    }
+    *abort_flag = 1;
+    atomicExch(err, code);
+    return false;
+}
+__device__ __forceinline__ void mma_f16_ts_pair(unsigned tmem_d, unsigned tmem_a, std::uint64_t b, unsigned idesc,
+                                                int acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
+// arrives on the barrier at this shared::cta offset in both CTAs once the MMAs issued so far complete
+__device__ __forceinline__ void mma_commit_pair(std::uint64_t* bar) {
+    const unsigned short both = 3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(both)
+        : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 template <bool kTmemA>
 struct Q4kpForm {
     static constexpr int kRing = kTmemA ? 8 : kStages;
@@ -1058,6 +1117,269 @@ struct Q4kpForm {
     }
 };
 constexpr int kQ4kpTmemMaxN = Q4kpForm<true>::kMaxTok;
+
+// The CTA-pair form's layout.  A stage's x tiles land ~2 us after their TMA
+// issue (measured), so the x ring is four stages of four K-steps: per CTA an
+// x slot holds only N/2 tokens (12 KB at 192), sixteen slots fit in 192 KB.
+// The A ring (sc*q in tensor memory, written by the producers in ~0.6 us a
+// stage) stays two stages of four 16-column slots beside two 192-column block
+// accumulators.  The two rings have their own full / empty barriers; the
+// producers see only the A ring (kRing, kStagesB below).
+struct Q4kPairForm {
+    static constexpr int kRing = 8;      // A slots
+    static constexpr int kRingX = 16;    // x slots
+    static constexpr int kMaxTok = 192;
+    static constexpr int kBTile = (kMaxTok / 2) * kBK * 2;  // one CTA's x_hi or x_lo tile
+    static constexpr int kStageBytes = 2 * kBTile;          // one x slot
+    static constexpr unsigned kAccCols = 192u;
+    static constexpr unsigned kACol = 384;
+    static constexpr int kPkSteps = 4;
+    static constexpr int kPkDepth = 4;
+    static constexpr int kPkBytes = kBM * 16 * kPkSteps;
+    static constexpr int kSub = 4;
+    static constexpr int kStagesB = kRing / kSub;   // A stages
+    static constexpr int kStagesX = kRingX / kSub;  // x stages
+    static constexpr int kBarrierBytes = 512;
+    static constexpr int smem_bytes() {
+        return kRingX * kStageBytes + kPkDepth * kPkBytes + 1024 + kBarrierBytes;
+    }
+};
+static_assert(2 * Q4kPairForm::kAccCols + 16 * Q4kPairForm::kRing <= 512, "pair form exceeds tensor memory");
+constexpr int kQ4kPairMaxN = Q4kPairForm::kMaxTok;
+
+// Producers of the tensor-memory forms (four warps, thread r = weight row
+// row0 + row_off + r): per stage of kSub K-steps, sc*q of the four K-steps of
+// one packed-ring stage (or the min term's split minima) into the stage's
+// tensor-memory slots, then one arrival per warp on the stage's full barrier
+// of this CTA (kPair: the slot waits see the other CTA's commits, cluster
+// scope).
+template <class F, bool kPair>
+__device__ __forceinline__ void q4k_tmem_producers(const Q4kArgs& q, const TileSpace& ts, int t_first, int t_step,
+                                                   int row_off, unsigned tmem, const unsigned char* pk_ring,
+                                                   std::uint64_t* full, std::uint64_t* empty, std::uint64_t* pk_full,
+                                                   std::uint64_t* pk_empty, volatile int* abort_flag) {
+    const TcArgs& a = q.t;
+    constexpr int kSt = F::kRing;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = a.w.cols / 32;
+    const int min_ring = 2 * q.min_steps;
+    auto wait_for = [&](std::uint64_t* bar, unsigned parity, int code) {
+        return kPair ? mbar_wait_cluster(bar, parity, abort_flag, a.err, code) : mbar_wait(bar, parity, abort_flag, a.err, code);
+    };
+    const int r = threadIdx.x - kProducerWarp0 * 32;
+    const unsigned lane_row = (unsigned)((warp % 4) * 32) << 16;
+    int qq = 0, pq = 0;
+    bool go = true;
+    for (int t = t_first; t < ts.n_tiles && go; t += t_step) {
+        int row0, tok0, kstep0;
+        tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPair ? kPairRows : kBM);
+        const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
+        const long long row = row0 + row_off + r;
+        const bool live = row < a.w.rows;
+        const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
+        uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
+        uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
+        static_assert(F::kSub == F::kPkSteps, "a stage is one packed-ring stage");
+        for (int p = 0; p < steps; p += F::kSub, qq += F::kSub) {
+            const bool main = p < a.k_steps;  // main steps come in whole blocks of 8
+            const int G = min(F::kSub, steps - p);
+            const int bs = (qq / F::kSub) % F::kStagesB;
+            // the stage's slots are free once the MMAs of their previous use are done
+            if (!__all_sync(0xffffffffu, wait_for(&empty[bs], ((qq / kSt) & 1) ^ 1, 16) ? 1 : 0)) {
+                go = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            if (main) {
+                const int ps = pq % F::kPkDepth;
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait(&pk_full[ps], (pq / F::kPkDepth) & 1, abort_flag, a.err, 17) ? 1 : 0)) {
+                    go = false;
+                    break;
+                }
+                if ((p & 7) == 0 && p > 0) {
+                    sc_cur = sc_next;
+                    sc_next = live && p + 8 < a.k_steps ? __ldg(reinterpret_cast<const uint2*>(sc_row + p + 8))
+                                                        : make_uint2(0, 0);
+                }
+                const unsigned char* pk = pk_ring + ps * F::kPkBytes;
+#pragma unroll
+                for (int i = 0; i < F::kPkSteps; ++i) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(pk + sw64(r, i));
+                    const int pi = p + i;
+                    const unsigned sc = (((pi & 4) ? sc_cur.y : sc_cur.x) >> (8 * (pi & 3))) & 255u;
+                    const __half2 sc2 = __half2half2(__uint2half_rn(sc));
+                    const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
+                    const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
+                    const unsigned words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf)      // low nibbles: elements 0..15, high: 16..31
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {   // elements 16 hf + 8 c .. + 7: columns 4 (2 hf + c) ..
+                            unsigned out[4];
+#pragma unroll
+                            for (int k = 0; k < 2; ++k) {
+                                const unsigned word = words[2 * c + k];
+                                const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+                                const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
+                                const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
+                                const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
+                                const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
+                                out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
+                                out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
+                            }
+                            asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                             slot + unsigned((2 * hf + c) * 4)),
+                                         "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
+                                         : "memory");
+                        }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pk_empty[ps]);
+                ++pq;
+            } else {
+                // min term: this row's 32 split minima of each chunk (qmin_hi on even
+                // min steps, qmin_lo on odd ones) into the slot; zero past the row's units
+                for (int i = 0; i < G; ++i) {
+                    const int mi = p + i - a.k_steps;
+                    const int c0 = (mi >> 1) * kBK;
+                    const unsigned short* src = ((mi & 1) ? a.w.qmin_lo : a.w.qmin_hi) + (live ? row : 0) * units;
+                    const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint4 v = live && c0 + 8 * j < units
+                                            ? __ldg(reinterpret_cast<const uint4*>(src + c0 + 8 * j))
+                                            : make_uint4(0, 0, 0, 0);
+                        asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                         slot + unsigned(j * 4)),
+                                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                                     : "memory");
+                    }
+                }
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[bs]);
+        }
+    }
+}
+
+// Epilogue of the packed Q4_K kernels (eight warps; TMEM lane r = weight row
+// row0 + row_off + r): per block, d times the block accumulator into
+// registers (the min term with its own scale), the tile stored at the end.
+// kPair: the arrivals that free an accumulator go to rank 0's barrier.
+template <unsigned kAccCols, bool kPair>
+__device__ __forceinline__ void q4k_epilogue(const Q4kArgs& q, const TileSpace& ts, int t_first, int t_step, int row_off,
+                                             unsigned tmem, std::uint64_t* acc_full, std::uint64_t* acc_empty,
+                                             volatile int* abort_flag) {
+    const TcArgs& a = q.t;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = a.w.cols / 256;
+    auto wait_for = [&](std::uint64_t* bar, unsigned parity, int code) {
+        return kPair ? mbar_wait_cluster(bar, parity, abort_flag, a.err, code) : mbar_wait(bar, parity, abort_flag, a.err, code);
+    };
+    // epilogue: TMEM lane r = weight row row0 + r; warps w and w+4 share
+    // lanes 32*(w%4).. and take token columns [0, 128) and [128, 256)
+    const int r = threadIdx.x % kBM;
+    const int hf = threadIdx.x / kBM;
+    int gb = 0;
+    bool go = true;
+    for (int t = t_first; t < ts.n_tiles && go; t += t_step) {
+        int row0, tok0, kstep0;
+        tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPair ? kPairRows : kBM);
+        const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+        const long long row = row0 + row_off + r;
+        const bool live = row < a.w.rows;
+        float acc[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+        const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
+        const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
+        float next = live && q.blocks > 0 ? qs_row[0] : 0.f;
+        for (int j = 0; j < nb; ++j, ++gb) {
+            const int b = gb & 1;
+            const float scale = !live ? 0.f : j < q.blocks ? next : min_scale;
+            if (live && j + 1 < q.blocks) next = qs_row[j + 1];
+            if (!__all_sync(0xffffffffu, wait_for(&acc_full[b], (gb >> 1) & 1, 12) ? 1 : 0)) {
+                go = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
+                unsigned u[32];
+                const unsigned taddr =
+                    tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b) * kAccCols + unsigned(hf * 128 + c * 32);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                      "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                      "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+                      "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+                      "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) {
+                if (kPair) mbar_arrive_cluster(cluster_addr(smem_u32(&acc_empty[b]), 0));
+                else mbar_arrive(&acc_empty[b]);
+            }
+        }
+        if (!go) break;
+        // store, 32 token columns at a time (as tc_gemm_q4k_kernel)
+        for (int c = 0; c < 4; ++c) {
+            const int col0 = hf * 128 + c * 32;
+            if (col0 >= a.n_tile) break;  // warp-uniform
+            float v[32];
+            switch (c) {
+#define TVARA_TAKE(C)                                        \
+case C:                                                  \
+    _Pragma("unroll") for (int jj = 0; jj < 32; ++jj) v[jj] = acc[C * 32 + jj]; \
+    break;
+                TVARA_TAKE(0)
+                TVARA_TAKE(1)
+                TVARA_TAKE(2)
+                TVARA_TAKE(3)
+#undef TVARA_TAKE
+            }
+            const int tl = tok0 + col0 + lane;
+            const float inv_l = tl < a.tokens ? pow2(-a.x_shift[tl]) : 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] *= __shfl_sync(0xffffffffu, inv_l, jj);
+            const int ncol = min(32, min(a.n_tile - col0, a.tokens - (tok0 + col0)));
+            if (a.epilogue == kSwiGLU) {
+                const bool odd = r & 1;
+                float* dst = a.y + (long long)(tok0 + col0 + odd) * a.ldy + row / 2;
+#pragma unroll
+                for (int pr = 0; pr < 16; ++pr) {
+                    const float pe = __shfl_xor_sync(0xffffffffu, v[2 * pr], 1);
+                    const float po = __shfl_xor_sync(0xffffffffu, v[2 * pr + 1], 1);
+                    if (live && 2 * pr + odd < ncol) {
+                        const float g = odd ? po : v[2 * pr];
+                        const float u = odd ? v[2 * pr + 1] : pe;
+                        dst[(long long)(2 * pr) * a.ldy] = swiglu_12(g, u);
+                    }
+                }
+            } else if (live) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    if (jj >= ncol) break;
+                    float* dst = a.y + (long long)(tok0 + col0 + jj) * a.ldy + row;
+                    if (a.atomic || a.epilogue == kAdd) atomicAdd(dst, v[jj]);
+                    else *dst = v[jj];
+                }
+            }
+        }
+    }
+}
+
 
 template <bool kTmemA>
 __global__ void __launch_bounds__(kQ4kpThreads, 1)
@@ -1340,107 +1662,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         }
     } else if (kTmemA && warp >= kProducerWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
-        // producers, tensor-memory form: thread r = weight row row0 + r.  Ring
-        // steps go in groups of up to four (one packed-ring stage holds four
-        // K-steps): the group's slot waits and full arrivals are issued by
-        // lanes 0..G-1 together, so the barrier latency is paid once a group.
-        const int r = threadIdx.x - kProducerWarp0 * 32;
-        const unsigned lane_row = (unsigned)((warp % 4) * 32) << 16;
-        int qq = 0, pq = 0;
-        bool go = true;
-        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
-            int row0, tok0, kstep0;
-            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
-            const long long row = row0 + r;
-            const bool live = row < a.w.rows;
-            const unsigned char* sc_row = a.w.qsc + (live ? row : 0) * (long long)units + kstep0;
-            uint2 sc_cur = live ? __ldg(reinterpret_cast<const uint2*>(sc_row)) : make_uint2(0, 0);
-            uint2 sc_next = live && a.k_steps > 8 ? __ldg(reinterpret_cast<const uint2*>(sc_row + 8)) : make_uint2(0, 0);
-            static_assert(F::kSub == F::kPkSteps, "a stage is one packed-ring stage");
-            for (int p = 0; p < steps; p += F::kSub, qq += F::kSub) {
-                const bool main = p < a.k_steps;  // main steps come in whole blocks of 8
-                const int G = min(F::kSub, steps - p);
-                const int bs = (qq / F::kSub) % F::kStagesB;
-                // the stage's slots are free once the MMAs of their previous use are done
-                if (!__all_sync(0xffffffffu, mbar_wait(&empty[bs], ((qq / kSt) & 1) ^ 1, abort_flag, a.err, 16) ? 1 : 0)) {
-                    go = false;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                if (main) {
-                    const int ps = pq % F::kPkDepth;
-                    if (!__all_sync(0xffffffffu,
-                                    mbar_wait(&pk_full[ps], (pq / F::kPkDepth) & 1, abort_flag, a.err, 17) ? 1 : 0)) {
-                        go = false;
-                        break;
-                    }
-                    if ((p & 7) == 0 && p > 0) {
-                        sc_cur = sc_next;
-                        sc_next = live && p + 8 < a.k_steps ? __ldg(reinterpret_cast<const uint2*>(sc_row + p + 8))
-                                                            : make_uint2(0, 0);
-                    }
-                    const unsigned char* pk = pk_ring + ps * F::kPkBytes;
-#pragma unroll
-                    for (int i = 0; i < F::kPkSteps; ++i) {
-                        const uint4 w = *reinterpret_cast<const uint4*>(pk + sw64(r, i));
-                        const int pi = p + i;
-                        const unsigned sc = (((pi & 4) ? sc_cur.y : sc_cur.x) >> (8 * (pi & 3))) & 255u;
-                        const __half2 sc2 = __half2half2(__uint2half_rn(sc));
-                        const __half2 off2 = __hneg2(__half2half2(__uint2half_rn(1024u * sc)));
-                        const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
-                        const unsigned words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                        for (int hf = 0; hf < 2; ++hf)      // low nibbles: elements 0..15, high: 16..31
-#pragma unroll
-                            for (int c = 0; c < 2; ++c) {   // elements 16 hf + 8 c .. + 7: columns 4 (2 hf + c) ..
-                                unsigned out[4];
-#pragma unroll
-                                for (int k = 0; k < 2; ++k) {
-                                    const unsigned word = words[2 * c + k];
-                                    const unsigned nib = hf ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
-                                    const unsigned p0 = __byte_perm(nib, 0x64646464u, 0x4140);  // 1024 + q, bytes 0, 1
-                                    const unsigned p1 = __byte_perm(nib, 0x64646464u, 0x4342);  // bytes 2, 3
-                                    const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&p0), sc2, off2);
-                                    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&p1), sc2, off2);
-                                    out[2 * k] = *reinterpret_cast<const unsigned*>(&h0);
-                                    out[2 * k + 1] = *reinterpret_cast<const unsigned*>(&h1);
-                                }
-                                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                                 slot + unsigned((2 * hf + c) * 4)),
-                                             "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
-                                             : "memory");
-                            }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
-                    ++pq;
-                } else {
-                    // min term: this row's 32 split minima of each chunk (qmin_hi on even
-                    // min steps, qmin_lo on odd ones) into the slot; zero past the row's units
-                    for (int i = 0; i < G; ++i) {
-                        const int mi = p + i - a.k_steps;
-                        const int c0 = (mi >> 1) * kBK;
-                        const unsigned short* src = ((mi & 1) ? a.w.qmin_lo : a.w.qmin_hi) + (live ? row : 0) * units;
-                        const unsigned slot = tmem + lane_row + F::kACol + unsigned(((qq + i) % kSt) * 16);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const uint4 v = live && c0 + 8 * j < units
-                                                ? __ldg(reinterpret_cast<const uint4*>(src + c0 + 8 * j))
-                                                : make_uint4(0, 0, 0, 0);
-                            asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                             slot + unsigned(j * 4)),
-                                         "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                                         : "memory");
-                        }
-                    }
-                }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                asm volatile("tcgen05.fence::before_thread_sync;");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[bs]);
-            }
-        }
+        q4k_tmem_producers<Q4kpForm<true>, false>(q, ts, blockIdx.x, gridDim.x, 0, tmem, pk_ring, full, empty, pk_full, pk_empty, abort_flag);
     } else if (warp >= kProducerWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
         // producers: thread r = weight row row0 + r, both nibble halves
@@ -1547,102 +1769,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
-        // epilogue: TMEM lane r = weight row row0 + r; warps w and w+4 share
-        // lanes 32*(w%4).. and take token columns [0, 128) and [128, 256)
-        const int r = threadIdx.x % kBM;
-        const int hf = threadIdx.x / kBM;
-        int gb = 0;
-        bool go = true;
-        for (int t = blockIdx.x; t < ts.n_tiles && go; t += gridDim.x) {
-            int row0, tok0, kstep0;
-            tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0);
-            const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
-            const long long row = row0 + r;
-            const bool live = row < a.w.rows;
-            float acc[128];
-#pragma unroll
-            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
-            const float* qs_row = a.w.qscale + (live ? row : 0) * kblocks + kstep0 / 8;
-            const float min_scale = live ? -32.f * pow2(-a.w.qmin_shift[row]) : 0.f;
-            float next = live && q.blocks > 0 ? qs_row[0] : 0.f;
-            for (int j = 0; j < nb; ++j, ++gb) {
-                const int b = gb & 1;
-                const float scale = !live ? 0.f : j < q.blocks ? next : min_scale;
-                if (live && j + 1 < q.blocks) next = qs_row[j + 1];
-                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (gb >> 1) & 1, abort_flag, a.err, 12) ? 1 : 0)) {
-                    go = false;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;");
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (hf * 128 + c * 32 >= a.n_tile) break;  // warp-uniform
-                    unsigned u[32];
-                    const unsigned taddr =
-                        tmem + ((unsigned)((warp % 4) * 32) << 16) + unsigned(b) * kAccCols + unsigned(hf * 128 + c * 32);
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
-                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
-                          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
-                          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
-                          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
-                        : "r"(taddr));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) acc[c * 32 + jj] = fmaf(scale, __uint_as_float(u[jj]), acc[c * 32 + jj]);
-                }
-                asm volatile("tcgen05.fence::before_thread_sync;");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[b]);
-            }
-            if (!go) break;
-            // store, 32 token columns at a time (as tc_gemm_q4k_kernel)
-            for (int c = 0; c < 4; ++c) {
-                const int col0 = hf * 128 + c * 32;
-                if (col0 >= a.n_tile) break;  // warp-uniform
-                float v[32];
-                switch (c) {
-#define TVARA_TAKE(C)                                        \
-    case C:                                                  \
-        _Pragma("unroll") for (int jj = 0; jj < 32; ++jj) v[jj] = acc[C * 32 + jj]; \
-        break;
-                    TVARA_TAKE(0)
-                    TVARA_TAKE(1)
-                    TVARA_TAKE(2)
-                    TVARA_TAKE(3)
-#undef TVARA_TAKE
-                }
-                const int tl = tok0 + col0 + lane;
-                const float inv_l = tl < a.tokens ? pow2(-a.x_shift[tl]) : 0.f;
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) v[jj] *= __shfl_sync(0xffffffffu, inv_l, jj);
-                const int ncol = min(32, min(a.n_tile - col0, a.tokens - (tok0 + col0)));
-                if (a.epilogue == kSwiGLU) {
-                    const bool odd = r & 1;
-                    float* dst = a.y + (long long)(tok0 + col0 + odd) * a.ldy + row / 2;
-#pragma unroll
-                    for (int pr = 0; pr < 16; ++pr) {
-                        const float pe = __shfl_xor_sync(0xffffffffu, v[2 * pr], 1);
-                        const float po = __shfl_xor_sync(0xffffffffu, v[2 * pr + 1], 1);
-                        if (live && 2 * pr + odd < ncol) {
-                            const float g = odd ? po : v[2 * pr];
-                            const float u = odd ? v[2 * pr + 1] : pe;
-                            dst[(long long)(2 * pr) * a.ldy] = swiglu_12(g, u);
-                        }
-                    }
-                } else if (live) {
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) {
-                        if (jj >= ncol) break;
-                        float* dst = a.y + (long long)(tok0 + col0 + jj) * a.ldy + row;
-                        if (a.atomic || a.epilogue == kAdd) atomicAdd(dst, v[jj]);
-                        else *dst = v[jj];
-                    }
-                }
-            }
-        }
+        q4k_epilogue<kAccCols, false>(q, ts, blockIdx.x, gridDim.x, 0, tmem, acc_full, acc_empty, abort_flag);
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -1651,6 +1778,279 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
+}
+
+// ---------------------------------------------------------------------------
+// The CTA-pair form (tcgen05 cta_group::2): a cluster of two CTAs on the two
+// SMs of a TPC computes a 256-row x N-token tile with one M=256 MMA stream.
+// CTA rank r holds weight rows [128 r, 128 r + 128) of the tile -- its
+// producers build their rows' sc*q into its own tensor memory (same slots and
+// lanes as the one-CTA tensor-memory form), its epilogue reads and stores its
+// own 128 x N accumulator -- and x tokens [N/2 r, N/2 r + N/2) of the tile in
+// its shared memory; the MMAs (issued by rank 0) read A and B from both.  Per
+// SM this halves the x bytes streamed from L2 per multiply-add, which is what
+// bounds the one-CTA form.  Barriers: each CTA's TMA and producers complete a
+// stage on that CTA's own full barrier (plain per-CTA TMA loads; a load that
+// completed on the other CTA's barrier measured three times slower per byte);
+// rank 1's MMA-warp lane relays its stage completion with one arrival on rank
+// 0's full barrier; rank 0's acc_empty collects both epilogues; the commits
+// after a stage and after a block arrive on the empty / acc_full barriers of
+// both CTAs.  No load uses multicast.
+// Measured (B200, 6144 x 4096 x 512 tokens): 1.57 us per stage of four K-steps
+// at N = 176 against 0.96 us of MMA issue -- the two-stage A ring waits on the
+// cross-CTA round trip (MMA completion -> both CTAs' producers -> relay) --
+// 86 us against 67 us for the one-CTA form; a four-stage A ring needs N <= 128
+// and is then bound by MMA issue (~100 cycles per M=256 instruction).
+// Warp roles as tc_gemm_q4kp_kernel<true> in both CTAs (rank 1's MMA warp
+// allocates and frees tensor memory with rank 0's and runs the relay); tiles
+// are 256 rows (TileSpace row tiles count pairs of 128-row halves), one per
+// cluster at a time.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ4kpThreads, 1)
+    tc_gemm_q4k2_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                        const __grid_constant__ CUtensorMap map_pk, const __grid_constant__ CUtensorMap map_shi,
+                        const __grid_constant__ CUtensorMap map_slo, Q4kArgs q, TileSpace ts) {
+    const TcArgs& a = q.t;
+    using F = Q4kPairForm;
+    constexpr int kSt = F::kRing;    // A slots (tensor memory)
+    constexpr int kSx = F::kRingX;   // x slots (shared memory)
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the carve-up must sit at the same shared::cta offsets in both CTAs (the
+    // MMA's B descriptors and the commits name one offset for both)
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int half_n = a.n_tile / 2;
+    const int b_bytes = a.n_tile * kBK * 2;  // x bytes of one part (hi or lo) of a K-step, both CTAs
+    const int stage_bytes = F::kStageBytes;
+    unsigned char* stages = base;  // kSx x slots
+    unsigned char* pk_ring = base + kSx * stage_bytes;
+    std::uint64_t* x_full = reinterpret_cast<std::uint64_t*>(pk_ring + F::kPkDepth * F::kPkBytes);
+    std::uint64_t* x_empty = x_full + F::kStagesX;
+    std::uint64_t* full = x_empty + F::kStagesX;   // A ring
+    std::uint64_t* empty = full + F::kStagesB;
+    std::uint64_t* pk_full = empty + F::kStagesB;
+    std::uint64_t* pk_empty = pk_full + F::kPkDepth;
+    std::uint64_t* acc_full = pk_empty + F::kPkDepth;  // [2] block accumulator ready (this CTA's half)
+    std::uint64_t* acc_empty = acc_full + 2;           // [2] rank 0's: both epilogues done with it
+    unsigned* tmem_slot = reinterpret_cast<unsigned*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned rank = cluster_rank();
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int kblocks = a.w.cols / 256;
+    const int units = a.w.cols / 32;
+    constexpr unsigned kAccCols = F::kAccCols;
+    const int min_ring = 2 * q.min_steps;
+    auto tile_bhi = [&](unsigned char* st) { return st; };
+    auto tile_blo = [&](unsigned char* st) { return st + F::kBTile; };
+
+    if (threadIdx.x == 0) {
+        // this CTA's TMA (expect_tx) / producer warps; on rank 0 also rank 1's relay
+        for (int s = 0; s < F::kStagesX; ++s) {
+            mbar_init(&x_full[s], 1 + (rank == 0 ? 1 : 0));
+            mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < F::kStagesB; ++s) {
+            mbar_init(&full[s], kProducerWarpsP + (rank == 0 ? 1 : 0));
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < F::kPkDepth; ++s) {
+            mbar_init(&pk_full[s], 1);
+            mbar_init(&pk_empty[s], kProducerWarpsP);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * kEpilogueWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarpQ) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers initialised before any remote arrival
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp >= kMmaWarpQ) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 48;");
+        if (warp == kTmaWarpQ) {
+            // x tiles of this CTA's half of the tokens, a stage at a time, on
+            // this CTA's own x_full barrier
+            unsigned issued = 0, phase = 0;
+            int qq = 0;
+            bool go = true;
+            for (int t = pair; t < ts.n_tiles && go; t += pairs) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPairRows);
+                const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
+                const int my_tok = tok0 + int(rank) * half_n;
+                for (int p0 = 0; p0 < steps && go; p0 += F::kSub, qq += F::kSub) {
+                    int ok = 1;
+                    if (lane == 0) {
+                        const int bs = (qq / F::kSub) % F::kStagesX;
+                        const unsigned ph = (qq / kSx) & 1;
+                        ok = !*abort_flag && mbar_wait_cluster(&x_empty[bs], ph ^ 1, abort_flag, a.err, 11, false);
+                        if (ok) {
+                            const int n = min(F::kSub, steps - p0);
+                            unsigned bytes = 0;
+                            for (int i = 0; i < n; ++i) {
+                                const int p = p0 + i;
+                                bytes += unsigned(p < a.k_steps || !((p - a.k_steps) & 1) ? 2 : 1) * unsigned(b_bytes / 2);
+                            }
+                            mbar_expect_tx(&x_full[bs], bytes);
+                            const unsigned bar = smem_u32(&x_full[bs]);
+                            for (int i = 0; i < n; ++i) {
+                                const int p = p0 + i;
+                                unsigned char* st = stages + ((qq + i) % kSx) * stage_bytes;
+                                if (p < a.k_steps) {
+                                    const int k0 = (kstep0 + p) * kBK;
+                                    tma_load_2d(smem_u32(tile_bhi(st)), &map_xhi, k0, my_tok, bar);
+                                    tma_load_2d(smem_u32(tile_blo(st)), &map_xlo, k0, my_tok, bar);
+                                } else {
+                                    const int mi = p - a.k_steps;
+                                    const int c0 = (mi >> 1) * kBK;
+                                    tma_load_2d(smem_u32(tile_bhi(st)), &map_shi, c0, my_tok, bar);
+                                    if (!(mi & 1)) tma_load_2d(smem_u32(tile_blo(st)), &map_slo, c0, my_tok, bar);
+                                }
+                            }
+                            issued |= 1u << bs;
+                            phase = (phase & ~(1u << bs)) | (ph << bs);
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) go = false;
+                }
+            }
+            if (lane == 0)
+                for (int bs = 0; bs < F::kStagesX; ++bs)
+                    if (issued >> bs & 1u)
+                        for (unsigned i = 0; i < kSpinLimit && !mbar_try_cluster(&x_full[bs], (phase >> bs) & 1u); ++i) {
+                        }
+        } else if (warp == kPkWarpQ) {
+            // packed codes of this CTA's 128 rows into its own ring
+            unsigned issued = 0, phase = 0;
+            int qq = 0;
+            bool go = true;
+            for (int t = pair; t < ts.n_tiles && go; t += pairs) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPairRows);
+                const int my_row0 = row0 + int(rank) * kBM;
+                const int groups = a.k_steps / F::kPkSteps;
+                for (int g = 0; g < groups; ++g, ++qq) {
+                    int ok = 1;
+                    if (lane == 0) {
+                        const int s = qq % F::kPkDepth;
+                        const unsigned ph = (qq / F::kPkDepth) & 1;
+                        ok = !*abort_flag && mbar_wait(&pk_empty[s], ph ^ 1, abort_flag, a.err, 11, false);
+                        if (ok) {
+                            mbar_expect_tx(&pk_full[s], F::kPkBytes);
+                            tma_load_2d(smem_u32(pk_ring + s * F::kPkBytes), &map_pk, (kstep0 + g * F::kPkSteps) * kBK / 2,
+                                        my_row0, smem_u32(&pk_full[s]));
+                            issued |= 1u << s;
+                            phase = (phase & ~(1u << s)) | (ph << s);
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                        go = false;
+                        break;
+                    }
+                }
+            }
+            if (lane == 0)
+                for (int s = 0; s < F::kPkDepth; ++s)
+                    if (issued >> s & 1u)
+                        for (unsigned i = 0; i < kSpinLimit && !mbar_try(&pk_full[s], (phase >> s) & 1u); ++i) {
+                        }
+        } else if (warp == kMmaWarpQ && lane == 0 && rank == 1) {
+            // relay: once this CTA's x tiles and A slots of a stage are in place,
+            // one arrival on each of rank 0's two full barriers of that stage
+            int qq = 0;
+            bool go = true;
+            for (int t = pair; t < ts.n_tiles && go; t += pairs) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPairRows);
+                const int steps = a.k_steps + (kstep0 == 0 ? min_ring : 0);
+                for (int p0 = 0; p0 < steps; p0 += F::kSub, qq += F::kSub) {
+                    const int xs = (qq / F::kSub) % F::kStagesX, as = (qq / F::kSub) % F::kStagesB;
+                    if (!mbar_wait_cluster(&x_full[xs], (qq / kSx) & 1, abort_flag, a.err, 14, false) ||
+                        !mbar_wait_cluster(&full[as], (qq / kSt) & 1, abort_flag, a.err, 14, false)) {
+                        go = false;
+                        break;
+                    }
+                    mbar_arrive_cluster(cluster_addr(smem_u32(&x_full[xs]), 0));
+                    mbar_arrive_cluster(cluster_addr(smem_u32(&full[as]), 0));
+                }
+            }
+        } else if (warp == kMmaWarpQ && lane == 0 && rank == 0) {
+            // MMA thread (rank 0): M = 256 over both CTAs' tensor memory
+            const unsigned idesc = (a.idesc & ~(31u << 24)) | (unsigned(kPairRows >> 4) << 24);
+            int qq = 0, gb = 0;
+            bool go = true;
+            for (int t = pair; t < ts.n_tiles && go; t += pairs) {
+                int row0, tok0, kstep0;
+                tile_coords(ts, t, a.n_tile, a.k_steps, row0, tok0, kstep0, kPairRows);
+                const int nb = q.blocks + (kstep0 == 0 ? 1 : 0);
+                for (int j = 0; j < nb && go; ++j, ++gb) {
+                    const int b = gb & 1;
+                    if (!mbar_wait_cluster(&acc_empty[b], ((gb >> 1) & 1) ^ 1, abort_flag, a.err, 15, false)) {
+                        go = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const unsigned acc = tmem + unsigned(b) * kAccCols;
+                    const bool minterm = j == q.blocks;
+                    const int n_steps = minterm ? min_ring : 256 / kBK;
+                    for (int p0 = 0; p0 < n_steps; p0 += F::kSub, qq += F::kSub) {
+                        const int xs = (qq / F::kSub) % F::kStagesX, as = (qq / F::kSub) % F::kStagesB;
+                        if (!mbar_wait_cluster(&x_full[xs], (qq / kSx) & 1, abort_flag, a.err, 13, false) ||
+                            !mbar_wait_cluster(&full[as], (qq / kSt) & 1, abort_flag, a.err, 13, false)) {
+                            go = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;");
+                        const int n = min(F::kSub, n_steps - p0);
+                        for (int i = 0; i < n; ++i) {
+                            const int ks = p0 + i;
+                            unsigned char* st = stages + ((qq + i) % kSx) * stage_bytes;
+                            const std::uint64_t bhi = smem_desc(tile_bhi(st)), blo = smem_desc(tile_blo(st));
+                            const unsigned at = tmem + F::kACol + unsigned(((qq + i) % kSt) * 16);
+                            const bool two = !minterm || !(ks & 1);
+#pragma unroll
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                const std::uint64_t adv = (std::uint64_t)(kk * 32) >> 4;
+                                mma_f16_ts_pair(acc, at + unsigned(kk * 8), bhi + adv, idesc, ks > 0 || kk > 0);
+                                if (two) mma_f16_ts_pair(acc, at + unsigned(kk * 8), blo + adv, idesc, 1);
+                            }
+                        }
+                        mma_commit_pair(&x_empty[xs]);
+                        mma_commit_pair(&empty[as]);
+                    }
+                    if (go) mma_commit_pair(&acc_full[b]);
+                }
+            }
+        }
+    } else if (warp >= kProducerWarp0) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+        q4k_tmem_producers<Q4kPairForm, true>(q, ts, pair, pairs, int(rank) * kBM, tmem, pk_ring, full, empty, pk_full, pk_empty,
+                                 abort_flag);
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
+        q4k_epilogue<kAccCols, true>(q, ts, pair, pairs, int(rank) * kBM, tmem, acc_full, acc_empty, abort_flag);
+    }
+    // neither CTA leaves (or frees tensor memory) while the other may still
+    // read its tensor memory or signal its barriers
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == kMmaWarpQ) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+    (void)kblocks;
+    (void)units;
 }
 
 // ---------------------------------------------------------------------------
@@ -2073,14 +2473,22 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     const bool q4k_form = g.w.qplane || g.w.qsc;
-    // the packed Q4_K kernel builds A in tensor memory; TVARA_Q4K_A=smem
-    // selects the shared-memory form (kept for comparison)
-    static const bool q4k_smem_a = [] {
+    // packed Q4_K rows: the one-CTA tensor-memory form by default (fastest
+    // measured); TVARA_Q4K_A=smem the shared-memory form, =pair the CTA-pair
+    // form (both correct, kept for comparison)
+    static const int q4k_a_form = [] {
         const char* v = std::getenv("TVARA_Q4K_A");
-        return v && std::strcmp(v, "smem") == 0;
+        if (v && std::strcmp(v, "smem") == 0) return 0;
+        if (v && std::strcmp(v, "pair") == 0) return 2;
+        return 1;
     }();
-    const bool tmem_a = !g.w.qplane && g.w.qsc && !q4k_smem_a;
-    TilePlan plan = plan_tiles(row_tiles, T, steps, g.epilogue != kSwiGLU, sm_count(), tmem_a ? kQ4kpTmemMaxN : kMaxN);
+    const bool packed_q4k = !g.w.qplane && g.w.qsc;
+    const bool tmem_a = packed_q4k && q4k_a_form >= 1;
+    const bool pair = packed_q4k && q4k_a_form == 2 && sm_count() >= 2;
+    // the pair form's tiles are 256 rows, one per two SMs
+    const int plan_rows = pair ? (g.w.rows + kPairRows - 1) / kPairRows : row_tiles;
+    TilePlan plan = plan_tiles(plan_rows, T, steps, g.epilogue != kSwiGLU, pair ? sm_count() / 2 : sm_count(),
+                               pair ? kQ4kPairMaxN : tmem_a ? kQ4kpTmemMaxN : kMaxN);
     if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
     const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
@@ -2124,7 +2532,18 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         } else {
             if (g.w.qs_row % 16 || reinterpret_cast<std::uintptr_t>(g.w.qs) % 16)
                 throw std::invalid_argument("packed Q4_K rows must be 16-byte aligned");
-            if (tmem_a) {
+            if (pair) {
+                if (n_tile > kQ4kPairMaxN) throw std::logic_error("token tile too wide for the CTA-pair form");
+                constexpr int smem_p = Q4kPairForm::smem_bytes();
+                static_assert(smem_p <= 227 * 1024, "CTA-pair form exceeds shared memory");
+                // each CTA of a pair loads half of the tile's tokens
+                const CUtensorMap ph = make_map(hi, K, T, n_tile / 2), pl = make_map(lo, K, T, n_tile / 2);
+                const CUtensorMap psh = make_map(shi, units, T, n_tile / 2), psl = make_map(slo, units, T, n_tile / 2);
+                TileSpace pts{token_tiles, plan_rows, splits, token_tiles * plan_rows * splits};
+                const int pairs = std::min(pts.n_tiles, sm_count() / 2);
+                TVARA_CUDA(cudaFuncSetAttribute(tc_gemm_q4k2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
+                tc_gemm_q4k2_kernel<<<2 * pairs, kQ4kpThreads, smem_p, s>>>(ph, pl, mq, psh, psl, qa, pts);
+            } else if (tmem_a) {
                 if (n_tile > kQ4kpTmemMaxN) throw std::logic_error("token tile too wide for the tensor-memory A form");
                 constexpr int smem_p = Q4kpForm<true>::smem_bytes();
                 static_assert(smem_p <= 227 * 1024, "tensor-memory A form exceeds shared memory");
