@@ -1,11 +1,12 @@
 """The packed Q4_K tensor-core kernel in each of its selectable forms.
 
-The library picks the form once per process from TVARA_Q4K_A (default: A in
-tensor memory, one CTA per tile; "smem": A in shared memory; "pair": the
-cta_group::2 CTA-pair kernel), so each non-default form reruns the parity
-tests of the tensor-core and narrow-row projections in a child process:
-partial row tiles, several token tiles, split K, one to sixteen 256-element
-blocks, every result within the oracle tolerance."""
+The library reads TVARA_Q4K_A once per process (default: per launch, the
+tensor-memory or the shared-memory form, whichever its tile plans make
+faster; "tmem", "smem", "pair" force the one-CTA tensor-memory form, the
+shared-memory form, the cta_group::2 CTA-pair kernel), so each forced form
+reruns the parity tests of the tensor-core and narrow-row projections in a
+child process: partial row tiles, several token tiles, split K, one to
+sixteen 256-element blocks, every result within the oracle tolerance."""
 
 import os
 import subprocess
@@ -18,7 +19,7 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-@pytest.mark.parametrize("form", ["smem", "pair"])
+@pytest.mark.parametrize("form", ["tmem", "smem", "pair"])
 def test_q4k_form_matches_oracle(form):
     env = dict(os.environ, TVARA_Q4K_A=form)
     res = subprocess.run(

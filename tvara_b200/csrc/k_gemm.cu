@@ -2375,7 +2375,14 @@ struct TilePlan {
 // which is nonlinear).  Per tile: K-steps x (width + a fixed per-step cost)
 // plus a fixed cost for the pipeline fill and the epilogue (which grows with
 // the width and, for split K, with the atomic accumulation).
-TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sms, int max_n = kMaxN) {
+// flat_step > 0 (the tensor-memory Q4_K forms): a K-step costs about the
+// same at any tile width up to the maximum (the pace is set by the x-tile
+// round trip, not the MMA width: measured ~600 cycles at widths 96..192), so
+// wide tiles with split K beat narrow unsplit ones; the pipeline fill (two
+// stages) is charged per tile.  whole_blocks: splits divide the 256-element
+// blocks (8 K-steps).
+TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sms, int max_n = kMaxN,
+                    double flat_step = 0.0, bool whole_blocks = false) {
     TilePlan best{0, 0, 0};
     double best_cost = 0;
     for (int tt = (tokens + max_n - 1) / max_n; tt <= (tokens + 15) / 16 && tt <= 64; ++tt) {
@@ -2384,9 +2391,12 @@ TilePlan plan_tiles(int row_tiles, int tokens, int steps, bool can_split, int sm
         const int token_tiles = (tokens + width - 1) / width;
         for (int sp = 1; sp <= 16; sp *= 2) {
             if (sp > 1 && (!can_split || steps % sp || steps / sp < 8)) break;
+            if (sp > 1 && whole_blocks && (steps / 8) % sp) continue;
             const long long tiles = (long long)row_tiles * token_tiles * sp;
             const long long waves = (tiles + sms - 1) / sms;
-            const double per_tile = double(steps / sp) * (width + 48) + 6.0 * width + 1500.0 + (sp > 1 ? 8.0 * width : 0.0);
+            const double step_cost = flat_step > 0 ? flat_step : double(width + 48);
+            const double per_tile = double(steps / sp) * step_cost + (flat_step > 0 ? 8.0 * flat_step : 0.0) + 6.0 * width +
+                                    1500.0 + (sp > 1 ? 8.0 * width : 0.0);
             const double cost = double(waves) * per_tile;
             if (!best.n_tile || cost < best_cost) {
                 best = {width, token_tiles, sp};
@@ -2473,22 +2483,40 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     const int row_tiles = (g.w.rows + kBM - 1) / kBM;
     const int steps = K / kBK;
     const bool q4k_form = g.w.qplane || g.w.qsc;
-    // packed Q4_K rows: the one-CTA tensor-memory form by default (fastest
-    // measured); TVARA_Q4K_A=smem the shared-memory form, =pair the CTA-pair
-    // form (both correct, kept for comparison)
+    // packed Q4_K rows: by default the one-CTA tensor-memory form or the
+    // shared-memory form, whichever the tile plans make faster (below);
+    // TVARA_Q4K_A=tmem / smem / pair forces one form (tests, comparisons)
     static const int q4k_a_form = [] {
         const char* v = std::getenv("TVARA_Q4K_A");
         if (v && std::strcmp(v, "smem") == 0) return 0;
         if (v && std::strcmp(v, "pair") == 0) return 2;
+        if (v && std::strcmp(v, "tmem") == 0) return 3;
         return 1;
     }();
     const bool packed_q4k = !g.w.qplane && g.w.qsc;
-    const bool tmem_a = packed_q4k && q4k_a_form >= 1;
     const bool pair = packed_q4k && q4k_a_form == 2 && sm_count() >= 2;
+    bool tmem_a = packed_q4k && q4k_a_form >= 1;
     // the pair form's tiles are 256 rows, one per two SMs
     const int plan_rows = pair ? (g.w.rows + kPairRows - 1) / kPairRows : row_tiles;
-    TilePlan plan = plan_tiles(plan_rows, T, steps, g.epilogue != kSwiGLU, pair ? sm_count() / 2 : sm_count(),
-                               pair ? kQ4kPairMaxN : tmem_a ? kQ4kpTmemMaxN : kMaxN);
+    const bool can_split = g.epilogue != kSwiGLU;
+    TilePlan plan = plan_tiles(plan_rows, T, steps, can_split, pair ? sm_count() / 2 : sm_count(),
+                               pair ? kQ4kPairMaxN : tmem_a ? kQ4kpTmemMaxN : kMaxN,
+                               tmem_a ? double(kQ4kpTmemMaxN + 48) : 0.0, q4k_form);
+    if (tmem_a && !pair && q4k_a_form == 1) {
+        // the tensor-memory form's K-step is ~1.35x faster than the shared-memory
+        // form's at the same tile (measured on the 8B shapes), but its tiles stop
+        // at 192 tokens; where 256-wide tiles with split K need far fewer K-steps
+        // per SM (the 4096-row projections), the shared-memory form is faster
+        const TilePlan ps = plan_tiles(row_tiles, T, steps, can_split, sm_count(), kMaxN, 0.0, true);
+        auto per_sm = [&](const TilePlan& p) {
+            const long long tiles = (long long)row_tiles * p.token_tiles * p.splits;
+            return double((tiles + sm_count() - 1) / sm_count()) * double(steps / p.splits);
+        };
+        if (per_sm(plan) > 1.35 * per_sm(ps)) {
+            tmem_a = false;
+            plan = ps;
+        }
+    }
     if (q4k_form)  // whole 256-element blocks per split
         while (plan.splits > 1 && (steps / 8) % plan.splits) plan.splits /= 2;
     const int n_tile = plan.n_tile, token_tiles = plan.token_tiles, splits = plan.splits;
