@@ -55,7 +55,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # processes: attention per distinct K/V position per layer launch (2-layer,
 # 64-request case), the Q4_K projections per layer at 512 tokens (1-layer case:
 # QKV, o_proj, gate/up, down)
-NCU_TRAFFIC = {"attention_per_distinct_position": {"f16": 4150.0}, "projections_per_layer": 227.4e6}
+NCU_TRAFFIC = {"attention_per_distinct_position": {"f16": 4150.0}, "projections_per_layer": 226.4e6}
 
 
 def peaks():
@@ -828,7 +828,7 @@ def run_ours(args):
                          "position from a small capture (profiles/), times this launch's distinct positions"}
     ach = kernels["projections"]["achieved_tflops"]
     per_row = NCU_TRAFFIC["projections_per_layer"]
-    roof_proj = {"kernel": "tc_gemm_q4k_kernel (the Q4_K projections of a step)", "bound": "tensor", "achieved": ach,
+    roof_proj = {"kernel": "tc_gemm_q4kp_kernel (the Q4_K projections of a step)", "bound": "tensor", "achieved": ach,
                  "peak": tensor, "unit": "TFLOP/s", "frac": ach / tensor if ach else None,
                  "traffic": per_row / 4 if per_row and tp == 1 and args.requests == 512 else None,
                  "peak_source": pk_kind,
@@ -877,9 +877,10 @@ def run_ours(args):
                    "parallelism": f"tp{world}", "kv": args.kv, "block_tokens": tpb,
                    "weights_gb": {"packed": round(wbytes["packed"] / 1e9, 2),
                                   "tensor_core_forms": round(wbytes["planes"] / 1e9, 2)},
-                   "tensor_core_weight_form": {"auto": "Q4_K: packed rows, sc*q built in shared memory, block "
-                                                       "scales + minima in side arrays (2 MMAs per K-step); other "
-                                                       "types: exact hi/lo FP16 planes",
+                   "tensor_core_weight_form": {"auto": "Q4_K: packed rows, sc*q built per K-step in tensor memory or "
+                                                       "shared memory (chosen per launch), block scales + minima in "
+                                                       "side arrays (2 MMAs per K-step); other types: exact hi/lo "
+                                                       "FP16 planes",
                                                "q4kplane": "Q4_K: prebuilt FP16 plane of sc*q (2 MMAs per K-step); "
                                                            "other types: exact hi/lo FP16 planes",
                                                "hilo": "exact hi/lo FP16 planes (3 MMAs per K-step)",
