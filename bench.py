@@ -55,7 +55,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # processes: attention per distinct K/V position per layer launch (2-layer,
 # 64-request case), the Q4_K projections per layer at 512 tokens (1-layer case:
 # QKV, o_proj, gate/up, down)
-NCU_TRAFFIC = {"attention_per_distinct_position": {"f16": 4150.0}, "projections_per_layer": 226.4e6}
+NCU_TRAFFIC = {"attention_per_distinct_position": {"f16": 4150.0, "i8": 2150.0}, "projections_per_layer": 226.4e6}
 
 
 def peaks():
