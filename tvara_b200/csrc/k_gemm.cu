@@ -1381,7 +1381,7 @@ case C:                                                  \
 }
 
 
-template <bool kTmemA>
+template <bool kTmemA, class F = Q4kpForm<kTmemA>>
 __global__ void __launch_bounds__(kQ4kpThreads, 1)
     tc_gemm_q4kp_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                         const __grid_constant__ CUtensorMap map_pk, const __grid_constant__ CUtensorMap map_mhi,
@@ -1390,7 +1390,6 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
     const TcArgs& a = q.t;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
-    using F = Q4kpForm<kTmemA>;
     constexpr int kSt = F::kRing;
     const int b_bytes = a.n_tile * kBK * 2;
     const int stage_bytes = F::kStageBytes;
@@ -1662,7 +1661,7 @@ __global__ void __launch_bounds__(kQ4kpThreads, 1)
         }
     } else if (kTmemA && warp >= kProducerWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
-        q4k_tmem_producers<Q4kpForm<true>, false>(q, ts, blockIdx.x, gridDim.x, 0, tmem, pk_ring, full, empty, pk_full, pk_empty, abort_flag);
+        q4k_tmem_producers<F, false>(q, ts, blockIdx.x, gridDim.x, 0, tmem, pk_ring, full, empty, pk_full, pk_empty, abort_flag);
     } else if (warp >= kProducerWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
         // producers: thread r = weight row row0 + r, both nibble halves
