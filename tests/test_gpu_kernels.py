@@ -161,6 +161,25 @@ def test_narrow_q4k_rows_matches_oracle(capi, tokens, rows, cols):
     assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
 
 
+@pytest.mark.parametrize("kind", [gguf.Q8_0, gguf.Q4_0])
+@pytest.mark.parametrize("tokens", [5, 8, 9, 17, 33, 64, 65, 100, 128, 129])
+@pytest.mark.parametrize("rows,cols", [(300, 576), (129, 4096), (77, 2816)])
+def test_small_batch_q8_q4_matches_oracle(capi, kind, tokens, rows, cols):
+    """Small batches of Q8_0 / Q4_0 rows (5..32 tokens: the mma.sync kernel
+    on the packed rows; more: the tensor-core path): token tiles of 8/16/32,
+    partial row tiles, K of 18 blocks
+    (a short last chunk, no split), 128 blocks (split K) and 88 blocks (a
+    short last chunk), activations spanning four orders of magnitude per
+    token with a few outliers."""
+    rng = np.random.default_rng(tokens * 37 + rows + cols + kind)
+    raw = make_weights(kind, rows, cols, rng)
+    x = (rng.standard_normal((tokens, cols)) * rng.uniform(0.01, 30, (tokens, 1))).astype(np.float32)
+    x[0, rng.choice(cols, 3, replace=False)] = [1e3, -2e3, 0.0]
+    got = matmul(capi, kind, packed(capi, kind, raw, rows, cols), rows, cols, x)
+    ref, mag = oracle_matmul(kind, raw, rows, cols, x)
+    assert np.all(np.abs(got - ref) <= 2e-5 * mag + 1e-6), np.abs(got - ref).max()
+
+
 @pytest.mark.parametrize("kind", [gguf.Q4_K, gguf.Q8_0, gguf.Q4_0])
 def test_quant_matmul_standalone_config_shape(capi, kind):
     """BASELINE standalone config: 11008 x 4096, d/dmin ~ U(0.001, 0.05)."""
@@ -168,7 +187,7 @@ def test_quant_matmul_standalone_config_shape(capi, kind):
     rows, cols = 11008, 4096
     raw = np.frombuffer(gguf.random_blocks(kind, rows, cols, rng), np.uint8).copy()
     buf = packed(capi, kind, raw, rows, cols)
-    for tokens in (1, 8, 128, 512):
+    for tokens in (1, 8, 32, 128, 512):
         x = rng.standard_normal((tokens, cols)).astype(np.float32)
         got = matmul(capi, kind, buf, rows, cols, x)
         sel = rng.choice(rows, 256, replace=False)

@@ -31,6 +31,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "split.cuh"
@@ -2263,6 +2264,199 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMat
         }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches (5 .. 32 tokens) of Q8_0 / Q4_0 rows on mma.sync, straight
+// from the packed rows, with the activations' exact hi / lo FP16 split of
+// split_kernel.  A Q8_0 code is an int8, a Q4_0 code minus 8 lies in -8..7:
+// both are exact in FP16 (a byte permute onto 0x64xx = 1024 + byte and one
+// half2 subtraction), so each 32-element block's products are exact and its
+// two k16 MMAs (hi and lo chains) accumulate in F32 before the block is added
+// with its scale d.  A CTA is eight warps on 128 weight rows (16 per warp),
+// one slice of K and up to 32 tokens.  Per
+// block a lane takes, of each of its two rows, the 8 code bytes 8tq .. 8tq+7
+// (Q8_0, one 8-byte load) or the code word tq (Q4_0: elements 4tq .. 4tq+3
+// in the low nibbles, 16 + 4tq .. in the high ones), from a register ring
+// kSmallQDepth blocks ahead, with the block's fp16 scale d.  The fragments' K order is a fixed
+// permutation of the block's (Q8_0: k16 #0 <- elements {0-3, 8-11, 16-19,
+// 24-27}, #1 <- the rest; Q4_0: #0 <- the low nibbles, #1 <- the high ones),
+// and the activations are read with the same permutation, so every dot
+// product is unchanged.  Shared-memory rows of x are padded so that the
+// fragment loads are free of bank conflicts.
+constexpr int kSmallQChunk = 256;  // K elements of x staged at a time: 8 blocks
+constexpr int kSmallQDepth = 8;    // blocks of packed codes in flight per lane
+constexpr int kSmallQMaxTokens = 32;  // above it the exact-plane kernels are faster
+
+template <int TYPE>
+constexpr int smallq_xs() { return kSmallQChunk * 2 + (TYPE == kQ8_0 ? 64 : 32); }  // bytes per token row
+template <int TYPE>
+constexpr std::size_t smallq_smem_bytes(int nt) { return std::size_t(8 * nt) * smallq_xs<TYPE>() * 2; }
+
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// Two FP16 codes (bytes sel of w, w already biased to 0..255) as a half2 minus bias.
+__device__ __forceinline__ unsigned code_pair(unsigned w, unsigned sel, __half2 bias) {
+    const unsigned p = __byte_perm(w, 0x64646464u, sel);
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&p), bias);
+    return *reinterpret_cast<const unsigned*>(&h);
+}
+
+template <int TYPE, int NT>  // 8-token tiles: up to 8 * NT tokens per CTA
+__global__ void __launch_bounds__(kSmallThreads) gemm_small_q8_kernel(DeviceMatrix w, const __half* xhi,
+                                                                     const __half* xlo, const int* xshift, int tokens,
+                                                                     int kslice, float* y, int ldy, int epilogue,
+                                                                     int atomic) {
+    static_assert(TYPE == kQ8_0 || TYPE == kQ4_0, "Q8_0 / Q4_0 only");
+    constexpr int MT = 8 * NT;
+    constexpr int XS = smallq_xs<TYPE>();
+    constexpr int CB = kSmallQChunk / 32;  // blocks per chunk
+    static_assert(CB == kSmallQDepth, "the ring holds one chunk of blocks");
+    using Word = std::conditional_t<TYPE == kQ8_0, uint2, unsigned>;
+    constexpr int kBlockBytes = TYPE == kQ8_0 ? 32 : 16;  // packed code bytes per block
+    extern __shared__ __align__(16) unsigned char smallq_smem[];
+    unsigned char* xh_s = smallq_smem;
+    unsigned char* xl_s = xh_s + MT * XS;
+    const int t0 = blockIdx.z * MT;             // first token of this CTA
+    const int b0 = blockIdx.y * (kslice / 32);  // first block of this CTA's slice
+    const int sb = kslice / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int row_a = blockIdx.x * kSmallRows + warp * 16 + gq, row_b = row_a + 8;
+    const bool live_a = row_a < w.rows, live_b = row_b < w.rows;
+    const long long ra = live_a ? row_a : 0, rb = live_b ? row_b : 0;
+    const unsigned char* qa = w.qs + ra * (long long)w.qs_row + (long long)b0 * kBlockBytes +
+                              (TYPE == kQ8_0 ? 8 * tq : 4 * tq);
+    const unsigned char* qb = w.qs + rb * (long long)w.qs_row + (long long)b0 * kBlockBytes +
+                              (TYPE == kQ8_0 ? 8 * tq : 4 * tq);
+    const unsigned short* da_p = reinterpret_cast<const unsigned short*>(w.meta + ra * (long long)w.meta_row) + b0;
+    const unsigned short* db_p = reinterpret_cast<const unsigned short*>(w.meta + rb * (long long)w.meta_row) + b0;
+    auto load = [&](const unsigned char* q, int i) -> Word {
+        return *reinterpret_cast<const Word*>(q + (long long)i * kBlockBytes);
+    };
+    float tot[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tot[n][e] = 0.f;
+    Word ring_a[kSmallQDepth], ring_b[kSmallQDepth];
+    unsigned short dr_a[kSmallQDepth], dr_b[kSmallQDepth];
+#pragma unroll
+    for (int i = 0; i < kSmallQDepth; ++i) {
+        ring_a[i] = i < sb ? load(qa, i) : Word{};
+        ring_b[i] = i < sb ? load(qb, i) : Word{};
+        dr_a[i] = i < sb ? da_p[i] : 0;
+        dr_b[i] = i < sb ? db_p[i] : 0;
+    }
+    const __half2 bias = __half2half2(__ushort_as_half(TYPE == kQ8_0 ? 0x6480 : 0x6408));  // 1152 / 1032
+    for (int c0 = 0; c0 < sb; c0 += CB) {
+        const int cb = min(CB, sb - c0);
+        __syncthreads();  // the previous chunk of x is no longer read
+        for (int i = threadIdx.x; i < MT * cb * 4; i += blockDim.x) {
+            const int t = i / (cb * 4), c = i % (cb * 4);  // c: 8 elements (16 bytes)
+            uint4 h = make_uint4(0, 0, 0, 0), l = h;
+            if (t0 + t < tokens) {
+                const long long off = (long long)(t0 + t) * w.cols + (long long)(b0 + c0) * 32 + 8 * c;
+                h = *reinterpret_cast<const uint4*>(xhi + off);
+                l = *reinterpret_cast<const uint4*>(xlo + off);
+            }
+            *reinterpret_cast<uint4*>(xh_s + t * XS + 16 * c) = h;
+            *reinterpret_cast<uint4*>(xl_s + t * XS + 16 * c) = l;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kSmallQDepth; ++i) {
+            if (i >= cb) break;  // uniform: a short last chunk
+            const Word wa = ring_a[i], wb = ring_b[i];
+            const float da = live_a ? __half2float(__ushort_as_half(dr_a[i])) : 0.f;
+            const float db = live_b ? __half2float(__ushort_as_half(dr_b[i])) : 0.f;
+            const int nxt = c0 + i + kSmallQDepth;
+            if (nxt < sb) {
+                ring_a[i] = load(qa, nxt);
+                ring_b[i] = load(qb, nxt);
+                dr_a[i] = da_p[nxt];
+                dr_b[i] = db_p[nxt];
+            }
+            unsigned A0[4], A1[4];
+            if constexpr (TYPE == kQ8_0) {
+                const unsigned ax = wa.x ^ 0x80808080u, ay = wa.y ^ 0x80808080u;
+                const unsigned bx = wb.x ^ 0x80808080u, by = wb.y ^ 0x80808080u;
+                A0[0] = code_pair(ax, 0x4140, bias);
+                A0[1] = code_pair(bx, 0x4140, bias);
+                A0[2] = code_pair(ax, 0x4342, bias);
+                A0[3] = code_pair(bx, 0x4342, bias);
+                A1[0] = code_pair(ay, 0x4140, bias);
+                A1[1] = code_pair(by, 0x4140, bias);
+                A1[2] = code_pair(ay, 0x4342, bias);
+                A1[3] = code_pair(by, 0x4342, bias);
+            } else {
+                const unsigned al = wa & 0x0F0F0F0Fu, ah = (wa >> 4) & 0x0F0F0F0Fu;
+                const unsigned bl = wb & 0x0F0F0F0Fu, bh = (wb >> 4) & 0x0F0F0F0Fu;
+                A0[0] = code_pair(al, 0x4140, bias);
+                A0[1] = code_pair(bl, 0x4140, bias);
+                A0[2] = code_pair(al, 0x4342, bias);
+                A0[3] = code_pair(bl, 0x4342, bias);
+                A1[0] = code_pair(ah, 0x4140, bias);
+                A1[1] = code_pair(bh, 0x4140, bias);
+                A1[2] = code_pair(ah, 0x4342, bias);
+                A1[3] = code_pair(bh, 0x4342, bias);
+            }
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int xo = (8 * n + gq) * XS;
+                unsigned h[4], l[4];  // B of k16 #0 (h[0], h[1]) and #1 (h[2], h[3])
+                if constexpr (TYPE == kQ8_0) {
+                    const int ko = (i * 32 + 8 * tq) * 2;  // elements 8tq .. 8tq + 7
+                    const uint4 vh = *reinterpret_cast<const uint4*>(xh_s + xo + ko);
+                    const uint4 vl = *reinterpret_cast<const uint4*>(xl_s + xo + ko);
+                    h[0] = vh.x, h[1] = vh.y, h[2] = vh.z, h[3] = vh.w;
+                    l[0] = vl.x, l[1] = vl.y, l[2] = vl.z, l[3] = vl.w;
+                } else {
+                    const int k0 = (i * 32 + 4 * tq) * 2, k1 = k0 + 32;  // elements 4tq .., 16 + 4tq ..
+                    const uint2 h0 = *reinterpret_cast<const uint2*>(xh_s + xo + k0);
+                    const uint2 h1 = *reinterpret_cast<const uint2*>(xh_s + xo + k1);
+                    const uint2 l0 = *reinterpret_cast<const uint2*>(xl_s + xo + k0);
+                    const uint2 l1 = *reinterpret_cast<const uint2*>(xl_s + xo + k1);
+                    h[0] = h0.x, h[1] = h0.y, h[2] = h1.x, h[3] = h1.y;
+                    l[0] = l0.x, l[1] = l0.y, l[2] = l1.x, l[3] = l1.y;
+                }
+                float ch[4], cl[4];
+                mma_16816_z(ch, A0, h[0], h[1]);
+                mma_16816_z(cl, A0, l[0], l[1]);
+                mma_16816(ch, A1, h[2], h[3]);
+                mma_16816(cl, A1, l[2], l[3]);
+                tot[n][0] = fmaf(da, ch[0] + cl[0], tot[n][0]);
+                tot[n][1] = fmaf(da, ch[1] + cl[1], tot[n][1]);
+                tot[n][2] = fmaf(db, ch[2] + cl[2], tot[n][2]);
+                tot[n][3] = fmaf(db, ch[3] + cl[3], tot[n][3]);
+            }
+        }
+    }
+    // out: accumulator (row gq / gq + 8, tokens t0 + 8n + 2tq, + 1), scaled back by 2^-shift
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int t = t0 + 8 * n + 2 * tq + (e & 1);
+            const bool rlive = e < 2 ? live_a : live_b;
+            const int row = e < 2 ? row_a : row_b;
+            const float v = t < tokens ? tot[n][e] * pow2(-xshift[t]) : 0.f;
+            if (epilogue == kSwiGLU) {
+                // rows (2i, 2i + 1) = (gate_i, up_i) sit in lanes gq and gq ^ 1 (4 lanes apart)
+                const float other = __shfl_xor_sync(0xffffffffu, v, 4);
+                if (rlive && t < tokens && !(gq & 1)) y[(long long)t * ldy + row / 2] = swiglu_12(v, other);
+            } else if (rlive && t < tokens) {
+                float* dst = y + (long long)t * ldy + row;
+                if (atomic || epilogue == kAdd) atomicAdd(dst, v);
+                else *dst = v;
+            }
+        }
+}
+
 // X [T][K] F32 -> hi, lo FP16 [T][K] with a per-token power-of-two scale
 // that puts max|x| in [2^14, 2^15), then the exact split (split.cuh).  One
 // block per token; float4 loads and 8-byte stores (K % 4 == 0, rows 16-byte
@@ -2475,6 +2669,39 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
             TVARA_SMALL(4)
             TVARA_SMALL(8)
 #undef TVARA_SMALL
+        }
+        TVARA_LAUNCHED();
+        return;
+    }
+    if ((g.w.type == kQ8_0 || g.w.type == kQ4_0) && T <= kSmallQMaxTokens && g_small_batches && g.w.qs_row % 8 == 0) {
+        // small batches: packed Q8_0 / Q4_0 rows on mma.sync, weights read once per 64 tokens
+        const int nt = T <= 8 ? 1 : T <= 16 ? 2 : 4;
+        const int groups = (T + 8 * nt - 1) / (8 * nt);
+        const int row_tiles = (g.w.rows + kSmallRows - 1) / kSmallRows;
+        int splits = 1;  // K slices of whole 256-element chunks
+        if (g.epilogue != kSwiGLU)
+            while (K % (splits * 2 * kSmallQChunk) == 0 && row_tiles * splits * groups < 3 * sm_count()) splits *= 2;
+        if (splits > 1 && g.epilogue == kStore)
+            TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
+        const dim3 grid(row_tiles, splits, groups);
+        const int kslice = K / splits;
+        const int code = (g.w.type == kQ8_0 ? 0 : 16) + nt;
+        switch (code) {
+#define TVARA_SMALLQ(C, TY, N)                                                                                     \
+    case C: {                                                                                                      \
+        const int smem = int(smallq_smem_bytes<TY>(N));                                                            \
+        TVARA_CUDA(cudaFuncSetAttribute(gemm_small_q8_kernel<TY, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
+        gemm_small_q8_kernel<TY, N><<<grid, kSmallThreads, smem, s>>>(g.w, hi, lo, shift, T, kslice, g.y, g.ldy,    \
+                                                                      g.epilogue, splits > 1);                     \
+        break;                                                                                                     \
+    }
+            TVARA_SMALLQ(1, kQ8_0, 1)
+            TVARA_SMALLQ(2, kQ8_0, 2)
+            TVARA_SMALLQ(4, kQ8_0, 4)
+            TVARA_SMALLQ(17, kQ4_0, 1)
+            TVARA_SMALLQ(18, kQ4_0, 2)
+            TVARA_SMALLQ(20, kQ4_0, 4)
+#undef TVARA_SMALLQ
         }
         TVARA_LAUNCHED();
         return;

@@ -963,7 +963,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
 // Single-token projection of a quantised matrix with the weights streamed
 // through shared memory.  A copy warp moves each stage -- the codes and block
 // headers of RG rows over KCU units of K -- with cp.async.bulk (one copy per
-// row and array) onto the stage's mbarrier, kStreamStages stages ahead,
+// row and array) onto the stage's mbarrier, stream_stages() stages ahead,
 // starting before the wait on the previous kernel since the weights do not
 // depend on it.  Eight consumer warps compute from shared memory: a lane owns
 // one unit position of the stage for a set of four rows, so it sees the same
@@ -976,7 +976,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv1_kernel(GemmArgs a) {
 constexpr int kStreamWarps = 8;                          // consumer warps
 constexpr int kStreamThreads = (kStreamWarps + 1) * 32;  // + the copy warp
 constexpr int kStreamSlots = kStreamWarps * 32;          // (unit, 4-row set) slots per stage
-constexpr int kStreamStages = 4;
+// Stages per CTA: six of 18 KB for the 4-bit formats keep two CTAs per SM
+// (2 x 108 KB of the SM's 228 KB), so an 11008 x 4096 Q4_K or Q4_0 matrix
+// (172 KB per SM) is requested whole at launch; Q8_0 (twice the bytes per
+// row) measured faster with four.
+template <int TYPE>
+constexpr int stream_stages() { return TYPE == kQ8_0 ? 4 : 6; }
 constexpr int kStreamQs = kStreamSlots * 4 * 16;         // 16 KB of codes per stage
 constexpr int kStreamMeta = kStreamSlots * 4 * 2;        // block headers: <= 2 bytes per unit
 constexpr unsigned kStreamSpin = 1u << 24;
@@ -1033,19 +1038,20 @@ template <int TYPE, int CH>
 __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs a, StreamShape sp) {
     constexpr int E = Unit<TYPE>::kElems;
     constexpr int MPU = TYPE == kQ8_0 ? 1 : 2;  // block-header bytes per unit
+    constexpr int kSt = stream_stages<TYPE>();
     // [stages][16 KB] codes, then [stages][2 KB] headers
     extern __shared__ __align__(16) unsigned char stream_smem[];
     unsigned char* st_qs = stream_smem;
-    unsigned char* st_meta = stream_smem + kStreamStages * kStreamQs;
-    __shared__ std::uint64_t full[kStreamStages], empty[kStreamStages];
-    __shared__ float red[2][kStreamWarps][4];
+    unsigned char* st_meta = stream_smem + kSt * kStreamQs;
+    __shared__ std::uint64_t full[kSt], empty[kSt];
+    __shared__ float red[kSt][kStreamWarps][4];
     __shared__ int abort_word;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = a.w.cols / E;
     int* err = a.err ? a.err : &g_gemv_stream_err;
     volatile int* abort_flag = &abort_word;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStreamStages; ++i) {
+        for (int i = 0; i < kSt; ++i) {
             sb_init(&full[i], 1);
             sb_init(&empty[i], kStreamWarps);
         }
@@ -1062,8 +1068,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs
             const int nr = min(sp.rg, a.w.rows - row0);
             bool ok = true;
             for (int c = 0; c < sp.chunks; ++c) {
-                const int st = it % kStreamStages;
-                const unsigned ph = (unsigned(it) / kStreamStages) & 1u;
+                const int st = it % kSt;
+                const unsigned ph = (unsigned(it) / kSt) & 1u;
                 int go = lane == 0 ? int(sb_wait(&empty[st], ph ^ 1u, abort_flag, err, 21)) : 0;
                 go = __shfl_sync(0xffffffffu, go, 0);
                 if (!go) {
@@ -1088,8 +1094,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs
         }
         // the copies issued land before the CTA exits (bounded, even after an abort)
         if (lane == 0)
-            for (int j = max(0, it - kStreamStages); j < it; ++j)
-                sb_wait(&full[j % kStreamStages], (unsigned(j) / kStreamStages) & 1u, nullptr, err, 22);
+            for (int j = max(0, it - kSt); j < it; ++j)
+                sb_wait(&full[j % kSt], (unsigned(j) / kSt) & 1u, nullptr, err, 22);
         return;
     }
 
@@ -1103,24 +1109,85 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs
     for (int c = 0; c < CH; ++c)
         if (c * sp.kcu + ul < units) load_xunit<TYPE>(a.x, c * sp.kcu + ul, xu[c]);
     const Q4kSel sel(ul & 7);  // stage offsets are multiples of 8 units
+    // this warp's sums for the rows of stage st (one unit of K, four rows)
+    auto stage_dot = [&](int st, int c, float (&acc)[kRows1]) {
+        if (c * sp.kcu + ul < units) {
+            const unsigned char* q = st_qs + st * kStreamQs + (rs * 4 * sp.kcu + ul) * 16;
+            uint4 wv[kRows1];
+#pragma unroll
+            for (int r = 0; r < kRows1; ++r) wv[r] = *reinterpret_cast<const uint4*>(q + r * sp.kcu * 16);
+            rows_unit_dot_x<TYPE>(wv, xu[c], st_meta + st * kStreamMeta + rs * 4 * sp.kcu * MPU, sp.kcu * MPU, ul,
+                                  sel, acc);
+        }
+    };
+    // group g's rows from the warps' partial sums in red[slot] (one warp, lane = row)
+    auto group_out = [&](int g, int slot) {
+        float v = 0.f;
+        if (lane < sp.rg)
+            for (int w = 0; w < wpr; ++w) v += red[slot][(lane >> 2) * wpr + w][lane & 3];
+        const float partner = __shfl_down_sync(0xffffffffu, v, 1);
+        const int row = g * sp.rg + lane;
+        if (lane < sp.rg && row < a.w.rows) {
+            if (a.epilogue == kSwiGLU) {
+                if (!(lane & 1)) a.y[row / 2] = swiglu(v, partner);
+            } else if (a.epilogue == kAdd) {
+                a.y[row] += v;
+            } else {
+                a.y[row] = v;
+            }
+        }
+    };
+    const int mine = (sp.groups - 1 - int(blockIdx.x)) / int(gridDim.x) + 1;  // groups of this CTA
+    if (CH == 1 && mine <= kSt) {
+        // Every group of this CTA has a stage of its own, filled once (phase
+        // 0): take the stages in the order they land, keep each warp's sums
+        // per stage and reduce all the groups after one barrier.  A stage
+        // counts as landed when every lane has observed its barrier.
+        unsigned done = 0;
+        int left = mine;
+        for (unsigned spin = 0; left > 0;) {
+            bool moved = false;
+            for (int j = 0; j < mine; ++j) {
+                if ((done >> j) & 1u) continue;
+                if (!__all_sync(0xffffffffu, sb_try(&full[j], 0u))) continue;
+                float acc[kRows1] = {0.f, 0.f, 0.f, 0.f};
+                stage_dot(j, 0, acc);
+#pragma unroll
+                for (int r = 0; r < kRows1; ++r)
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+                if (lane == 0) {
+#pragma unroll
+                    for (int r = 0; r < kRows1; ++r) red[j][warp][r] = acc[r];
+                }
+                done |= 1u << j;
+                --left;
+                moved = true;
+            }
+            if (moved) continue;
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            if (++spin >= kStreamSpin) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(err, 23);
+                break;
+            }
+            __nanosleep(64);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kStreamSlots) : "memory");
+        if (warp < mine) group_out(int(blockIdx.x) + warp * int(gridDim.x), warp);
+        return;
+    }
     int it = 0, gi = 0;
     for (int g = blockIdx.x; g < sp.groups; g += gridDim.x, ++gi) {
         float acc[kRows1] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < CH; ++c, ++it) {
-            const int st = it % kStreamStages;
-            const unsigned ph = (unsigned(it) / kStreamStages) & 1u;
+            const int st = it % kSt;
+            const unsigned ph = (unsigned(it) / kSt) & 1u;
             // after an abort the warps keep the same steps (no early exit) so
             // every barrier below is still reached by all of them
             if (!*abort_flag) sb_wait(&full[st], ph, abort_flag, err, 23);
-            if (c * sp.kcu + ul < units) {
-                const unsigned char* q = st_qs + st * kStreamQs + (rs * 4 * sp.kcu + ul) * 16;
-                uint4 wv[kRows1];
-#pragma unroll
-                for (int r = 0; r < kRows1; ++r) wv[r] = *reinterpret_cast<const uint4*>(q + r * sp.kcu * 16);
-                rows_unit_dot_x<TYPE>(wv, xu[c], st_meta + st * kStreamMeta + rs * 4 * sp.kcu * MPU, sp.kcu * MPU,
-                                      ul, sel, acc);
-            }
+            stage_dot(st, c, acc);
             __syncwarp();
             if (lane == 0) sb_arrive(&empty[st]);
         }
@@ -1133,24 +1200,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_stream_kernel(GemmArgs
             for (int r = 0; r < kRows1; ++r) red[gi & 1][warp][r] = acc[r];
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kStreamSlots) : "memory");
-        if (warp == 0) {
-            // lane = row within the group; red is double-buffered by group, so
-            // the next group's partial sums do not overwrite these
-            float v = 0.f;
-            if (lane < sp.rg)
-                for (int w = 0; w < wpr; ++w) v += red[gi & 1][(lane >> 2) * wpr + w][lane & 3];
-            const float partner = __shfl_down_sync(0xffffffffu, v, 1);
-            const int row = g * sp.rg + lane;
-            if (lane < sp.rg && row < a.w.rows) {
-                if (a.epilogue == kSwiGLU) {
-                    if (!(lane & 1)) a.y[row / 2] = swiglu(v, partner);
-                } else if (a.epilogue == kAdd) {
-                    a.y[row] += v;
-                } else {
-                    a.y[row] = v;
-                }
-            }
-        }
+        // red is double-buffered by group, so the next group's partial sums
+        // do not overwrite these
+        if (warp == 0) group_out(g, gi & 1);
     }
 }
 
@@ -1184,7 +1236,7 @@ int gemv_sm_count() {
 template <int TYPE, int CH>
 bool launch_gemv_stream_ch(const GemmArgs& a, const StreamShape& sp, cudaStream_t s) {
     auto kernel = gemv_stream_kernel<TYPE, CH>;
-    constexpr int smem = kStreamStages * (kStreamQs + kStreamMeta);
+    constexpr int smem = stream_stages<TYPE>() * (kStreamQs + kStreamMeta);
     // a per-device attribute: set on every launch
     TVARA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     static const int per_sm = [&] {  // resident CTAs per SM (the same on every B200)
