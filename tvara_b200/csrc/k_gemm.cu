@@ -2055,27 +2055,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ4kpThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Small batches (5 .. 64 tokens) of Q4_K rows on mma.sync, straight from the
-// packed rows: the weights are read once per launch for all the tokens, the
-// activations (hi / lo FP16 with their per-token power of two, as the
-// tensor-core path splits them) pass through shared memory in chunks of
-// kSmallChunk elements.  A CTA is eight warps on 128 weight rows -- 16 per
-// warp -- and one slice of K (split K across CTAs so that the grid covers the
-// SMs; none for the SwiGLU epilogue, which needs whole sums).  Per 32-element
+// packed rows: the weights are read once per launch for all the tokens.
+//
+// Work comes in items of 128 weight rows x one chunk of K (small_ck<NT>()
+// elements, whole 256-element blocks: 512 up to 16 tokens, 256 above, so that
+// the stages fit in shared memory).  Where the epilogue allows it (not
+// SwiGLU, which needs whole sums) every chunk of K is an independent item
+// whose partial rows are added to y with atomics; for SwiGLU a CTA runs the
+// chunks of a row tile in order and stores the whole sums.  The grid is
+// persistent (the resident CTAs) and takes items in turn through a ring of
+// cp.async stages: everything an item reads -- the rows' packed codes,
+// sub-block scales, split minima, block scales and min shifts, the
+// activations' exact hi / lo FP16 split and their sub-block sums -- is copied
+// into its stage while earlier items compute, so a CTA waits on memory once
+// per launch rather than once per chunk.  The weights do not depend on the
+// previous kernel: the first item's are requested before the programmatic
+// launch wait, its activations after it.
+//
+// Compute (per warp: 16 rows; per lane: rows gq and gq + 8): per 32-element
 // sub-block a lane takes one 32-bit word of each of its two rows (bytes
 // 4tq .. 4tq + 3 of the row's 16 packed bytes: elements 4tq .. 4tq + 3 in the
-// low nibbles, 16 + 4tq .. in the high ones) from a register ring kept
-// kSmallDepth sub-blocks ahead, and builds the A fragments of both K-halves
-// from it, sc*q exact in FP16 as in tc_gemm_q4kp_kernel.  The fragment's K
-// order is a fixed permutation of the sub-block's (logical k 2tq + e <->
-// element 4tq + e, 2tq + 8 + e <-> element 4tq + 2 + e); the activations are
-// read with the same permutation, so every dot product is unchanged.  Each
-// 256-element block accumulates on its own and is added with its scale d;
-// the min term sum_sub dmin*m * sum(x) is F32 multiply-adds on the sub-block
-// sums.  Partial rows are added to y with atomics when K is split.
+// low nibbles, 16 + 4tq .. in the high ones) and builds the A fragments of
+// both K-halves from it, sc*q exact in FP16 as in tc_gemm_q4kp_kernel.  The
+// fragment's K order is a fixed permutation of the sub-block's (logical k
+// 2tq + e <-> element 4tq + e, 2tq + 8 + e <-> element 4tq + 2 + e); the
+// activations are read with the same permutation, so every dot product is
+// unchanged.  Each group of four sub-blocks accumulates on its own (in four
+// independent chains up to 16 tokens) and is added with its block's scale d.  The min term sum_sub dmin*m * sum(x) is
+// four more MMAs per item: the rows' exact hi / lo FP16 split of
+// dmin*m*2^shift against the tokens' hi / lo sub-block sums, K = the item's
+// sub-blocks.  Up to 16 tokens a CTA runs two warp groups, each on half of
+// an item's sub-blocks (the register budget allows it there), and the groups'
+// sums meet in shared memory before the output.
 constexpr int kSmallRows = 128;
 constexpr int kSmallThreads = 256;
-constexpr int kSmallChunk = 512;  // K elements of x staged at a time
-constexpr int kSmallDepth = 8;    // sub-blocks of packed words in flight per lane
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
     asm volatile(
@@ -2085,115 +2098,258 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const unsigned (&a)[4],
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-constexpr int small_xs(int chunk) { return chunk * 2 + 32; }  // bytes per token row (padded)
-// x hi / lo rows, the sub-block sums of x, and the chunk's min terms of the CTA's rows
-constexpr std::size_t small_smem_bytes(int nt) {
-    return std::size_t(8 * nt) * small_xs(kSmallChunk) * 2 + std::size_t(8 * nt) * (kSmallChunk / 32) * 4 +
-           std::size_t(kSmallRows) * (kSmallChunk / 32) * 4;
+// cp.async of 16 / 8 / 4 bytes; `valid` bytes are read from src (0: the
+// destination is zero-filled and src is not read).
+__device__ __forceinline__ void cpa16(void* dst, const void* src, unsigned valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid)
+                 : "memory");
 }
+__device__ __forceinline__ void cpa8(void* dst, const void* src, unsigned valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid)
+                 : "memory");
+}
+__device__ __forceinline__ void cpa4(void* dst, const void* src, unsigned valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid)
+                 : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int NT>
+constexpr int small_ck() { return NT <= 2 ? 512 : 256; }
+
+// One stage of the small-batch ring: byte offsets of its arrays.
+template <int NT>
+struct SmallStage {
+    static constexpr int CK = small_ck<NT>(), CU = CK / 32, CB = CK / 256, MT = 8 * NT;
+    static constexpr int WS = CU * 16 + 16;  // a row's codes, padded: conflict-free fragment loads
+    static constexpr int XS = CK * 2 + 32;   // a token's hi (or lo) activations, padded likewise
+    static constexpr int kCodes = 0;                                  // [rows][WS]
+    static constexpr int kX = kCodes + kSmallRows * WS;               // hi, then lo: [MT][XS] each
+    static constexpr int kSum = kX + 2 * MT * XS;                     // shi, then slo: [MT][CU] halves each
+    static constexpr int kMin = kSum + 2 * MT * CU * 2;               // qmin hi, then lo: [rows][CU] halves each
+    static constexpr int kSc = kMin + 2 * kSmallRows * CU * 2;        // [rows][CU] bytes
+    static constexpr int kD = kSc + kSmallRows * CU;                  // [rows][CB] floats
+    static constexpr int kShift = kD + kSmallRows * CB * 4;           // [rows] min shifts
+    static constexpr int kBytes = (kShift + kSmallRows + 127) / 128 * 128;
+    // as many stages (2..3) as fit beside one another in 220 KB
+    static constexpr int kStages = 3 * kBytes <= 220 * 1024 ? 3 : 2;
+};
+template <int NT>
+constexpr int small_groups() { return NT <= 2 ? 2 : 1; }  // warp groups of eight per CTA
+// the stages, then (two groups) the second group's partial sums [rows][MT]
+template <int NT>
+constexpr std::size_t small_smem_bytes() {
+    return std::size_t(SmallStage<NT>::kStages) * SmallStage<NT>::kBytes +
+           (small_groups<NT>() > 1 ? std::size_t(kSmallRows) * 8 * NT * 4 : 0);
+}
+template <int NT>
+constexpr int small_log2(int v) { return v <= 1 ? 0 : 1 + small_log2<NT>(v / 2); }
+
+struct SmallWork {
+    int row_tiles;    // 128-row tiles
+    int pairs;        // row tiles x K slices
+    int slice_units;  // sub-blocks per K slice (whole blocks)
+    int chunks;       // items per (row tile, slice)
+};
 
 template <int NT>  // 8-token tiles: up to 8 * NT tokens
-__global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMatrix w, const __half* xhi,
-                                                                      const __half* xlo, const int* xshift,
-                                                                      const __half* shi, const __half* slo, int tokens,
-                                                                      int kslice, float* y, int ldy, int epilogue,
-                                                                      int atomic) {
-    constexpr int MT = 8 * NT;
-    constexpr int XS = small_xs(kSmallChunk);
-    constexpr int CU = kSmallChunk / 32;  // sub-blocks per chunk
-    extern __shared__ __align__(16) unsigned char small_smem[];
-    unsigned char* xh_s = small_smem;
-    unsigned char* xl_s = xh_s + MT * XS;
-    float* sx_s = reinterpret_cast<float*>(xl_s + MT * XS);  // [MT][CU] sub-block sums (x 2^(shift - 5))
-    float* mn_s = sx_s + MT * CU;                             // [rows][CU] dmin*m * 32 of the CTA's rows
+__global__ void __launch_bounds__(kSmallThreads * small_groups<NT>(), 1) gemm_small_q4k_kernel(DeviceMatrix w, const __half* xhi,
+                                                                         const __half* xlo, const int* xshift,
+                                                                         const __half* shi, const __half* slo,
+                                                                         int tokens, SmallWork wk, float* y, int ldy,
+                                                                         int epilogue, int atomic) {
+    using S = SmallStage<NT>;
+    constexpr int MT = S::MT, CU = S::CU, CB = S::CB, WS = S::WS, XS = S::XS, NS = S::kStages;
+    constexpr int G = small_groups<NT>(), TH = kSmallThreads * G, LMT = small_log2<NT>(MT);
+    extern __shared__ __align__(128) unsigned char small_smem[];
     const int units = w.cols / 32, kblocks = w.cols / 256;
-    const int u0 = blockIdx.y * (kslice / 32);  // first sub-block of this CTA
-    const int su = kslice / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
-    const int row_a = blockIdx.x * kSmallRows + warp * 16 + gq, row_b = row_a + 8;
-    const bool live_a = row_a < w.rows, live_b = row_b < w.rows;
-    const long long ra = live_a ? row_a : 0, rb = live_b ? row_b : 0;
-    const unsigned* qa = reinterpret_cast<const unsigned*>(w.qs + ra * (long long)w.qs_row + u0 * 16 + 4 * tq);
-    const unsigned* qb = reinterpret_cast<const unsigned*>(w.qs + rb * (long long)w.qs_row + u0 * 16 + 4 * tq);
-    const unsigned char* sca = w.qsc + ra * units + u0;
-    const unsigned char* scb = w.qsc + rb * units + u0;
-    float tot[NT][4], blk[NT][4];
+    const int mine = wk.pairs > int(blockIdx.x) ? (wk.pairs - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+    const int n_items = mine * wk.chunks;
+
+    // Items in the order this CTA takes them: its (row tile, slice) pairs
+    // blockIdx.x, + gridDim.x, ..., each as `chunks` consecutive chunks.  A
+    // cursor walks them without divisions; one runs ahead for the copies.
+    struct Cursor {
+        int rt, sp, c;
+        __device__ void next(const SmallWork& wk) {
+            if (++c < wk.chunks) return;
+            c = 0;
+            rt += int(gridDim.x);
+            while (rt >= wk.row_tiles) {
+                rt -= wk.row_tiles;
+                ++sp;
+            }
+        }
+    };
+    struct Item {
+        int row0, u_begin, cu;
+        bool first, last;
+    };
+    auto item = [&](const Cursor& k) {
+        const int lo = k.sp * wk.slice_units, hi = min(lo + wk.slice_units, units);
+        Item it;
+        it.row0 = k.rt * kSmallRows;
+        it.u_begin = lo + k.c * CU;
+        it.cu = min(CU, hi - it.u_begin);  // 8 or 16 (whole blocks)
+        it.first = k.c == 0;
+        it.last = k.c == wk.chunks - 1;
+        return it;
+    };
+    // the weight-side copies of an item into stage st: each thread keeps one
+    // 16-byte column of the rows and steps down them
+    auto issue_weights = [&](const Item& it, int st) {
+        unsigned char* b = small_smem + st * S::kBytes;
+        {
+            const int lg = it.cu == 16 ? 4 : 3, k = threadIdx.x & (it.cu - 1), rp = TH >> lg;
+            int r = threadIdx.x >> lg;
+            const unsigned char* src = w.qs + (long long)(it.row0 + r) * (long long)w.qs_row + (it.u_begin + k) * 16;
+            unsigned char* dst = b + S::kCodes + r * WS + k * 16;
+            const long long step = (long long)rp * (long long)w.qs_row;
+            for (; r < kSmallRows; r += rp, src += step, dst += rp * WS) {
+                const bool ok = it.row0 + r < w.rows;
+                cpa16(dst, ok ? src : w.qs, ok ? 16u : 0u);
+            }
+        }
+        {
+            const int c8 = it.cu >> 3, k = threadIdx.x & (c8 - 1), r = threadIdx.x >> (c8 - 1);
+            if (r < kSmallRows) {  // TH / c8 >= 128: one piece per array and thread at most
+                const int row = it.row0 + r;
+                const bool ok = row < w.rows;
+                const long long off = (long long)(ok ? row : 0) * units + it.u_begin + 8 * k;
+                cpa8(b + S::kSc + r * CU + 8 * k, w.qsc + off, ok ? 8u : 0u);
+                cpa16(b + S::kMin + (r * CU + 8 * k) * 2, w.qmin_hi + off, ok ? 16u : 0u);
+                cpa16(b + S::kMin + (kSmallRows * CU + r * CU + 8 * k) * 2, w.qmin_lo + off, ok ? 16u : 0u);
+                cpa4(b + S::kD + (r * CB + k) * 4,
+                     w.qscale + (long long)(ok ? row : 0) * kblocks + it.u_begin / 8 + k, ok ? 4u : 0u);
+            }
+        }
+        if (threadIdx.x < kSmallRows / 4) {
+            const int r = 4 * threadIdx.x;
+            const int have = max(0, min(4, w.rows - (it.row0 + r)));
+            cpa4(b + S::kShift + r, w.qmin_shift + (have ? it.row0 + r : 0), unsigned(have));
+        }
+    };
+    // the activation-side copies of an item into stage st (rows: hi tokens, then lo)
+    auto issue_acts = [&](const Item& it, int st) {
+        unsigned char* b = small_smem + st * S::kBytes;
+        {
+            const int lp = it.cu == 16 ? 6 : 5;  // 16-byte pieces per token row: cu * 4
+            const int k = threadIdx.x & ((1 << lp) - 1), rp = TH >> lp;
+            for (int q = threadIdx.x >> lp; q < 2 * MT; q += rp) {
+                const int part = q >> LMT, t = q & (MT - 1);
+                const bool ok = t < tokens;
+                const __half* src = (part ? xlo : xhi) + (long long)(ok ? t : 0) * w.cols + it.u_begin * 32 + 8 * k;
+                cpa16(b + S::kX + q * XS + 16 * k, src, ok ? 16u : 0u);
+            }
+        }
+        {
+            const int c8 = it.cu >> 3, k = threadIdx.x & (c8 - 1), q = threadIdx.x >> (c8 - 1);
+            if (q < 2 * MT) {
+                const int part = q >> LMT, t = q & (MT - 1);
+                const bool ok = t < tokens;
+                const __half* src = (part ? slo : shi) + (long long)(ok ? t : 0) * units + it.u_begin + 8 * k;
+                cpa16(b + S::kSum + (q * CU + 8 * k) * 2, src, ok ? 16u : 0u);
+            }
+        }
+    };
+
+    // prologue: item 0's weights before the wait on the previous kernel, its
+    // activations after it; then the rest of the ring
+    Cursor ic{int(blockIdx.x) % wk.row_tiles, int(blockIdx.x) / wk.row_tiles, 0};
+    Cursor cc = ic;
+    int issued = 0;
+    if (issued < n_items) issue_weights(item(ic), 0);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (issued < n_items) {
+        issue_acts(item(ic), 0);
+        ic.next(wk);
+        ++issued;
+    }
+    cpa_commit();
+#pragma unroll
+    for (int s = 1; s < NS - 1; ++s) {
+        if (issued < n_items) {
+            const Item it = item(ic);
+            issue_weights(it, s);
+            issue_acts(it, s);
+            ic.next(wk);
+            ++issued;
+        }
+        cpa_commit();
+    }
+    float xs[NT][2];  // 2^-shift of the lane's output tokens
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) tot[n][e] = blk[n][e] = 0.f;
-    unsigned ring_a[kSmallDepth], ring_b[kSmallDepth];
-#pragma unroll
-    for (int i = 0; i < kSmallDepth; ++i) {
-        ring_a[i] = i < su ? __ldg(qa + 4 * i) : 0u;
-        ring_b[i] = i < su ? __ldg(qb + 4 * i) : 0u;
-    }
-    // sub-block scales of the next eight sub-blocks (one block), a group ahead
-    uint2 sc_a = live_a ? __ldg(reinterpret_cast<const uint2*>(sca)) : make_uint2(0, 0);
-    uint2 sc_b = live_b ? __ldg(reinterpret_cast<const uint2*>(scb)) : make_uint2(0, 0);
-    for (int c0 = 0; c0 < su; c0 += CU) {  // one chunk of x at a time
-        const int cu = min(CU, su - c0);
-        __syncthreads();  // the previous chunk is no longer read
-        for (int i = threadIdx.x; i < MT * (cu * 4); i += blockDim.x) {
-            const int t = i / (cu * 4), c = i % (cu * 4);
-            uint4 h = make_uint4(0, 0, 0, 0), l = h;
-            if (t < tokens) {
-                const long long off = (long long)t * w.cols + (u0 + c0) * 32 + 8 * c;
-                h = *reinterpret_cast<const uint4*>(xhi + off);
-                l = *reinterpret_cast<const uint4*>(xlo + off);
-            }
-            *reinterpret_cast<uint4*>(xh_s + t * XS + 16 * c) = h;
-            *reinterpret_cast<uint4*>(xl_s + t * XS + 16 * c) = l;
+        for (int e = 0; e < 2; ++e) {
+            const int t = 8 * n + 2 * tq + e;
+            xs[n][e] = t < tokens ? pow2(-__ldg(xshift + t)) : 0.f;
         }
-        for (int i = threadIdx.x; i < MT * cu; i += blockDim.x) {
-            const int t = i / cu, u = i % cu;
-            const long long off = (long long)t * units + u0 + c0 + u;
-            sx_s[t * CU + u] = t < tokens ? __half2float(shi[off]) + __half2float(slo[off]) : 0.f;
+
+    const int wg = warp >> 3;                           // warp group
+    const int la = (warp & 7) * 16 + gq, lb = la + 8;  // the lane's rows within the tile
+    float* red = reinterpret_cast<float*>(small_smem + NS * S::kBytes);  // [rows][MT] (two groups)
+    float tot[NT][4];
+    for (int j = 0; j < n_items; ++j) {
+        cpa_wait<NS - 2>();
+        __syncthreads();  // item j's stage is complete; the stage refilled below is no longer read
+        if (issued < n_items) {  // item j + NS - 1
+            const Item nx = item(ic);
+            issue_weights(nx, (j + NS - 1) % NS);
+            issue_acts(nx, (j + NS - 1) % NS);
+            ic.next(wk);
+            ++issued;
         }
-        // the min terms of this chunk, for all the CTA's rows (off the sub-block loop's critical path):
-        // thread (row, 8 sub-blocks) issues its three loads at once
-        for (int i = threadIdx.x; i < kSmallRows * (cu / 8); i += blockDim.x) {
-            const int rr = i / (cu / 8), g = i % (cu / 8);
-            const long long row = (long long)blockIdx.x * kSmallRows + rr;
-            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (row < w.rows) {
-                const long long off = row * units + u0 + c0 + 8 * g;  // a multiple of 8: 16-byte aligned
-                const uint4 hi = __ldg(reinterpret_cast<const uint4*>(w.qmin_hi + off));
-                const uint4 lo = __ldg(reinterpret_cast<const uint4*>(w.qmin_lo + off));
-                const float f = pow2(-w.qmin_shift[row]) * 32.f;
-                const unsigned hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+        cpa_commit();
+
+        const Item it = item(cc);
+        cc.next(wk);
+        const unsigned char* b = small_smem + (j % NS) * S::kBytes;
+        const unsigned char* codes = b + S::kCodes;
+        const unsigned char* xh_s = b + S::kX;
+        const unsigned char* xl_s = b + S::kX + MT * XS;
+        if (it.first) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const unsigned short hh = (unsigned short)(hw[k >> 1] >> (16 * (k & 1)));
-                    const unsigned short ll = (unsigned short)(lw[k >> 1] >> (16 * (k & 1)));
-                    v[k] = (__half2float(__ushort_as_half(hh)) + __half2float(__ushort_as_half(ll))) * f;
-                }
-            }
+            for (int n = 0; n < NT; ++n)
 #pragma unroll
-            for (int k = 0; k < 8; ++k) mn_s[rr * CU + 8 * g + k] = v[k];
+                for (int e = 0; e < 4; ++e) tot[n][e] = 0.f;
         }
-        __syncthreads();
-        for (int uu = 0; uu < cu; uu += kSmallDepth) {
-            const uint2 ga = sc_a, gbk = sc_b;  // this group's scales; the next group's are loaded now
-            const float da = live_a ? w.qscale[ra * kblocks + ((u0 + c0 + uu) >> 3)] : 0.f;
-            const float db = live_b ? w.qscale[rb * kblocks + ((u0 + c0 + uu) >> 3)] : 0.f;
-            if (c0 + uu + kSmallDepth < su) {
-                sc_a = live_a ? __ldg(reinterpret_cast<const uint2*>(sca + c0 + uu + kSmallDepth)) : make_uint2(0, 0);
-                sc_b = live_b ? __ldg(reinterpret_cast<const uint2*>(scb + c0 + uu + kSmallDepth)) : make_uint2(0, 0);
-            }
+        const int half = it.cu / G;  // this group's sub-blocks: [wg * half, (wg + 1) * half)
+        for (int u4 = wg * half; u4 < (wg + 1) * half; u4 += 4) {
+            const int bk = u4 >> 3;  // the sub-blocks' 256-element block
+            const float da = reinterpret_cast<const float*>(b + S::kD)[la * CB + bk];
+            const float db = reinterpret_cast<const float*>(b + S::kD)[lb * CB + bk];
+            const unsigned ga = *reinterpret_cast<const unsigned*>(b + S::kSc + la * CU + u4);
+            const unsigned gbk = *reinterpret_cast<const unsigned*>(b + S::kSc + lb * CU + u4);
+            // NA independent accumulator chains per token tile (hi / lo part x
+            // sub-block parity) when there are too few tiles to hide the MMA latency
+            constexpr int NA = NT <= 2 ? 4 : 1;
+            float blk[NA][NT][4];
 #pragma unroll
-            for (int i = 0; i < kSmallDepth; ++i) {
-                const int u = c0 + uu + i;  // sub-block within the CTA's slice
-                const unsigned wa = ring_a[i], wb = ring_b[i];
-                const int nxt = u + kSmallDepth;
-                ring_a[i] = nxt < su ? __ldg(qa + 4 * nxt) : 0u;
-                ring_b[i] = nxt < su ? __ldg(qb + 4 * nxt) : 0u;
-                const unsigned sa = ((i < 4 ? ga.x : ga.y) >> (8 * (i & 3))) & 255u;
-                const unsigned sb = ((i < 4 ? gbk.x : gbk.y) >> (8 * (i & 3))) & 255u;
-                const __half2 sa2 = __half2half2(__uint2half_rn(sa)), sb2 = __half2half2(__uint2half_rn(sb));
-                const __half2 oa2 = __hneg2(__half2half2(__uint2half_rn(1024u * sa)));
-                const __half2 ob2 = __hneg2(__half2half2(__uint2half_rn(1024u * sb)));
+            for (int c = 0; c < NA; ++c)
+#pragma unroll
+                for (int n = 0; n < NT; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) blk[c][n][e] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int u = u4 + i;  // sub-block within the item
+                const unsigned wa = *reinterpret_cast<const unsigned*>(codes + la * WS + u * 16 + 4 * tq);
+                const unsigned wb = *reinterpret_cast<const unsigned*>(codes + lb * WS + u * 16 + 4 * tq);
+                // sc (below 64) in both halves: 0x64xx = 1024 + sc exactly, minus 1024
+                const __half2 k1024 = __half2half2(__ushort_as_half(0x6400)), km1024 = __hneg2(k1024);
+                const unsigned qa = __byte_perm(ga, 0x64646464u, 0x4040u + 0x0101u * i);
+                const unsigned qb = __byte_perm(gbk, 0x64646464u, 0x4040u + 0x0101u * i);
+                const __half2 sa2 = __hsub2(*reinterpret_cast<const __half2*>(&qa), k1024);
+                const __half2 sb2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1024);
+                const __half2 oa2 = __hmul2(sa2, km1024), ob2 = __hmul2(sb2, km1024);
 #pragma unroll
                 for (int hk = 0; hk < 2; ++hk) {  // low nibbles: elements 0..15, high: 16..31
                     const unsigned ma = hk ? (wa >> 4) & 0x0F0F0F0Fu : wa & 0x0F0F0F0Fu;
@@ -2209,59 +2365,99 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q4k_kernel(DeviceMat
                     a[1] = *reinterpret_cast<const unsigned*>(&h1);  // row gq + 8
                     a[2] = *reinterpret_cast<const unsigned*>(&h2);  // row gq, elements 4tq + 2, 4tq + 3
                     a[3] = *reinterpret_cast<const unsigned*>(&h3);
-                    const int koff = ((uu + i) * 32 + 16 * hk + 4 * tq) * 2;
+                    const int koff = (u * 32 + 16 * hk + 4 * tq) * 2;
 #pragma unroll
                     for (int n = 0; n < NT; ++n) {
                         const uint2 bh = *reinterpret_cast<const uint2*>(xh_s + (8 * n + gq) * XS + koff);
                         const uint2 bl = *reinterpret_cast<const uint2*>(xl_s + (8 * n + gq) * XS + koff);
-                        mma_16816(blk[n], a, bh.x, bh.y);
-                        mma_16816(blk[n], a, bl.x, bl.y);
-                    }
-                }
-                if (i == kSmallDepth - 1) {  // end of a 256-element block: add it with its scale d
-#pragma unroll
-                    for (int n = 0; n < NT; ++n) {
-                        tot[n][0] = fmaf(da, blk[n][0], tot[n][0]);
-                        tot[n][1] = fmaf(da, blk[n][1], tot[n][1]);
-                        tot[n][2] = fmaf(db, blk[n][2], tot[n][2]);
-                        tot[n][3] = fmaf(db, blk[n][3], tot[n][3]);
-                        blk[n][0] = blk[n][1] = blk[n][2] = blk[n][3] = 0.f;
+                        mma_16816(blk[NA > 1 ? 2 * (i & 1) : 0][n], a, bh.x, bh.y);
+                        mma_16816(blk[NA > 1 ? 2 * (i & 1) + 1 : 0][n], a, bl.x, bl.y);
                     }
                 }
             }
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float v = blk[0][n][e];
+#pragma unroll
+                    for (int c = 1; c < NA; ++c) v += blk[c][n][e];
+                    tot[n][e] = fmaf(e < 2 ? da : db, v, tot[n][e]);
+                }
         }
-        // min term of this chunk: - sum_sub dmin*m * sum(x) (sums are x 2^(shift - 5): times 32)
-        for (int u = 0; u < cu; ++u) {
-            const float ma = mn_s[(warp * 16 + gq) * CU + u], mb = mn_s[(warp * 16 + gq + 8) * CU + u];
+        if (wg == 0) {
+            // min term: - 2^-shift * 32 * sum_sub (hi + lo)(dmin*m*2^shift) * (hi + lo)(sum x * 2^(xshift - 5)),
+            // one m16n8k16 per pair of parts with K = the item's sub-blocks (the upper eight are zero
+            // when the item has eight)
+            const signed char* shf = reinterpret_cast<const signed char*>(b + S::kShift);
+            const float fa = pow2(-shf[la]) * 32.f, fb = pow2(-shf[lb]) * 32.f;
+            const unsigned char* mhi = b + S::kMin;
+            const unsigned char* mlo = mhi + kSmallRows * CU * 2;
+            const unsigned char* sh = b + S::kSum;
+            const unsigned char* sl = sh + MT * CU * 2;
+            const bool upper = CU == 16 && it.cu == 16;
+            auto word = [&](const unsigned char* base, int r, int u, bool ok) {
+                return ok ? *reinterpret_cast<const unsigned*>(base + (r * CU + u) * 2) : 0u;
+            };
+            const unsigned ah[4] = {word(mhi, la, 2 * tq, true), word(mhi, lb, 2 * tq, true),
+                                    word(mhi, la, 2 * tq + 8, upper), word(mhi, lb, 2 * tq + 8, upper)};
+            const unsigned al[4] = {word(mlo, la, 2 * tq, true), word(mlo, lb, 2 * tq, true),
+                                    word(mlo, la, 2 * tq + 8, upper), word(mlo, lb, 2 * tq + 8, upper)};
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-                const float s0 = sx_s[(8 * n + 2 * tq) * CU + u], s1 = sx_s[(8 * n + 2 * tq + 1) * CU + u];
-                tot[n][0] = fmaf(-ma, s0, tot[n][0]);
-                tot[n][1] = fmaf(-ma, s1, tot[n][1]);
-                tot[n][2] = fmaf(-mb, s0, tot[n][2]);
-                tot[n][3] = fmaf(-mb, s1, tot[n][3]);
+                const int t = 8 * n + gq;
+                const unsigned bh0 = word(sh, t, 2 * tq, true), bh1 = word(sh, t, 2 * tq + 8, upper);
+                const unsigned bl0 = word(sl, t, 2 * tq, true), bl1 = word(sl, t, 2 * tq + 8, upper);
+                float m[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_16816(m, ah, bh0, bh1);
+                mma_16816(m, ah, bl0, bl1);
+                mma_16816(m, al, bh0, bh1);
+                mma_16816(m, al, bl0, bl1);
+                tot[n][0] = fmaf(-fa, m[0], tot[n][0]);
+                tot[n][1] = fmaf(-fa, m[1], tot[n][1]);
+                tot[n][2] = fmaf(-fb, m[2], tot[n][2]);
+                tot[n][3] = fmaf(-fb, m[3], tot[n][3]);
             }
         }
+        if (!it.last) continue;
+        if (G > 1) {  // the second group's sums join the first's
+            if (wg == 1) {
+#pragma unroll
+                for (int n = 0; n < NT; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        red[(e < 2 ? la : lb) * MT + 8 * n + 2 * tq + (e & 1)] = tot[n][e];
+            }
+            __syncthreads();
+            if (wg == 1) continue;
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) tot[n][e] += red[(e < 2 ? la : lb) * MT + 8 * n + 2 * tq + (e & 1)];
+        }
+        // out: accumulator (row gq / gq + 8, tokens 8n + 2tq, + 1), scaled back by 2^-shift
+        const int row_a = it.row0 + la, row_b = it.row0 + lb;
+        const bool live_a = row_a < w.rows, live_b = row_b < w.rows;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = 8 * n + 2 * tq + (e & 1);
+                const bool rlive = e < 2 ? live_a : live_b;
+                const int row = e < 2 ? row_a : row_b;
+                const float v = tot[n][e] * xs[n][e & 1];
+                if (epilogue == kSwiGLU) {
+                    // rows (2i, 2i + 1) = (gate_i, up_i) sit in lanes gq and gq ^ 1 (4 lanes apart)
+                    const float other = __shfl_xor_sync(0xffffffffu, v, 4);
+                    if (rlive && t < tokens && !(gq & 1)) y[(long long)t * ldy + row / 2] = swiglu_12(v, other);
+                } else if (rlive && t < tokens) {
+                    float* dst = y + (long long)t * ldy + row;
+                    if (atomic || epilogue == kAdd) atomicAdd(dst, v);
+                    else *dst = v;
+                }
+            }
     }
-    // out: accumulator (row gq / gq + 8, tokens 8n + 2tq, + 1), scaled back by 2^-shift
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int t = 8 * n + 2 * tq + (e & 1);
-            const bool rlive = e < 2 ? live_a : live_b;
-            const int row = e < 2 ? row_a : row_b;
-            const float v = t < tokens ? tot[n][e] * pow2(-xshift[t]) : 0.f;
-            if (epilogue == kSwiGLU) {
-                // rows (2i, 2i + 1) = (gate_i, up_i) sit in lanes gq and gq ^ 1 (4 lanes apart)
-                const float other = __shfl_xor_sync(0xffffffffu, v, 4);
-                if (rlive && t < tokens && !(gq & 1)) y[(long long)t * ldy + row / 2] = swiglu_12(v, other);
-            } else if (rlive && t < tokens) {
-                float* dst = y + (long long)t * ldy + row;
-                if (atomic || epilogue == kAdd) atomicAdd(dst, v);
-                else *dst = v;
-            }
-        }
+    cpa_wait<0>();  // no copy is left in flight when the CTA exits
 }
 
 // ---------------------------------------------------------------------------
@@ -2463,6 +2659,9 @@ __global__ void __launch_bounds__(kSmallThreads) gemm_small_q8_kernel(DeviceMatr
 // aligned, which the launcher checks).
 __global__ void split_kernel(const float* x, int ldx, int K, __half* hi, __half* lo, int* shift, __half* shi,
                              __half* slo) {
+    // a programmatically launched projection may start its weight copies now;
+    // it reads these outputs only after its grid-dependency wait
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int t = blockIdx.x;
     const float4* row = reinterpret_cast<const float4*>(x + (long long)t * ldx);
     const int K4 = K / 4;
@@ -2637,6 +2836,28 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
     gemm_tc_split_buffers(workspace, workspace_bytes, T, K, hi, lo, shift, &shi, &slo);
     // callers without an error flag get one in the workspace (never null)
     int* err = g.err ? g.err : shift + ((T + 63) / 64) * 64;
+    // small batches of packed Q4_K rows (gemm_small_q4k_kernel): the stages
+    // take 16- and 8-byte copies of the side arrays and activations
+    const auto a16 = [](const void* p) { return reinterpret_cast<std::uintptr_t>(p) % 16 == 0; };
+    const bool small_q4k = g.w.qsc && T <= 64 && g_small_batches && a16(g.w.qs) && g.w.qs_row % 16 == 0 &&
+                           a16(g.w.qsc) && a16(g.w.qmin_hi) && a16(g.w.qmin_lo) && a16(g.w.qscale) &&
+                           a16(g.w.qmin_shift) && a16(hi) && a16(lo) && a16(shi) && a16(slo);
+    SmallWork wk{};
+    if (small_q4k) {
+        const int nt = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
+        const int cb = nt <= 2 ? 2 : 1;  // blocks per chunk (small_ck)
+        const int blocks = K / 256, chunks = (blocks + cb - 1) / cb;
+        const bool split = g.epilogue != kSwiGLU;  // SwiGLU needs whole sums
+        wk.row_tiles = (g.w.rows + kSmallRows - 1) / kSmallRows;
+        wk.pairs = wk.row_tiles * (split ? chunks : 1);
+        wk.slice_units = split ? cb * 8 : K / 32;
+        wk.chunks = split ? 1 : chunks;
+        // split partial sums are added into y: zero it before the split kernel,
+        // so that the projection's predecessor on the stream is a kernel (its
+        // programmatic launch then overlaps the weight copies with the split)
+        if (split && chunks > 1 && g.epilogue == kStore)
+            TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
+    }
     if (!g.presplit) {
         if (reinterpret_cast<std::uintptr_t>(g.x) % 16 || g.ldx % 4 || K % 4)
             throw std::invalid_argument("tensor-core projection input must be 16-byte aligned rows");
@@ -2644,26 +2865,36 @@ void launch_gemm_tc(const GemmArgs& g, void* workspace, std::size_t workspace_by
         TVARA_LAUNCHED();
     }
 
-    if (g.w.qsc && T <= 64 && g_small_batches) {
+    if (small_q4k) {
         // small batches: packed Q4_K rows on mma.sync, weights read once for all tokens
         const int nt = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
-        const int row_tiles = (g.w.rows + kSmallRows - 1) / kSmallRows;
-        const int blocks = K / 256;
-        int splits = 1;
-        if (g.epilogue != kSwiGLU)
-            while (splits * 2 <= blocks && blocks % (splits * 2) == 0 && row_tiles * splits < 3 * sm_count()) splits *= 2;
-        if (splits > 1 && g.epilogue == kStore)
-            TVARA_CUDA(cudaMemset2DAsync(g.y, std::size_t(g.ldy) * 4, 0, std::size_t(g.w.rows) * 4, T, s));
-        const dim3 grid(row_tiles, splits);
-        const int kslice = K / splits;
-        const int smem = int(small_smem_bytes(nt));
+        const int atomic = wk.pairs > wk.row_tiles;
         switch (nt) {
 #define TVARA_SMALL(N)                                                                                             \
-    case N:                                                                                                        \
-        TVARA_CUDA(cudaFuncSetAttribute(gemm_small_q4k_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
-        gemm_small_q4k_kernel<N><<<grid, kSmallThreads, smem, s>>>(g.w, hi, lo, shift, shi, slo, T, kslice, g.y, g.ldy, \
-                                                                   g.epilogue, splits > 1);                        \
-        break;
+    case N: {                                                                                                      \
+        auto kernel = gemm_small_q4k_kernel<N>;                                                                    \
+        constexpr int smem = int(small_smem_bytes<N>());                                                           \
+        TVARA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));               \
+        static const int per_sm = [&] {                                                                            \
+            int n = 0;                                                                                             \
+            TVARA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kSmallThreads * small_groups<N>(), smem)); \
+            return n > 0 ? n : 1;                                                                                  \
+        }();                                                                                                       \
+        cudaLaunchConfig_t cfg = {};                                                                               \
+        cfg.gridDim = dim3(std::min(wk.pairs, sm_count() * per_sm));                                               \
+        cfg.blockDim = dim3(kSmallThreads * small_groups<N>());                                                    \
+        cfg.dynamicSmemBytes = smem;                                                                               \
+        cfg.stream = s;                                                                                            \
+        cudaLaunchAttribute attr[1];                                                                               \
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                           \
+        attr[0].val.programmaticStreamSerializationAllowed = 1;                                                    \
+        cfg.attrs = attr;                                                                                          \
+        cfg.numAttrs = 1;                                                                                          \
+        TVARA_CUDA(cudaLaunchKernelEx(&cfg, kernel, g.w, (const __half*)hi, (const __half*)lo, (const int*)shift,  \
+                                      (const __half*)shi, (const __half*)slo, T, wk, g.y, g.ldy, g.epilogue,       \
+                                      atomic));                                                                    \
+        break;                                                                                                     \
+    }
             TVARA_SMALL(1)
             TVARA_SMALL(2)
             TVARA_SMALL(4)
