@@ -134,6 +134,21 @@ def test_iter_tokens_reproduce_reference_golden(tiny, name):
     assert toks == g[name].tolist()
 
 
+def test_greedy_fast_path_matches_sampler_path(tiny):
+    """Plain greedy generation (temperature 0, default penalties, no
+    constraint) runs one tvara_batch_step per token with the device's
+    finite-checked argmax; the general path (tvara_batch_sample) gives the
+    same tokens, and both stop at the same EOS."""
+    prompt = [int(t) for t in np.random.default_rng(4).integers(0, tiny.vocab_size, 37)]
+    fast = tiny.generate(prompt, max_new_tokens=48)
+    slow = list(tiny._iter_tokens_device(prompt, 48, 0.0, None, None, 1.0, 0, 0.0, 1.0, 0.0, 0.0, None))
+    assert fast == slow and len(fast) == 48
+    eos = fast[20]
+    stop = fast.index(eos) + 1
+    assert tiny.generate(prompt, max_new_tokens=48, eos_id=eos) == fast[:stop]
+    assert tiny.generate(prompt, max_new_tokens=0) == []
+
+
 def test_iter_tokens_argument_errors(tiny):
     """The reference's checks and texts (python/tvara/native.py:220-262)."""
     cases = [(dict(prompt=[]), "Invalid prompt token IDs"), (dict(prompt=[True]), "Invalid prompt token IDs"),

@@ -472,9 +472,47 @@ class NativeModel:
         if not (s.temperature == 0 or 1 <= s.top_k <= SAMPLE_MAX_K - SAMPLE_MARGIN):
             raise ValueError("device sampling needs temperature 0 or 1 <= top_k <= 48; use the reference "
                              "NativeModel on this library for other settings")
+        if s.temperature == 0 and token_constraint is None and (s.repetition, s.frequency, s.presence) == (1, 0, 0):
+            # plain greedy decoding: the adjusted logits are the logits, so the
+            # step's own finite-checked argmax is the token
+            yield from self._iter_greedy_device(s.prompt, s.max_new_tokens, s.eos_id)
+            return
         yield from self._iter_tokens_device(s.prompt, s.max_new_tokens, s.temperature, s.rng, s.eos_id, s.top_p,
                                             s.top_k, s.min_p, s.repetition, s.frequency, s.presence,
                                             token_constraint)
+
+    def _iter_greedy_device(self, prompt, max_new_tokens, eos_id):
+        """Greedy tokens with default penalties and no constraint: one
+        tvara_batch_step per token with the device argmax and its finiteness
+        check (STEP_FINITE_ARGMAX), into arrays allocated once, so only the
+        token crosses to the host.  Same tokens and errors as the sampler path
+        (python/tvara/native.py:301-336 at temperature 0)."""
+        sequence = self._new_sequence()
+        try:
+            seqs = np.array([sequence], dtype=np.uint64)
+            feed = np.ascontiguousarray(prompt, dtype=np.uint32)
+            cu = np.array([0, len(feed)], dtype=np.uint32)
+            nxt = np.zeros(1, dtype=np.uint32)
+            cu1 = np.array([0, 1], dtype=np.uint32)
+            am = np.empty(1, dtype=np.uint32)
+            p_seq, p_am = _ptr(seqs, U64P), _ptr(am, U32P)
+            p_cu, p_tok = _ptr(cu, U32P), _ptr(feed, U32P)
+            for index in range(max_new_tokens):
+                with self._lock:
+                    self._check_open()
+                    if self._library.tvara_batch_step(self._handle, 1, p_seq, p_cu, p_tok, STEP_FINITE_ARGMAX, None,
+                                                      0, p_am, 1):
+                        self._raise_error()
+                token = int(am[0])
+                if token == ARGMAX_NONFINITE:
+                    raise ValueError("Nonfinite model logits")
+                yield token
+                if token == eos_id or index + 1 == max_new_tokens:
+                    break
+                nxt[0] = token
+                p_cu, p_tok = _ptr(cu1, U32P), _ptr(nxt, U32P)
+        finally:
+            self._drop_sequence(sequence)
 
     def _iter_tokens_device(self, prompt, max_new_tokens, temperature, rng, eos_id, top_p, top_k, min_p, repetition,
                             frequency, presence, token_constraint):
