@@ -2147,8 +2147,7 @@ constexpr std::size_t small_smem_bytes() {
     return std::size_t(SmallStage<NT>::kStages) * SmallStage<NT>::kBytes +
            (small_groups<NT>() > 1 ? std::size_t(kSmallRows) * 8 * NT * 4 : 0);
 }
-template <int NT>
-constexpr int small_log2(int v) { return v <= 1 ? 0 : 1 + small_log2<NT>(v / 2); }
+constexpr int small_log2(int v) { return v <= 1 ? 0 : 1 + small_log2(v / 2); }
 
 struct SmallWork {
     int row_tiles;    // 128-row tiles
@@ -2165,7 +2164,7 @@ __global__ void __launch_bounds__(kSmallThreads * small_groups<NT>(), 1) gemm_sm
                                                                          int epilogue, int atomic) {
     using S = SmallStage<NT>;
     constexpr int MT = S::MT, CU = S::CU, CB = S::CB, WS = S::WS, XS = S::XS, NS = S::kStages;
-    constexpr int G = small_groups<NT>(), TH = kSmallThreads * G, LMT = small_log2<NT>(MT);
+    constexpr int G = small_groups<NT>(), TH = kSmallThreads * G, LMT = small_log2(MT);
     extern __shared__ __align__(128) unsigned char small_smem[];
     const int units = w.cols / 32, kblocks = w.cols / 256;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
